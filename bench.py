@@ -1,0 +1,376 @@
+"""Benchmark of the 3D deformable slide attention hot path (DeformableSlideAttention3D fwd+bwd).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+A "step" is one forward + backward of the module over one batch of synthetic tokens (loss =
+sum(y * G) with a fixed G).  The default workload is BASELINE config 2: B=2, T=64, H=W=32
+(131,072 tokens), C=1152, 16 heads x 72, window (3,7,7), bf16 activations with float32
+accumulation, offset-conv weights ~N(0, 0.05).  Under torchrun each rank runs that workload on its
+own GPU (weak scaling); the time is the max over ranks.
+
+Prints one JSON line (rank 0): value = Mtokens/s with inputs resident in HBM; e2e = the same
+through the module's public API with the input copied from pinned host memory and the loss read
+back every step; roofline of the dominant kernel timed live with CUDA events; clocks sampled by
+nvidia-smi during the timed region; cpu_baseline = the CPU oracle (oracle/) on a bounded sample.
+
+``--impl reference`` times the reference algorithm's CPU implementation instead (the oracle port,
+all host threads) on a bounded sample of the same workload; under torchrun only rank 0 works.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: B, T, H, W, C, nh, kernel, dtype, offset weight std
+    "c1": dict(B=1, T=8, H=16, W=16, C=256, nh=4, kernel=(3, 7, 7), dtype="float32", ostd=1e-2),
+    "c2": dict(B=2, T=64, H=32, W=32, C=1152, nh=16, kernel=(3, 7, 7), dtype="bfloat16", ostd=0.05),
+}
+METRIC = "3D-DSA fwd+bwd Mtokens/s"
+# reduced-volume sample of a config timed on the CPU (same C, heads, window; fewer frames)
+CPU_SAMPLE = {"c1": dict(B=1, T=8, H=16, W=16), "c2": dict(B=1, T=8, H=16, W=16)}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- CPU (oracle)
+def cpu_sample_step(cfg_name: str, threads: int):
+    """One fwd+bwd of the CPU oracle on the config's reduced-volume sample; returns (seconds, tokens)."""
+    import numpy as np
+
+    from oracle import dsa_oracle as O
+
+    O.set_num_threads(threads)
+    c = CONFIGS[cfg_name]
+    s = CPU_SAMPLE[cfg_name]
+    B, T, H, W = s["B"], s["T"], s["H"], s["W"]
+    C, nh, ks = c["C"], c["nh"], c["kernel"]
+    rng = np.random.default_rng(0)
+    K = ks[0] * ks[1] * ks[2]
+    lim = math.sqrt(6.0 / (2 * C))
+    params = {}
+    for nm in ("q_proj", "k_proj", "v_proj", "out_proj"):
+        params[nm + ".weight"] = rng.uniform(-lim, lim, (C, C))
+        params[nm + ".bias"] = np.zeros(C)
+    params["dw_conv.weight"] = rng.normal(0, 1 / math.sqrt(K), (C, 1, *ks))
+    params["dw_conv.bias"] = np.zeros(C)
+    params["offset_net.0.weight"] = rng.normal(0, 1 / math.sqrt(27), (C, 1, 3, 3, 3))
+    params["offset_net.0.bias"] = np.zeros(C)
+    params["offset_net.2.weight"] = rng.normal(0, c["ostd"], (nh * K * 3, C, 1, 1, 1))
+    params["offset_net.2.bias"] = np.zeros(nh * K * 3)
+    x = rng.normal(size=(B, T * H * W, C))
+    g = rng.normal(size=(B, T * H * W, C))
+    t0 = time.perf_counter()
+    _, cache = O.module_forward(params, x, (T, H, W), heads=nh, kernel_size=ks)
+    O.module_backward(cache, g)
+    return time.perf_counter() - t0, B * T * H * W
+
+
+def cpu_baseline(cfg_name: str, reps: int = 3):
+    threads = os.cpu_count() or 1
+    cpu_sample_step(cfg_name, threads)  # warm-up (page-in, thread pool)
+    times = []
+    for _ in range(reps):
+        dt, tok = cpu_sample_step(cfg_name, threads)
+        times.append(dt)
+    med = statistics.median(times)
+    s = CPU_SAMPLE[cfg_name]
+    return {"value": tok / med / 1e6, "unit": "Mtokens/s", "cores": threads, "kind": "port",
+            "sample": f"oracle/ (C + numpy float64) fwd+bwd of {cfg_name}'s C/heads/window on a reduced volume "
+                      f"B={s['B']} T={s['T']} H={s['H']} W={s['W']} ({tok} tokens), median of {reps} after 1 warm-up",
+            "seconds_per_sample": med}
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_sample_step(args.config, threads)
+    times = []
+    tok = 0
+    for _ in range(args.steps):
+        dt, tok = cpu_sample_step(args.config, threads)
+        times.append(dt)
+    total = sum(times)
+    value = tok * args.steps / total / 1e6
+    s = CPU_SAMPLE[args.config]
+    c = CONFIGS[args.config]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "Mtokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": _workload_name(args.config, c), "sample": f"B={s['B']} T={s['T']} H={s['H']} W={s['W']}"},
+        "cpu_baseline": {"value": value, "unit": "Mtokens/s", "cores": threads, "kind": "port",
+                         "sample": f"oracle/ fwd+bwd on {tok} tokens of {args.config}'s C/heads/window per step"},
+        "e2e": {"value": value, "unit": "Mtokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _workload_name(name, c):
+    return (f"{name}: DeformableSlideAttention3D fwd+bwd B={c['B']} T={c['T']} H={c['H']} W={c['W']} "
+            f"C={c['C']} heads={c['nh']}x{c['C'] // c['nh']} window={c['kernel']} {c['dtype']}")
+
+
+# ----------------------------------------------------------------------------- GPU
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v and "Not" not in v})
+        pw = [float(r[3]) for r in rows if r[3].strip().replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def _alg_bytes_per_token(name, C, nh, K, es):
+    """Algorithmic HBM bytes per token of one launch of each entry point (operands crossing the
+    entry point once; float32 accumulators inside msl_dsa_attn_bwd are scratch, not counted)."""
+    off = 4 * nh * K * 3
+    if name == "msl_dsa_attn_bwd":  # read q k v out dout offsets lse, write dq dk dv doffsets
+        return 5 * C * es + off + 4 * nh + 3 * C * es + off
+    if name == "msl_dsa_attn_fwd":  # read q k v offsets, write out lse
+        return 3 * C * es + off + C * es + 4 * nh
+    if name == "msl_dwconv3d_bwd_weight":  # read dy, x
+        return 2 * C * es
+    return 2 * C * es  # read x, write y
+
+
+def _flops_per_token(name, C, nh, K, d):
+    """CUDA-core float32 FLOPs per token of the gather kernels (corner dot products and value
+    interpolation: 8 corners x d MACs per K/V use)."""
+    if name == "msl_dsa_attn_fwd":
+        return nh * K * 8 * d * 2 * 2  # q.k_c and p*w*v_c
+    if name == "msl_dsa_attn_bwd":
+        return nh * K * 8 * d * 2 * 5  # q.k_c, dout.v_c, dq, dk, dv
+    return None
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    import megaslide_b200 as msl
+    from megaslide_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    c = CONFIGS[args.config]
+    B, T, H, W, C, nh, ks = c["B"], c["T"], c["H"], c["W"], c["C"], c["nh"], c["kernel"]
+    dt = getattr(torch, c["dtype"])
+    N = T * H * W
+    K = ks[0] * ks[1] * ks[2]
+    d = C // nh
+    es = 2 if dt == torch.bfloat16 else 4
+
+    torch.manual_seed(1234 + rank)
+    mod = msl.DeformableSlideAttention3D(C, nh, ks)
+    with torch.no_grad():
+        for p in (mod.offset_net[2].weight, mod.offset_net[2].bias):
+            p.normal_(0, c["ostd"])
+    mod = mod.to(dev, dt)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321 + rank)
+    x = torch.randn(B, N, C, device=dev, dtype=dt, generator=gen)
+    G = torch.randn(B, N, C, device=dev, dtype=dt, generator=gen)
+    params = list(mod.parameters())
+
+    def step(inp):
+        y = mod(inp, (T, H, W))
+        y.backward(G)
+        for p in params:
+            p.grad = None
+        return y
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(x)
+    barrier()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    n0 = msl.launch_count()
+    stream = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ops.kernel_timer() as rec:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(x)
+        e1.record(stream)
+    launches = msl.launch_count() - n0
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens = B * N * world
+    value = tokens * args.steps / (ms / 1e3) / 1e6
+
+    # per entry point device time inside the timed region
+    per = {}
+    for name, s, e in rec:
+        tot, cnt = per.get(name, (0.0, 0))
+        per[name] = (tot + s.elapsed_time(e), cnt + 1)
+    dom = max(per, key=lambda n: per[n][0])
+    dom_ms = per[dom][0] / per[dom][1]
+    hbm_peak, tc_peak, peak_kind = _peaks()
+    alg_bytes = _alg_bytes_per_token(dom, C, nh, K, es) * B * N
+    achieved = alg_bytes / (dom_ms / 1e3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        tj = json.loads(tfile.read_text()).get(dom, {}).get(args.config)
+        if tj:
+            traffic = float(tj["bytes_per_token"]) * B * N
+    roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+            "traffic": traffic, "kernel": dom, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+            "algorithmic_bytes_per_launch": alg_bytes, "launch_ms": dom_ms}
+    fl = _flops_per_token(dom, C, nh, K, d)
+    if fl:
+        clk = clocks.get("sm_mhz") or 1965.0
+        fp32_peak = 148 * 128 * 2 * clk * 1e6 / 1e12
+        ach = fl * B * N / (dom_ms / 1e3) / 1e12
+        roof["fp32_cuda_core"] = {"achieved": ach, "peak": fp32_peak, "unit": "TFLOP/s", "frac": ach / fp32_peak,
+                                  "peak_source": "nominal 148 SMs x 128 FMA/clk at the sampled median SM clock"}
+    kernels = {n: {"ms_per_launch": v[0] / v[1], "launches": v[1], "share": v[0] / sum(t for t, _ in per.values())}
+               for n, v in sorted(per.items(), key=lambda kv: -kv[1][0])}
+
+    e2e = None
+    if not args.no_e2e:
+        xh = x.detach().cpu().pin_memory()
+        xd = torch.empty_like(x)
+        loss_h = torch.empty(1, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            y = step(xd)
+            loss = (y.float() * G.float()).sum()
+            loss_h.copy_(loss.view(1), non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        ms2 = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms2], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms2 = float(t.item())
+        e2e = {"value": tokens * args.steps / (ms2 / 1e3) / 1e6, "unit": "Mtokens/s",
+               "h2d_bytes_per_step": xh.numel() * xh.element_size(), "d2h_bytes_per_step": 4,
+               "ms_per_step": ms2 / args.steps}
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.config)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "Mtokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if dt == torch.bfloat16 else "f32",
+            "data": "synthetic (seeded torch.randn tokens; random-init weights)",
+            "config": {"workload": _workload_name(args.config, c), "tokens_per_step": tokens,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": f"inputs larger than L2 (x = {x.numel() * x.element_size() / 1e6:.0f} MB per GPU)"},
+            "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": launches,
+            "kernels": kernels,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

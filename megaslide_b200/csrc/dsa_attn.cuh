@@ -1,0 +1,62 @@
+// Internal launch interface of the deformable-attention kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace msl {
+
+// Flattened, validated arguments of one attention call (host fills, kernels read by value).
+struct AttnParams {
+  int B, T, H, W, nh, d, kt, kh, kw, K, G;
+  int q_frame0, q_frames, kv_frame0, kv_frames;
+  int HW;
+  long long Nq, Nkv;  // rows per sample
+  int dtype;
+  float scale;        // softmax scale
+  float scale_log2;   // softmax scale * log2(e)
+  float oscale;       // offset scale
+  uint32_t drop_thresh;  // 0 = no dropout, else keep iff rng >= thresh (thresh = p * 2^32)
+  float drop_keep_scale; // 1 / (1 - p)
+  uint64_t seed;
+  // operands (element strides)
+  const void* q;  long long q_ld;
+  const void* k;  long long k_ld;
+  const void* v;  long long v_ld;
+  const float* offsets; long long off_ld;
+  const void* ek; const void* ev; long long e_ld;
+  void* out; long long out_ld;        // forward: written; backward: read
+  float* lse;
+  const void* dout; long long dout_ld;
+  void* dq; long long dq_ld;
+  float* dk_acc; float* dv_acc; long long acc_ld;
+  float* doffsets; long long doff_ld;
+  float* extra_ds; float* extra_p;   // [B, nh, Nq, G] scratch
+  float* dek; float* dev;            // [B, G, nh*d]
+  uint32_t* status;
+};
+
+bool attn_chunking(int dtype, int d, int* vec, int* maxc);
+cudaError_t launch_attn_fwd(const AttnParams& P, int vec, int maxc, cudaStream_t s);
+cudaError_t launch_attn_bwd(const AttnParams& P, int vec, int maxc, cudaStream_t s);
+cudaError_t launch_attn_extra_grad(const AttnParams& P, cudaStream_t s);
+
+// Depthwise 3D convolution (channels-last).
+struct ConvParams {
+  int B, T, H, W, C, kt, kh, kw;
+  int in_frame0, in_frames, out_frame0, out_frames;
+  int dtype;
+  int HW;
+};
+cudaError_t launch_dwconv_fwd(const ConvParams& P, const void* x, long long x_ld, const float* wt,
+                              const float* bias, const float* bias2, int epi, const void* aux,
+                              long long aux_ld, void* y, long long y_ld, bool flip, cudaStream_t s);
+cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long dy_ld, const void* x,
+                                long long x_ld, float* dw, float* db, cudaStream_t s);
+
+cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, int heads, int taps,
+                                  float oscale, float* out3, cudaStream_t s);
+cudaError_t launch_convert_f32(const float* src, long long src_ld, void* dst, long long dst_ld,
+                               int dtype, long long rows, long long cols, cudaStream_t s);
+
+}  // namespace msl

@@ -1,0 +1,302 @@
+// Depthwise 3D convolution over channels-last tokens, forward / input-gradient / weight-gradient,
+// plus the small utility kernels (offset magnitude reduction, float32 -> dtype conversion).
+//
+// Replaces nn.Conv3d(C, C, k, padding=k//2, groups=C) of the reference's dw_conv
+// (infinity/video/attention.py:58-65, 102) and offset_net[0] + GELU (attention.py:70-72, 105).
+// Tokens are [B, frames*H*W, C] rows (the layout x already has at attention.py:85), so no
+// [B, C, T, H, W] transpose is materialised (the reference does it at :99 and :190).
+
+#include <math.h>
+
+#include "dsa_attn.cuh"
+#include "msl_common.cuh"
+
+namespace msl {
+
+namespace {
+
+__device__ __forceinline__ float gelu_erf(float u) { return 0.5f * u * (1.f + erff(u * 0.70710678118654752f)); }
+
+__device__ __forceinline__ float gelu_erf_grad(float u) {
+  const float cdf = 0.5f * (1.f + erff(u * 0.70710678118654752f));
+  const float pdf = 0.39894228040143268f * expf(-0.5f * u * u);
+  return fmaf(u, pdf, cdf);
+}
+
+template <typename T, int CV>
+struct ChanVec;
+template <>
+struct ChanVec<float, 1> {
+  static __device__ __forceinline__ void load(const float* p, float (&o)[1]) { o[0] = __ldg(p); }
+  static __device__ __forceinline__ void store(float* p, const float (&o)[1]) { p[0] = o[0]; }
+};
+template <>
+struct ChanVec<float, 2> {
+  static __device__ __forceinline__ void load(const float* p, float (&o)[2]) {
+    const float2 v = __ldg(reinterpret_cast<const float2*>(p));
+    o[0] = v.x; o[1] = v.y;
+  }
+  static __device__ __forceinline__ void store(float* p, const float (&o)[2]) {
+    *reinterpret_cast<float2*>(p) = make_float2(o[0], o[1]);
+  }
+};
+template <>
+struct ChanVec<__nv_bfloat16, 1> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&o)[1]) { o[0] = __bfloat162float(p[0]); }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, const float (&o)[1]) { p[0] = __float2bfloat16_rn(o[0]); }
+};
+template <>
+struct ChanVec<__nv_bfloat16, 2> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&o)[2]) {
+    const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(p));
+    o[0] = bf16_lo(w); o[1] = bf16_hi(w);
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, const float (&o)[2]) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(o[0], o[1]);
+  }
+};
+
+}  // namespace
+
+// One thread per (output token, CV channels).  FLIP = transposed convolution (input gradient):
+// dx[p] = sum_taps w[tap] * dy[p - (tap - pad)].
+template <typename T, int CV, bool FLIP>
+__global__ void __launch_bounds__(256) dwconv_fwd_kernel(const ConvParams P, const T* __restrict__ x, long long x_ld,
+                                                         const float* __restrict__ wt, const float* __restrict__ bias,
+                                                         const float* __restrict__ bias2, int epi,
+                                                         const T* __restrict__ aux, long long aux_ld, T* __restrict__ y,
+                                                         long long y_ld) {
+  const int ncg = P.C / CV;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long rows_out = static_cast<long long>(P.out_frames) * P.HW;
+  const long long total = static_cast<long long>(P.B) * rows_out * ncg;
+  if (idx >= total) return;
+  const int cg = static_cast<int>(idx % ncg);
+  const long long pos = idx / ncg;
+  const int c = cg * CV;
+  const int b = static_cast<int>(pos / rows_out);
+  const long long row = pos - static_cast<long long>(b) * rows_out;
+  const int tl = static_cast<int>(row / P.HW);
+  const int rem = static_cast<int>(row - static_cast<long long>(tl) * P.HW);
+  const int h = rem / P.W, w = rem - (rem / P.W) * P.W;
+  const int tg = P.out_frame0 + tl;
+  const int pt = P.kt / 2, ph = P.kh / 2, pw = P.kw / 2;
+  const long long xb = static_cast<long long>(b) * P.in_frames * P.HW;
+
+  float acc[CV];
+#pragma unroll
+  for (int e = 0; e < CV; ++e) acc[e] = 0.f;
+  for (int it = 0; it < P.kt; ++it) {
+    const int ti = FLIP ? tg - it + pt : tg + it - pt;
+    if (ti < 0 || ti >= P.T) continue;
+    const int til = ti - P.in_frame0;
+    for (int ih = 0; ih < P.kh; ++ih) {
+      const int hi = FLIP ? h - ih + ph : h + ih - ph;
+      if (hi < 0 || hi >= P.H) continue;
+      const long long rbase = xb + (static_cast<long long>(til) * P.H + hi) * P.W;
+      const float* wrow = wt + static_cast<long long>((it * P.kh + ih) * P.kw) * P.C + c;
+      for (int iw = 0; iw < P.kw; ++iw) {
+        const int wi = FLIP ? w - iw + pw : w + iw - pw;
+        if (wi < 0 || wi >= P.W) continue;
+        float xv[CV];
+        ChanVec<T, CV>::load(x + (rbase + wi) * x_ld + c, xv);
+        const float* wp = wrow + static_cast<long long>(iw) * P.C;
+#pragma unroll
+        for (int e = 0; e < CV; ++e) acc[e] = fmaf(__ldg(wp + e), xv[e], acc[e]);
+      }
+    }
+  }
+  float out[CV];
+  const long long orow = static_cast<long long>(b) * rows_out + row;
+  float av[CV];
+  if (epi == MSL_EPI_GELU_GRAD) ChanVec<T, CV>::load(aux + orow * aux_ld + c, av);
+#pragma unroll
+  for (int e = 0; e < CV; ++e) {
+    float u = acc[e] + (bias ? __ldg(bias + c + e) : 0.f);
+    if (epi == MSL_EPI_GELU)
+      u = gelu_erf(u);
+    else if (epi == MSL_EPI_GELU_GRAD)
+      u = av[e] * gelu_erf_grad(u);
+    else if (bias2)
+      u += __ldg(bias2 + c + e);
+    out[e] = u;
+  }
+  ChanVec<T, CV>::store(y + orow * y_ld + c, out);
+}
+
+// Weight gradient: block = 32 channel lanes x (blockDim.y) tap groups; each thread owns one
+// (channel, tap) accumulator at a time and sums dy * shifted x over the block's token rows.
+// The extra tap index K accumulates the bias gradient (sum of dy).
+template <typename T>
+__global__ void __launch_bounds__(512) dwconv_wgrad_kernel(const ConvParams P, const T* __restrict__ dy, long long dy_ld,
+                                                           const T* __restrict__ x, long long x_ld, float* dw, float* db,
+                                                           int rows_per_block) {
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  const bool cvalid = c < P.C;
+  const int cc = cvalid ? c : 0;
+  const int K = P.kt * P.kh * P.kw;
+  const int ntap = db ? K + 1 : K;
+  const long long total_rows = static_cast<long long>(P.B) * P.out_frames * P.H;
+  const long long r0 = static_cast<long long>(blockIdx.y) * rows_per_block;
+  const long long r1 = min(total_rows, r0 + rows_per_block);
+  const int pt = P.kt / 2, ph = P.kh / 2, pw = P.kw / 2;
+  for (int tap = threadIdx.y; tap < ntap; tap += blockDim.y) {
+    int it = 0, ih = 0, iw = 0;
+    if (tap < K) {
+      it = tap / (P.kh * P.kw);
+      const int r = tap - it * P.kh * P.kw;
+      ih = r / P.kw;
+      iw = r - ih * P.kw;
+    }
+    float acc = 0.f;
+    for (long long rr = r0; rr < r1; ++rr) {
+      const int b = static_cast<int>(rr / (static_cast<long long>(P.out_frames) * P.H));
+      const int rem = static_cast<int>(rr - static_cast<long long>(b) * P.out_frames * P.H);
+      const int tl = rem / P.H, h = rem - (rem / P.H) * P.H;
+      const T* dyrow = dy + ((static_cast<long long>(b) * P.out_frames + tl) * P.H + h) * P.W * dy_ld + cc;
+      if (tap == K) {
+        for (int w = 0; w < P.W; ++w) acc += to_f32<T>(dyrow[w * dy_ld]);
+        continue;
+      }
+      const int ti = P.out_frame0 + tl + it - pt;
+      const int hi = h + ih - ph;
+      if (ti < 0 || ti >= P.T || hi < 0 || hi >= P.H) continue;
+      const int til = ti - P.in_frame0;
+      const T* xrow = x + ((static_cast<long long>(b) * P.in_frames + til) * P.H + hi) * P.W * x_ld + cc;
+      const int wlo = max(0, pw - iw), whi = min(P.W, P.W + pw - iw);
+      for (int w = wlo; w < whi; ++w)
+        acc = fmaf(to_f32<T>(dyrow[static_cast<long long>(w) * dy_ld]),
+                   to_f32<T>(xrow[static_cast<long long>(w + iw - pw) * x_ld]), acc);
+    }
+    if (cvalid) {
+      if (tap < K)
+        atomicAdd(dw + static_cast<long long>(tap) * P.C + c, acc);
+      else
+        atomicAdd(db + c, acc);
+    }
+  }
+}
+
+template <typename T>
+static cudaError_t dwconv_fwd_t(const ConvParams& P, const void* x, long long x_ld, const float* wt,
+                                const float* bias, const float* bias2, int epi, const void* aux,
+                                long long aux_ld, void* y, long long y_ld, bool flip, bool vec2,
+                                cudaStream_t s) {
+  const int cv = vec2 ? 2 : 1;
+  const long long total = static_cast<long long>(P.B) * P.out_frames * P.HW * (P.C / cv);
+  const dim3 grid(static_cast<unsigned>((total + 255) / 256)), block(256);
+  const T* xp = static_cast<const T*>(x);
+  const T* ap = static_cast<const T*>(aux);
+  T* yp = static_cast<T*>(y);
+  if (vec2) {
+    if (flip)
+      dwconv_fwd_kernel<T, 2, true><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
+    else
+      dwconv_fwd_kernel<T, 2, false><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
+  } else {
+    if (flip)
+      dwconv_fwd_kernel<T, 1, true><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
+    else
+      dwconv_fwd_kernel<T, 1, false><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dwconv_fwd(const ConvParams& P, const void* x, long long x_ld, const float* wt,
+                              const float* bias, const float* bias2, int epi, const void* aux,
+                              long long aux_ld, void* y, long long y_ld, bool flip, cudaStream_t s) {
+  const size_t es = P.dtype == MSL_DTYPE_BF16 ? 2 : 4;
+  const bool vec2 = (P.C % 2 == 0) && (x_ld % 2 == 0) && (y_ld % 2 == 0) &&
+                    (epi != MSL_EPI_GELU_GRAD || aux_ld % 2 == 0) &&
+                    (reinterpret_cast<uintptr_t>(x) % (2 * es) == 0) && (reinterpret_cast<uintptr_t>(y) % (2 * es) == 0) &&
+                    (epi != MSL_EPI_GELU_GRAD || reinterpret_cast<uintptr_t>(aux) % (2 * es) == 0) &&
+                    (reinterpret_cast<uintptr_t>(wt) % 8 == 0);
+  if (P.dtype == MSL_DTYPE_BF16)
+    return dwconv_fwd_t<__nv_bfloat16>(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, flip, vec2, s);
+  return dwconv_fwd_t<float>(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, flip, vec2, s);
+}
+
+cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long dy_ld, const void* x,
+                                long long x_ld, float* dw, float* db, cudaStream_t s) {
+  const long long total_rows = static_cast<long long>(P.B) * P.out_frames * P.H;
+  const int rows_per_block = max(1, 2048 / max(1, P.W));
+  const dim3 grid(static_cast<unsigned>((P.C + 31) / 32),
+                  static_cast<unsigned>((total_rows + rows_per_block - 1) / rows_per_block));
+  const dim3 block(32, 16);
+  if (P.dtype == MSL_DTYPE_BF16)
+    dwconv_wgrad_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(P, static_cast<const __nv_bfloat16*>(dy), dy_ld,
+                                                              static_cast<const __nv_bfloat16*>(x), x_ld, dw, db,
+                                                              rows_per_block);
+  else
+    dwconv_wgrad_kernel<float><<<grid, block, 0, s>>>(P, static_cast<const float*>(dy), dy_ld,
+                                                      static_cast<const float*>(x), x_ld, dw, db, rows_per_block);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ utilities
+__global__ void __launch_bounds__(256) offsets_absmax_kernel(const float* __restrict__ off, long long rows, long long ld,
+                                                             int ncol, float oscale, float* out3) {
+  float m0 = 0.f, m1 = 0.f, m2 = 0.f;
+  const long long n = rows * ncol;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / ncol;
+    const int cidx = static_cast<int>(i - r * ncol);
+    const float v = fabsf(off[r * ld + cidx] * oscale);
+    const int axis = cidx % 3;
+    if (axis == 0) m0 = fmaxf(m0, v);
+    else if (axis == 1) m1 = fmaxf(m1, v);
+    else m2 = fmaxf(m2, v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(kFull, m0, o));
+    m1 = fmaxf(m1, __shfl_xor_sync(kFull, m1, o));
+    m2 = fmaxf(m2, __shfl_xor_sync(kFull, m2, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    // non-negative floats order like their bit patterns
+    atomicMax(reinterpret_cast<int*>(out3) + 0, __float_as_int(m0));
+    atomicMax(reinterpret_cast<int*>(out3) + 1, __float_as_int(m1));
+    atomicMax(reinterpret_cast<int*>(out3) + 2, __float_as_int(m2));
+  }
+}
+
+cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, int heads, int taps,
+                                  float oscale, float* out3, cudaStream_t s) {
+  const int ncol = heads * taps * 3;
+  const long long n = rows * ncol;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  if (blocks < 1) blocks = 1;
+  offsets_absmax_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, rows, ld, ncol, oscale, out3);
+  return cudaGetLastError();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) convert_f32_kernel(const float* __restrict__ src, long long src_ld, T* __restrict__ dst,
+                                                          long long dst_ld, long long rows, long long cols) {
+  const long long n = rows * cols;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / cols, c = i - (i / cols) * cols;
+    dst[r * dst_ld + c] = from_f32<T>(src[r * src_ld + c]);
+  }
+}
+
+cudaError_t launch_convert_f32(const float* src, long long src_ld, void* dst, long long dst_ld, int dtype,
+                               long long rows, long long cols, cudaStream_t s) {
+  const long long n = rows * cols;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148LL * 32) blocks = 148LL * 32;
+  if (blocks < 1) blocks = 1;
+  if (dtype == MSL_DTYPE_BF16)
+    convert_f32_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        src, src_ld, static_cast<__nv_bfloat16*>(dst), dst_ld, rows, cols);
+  else
+    convert_f32_kernel<float><<<static_cast<unsigned>(blocks), 256, 0, s>>>(src, src_ld, static_cast<float*>(dst),
+                                                                            dst_ld, rows, cols);
+  return cudaGetLastError();
+}
+
+}  // namespace msl

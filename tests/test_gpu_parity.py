@@ -1,0 +1,292 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the reference's golden fixtures and
+the CPU oracle.  Tolerances are the north star's: 1e-4 relative in float32, 2e-2 in bfloat16
+(bf16 results are compared with the float64 oracle run on the same bf16-rounded inputs)."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import golden_cases as gc
+import megaslide_b200 as msl
+from megaslide_b200 import ops
+from oracle import dsa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+RTOL_F32 = 1e-4
+RTOL_BF16 = 2e-2
+DEV = "cuda:0"
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def run_module(case, dtype=torch.float32):
+    C = case["x"].shape[-1]
+    m = msl.DeformableSlideAttention3D(C, case["heads"], case["kernel"], offset_scale=case["offset_scale"])
+    m.load_state_dict({k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in case["params"].items()})
+    m = m.to(DEV)
+    x = torch.from_numpy(case["x"]).to(DEV, dtype).requires_grad_(True)
+    extra = None
+    if case["extra"] is not None:
+        extra = torch.from_numpy(case["extra"]).to(DEV, dtype).requires_grad_(True)
+    y = m(x, case["video_shape"], extra_kv=extra)
+    y.backward(torch.from_numpy(case["dy"]).to(DEV, dtype))
+    torch.cuda.synchronize()
+    return dict(y=y.detach().float().cpu().numpy(), dx=x.grad.float().cpu().numpy(),
+                grads={k: p.grad.float().cpu().numpy() for k, p in m.named_parameters()},
+                d_extra=None if extra is None else extra.grad.float().cpu().numpy(), offsets=None)
+
+
+@pytest.mark.parametrize("name", gc.NAMES)
+def test_module_fp32_matches_reference_golden(name):
+    case = gc.load(name)
+    res = run_module(case)
+    errs = gc.case_errors(res, case)
+    bad = {k: v for k, v in errs.items() if not v <= RTOL_F32}
+    assert not bad, f"{name}: {bad}"
+
+
+def _round_bf16(a):
+    return torch.from_numpy(np.asarray(a, np.float32)).bfloat16().float().numpy()
+
+
+@pytest.mark.parametrize("name", ["c1_window_small", "head_dim_72", "extra_kv", "tiny_large_offsets"])
+def test_module_bf16_matches_oracle(name):
+    case = gc.load(name)
+    case = dict(case)
+    case["params"] = {k: _round_bf16(v) for k, v in case["params"].items()}
+    case["x"] = _round_bf16(case["x"])
+    case["dy"] = _round_bf16(case["dy"])
+    if case["extra"] is not None:
+        case["extra"] = _round_bf16(case["extra"])
+    res = run_module(case, torch.bfloat16)
+    ref = gc.run_oracle(case)
+    assert rel(res["y"], ref["y"]) < RTOL_BF16
+    assert rel(res["dx"], ref["dx"]) < RTOL_BF16
+    for k, g in ref["grads"].items():
+        if k == "k_proj.bias":
+            continue  # mathematically zero: rounding noise only
+        assert rel(res["grads"][k], g) < RTOL_BF16 * 2.5, k
+
+
+CORE_CASES = [
+    # B, T, H, W, nh, d, kernel, G, offset_std
+    (2, 3, 5, 6, 2, 8, (3, 3, 3), 0, 1.5),
+    (1, 4, 6, 5, 2, 72, (3, 7, 7), 0, 1.0),
+    (1, 3, 4, 4, 1, 128, (3, 7, 7), 2, 2.0),
+    (1, 2, 3, 4, 3, 2, (1, 3, 3), 3, 0.5),
+    (1, 1, 4, 4, 2, 16, (3, 3, 3), 0, 1.0),
+    (2, 2, 1, 1, 1, 4, (3, 1, 1), 1, 0.0),
+    (1, 5, 3, 7, 3, 12, (3, 3, 3), 0, 0.0),
+    (1, 3, 5, 5, 2, 64, (3, 5, 5), 4, 3.0),
+]
+
+
+def _core_inputs(case, seed=0):
+    B, T, H, W, nh, d, ks, G, ostd = case
+    rng = np.random.default_rng(seed)
+    N = T * H * W
+    C = nh * d
+    K = ks[0] * ks[1] * ks[2]
+    q, k, v = (rng.normal(size=(B, N, C)).astype(np.float32) for _ in range(3))
+    off = (rng.normal(size=(B, N, nh * K * 3)) * ostd).astype(np.float32)
+    ek = rng.normal(size=(B, G, C)).astype(np.float32) if G else None
+    ev = rng.normal(size=(B, G, C)).astype(np.float32) if G else None
+    dout = rng.normal(size=(B, N, C)).astype(np.float32)
+    return q, k, v, off, ek, ev, dout
+
+
+def _run_core(case, arrays, dtype, dropout_p=0.0, seed=0):
+    B, T, H, W, nh, d, ks, G, _ = case
+    q, k, v, off, ek, ev, dout = arrays
+    N = T * H * W
+    C = nh * d
+    t = lambda a: None if a is None else torch.from_numpy(a).to(DEV, dtype).reshape(-1, C)  # noqa: E731
+    shape = ops.DsaShape(B, T, H, W, nh, d, ks, extra=G, dropout_p=dropout_p, dropout_seed=seed)
+    offt = torch.from_numpy(off).to(DEV).reshape(B * N, -1)
+    qt, kt_, vt, ekt, evt, dot = t(q), t(k), t(v), t(ek), t(ev), t(dout)
+    out, lse = ops.attn_fwd(shape, qt, kt_, vt, offt, ekt, evt)
+    dq, dk, dv, doff, dek, dev_ = ops.attn_bwd(shape, qt, kt_, vt, offt, out, lse, dot, ek=ekt, ev=evt)
+    torch.cuda.synchronize()
+    f = lambda a: None if a is None else a.float().cpu().numpy().reshape(B, -1, C)  # noqa: E731
+    return dict(out=f(out), lse=lse.cpu().numpy(), dq=f(dq), dk=f(dk), dv=f(dv),
+                doff=doff.cpu().numpy().reshape(B, N, -1), dek=f(dek), dev=f(dev_))
+
+
+def _oracle_core(case, arrays, dropout_p=0.0, seed=0):
+    B, T, H, W, nh, d, ks, G, _ = case
+    q, k, v, off, ek, ev, dout = arrays
+    out, lse = O.attn_forward(q, k, v, off, (T, H, W), nh, ks, ek, ev, dropout_p=dropout_p, seed=seed)
+    dq, dk, dv, doff, dek, dev_ = O.attn_backward(q, k, v, off, dout, (T, H, W), nh, ks, ek, ev,
+                                                  dropout_p=dropout_p, seed=seed)
+    return dict(out=out, lse=lse / math.log(2.0), dq=dq, dk=dk, dv=dv, doff=doff, dek=dek, dev=dev_)
+
+
+def _compare(got, ref, tol, skip=()):
+    for key in ("out", "lse", "dq", "dk", "dv", "doff", "dek", "dev"):
+        if key in skip or ref[key] is None:
+            continue
+        e = rel(got[key], ref[key])
+        assert e < tol, f"{key}: rel err {e:.3e}"
+
+
+@pytest.mark.parametrize("case", CORE_CASES, ids=lambda c: f"B{c[0]}T{c[1]}H{c[2]}W{c[3]}nh{c[4]}d{c[5]}k{''.join(map(str, c[6]))}G{c[7]}")
+def test_core_fp32_matches_oracle(case):
+    arrays = _core_inputs(case)
+    _compare(_run_core(case, arrays, torch.float32), _oracle_core(case, arrays), RTOL_F32)
+
+
+@pytest.mark.parametrize("case", CORE_CASES, ids=lambda c: f"B{c[0]}T{c[1]}H{c[2]}W{c[3]}nh{c[4]}d{c[5]}k{''.join(map(str, c[6]))}G{c[7]}")
+def test_core_bf16_matches_oracle(case):
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a)) for i, a in enumerate(_core_inputs(case)))
+    _compare(_run_core(case, arrays, torch.bfloat16), _oracle_core(case, arrays), RTOL_BF16)
+
+
+def test_core_dropout_matches_oracle_mask():
+    case = (1, 3, 4, 4, 2, 8, (3, 3, 3), 2, 1.0)
+    arrays = _core_inputs(case, seed=3)
+    got = _run_core(case, arrays, torch.float32, dropout_p=0.25, seed=99)
+    ref = _oracle_core(case, arrays, dropout_p=0.25, seed=99)
+    _compare(got, ref, RTOL_F32)
+    plain = _oracle_core(case, arrays)
+    assert rel(ref["out"], plain["out"]) > 1e-2  # the mask did something
+
+
+def test_dwconv_kernels_match_oracle():
+    rng = np.random.default_rng(5)
+    for (B, T, H, W, C, ks) in [(1, 4, 5, 6, 16, (3, 7, 7)), (2, 3, 4, 4, 9, (3, 3, 3)), (1, 1, 3, 3, 8, (1, 3, 3))]:
+        N = T * H * W
+        K = ks[0] * ks[1] * ks[2]
+        x = rng.normal(size=(B, N, C)).astype(np.float32)
+        w = rng.normal(size=(K, C)).astype(np.float32)
+        b = rng.normal(size=(C,)).astype(np.float32)
+        dy = rng.normal(size=(B, N, C)).astype(np.float32)
+        shape = ops.ConvShape(B, T, H, W, C, ks)
+        for dt, tol in ((torch.float32, 1e-5), (torch.bfloat16, 2e-2)):
+            xr = x if dt == torch.float32 else _round_bf16(x)
+            dyr = dy if dt == torch.float32 else _round_bf16(dy)
+            xt = torch.from_numpy(xr).to(DEV, dt).reshape(B * N, C)
+            dyt = torch.from_numpy(dyr).to(DEV, dt).reshape(B * N, C)
+            wt = torch.from_numpy(w).to(DEV)
+            bt = torch.from_numpy(b).to(DEV)
+            y = ops.dwconv_fwd(shape, xt, wt, bt)
+            dx = ops.dwconv_bwd_data(shape, dyt, wt)
+            gw = torch.zeros_like(wt)
+            gb = torch.zeros_like(bt)
+            ops.dwconv_bwd_weight(shape, dyt, xt, gw, gb)
+            yo = O.dwconv3d(xr, w, b, (T, H, W), ks)
+            dxo, gwo, gbo = O.dwconv3d_backward(dyr, xr, w, (T, H, W), ks)
+            assert rel(y.float().cpu().numpy().reshape(B, N, C), yo) < tol
+            assert rel(dx.float().cpu().numpy().reshape(B, N, C), dxo) < tol
+            assert rel(gw.cpu().numpy(), gwo) < max(tol, 1e-5)
+            assert rel(gb.cpu().numpy(), gbo) < max(tol, 1e-5)
+
+
+# ----------------------------------------------------------------- reference's structural tests
+def test_reference_shape_finite_and_gradients():
+    """tests/test_megaslide_video.py:37-49 of the reference."""
+    torch.manual_seed(0)
+    attn = msl.DeformableSlideAttention3D(hidden_size=8, num_heads=2, kernel_size=(1, 3, 3)).to(DEV)
+    x = torch.randn(2, 18, 8, device=DEV, requires_grad=True)
+    y = attn(x, (2, 3, 3))
+    assert y.shape == x.shape and torch.isfinite(y).all()
+    y.square().mean().backward()
+    assert x.grad is not None and torch.isfinite(x.grad).all()
+    assert any(p.grad is not None for p in attn.parameters())
+
+
+def test_reference_non_causal_over_time():
+    """tests/test_megaslide_video.py:52-69 of the reference."""
+    attn = msl.DeformableSlideAttention3D(hidden_size=2, num_heads=1, kernel_size=(3, 1, 1))
+    with torch.no_grad():
+        for p in attn.parameters():
+            p.zero_()
+        attn.v_proj.weight.copy_(torch.eye(2))
+        attn.out_proj.weight.copy_(torch.eye(2))
+    attn = attn.to(DEV)
+    x = torch.zeros(1, 2, 2, device=DEV)
+    changed = x.clone()
+    changed[:, 1, :] = torch.tensor([3.0, -2.0], device=DEV)
+    assert not torch.allclose(attn(x, (2, 1, 1))[:, 0], attn(changed, (2, 1, 1))[:, 0])
+
+
+def test_reference_degenerate_grid():
+    """tests/test_megaslide_video.py:72-84 of the reference."""
+    attn = msl.DeformableSlideAttention3D(hidden_size=4, num_heads=2, kernel_size=(3, 3, 3)).to(DEV)
+    x = torch.randn(1, 1, 4, device=DEV, requires_grad=True)
+    y = attn(x, (1, 1, 1))
+    assert y.shape == x.shape and torch.isfinite(y).all()
+    y.sum().backward()
+    assert torch.isfinite(x.grad).all()
+    assert torch.count_nonzero(attn.offset_net[-1].weight) == 0
+
+
+def test_reference_extra_kv():
+    """tests/test_hybrid_attention.py:7-48 of the reference."""
+    B, T, H, W, D, nh, G = 1, 2, 2, 2, 16, 4, 4
+    attn = msl.DeformableSlideAttention3D(hidden_size=D, num_heads=nh, kernel_size=(1, 1, 1)).to(DEV)
+    x = torch.randn(B, T * H * W, D, device=DEV)
+    a = attn(x, (T, H, W))
+    b = attn(x, (T, H, W), extra_kv=torch.randn(B, G, D, device=DEV))
+    c = attn(x, (T, H, W), extra_kv=torch.zeros(B, G, D, device=DEV))
+    assert a.shape == b.shape == c.shape == (B, T * H * W, D)
+    assert not torch.allclose(a, b, atol=1e-5)
+
+
+def test_trainer_style_autograd_grad_and_no_grad():
+    """The CPU-master trainer runs the block under no_grad, then re-runs it with requires_grad toggled
+    on the parameters and calls torch.autograd.grad (trainer.py:284-308, 418-449)."""
+    torch.manual_seed(1)
+    m = msl.DeformableSlideAttention3D(32, 4, (3, 3, 3)).to(DEV)
+    for p in m.parameters():
+        p.requires_grad_(False)
+    x = torch.randn(1, 2 * 3 * 4, 32, device=DEV)
+    with torch.no_grad():
+        y0 = m(x, (2, 3, 4))
+    for p in m.parameters():
+        p.requires_grad_(True)
+    xi = x.clone().requires_grad_(True)
+    y1 = m(xi, (2, 3, 4))
+    assert torch.equal(y0, y1.detach())
+    grads = torch.autograd.grad(y1, (xi, *m.parameters()), grad_outputs=torch.ones_like(y1), allow_unused=True)
+    assert all(g is not None and torch.isfinite(g).all() for g in grads)
+
+
+def test_bf16_autocast_input():
+    torch.manual_seed(2)
+    m = msl.DeformableSlideAttention3D(32, 4, (3, 3, 3)).to(DEV)
+    x = torch.randn(1, 24, 32, device=DEV, requires_grad=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = m(x, (2, 3, 4))
+    assert y.dtype == torch.bfloat16
+    y.float().sum().backward()
+    assert x.grad.dtype == torch.float32 and torch.isfinite(x.grad).all()
+    y32 = m(x, (2, 3, 4))
+    assert rel(y.float().detach().cpu().numpy(), y32.detach().cpu().numpy()) < 3e-2
+
+
+def test_launches_counted_and_native_library_loaded():
+    n0 = msl.launch_count()
+    m = msl.DeformableSlideAttention3D(16, 2, (3, 3, 3)).to(DEV)
+    x = torch.randn(1, 27, 16, device=DEV, requires_grad=True)
+    m(x, (3, 3, 3)).sum().backward()
+    torch.cuda.synchronize()
+    assert msl.launch_count() - n0 >= 9
+    import os
+
+    maps = open(f"/proc/{os.getpid()}/maps").read()
+    assert "libmegaslide_b200.so" in maps

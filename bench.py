@@ -37,10 +37,13 @@ CONFIGS = {
     # name: B, T, H, W, C, nh, kernel, dtype, offset weight std
     "c1": dict(B=1, T=8, H=16, W=16, C=256, nh=4, kernel=(3, 7, 7), dtype="float32", ostd=1e-2),
     "c2": dict(B=2, T=64, H=32, W=32, C=1152, nh=16, kernel=(3, 7, 7), dtype="bfloat16", ostd=0.05),
+    # config-2 widths on 16 frames: the case profiled with ncu (inputs > L2, a few GB on the device)
+    "c2_prof": dict(B=1, T=16, H=32, W=32, C=1152, nh=16, kernel=(3, 7, 7), dtype="bfloat16", ostd=0.05),
 }
 METRIC = "3D-DSA fwd+bwd Mtokens/s"
 # reduced-volume sample of a config timed on the CPU (same C, heads, window; fewer frames)
-CPU_SAMPLE = {"c1": dict(B=1, T=8, H=16, W=16), "c2": dict(B=1, T=8, H=16, W=16)}
+CPU_SAMPLE = {"c1": dict(B=1, T=8, H=16, W=16), "c2": dict(B=1, T=8, H=16, W=16),
+              "c2_prof": dict(B=1, T=8, H=16, W=16)}
 
 
 def parse():

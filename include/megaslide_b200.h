@@ -148,20 +148,24 @@ typedef struct msl_dwconv_geometry {
 #define MSL_EPI_GELU 1      /* y = gelu_erf(conv(x) + bias) */
 #define MSL_EPI_GELU_GRAD 2 /* y = aux * gelu_erf'(conv(x) + bias)  (offset_net backward) */
 
-/* y[out frames] = epilogue(conv(x[in frames])).  bias, bias2 float32 [C] or NULL. */
+/* y[out frames] = epilogue(conv(x[in frames])).  bias, bias2 float32 [C] or NULL.  geom->dtype is
+ * the element type of x; y_dtype (MSL_DTYPE_*) that of y and aux (a bf16 input can produce a float32
+ * GELU-gradient). */
 int msl_dwconv3d_fwd(const msl_dwconv_geometry* geom, const void* x, int64_t x_ld,
                      const float* weight, const float* bias, const float* bias2, int32_t epilogue,
-                     const void* aux, int64_t aux_ld, void* y, int64_t y_ld, void* stream);
+                     const void* aux, int64_t aux_ld, void* y, int64_t y_ld, int32_t y_dtype,
+                     void* stream);
 
 /* dx[out frames] = conv_transpose(dy[in frames]) (gradient w.r.t. the conv input). */
 int msl_dwconv3d_bwd_data(const msl_dwconv_geometry* geom, const void* dy, int64_t dy_ld,
                           const float* weight, void* dx, int64_t dx_ld, void* stream);
 
 /* dweight[kt*kh*kw, C] += sum over dy positions (out frames) of dy * shifted x (in frames);
- * dbias[C] += sum of dy (dbias may be NULL).  Accumulates: the caller clears. */
+ * dbias[C] += sum of dy (dbias may be NULL).  Accumulates: the caller clears.  geom->dtype is the
+ * element type of x, dy_dtype that of dy. */
 int msl_dwconv3d_bwd_weight(const msl_dwconv_geometry* geom, const void* dy, int64_t dy_ld,
-                            const void* x, int64_t x_ld, float* dweight, float* dbias,
-                            void* stream);
+                            int32_t dy_dtype, const void* x, int64_t x_ld, float* dweight,
+                            float* dbias, void* stream);
 
 /* ----------------------------------------------------------------------------------------------
  * Utilities

@@ -85,10 +85,10 @@ SIGNATURES = {
     "msl_dsa_attn_bwd": (ctypes.c_int, [ctypes.POINTER(DsaGeometry), ctypes.POINTER(DsaBwdIO), _vp,
                                         ctypes.c_size_t, _vp]),
     "msl_dwconv3d_fwd": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _vp, _vp, _i32, _vp,
-                                        _i64, _vp, _i64, _vp]),
+                                        _i64, _vp, _i64, _i32, _vp]),
     "msl_dwconv3d_bwd_data": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _vp, _i64, _vp]),
-    "msl_dwconv3d_bwd_weight": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _i64, _vp, _vp,
-                                               _vp]),
+    "msl_dwconv3d_bwd_weight": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _i32, _vp, _i64, _vp,
+                                               _vp, _vp]),
     "msl_offsets_absmax": (ctypes.c_int, [_vp, _i64, _i64, _i32, _i32, _f32, _vp, _vp]),
     "msl_convert_f32": (ctypes.c_int, [_vp, _i64, _vp, _i64, _i32, _i64, _i64, _vp]),
     "msl_abi_version": (_i32, []),

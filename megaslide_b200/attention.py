@@ -108,8 +108,8 @@ class DSA3DFunction(torch.autograd.Function):
             dattn = torch.mm(dy2, wo.to(dt))
             g_wo = _mm_f32(dy2.t(), attn)
             g_bo = dy2.float().sum(0)
-            # depthwise conv term
-            dx = ops.dwconv_bwd_data(cfg.conv_k, dy2, wd_kc)
+            # depthwise conv term; dx accumulates in float32 across the three branches
+            dx = ops.dwconv_bwd_data(cfg.conv_k, dy2, wd_kc).float()
             g_wd = torch.zeros_like(wd_kc)
             g_bd = torch.zeros(C, device=dy2.device, dtype=torch.float32)
             ops.dwconv_bwd_weight(cfg.conv_k, dy2, x2, g_wd, g_bd)
@@ -120,7 +120,7 @@ class DSA3DFunction(torch.autograd.Function):
                 sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev,
                 dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:])
             # q/k/v projections
-            dx += torch.mm(dqkv, wqkv)
+            dx += _mm_f32(dqkv, wqkv)
             g_wqkv = _mm_f32(dqkv.t(), x2)
             g_bqkv = dqkv.float().sum(0)
             g_wq, g_wk, g_wv = g_wqkv[:C], g_wqkv[C:2 * C], g_wqkv[2 * C:]
@@ -136,12 +136,13 @@ class DSA3DFunction(torch.autograd.Function):
                 sums = dekv.sum(0)
                 g_bk = g_bk + sums[:C]
                 g_bv = g_bv + sums[C:]
-            # offset predictor
+            # offset predictor; dh and du stay float32 (bf16 operands, fp32 results)
             doff_c = doff.to(dt)
-            dh = torch.mm(doff_c, w2m.to(dt))
+            dh = _mm_f32(doff_c, w2m.to(dt))
             g_w2 = _mm_f32(doff_c.t(), hact)
             g_b2 = doff.sum(0)
-            du = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh)
+            du = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh,
+                                out_dtype=torch.float32)
             dx += ops.dwconv_bwd_data(cfg.conv_3, du, w1_kc)
             g_w1 = torch.zeros_like(w1_kc)
             g_b1 = torch.zeros(C, device=dy2.device, dtype=torch.float32)

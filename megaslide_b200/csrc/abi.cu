@@ -285,7 +285,7 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
 
 int msl_dwconv3d_fwd(const msl_dwconv_geometry* geom, const void* x, int64_t x_ld, const float* weight,
                      const float* bias, const float* bias2, int32_t epilogue, const void* aux, int64_t aux_ld,
-                     void* y, int64_t y_ld, void* stream) {
+                     void* y, int64_t y_ld, int32_t y_dtype, void* stream) {
   msl::ConvParams P;
   int rc = fill_conv(geom, P);
   if (rc) return rc;
@@ -294,8 +294,9 @@ int msl_dwconv3d_fwd(const msl_dwconv_geometry* geom, const void* x, int64_t x_l
     return fail(MSL_ERR_INVALID, "unknown epilogue %d", epilogue);
   if (epilogue == MSL_EPI_GELU_GRAD && (!aux || aux_ld < P.C)) return fail(MSL_ERR_INVALID, "GELU_GRAD needs aux rows");
   if (x_ld < P.C || y_ld < P.C) return fail(MSL_ERR_INVALID, "row strides must be >= channels");
-  cudaError_t e = msl::launch_dwconv_fwd(P, x, x_ld, weight, bias, bias2, epilogue, aux, aux_ld, y, y_ld, false,
-                                         static_cast<cudaStream_t>(stream));
+  if (y_dtype != MSL_DTYPE_F32 && y_dtype != MSL_DTYPE_BF16) return fail(MSL_ERR_INVALID, "unknown y_dtype %d", y_dtype);
+  cudaError_t e = msl::launch_dwconv_fwd(P, x, x_ld, weight, bias, bias2, epilogue, aux, aux_ld, y, y_ld, y_dtype,
+                                         false, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwconv_fwd_kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return MSL_OK;
@@ -309,20 +310,22 @@ int msl_dwconv3d_bwd_data(const msl_dwconv_geometry* geom, const void* dy, int64
   if (!dy || !weight || !dx) return fail(MSL_ERR_INVALID, "dy, weight and dx are required");
   if (dy_ld < P.C || dx_ld < P.C) return fail(MSL_ERR_INVALID, "row strides must be >= channels");
   cudaError_t e = msl::launch_dwconv_fwd(P, dy, dy_ld, weight, nullptr, nullptr, MSL_EPI_NONE, nullptr, 0, dx, dx_ld,
-                                         true, static_cast<cudaStream_t>(stream));
+                                         P.dtype, true, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwconv_fwd_kernel(transposed) launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return MSL_OK;
 }
 
-int msl_dwconv3d_bwd_weight(const msl_dwconv_geometry* geom, const void* dy, int64_t dy_ld, const void* x,
-                            int64_t x_ld, float* dweight, float* dbias, void* stream) {
+int msl_dwconv3d_bwd_weight(const msl_dwconv_geometry* geom, const void* dy, int64_t dy_ld, int32_t dy_dtype,
+                            const void* x, int64_t x_ld, float* dweight, float* dbias, void* stream) {
   msl::ConvParams P;
   int rc = fill_conv(geom, P);
   if (rc) return rc;
   if (!dy || !x || !dweight) return fail(MSL_ERR_INVALID, "dy, x and dweight are required");
   if (dy_ld < P.C || x_ld < P.C) return fail(MSL_ERR_INVALID, "row strides must be >= channels");
-  cudaError_t e = msl::launch_dwconv_wgrad(P, dy, dy_ld, x, x_ld, dweight, dbias, static_cast<cudaStream_t>(stream));
+  if (dy_dtype != MSL_DTYPE_F32 && dy_dtype != MSL_DTYPE_BF16) return fail(MSL_ERR_INVALID, "unknown dy_dtype %d", dy_dtype);
+  cudaError_t e = msl::launch_dwconv_wgrad(P, dy, dy_ld, dy_dtype, x, x_ld, dweight, dbias,
+                                           static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwconv_wgrad_kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return MSL_OK;

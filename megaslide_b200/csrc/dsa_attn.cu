@@ -488,9 +488,17 @@ template <typename T, int VEC>
 static cudaError_t launch_fwd_vec(const AttnParams& P, int maxc, cudaStream_t s) {
   const long long items = static_cast<long long>(P.B) * P.nh * P.Nq;
   const dim3 grid(static_cast<unsigned>((items + 7) / 8)), block(256);
+  // bf16 16-byte chunks stop at 4 chunks per slot (head_dim 128); attn_chunking never asks for more
+  constexpr int kLim = (VEC == 8) ? 4 : 8;
   switch (maxc) {
-#define MSL_CASE(MC) \
-  case MC: dsa_fwd_kernel<T, VEC, MC><<<grid, block, 0, s>>>(P); break;
+#define MSL_CASE(MC)                                            \
+  case MC:                                                      \
+    if constexpr (MC <= kLim) {                                 \
+      dsa_fwd_kernel<T, VEC, MC><<<grid, block, 0, s>>>(P);         \
+    } else {                                                    \
+      return cudaErrorInvalidValue;                             \
+    }                                                           \
+    break;
     MSL_CASE(1) MSL_CASE(2) MSL_CASE(3) MSL_CASE(4)
     MSL_CASE(5) MSL_CASE(6) MSL_CASE(7) MSL_CASE(8)
 #undef MSL_CASE
@@ -503,9 +511,17 @@ template <typename T, int VEC>
 static cudaError_t launch_bwd_vec(const AttnParams& P, int maxc, cudaStream_t s) {
   const long long items = static_cast<long long>(P.B) * P.nh * P.Nq;
   const dim3 grid(static_cast<unsigned>((items + 7) / 8)), block(256);
+  // bf16 16-byte chunks stop at 4 chunks per slot (head_dim 128); attn_chunking never asks for more
+  constexpr int kLim = (VEC == 8) ? 4 : 8;
   switch (maxc) {
-#define MSL_CASE(MC) \
-  case MC: dsa_bwd_kernel<T, VEC, MC><<<grid, block, 0, s>>>(P); break;
+#define MSL_CASE(MC)                                            \
+  case MC:                                                      \
+    if constexpr (MC <= kLim) {                                 \
+      dsa_bwd_kernel<T, VEC, MC><<<grid, block, 0, s>>>(P);         \
+    } else {                                                    \
+      return cudaErrorInvalidValue;                             \
+    }                                                           \
+    break;
     MSL_CASE(1) MSL_CASE(2) MSL_CASE(3) MSL_CASE(4)
     MSL_CASE(5) MSL_CASE(6) MSL_CASE(7) MSL_CASE(8)
 #undef MSL_CASE

@@ -48,11 +48,14 @@ struct ConvParams {
   int dtype;
   int HW;
 };
+// x has dtype P.dtype; aux and y have y_dtype.
 cudaError_t launch_dwconv_fwd(const ConvParams& P, const void* x, long long x_ld, const float* wt,
                               const float* bias, const float* bias2, int epi, const void* aux,
-                              long long aux_ld, void* y, long long y_ld, bool flip, cudaStream_t s);
-cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long dy_ld, const void* x,
-                                long long x_ld, float* dw, float* db, cudaStream_t s);
+                              long long aux_ld, void* y, long long y_ld, int y_dtype, bool flip,
+                              cudaStream_t s);
+// x has dtype P.dtype; dy has dy_dtype.
+cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long dy_ld, int dy_dtype,
+                                const void* x, long long x_ld, float* dw, float* db, cudaStream_t s);
 
 cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, int heads, int taps,
                                   float oscale, float* out3, cudaStream_t s);

@@ -60,12 +60,12 @@ struct ChanVec<__nv_bfloat16, 2> {
 
 // One thread per (output token, CV channels).  FLIP = transposed convolution (input gradient):
 // dx[p] = sum_taps w[tap] * dy[p - (tap - pad)].
-template <typename T, int CV, bool FLIP>
+template <typename T, typename TY, int CV, bool FLIP>
 __global__ void __launch_bounds__(256) dwconv_fwd_kernel(const ConvParams P, const T* __restrict__ x, long long x_ld,
                                                          const float* __restrict__ wt, const float* __restrict__ bias,
                                                          const float* __restrict__ bias2, int epi,
-                                                         const T* __restrict__ aux, long long aux_ld, T* __restrict__ y,
-                                                         long long y_ld) {
+                                                         const TY* __restrict__ aux, long long aux_ld,
+                                                         TY* __restrict__ y, long long y_ld) {
   const int ncg = P.C / CV;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long rows_out = static_cast<long long>(P.out_frames) * P.HW;
@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(256) dwconv_fwd_kernel(const ConvParams P, con
   float out[CV];
   const long long orow = static_cast<long long>(b) * rows_out + row;
   float av[CV];
-  if (epi == MSL_EPI_GELU_GRAD) ChanVec<T, CV>::load(aux + orow * aux_ld + c, av);
+  if (epi == MSL_EPI_GELU_GRAD) ChanVec<TY, CV>::load(aux + orow * aux_ld + c, av);
 #pragma unroll
   for (int e = 0; e < CV; ++e) {
     float u = acc[e] + (bias ? __ldg(bias + c + e) : 0.f);
@@ -121,14 +121,14 @@ __global__ void __launch_bounds__(256) dwconv_fwd_kernel(const ConvParams P, con
       u += __ldg(bias2 + c + e);
     out[e] = u;
   }
-  ChanVec<T, CV>::store(y + orow * y_ld + c, out);
+  ChanVec<TY, CV>::store(y + orow * y_ld + c, out);
 }
 
 // Weight gradient: block = 32 channel lanes x (blockDim.y) tap groups; each thread owns one
 // (channel, tap) accumulator at a time and sums dy * shifted x over the block's token rows.
 // The extra tap index K accumulates the bias gradient (sum of dy).
-template <typename T>
-__global__ void __launch_bounds__(512) dwconv_wgrad_kernel(const ConvParams P, const T* __restrict__ dy, long long dy_ld,
+template <typename TDY, typename T>
+__global__ void __launch_bounds__(512) dwconv_wgrad_kernel(const ConvParams P, const TDY* __restrict__ dy, long long dy_ld,
                                                            const T* __restrict__ x, long long x_ld, float* dw, float* db,
                                                            int rows_per_block) {
   const int c = blockIdx.x * 32 + threadIdx.x;
@@ -153,9 +153,9 @@ __global__ void __launch_bounds__(512) dwconv_wgrad_kernel(const ConvParams P, c
       const int b = static_cast<int>(rr / (static_cast<long long>(P.out_frames) * P.H));
       const int rem = static_cast<int>(rr - static_cast<long long>(b) * P.out_frames * P.H);
       const int tl = rem / P.H, h = rem - (rem / P.H) * P.H;
-      const T* dyrow = dy + ((static_cast<long long>(b) * P.out_frames + tl) * P.H + h) * P.W * dy_ld + cc;
+      const TDY* dyrow = dy + ((static_cast<long long>(b) * P.out_frames + tl) * P.H + h) * P.W * dy_ld + cc;
       if (tap == K) {
-        for (int w = 0; w < P.W; ++w) acc += to_f32<T>(dyrow[w * dy_ld]);
+        for (int w = 0; w < P.W; ++w) acc += to_f32<TDY>(dyrow[w * dy_ld]);
         continue;
       }
       const int ti = P.out_frame0 + tl + it - pt;
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(512) dwconv_wgrad_kernel(const ConvParams P, c
       const T* xrow = x + ((static_cast<long long>(b) * P.in_frames + til) * P.H + hi) * P.W * x_ld + cc;
       const int wlo = max(0, pw - iw), whi = min(P.W, P.W + pw - iw);
       for (int w = wlo; w < whi; ++w)
-        acc = fmaf(to_f32<T>(dyrow[static_cast<long long>(w) * dy_ld]),
+        acc = fmaf(to_f32<TDY>(dyrow[static_cast<long long>(w) * dy_ld]),
                    to_f32<T>(xrow[static_cast<long long>(w + iw - pw) * x_ld]), acc);
     }
     if (cvalid) {
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(512) dwconv_wgrad_kernel(const ConvParams P, c
   }
 }
 
-template <typename T>
+template <typename T, typename TY>
 static cudaError_t dwconv_fwd_t(const ConvParams& P, const void* x, long long x_ld, const float* wt,
                                 const float* bias, const float* bias2, int epi, const void* aux,
                                 long long aux_ld, void* y, long long y_ld, bool flip, bool vec2,
@@ -186,50 +186,60 @@ static cudaError_t dwconv_fwd_t(const ConvParams& P, const void* x, long long x_
   const long long total = static_cast<long long>(P.B) * P.out_frames * P.HW * (P.C / cv);
   const dim3 grid(static_cast<unsigned>((total + 255) / 256)), block(256);
   const T* xp = static_cast<const T*>(x);
-  const T* ap = static_cast<const T*>(aux);
-  T* yp = static_cast<T*>(y);
+  const TY* ap = static_cast<const TY*>(aux);
+  TY* yp = static_cast<TY*>(y);
   if (vec2) {
     if (flip)
-      dwconv_fwd_kernel<T, 2, true><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
+      dwconv_fwd_kernel<T, TY, 2, true><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
     else
-      dwconv_fwd_kernel<T, 2, false><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
+      dwconv_fwd_kernel<T, TY, 2, false><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
   } else {
     if (flip)
-      dwconv_fwd_kernel<T, 1, true><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
+      dwconv_fwd_kernel<T, TY, 1, true><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
     else
-      dwconv_fwd_kernel<T, 1, false><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
+      dwconv_fwd_kernel<T, TY, 1, false><<<grid, block, 0, s>>>(P, xp, x_ld, wt, bias, bias2, epi, ap, aux_ld, yp, y_ld);
   }
   return cudaGetLastError();
 }
 
 cudaError_t launch_dwconv_fwd(const ConvParams& P, const void* x, long long x_ld, const float* wt,
                               const float* bias, const float* bias2, int epi, const void* aux,
-                              long long aux_ld, void* y, long long y_ld, bool flip, cudaStream_t s) {
+                              long long aux_ld, void* y, long long y_ld, int y_dtype, bool flip, cudaStream_t s) {
   const size_t es = P.dtype == MSL_DTYPE_BF16 ? 2 : 4;
+  const size_t ys = y_dtype == MSL_DTYPE_BF16 ? 2 : 4;
   const bool vec2 = (P.C % 2 == 0) && (x_ld % 2 == 0) && (y_ld % 2 == 0) &&
                     (epi != MSL_EPI_GELU_GRAD || aux_ld % 2 == 0) &&
-                    (reinterpret_cast<uintptr_t>(x) % (2 * es) == 0) && (reinterpret_cast<uintptr_t>(y) % (2 * es) == 0) &&
-                    (epi != MSL_EPI_GELU_GRAD || reinterpret_cast<uintptr_t>(aux) % (2 * es) == 0) &&
-                    (reinterpret_cast<uintptr_t>(wt) % 8 == 0);
-  if (P.dtype == MSL_DTYPE_BF16)
-    return dwconv_fwd_t<__nv_bfloat16>(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, flip, vec2, s);
-  return dwconv_fwd_t<float>(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, flip, vec2, s);
+                    (reinterpret_cast<uintptr_t>(x) % (2 * es) == 0) && (reinterpret_cast<uintptr_t>(y) % (2 * ys) == 0) &&
+                    (epi != MSL_EPI_GELU_GRAD || reinterpret_cast<uintptr_t>(aux) % (2 * ys) == 0);
+  if (P.dtype == MSL_DTYPE_BF16) {
+    if (y_dtype == MSL_DTYPE_BF16)
+      return dwconv_fwd_t<__nv_bfloat16, __nv_bfloat16>(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, flip, vec2, s);
+    return dwconv_fwd_t<__nv_bfloat16, float>(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, flip, vec2, s);
+  }
+  if (y_dtype == MSL_DTYPE_BF16)
+    return dwconv_fwd_t<float, __nv_bfloat16>(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, flip, vec2, s);
+  return dwconv_fwd_t<float, float>(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, flip, vec2, s);
 }
 
-cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long dy_ld, const void* x,
+template <typename TDY, typename T>
+static void wgrad_t(const ConvParams& P, dim3 grid, dim3 block, const void* dy, long long dy_ld, const void* x,
+                    long long x_ld, float* dw, float* db, int rows_per_block, cudaStream_t s) {
+  dwconv_wgrad_kernel<TDY, T><<<grid, block, 0, s>>>(P, static_cast<const TDY*>(dy), dy_ld, static_cast<const T*>(x),
+                                                      x_ld, dw, db, rows_per_block);
+}
+
+cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long dy_ld, int dy_dtype, const void* x,
                                 long long x_ld, float* dw, float* db, cudaStream_t s) {
   const long long total_rows = static_cast<long long>(P.B) * P.out_frames * P.H;
   const int rows_per_block = max(1, 2048 / max(1, P.W));
   const dim3 grid(static_cast<unsigned>((P.C + 31) / 32),
                   static_cast<unsigned>((total_rows + rows_per_block - 1) / rows_per_block));
   const dim3 block(32, 16);
-  if (P.dtype == MSL_DTYPE_BF16)
-    dwconv_wgrad_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(P, static_cast<const __nv_bfloat16*>(dy), dy_ld,
-                                                              static_cast<const __nv_bfloat16*>(x), x_ld, dw, db,
-                                                              rows_per_block);
-  else
-    dwconv_wgrad_kernel<float><<<grid, block, 0, s>>>(P, static_cast<const float*>(dy), dy_ld,
-                                                      static_cast<const float*>(x), x_ld, dw, db, rows_per_block);
+  const bool xb = P.dtype == MSL_DTYPE_BF16, yb = dy_dtype == MSL_DTYPE_BF16;
+  if (yb && xb) wgrad_t<__nv_bfloat16, __nv_bfloat16>(P, grid, block, dy, dy_ld, x, x_ld, dw, db, rows_per_block, s);
+  else if (yb) wgrad_t<__nv_bfloat16, float>(P, grid, block, dy, dy_ld, x, x_ld, dw, db, rows_per_block, s);
+  else if (xb) wgrad_t<float, __nv_bfloat16>(P, grid, block, dy, dy_ld, x, x_ld, dw, db, rows_per_block, s);
+  else wgrad_t<float, float>(P, grid, block, dy, dy_ld, x, x_ld, dw, db, rows_per_block, s);
   return cudaGetLastError();
 }
 

@@ -240,19 +240,24 @@ def conv_weight_kc(w: torch.Tensor) -> torch.Tensor:
 
 def dwconv_fwd(shape: ConvShape, x: torch.Tensor, weight_kc: torch.Tensor, bias: Optional[torch.Tensor] = None,
                bias2: Optional[torch.Tensor] = None, epilogue: int = _lib.MSL_EPI_NONE,
-               aux: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y = epilogue(depthwise_conv(x) + bias [+ bias2]); x/y [rows, >=C] row views."""
+               aux: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+               out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """y = epilogue(depthwise_conv(x) + bias [+ bias2]); x/y [rows, >=C] row views.  y (and aux)
+    have ``out_dtype`` (default: x's dtype)."""
     _need_cuda(x, weight_kc, bias, bias2, aux)
     for t, nm in ((weight_kc, "weight"), (bias, "bias"), (bias2, "bias2")):
         if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
             raise TypeError(f"{nm} must be a contiguous float32 tensor")
     if out is None:
-        out = torch.empty(shape.out_rows, shape.channels, device=x.device, dtype=x.dtype)
+        out = torch.empty(shape.out_rows, shape.channels, device=x.device, dtype=out_dtype or x.dtype)
+    if aux is not None and aux.dtype != out.dtype:
+        raise TypeError("aux must have the output's dtype")
     g = shape.geometry(x.dtype)
     with torch.cuda.device(x.device):
         rc = _call("msl_dwconv3d_fwd", x.device, lambda: _lib.load().msl_dwconv3d_fwd(
             ctypes.byref(g), _ptr(x), _rows(x, "x"), _ptr(weight_kc), _ptr(bias), _ptr(bias2), int(epilogue),
-            _ptr(aux), _rows(aux, "aux") if aux is not None else 0, _ptr(out), _rows(out, "y"), _stream(x.device)))
+            _ptr(aux), _rows(aux, "aux") if aux is not None else 0, _ptr(out), _rows(out, "y"),
+            dtype_code(out.dtype), _stream(x.device)))
     _lib.check("msl_dwconv3d_fwd", rc)
     return out
 
@@ -276,11 +281,11 @@ def dwconv_bwd_weight(shape: ConvShape, dy: torch.Tensor, x: torch.Tensor, dweig
                       dbias: Optional[torch.Tensor] = None) -> None:
     """dweight_kc [K, C] += sum dy * shifted x ; dbias [C] += sum dy (float32, accumulated)."""
     _need_cuda(dy, x, dweight_kc, dbias)
-    g = shape.geometry(dy.dtype)
+    g = shape.geometry(x.dtype)
     with torch.cuda.device(dy.device):
         rc = _call("msl_dwconv3d_bwd_weight", dy.device, lambda: _lib.load().msl_dwconv3d_bwd_weight(
-            ctypes.byref(g), _ptr(dy), _rows(dy, "dy"), _ptr(x), _rows(x, "x"), _ptr(dweight_kc), _ptr(dbias),
-            _stream(dy.device)))
+            ctypes.byref(g), _ptr(dy), _rows(dy, "dy"), dtype_code(dy.dtype), _ptr(x), _rows(x, "x"),
+            _ptr(dweight_kc), _ptr(dbias), _stream(dy.device)))
     _lib.check("msl_dwconv3d_bwd_weight", rc)
 
 

@@ -136,8 +136,8 @@ def test_bwd_requires_workspace():
 def test_dwconv_halo_coverage_is_checked():
     lib = _lib.load()
     g = _lib.DwconvGeometry(1, 8, 4, 4, 16, 3, 3, 3, 2, 3, 2, 3, 0)  # input frames [2,5) for outputs [2,5)
-    rc = lib.msl_dwconv3d_fwd(ctypes.byref(g), 16, 16, 16, None, None, 0, None, 0, 16, 16, None)
+    rc = lib.msl_dwconv3d_fwd(ctypes.byref(g), 16, 16, 16, None, None, 0, None, 0, 16, 16, 0, None)
     assert rc == _lib.MSL_ERR_INVALID and "cover" in _err()
     g = _lib.DwconvGeometry(1, 4, 4, 4, 16, 3, 3, 3, 0, 4, 0, 4, 0)
-    rc = lib.msl_dwconv3d_fwd(ctypes.byref(g), 16, 16, 16, None, None, 9, None, 0, 16, 16, None)
+    rc = lib.msl_dwconv3d_fwd(ctypes.byref(g), 16, 16, 16, None, None, 9, None, 0, 16, 16, 0, None)
     assert rc == _lib.MSL_ERR_INVALID and "epilogue" in _err()

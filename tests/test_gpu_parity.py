@@ -17,6 +17,11 @@ pytestmark = pytest.mark.gpu
 
 RTOL_F32 = 1e-4
 RTOL_BF16 = 2e-2
+# bf16 gradients: relative Frobenius error <= RTOL_BF16 plus a max-abs sanity bound.  The reference's
+# own bf16 path (autocast, attention.py run by examples/run_hybrid_attention_experiment.py:150-167)
+# lands 4.7-4.8% (max-abs) / 1.5-2.4% (Frobenius) away from float64 on the extra_kv and
+# tiny_large_offsets fixtures, so a 2% max-abs bar on gradients is stricter than the reference meets.
+MAXREL_BF16_GRAD = 5e-2
 DEV = "cuda:0"
 
 
@@ -32,6 +37,12 @@ def rel(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def fro(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
 def run_module(case, dtype=torch.float32):
@@ -76,11 +87,11 @@ def test_module_bf16_matches_oracle(name):
     res = run_module(case, torch.bfloat16)
     ref = gc.run_oracle(case)
     assert rel(res["y"], ref["y"]) < RTOL_BF16
-    assert rel(res["dx"], ref["dx"]) < RTOL_BF16
+    assert fro(res["dx"], ref["dx"]) < RTOL_BF16 and rel(res["dx"], ref["dx"]) < MAXREL_BF16_GRAD
     for k, g in ref["grads"].items():
         if k == "k_proj.bias":
             continue  # mathematically zero: rounding noise only
-        assert rel(res["grads"][k], g) < RTOL_BF16 * 2.5, k
+        assert fro(res["grads"][k], g) < RTOL_BF16 and rel(res["grads"][k], g) < MAXREL_BF16_GRAD, k
 
 
 CORE_CASES = [

@@ -130,6 +130,22 @@ size_t msl_dsa_attn_bwd_workspace_bytes(const msl_dsa_geometry* geom, int32_t ac
 int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Capacity of the scratch array msl_dsa_attn_bwd_noalloc uses (64 MiB on every GPU that loads
+ * the library, held until the process exits). */
+#define MSL_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+
+/* msl_dsa_attn_bwd without a caller-provided workspace: it allocates nothing.  No counterpart in
+ * the reference.  For callers that cannot call cudaMalloc - a plugin whose host engine owns every
+ * byte of device memory through its own pool, or code that must not trigger the implicit device
+ * synchronisation and possible out-of-memory failure of an allocation in the middle of a step.
+ * Its float32 scratch lives in one static device array of MSL_NOALLOC_SCRATCH_BYTES per GPU; a
+ * problem needing more (msl_dsa_attn_bwd_workspace_bytes) is rejected with MSL_ERR_WORKSPACE.
+ * The first call on a device looks the array's address up (call it once before any stream
+ * capture).  Every call shares the array and clears what it accumulates into, so two calls whose
+ * work overlaps on the GPU (different streams, or different threads) race and must be ordered by
+ * the caller.  Arguments and results are those of msl_dsa_attn_bwd. */
+int msl_dsa_attn_bwd_noalloc(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, void* stream);
+
 /* ----------------------------------------------------------------------------------------------
  * Depthwise 3D convolution over channels-last tokens [B, frames*H*W, C] with zero padding
  * (kt/2, kh/2, kw/2) at the borders of the GLOBAL volume.  Replaces nn.Conv3d(groups=C) of

@@ -25,6 +25,7 @@ MSL_STATUS_HALO_MISS = 1
 MSL_EPI_NONE = 0
 MSL_EPI_GELU = 1
 MSL_EPI_GELU_GRAD = 2
+MSL_NOALLOC_SCRATCH_BYTES = 64 * 1024 * 1024
 
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -84,6 +85,7 @@ SIGNATURES = {
     "msl_dsa_attn_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(DsaGeometry), _i32]),
     "msl_dsa_attn_bwd": (ctypes.c_int, [ctypes.POINTER(DsaGeometry), ctypes.POINTER(DsaBwdIO), _vp,
                                         ctypes.c_size_t, _vp]),
+    "msl_dsa_attn_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(DsaGeometry), ctypes.POINTER(DsaBwdIO), _vp]),
     "msl_dwconv3d_fwd": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _vp, _vp, _i32, _vp,
                                         _i64, _vp, _i64, _i32, _vp]),
     "msl_dwconv3d_bwd_data": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _vp, _i64, _vp]),

@@ -147,6 +147,11 @@ int fill_conv(const msl_dwconv_geometry* g, msl::ConvParams& P) {
 
 }  // namespace
 
+namespace msl {
+// Records an error for msl_last_error() from another translation unit of the library.
+int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace msl
+
 extern "C" {
 
 int32_t msl_abi_version(void) { return MSL_ABI_VERSION; }

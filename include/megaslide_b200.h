@@ -45,6 +45,14 @@ extern "C" {
 
 /* bits of the optional device status word */
 #define MSL_STATUS_HALO_MISS 1u  /* a sample corner fell in a frame the K/V buffers do not hold */
+#define MSL_STATUS_TC_RANGE 2u   /* tensor-core path: a tile's key envelope needed more than 255
+                                    chunks per axis (offsets of hundreds of voxels); its results are
+                                    not valid - rerun with MSL_ALGO_SIMT */
+
+/* kernel family */
+#define MSL_ALGO_AUTO 0 /* tensor-core envelope kernels when supported (bf16, head_dim % 8 == 0, <= 128) */
+#define MSL_ALGO_SIMT 1 /* CUDA-core gather kernels (float32 and bf16, any head_dim <= 128) */
+#define MSL_ALGO_TC 2   /* tensor-core envelope kernels; MSL_ERR_UNSUPPORTED when not applicable */
 
 /* ----------------------------------------------------------------------------------------------
  * Geometry of one deformable-slide-attention call.
@@ -69,6 +77,7 @@ typedef struct msl_dsa_geometry {
   float offset_scale;  /* multiplies the raw offsets (attention.py:106) */
   float dropout_p;     /* dropout on the softmax weights (attention.py:180); 0 = off */
   uint64_t dropout_seed;
+  int32_t algo;        /* MSL_ALGO_* */
 } msl_dsa_geometry;
 
 /* Forward operands.  q: [B, q rows, >=nh*d]; k, v: [B, kv rows, >=nh*d];

@@ -22,6 +22,10 @@ MSL_ERR_WORKSPACE = -4
 MSL_DTYPE_F32 = 0
 MSL_DTYPE_BF16 = 1
 MSL_STATUS_HALO_MISS = 1
+MSL_STATUS_TC_RANGE = 2
+MSL_ALGO_AUTO = 0
+MSL_ALGO_SIMT = 1
+MSL_ALGO_TC = 2
 MSL_EPI_NONE = 0
 MSL_EPI_GELU = 1
 MSL_EPI_GELU_GRAD = 2
@@ -42,7 +46,7 @@ class DsaGeometry(ctypes.Structure):
         ("heads", _i32), ("head_dim", _i32), ("kt", _i32), ("kh", _i32), ("kw", _i32),
         ("extra", _i32), ("q_frame0", _i32), ("q_frames", _i32), ("kv_frame0", _i32), ("kv_frames", _i32),
         ("dtype", _i32), ("softmax_scale", _f32), ("offset_scale", _f32), ("dropout_p", _f32),
-        ("dropout_seed", _u64),
+        ("dropout_seed", _u64), ("algo", _i32),
     ]
 
 

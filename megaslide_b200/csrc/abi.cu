@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "dsa_attn.cuh"
 #include "megaslide_b200.h"
@@ -33,6 +34,14 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 size_t elem_size(int dtype) { return dtype == MSL_DTYPE_BF16 ? 2 : 4; }
+
+// Dynamic shared memory the tensor-core kernels may use (the device's opt-in maximum per block).
+int tc_smem_limit() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return 0;
+  return v - 1024;
+}
 
 // Validates the geometry and fills the scalar part of AttnParams.
 int fill_geometry(const msl_dsa_geometry* g, msl::AttnParams& P) {
@@ -75,6 +84,8 @@ int fill_geometry(const msl_dsa_geometry* g, msl::AttnParams& P) {
     P.drop_keep_scale = 1.f;
   }
   P.seed = g->dropout_seed;
+  if (g->algo != MSL_ALGO_AUTO && g->algo != MSL_ALGO_SIMT && g->algo != MSL_ALGO_TC)
+    return fail(MSL_ERR_INVALID, "unknown algo %d", g->algo);
   const long long items = static_cast<long long>(P.B) * P.nh * P.Nq;
   if ((items + 7) / 8 > 0x7fffffffLL) return fail(MSL_ERR_UNSUPPORTED, "too many (query, head) items for one launch");
   return MSL_OK;
@@ -177,6 +188,24 @@ int msl_dsa_attn_fwd(const msl_dsa_geometry* geom, const msl_dsa_fwd_io* io, voi
   P.offsets = io->offsets; P.off_ld = io->off_ld;
   P.ek = io->ek; P.ev = io->ev; P.e_ld = io->e_ld;
   P.out = io->out; P.out_ld = io->out_ld; P.lse = io->lse; P.status = io->status;
+  if (geom->algo != MSL_ALGO_SIMT) {
+    bool ok = msl::tc_supported(P);
+    for (const auto& r : {std::make_pair(io->q, io->q_ld), std::make_pair(io->k, io->k_ld), std::make_pair(io->v, io->v_ld),
+                          std::make_pair(static_cast<const void*>(io->out), io->out_ld),
+                          std::make_pair(P.G > 0 ? io->ek : nullptr, io->e_ld),
+                          std::make_pair(P.G > 0 ? io->ev : nullptr, io->e_ld)})
+      if (r.first && (!aligned16(r.first) || r.second % 8 != 0)) ok = false;
+    msl::TcLaunch L{};
+    if (ok) ok = msl::tc_plan(P, L, tc_smem_limit());
+    if (ok) {
+      cudaError_t e = msl::launch_attn_fwd_tc(P, L, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "dsa_fwd_tc_kernel launch");
+      g_launches.fetch_add(1, std::memory_order_relaxed);
+      return MSL_OK;
+    }
+    if (geom->algo == MSL_ALGO_TC)
+      return fail(MSL_ERR_UNSUPPORTED, "tensor-core path needs bf16, head_dim %% 8 == 0 in [16,128], 16-byte aligned rows");
+  }
   int vec = 1, maxc = 1;
   rc = choose_chunking(P, {{io->q, io->q_ld}, {io->k, io->k_ld}, {io->v, io->v_ld}, {io->out, io->out_ld},
                            {P.G > 0 ? io->ek : nullptr, io->e_ld}, {P.G > 0 ? io->ev : nullptr, io->e_ld}},

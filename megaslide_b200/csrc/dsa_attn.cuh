@@ -36,6 +36,19 @@ struct AttnParams {
   uint32_t* status;
 };
 
+// Launch plan of the tensor-core kernels (key-envelope chunk capacity and shared-memory layout).
+struct TcLaunch {
+  int maxkeys;  // keys per envelope chunk (multiple of 16)
+  int rs;       // shared-memory row stride of a key (bf16 elements)
+  int sld;      // row stride of the score / P~ buffer (floats)
+  int tiles_h, tiles_w;
+  long long tiles;
+  size_t smem;
+};
+bool tc_supported(const AttnParams& P);
+bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit);
+cudaError_t launch_attn_fwd_tc(const AttnParams& P, const TcLaunch& L, cudaStream_t s);
+
 bool attn_chunking(int dtype, int d, int* vec, int* maxc);
 cudaError_t launch_attn_fwd(const AttnParams& P, int vec, int maxc, cudaStream_t s);
 cudaError_t launch_attn_bwd(const AttnParams& P, int vec, int maxc, cudaStream_t s);

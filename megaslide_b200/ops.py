@@ -98,6 +98,7 @@ class DsaShape:
     offset_scale: float = 1.0
     dropout_p: float = 0.0
     dropout_seed: int = 0
+    algo: int = 0  # 0 auto, 1 CUDA-core gather, 2 tensor-core envelope
 
     @property
     def taps(self) -> int:
@@ -119,7 +120,7 @@ class DsaShape:
             self.q_frame0, self.q_frames if self.q_frames is not None else self.frames,
             self.kv_frame0, self.kv_frames if self.kv_frames is not None else self.frames,
             dtype_code(dtype), float(scale), float(self.offset_scale), float(self.dropout_p),
-            int(self.dropout_seed) & 0xFFFFFFFFFFFFFFFF)
+            int(self.dropout_seed) & 0xFFFFFFFFFFFFFFFF, int(self.algo))
 
 
 def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, offsets: torch.Tensor,

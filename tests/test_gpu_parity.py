@@ -301,3 +301,65 @@ def test_launches_counted_and_native_library_loaded():
 
     maps = open(f"/proc/{os.getpid()}/maps").read()
     assert "libmegaslide_b200.so" in maps
+
+
+# ----------------------------------------------------------------- tensor-core forward (bf16)
+TC_CASES = [
+    # B, T, H, W, nh, d, kernel, G, offset_std
+    (1, 3, 9, 11, 2, 72, (3, 7, 7), 0, 1.0),      # partial 8x8 tiles, config-2 head_dim
+    (2, 2, 16, 16, 2, 64, (3, 7, 7), 3, 0.5),     # extra keys, even chunk count (padded rows)
+    (1, 2, 8, 8, 1, 128, (3, 3, 3), 0, 3.0),      # config-5 head_dim
+    (1, 3, 6, 7, 2, 24, (3, 3, 3), 2, 2.0),       # odd number of 16-byte chunks: k8 tail
+    (1, 2, 32, 32, 1, 16, (1, 3, 3), 0, 20.0),    # offsets of ~10 voxels: envelope split in chunks
+    (1, 1, 5, 5, 2, 40, (1, 3, 3), 0, 0.0),       # T=1, zero offsets
+]
+
+
+def _tc_ids(c):
+    return f"B{c[0]}T{c[1]}H{c[2]}W{c[3]}nh{c[4]}d{c[5]}k{''.join(map(str, c[6]))}G{c[7]}o{c[8]}"
+
+
+def _run_fwd(case, arrays, algo, dropout_p=0.0, seed=0, status=None):
+    B, T, H, W, nh, d, ks, G, _ = case
+    q, k, v, off, ek, ev, _dout = arrays
+    N = T * H * W
+    C = nh * d
+    t = lambda a: None if a is None else torch.from_numpy(a).to(DEV, torch.bfloat16).reshape(-1, C)  # noqa: E731
+    shape = ops.DsaShape(B, T, H, W, nh, d, ks, extra=G, dropout_p=dropout_p, dropout_seed=seed, algo=algo)
+    offt = torch.from_numpy(off).to(DEV).reshape(B * N, -1)
+    out, lse = ops.attn_fwd(shape, t(q), t(k), t(v), offt, t(ek), t(ev), status=status)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy().reshape(B, N, C), lse.cpu().numpy()
+
+
+@pytest.mark.parametrize("case", TC_CASES, ids=_tc_ids)
+def test_tc_forward_matches_oracle_and_cuda_core_path(case):
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))
+                   for i, a in enumerate(_core_inputs(case, seed=7)))
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out_tc, lse_tc = _run_fwd(case, arrays, algo=2, status=status)
+    assert int(status.item()) == 0
+    out_simt, lse_simt = _run_fwd(case, arrays, algo=1)
+    ref = _oracle_core(case, arrays)
+    assert rel(out_tc, ref["out"]) < RTOL_BF16
+    assert rel(lse_tc, ref["lse"]) < 1e-3
+    assert rel(out_tc, out_simt) < RTOL_BF16
+
+
+def test_tc_forward_dropout_matches_oracle_mask():
+    case = (1, 3, 8, 8, 2, 32, (3, 3, 3), 2, 1.0)
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))
+                   for i, a in enumerate(_core_inputs(case, seed=9)))
+    out_tc, _ = _run_fwd(case, arrays, algo=2, dropout_p=0.3, seed=1234)
+    ref = _oracle_core(case, arrays, dropout_p=0.3, seed=1234)
+    assert rel(out_tc, ref["out"]) < RTOL_BF16
+
+
+def test_tc_path_rejects_float32():
+    case = (1, 2, 4, 4, 1, 16, (3, 3, 3), 0, 1.0)
+    B, T, H, W, nh, d, ks, G, _ = case
+    q = torch.randn(B * T * H * W, nh * d, device=DEV)
+    off = torch.zeros(B * T * H * W, nh * 27 * 3, device=DEV)
+    shape = ops.DsaShape(B, T, H, W, nh, d, ks, algo=2)
+    with pytest.raises(msl.MslError, match="tensor-core"):
+        ops.attn_fwd(shape, q, q, q, off)

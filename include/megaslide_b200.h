@@ -84,7 +84,10 @@ typedef struct msl_dsa_geometry {
  * ek, ev: [B, G, >=nh*d] already projected by k_proj / v_proj (attention.py:163-164), or NULL;
  * out: [B, q rows, >=nh*d] attention result before out_proj (attention.py:183-186);
  * lse: float32 [B, nh, q rows], base-2 log-sum-exp of the log2(e)-scaled scores (saved for
- * the backward pass); status: optional device word OR-ed with MSL_STATUS_* bits. */
+ * the backward pass); status: optional device word OR-ed with MSL_STATUS_* bits;
+ * probs: optional float32 [B, nh, q rows, kt*kh*kw], the softmax weight of every window sample
+ * before dropout (extra keys excluded), written only by the tensor-core path (MSL_ALGO_TC, or
+ * MSL_ALGO_AUTO when it applies) and consumed by the tensor-core backward; NULL = not saved. */
 typedef struct msl_dsa_fwd_io {
   const void* q;   int64_t q_ld;
   const void* k;   int64_t k_ld;
@@ -94,6 +97,7 @@ typedef struct msl_dsa_fwd_io {
   void* out;       int64_t out_ld;
   float* lse;
   uint32_t* status;
+  float* probs;
 } msl_dsa_fwd_io;
 
 /* Backward operands.  Inputs as in the forward plus out/lse from it and dout = dL/d out.
@@ -105,7 +109,9 @@ typedef struct msl_dsa_fwd_io {
  *                   live in the workspace.
  *   dk_acc != NULL: float32 dk_acc, dv_acc [B, kv rows, >=nh*d] (row stride acc_ld) are
  *                   ACCUMULATED into (not cleared), dk / dv are not touched.  Used by the
- *                   time-sharded path, which reduces halo rows across ranks before converting. */
+ *                   time-sharded path, which reduces halo rows across ranks before converting.
+ * probs: the forward's optional softmax weights (see msl_dsa_fwd_io).  When given (bf16, no extra
+ * keys) the tensor-core backward runs; NULL selects the CUDA-core backward. */
 typedef struct msl_dsa_bwd_io {
   const void* q;   int64_t q_ld;
   const void* k;   int64_t k_ld;
@@ -121,6 +127,7 @@ typedef struct msl_dsa_bwd_io {
   float* doffsets; int64_t doff_ld;
   float* dek;      float* dev;
   uint32_t* status;
+  const float* probs;
 } msl_dsa_bwd_io;
 
 /* Forward of the deformable gather attention: for every query, head and window sample, the

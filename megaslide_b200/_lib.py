@@ -56,7 +56,7 @@ class DsaFwdIO(ctypes.Structure):
     _fields_ = [
         ("q", _vp), ("q_ld", _i64), ("k", _vp), ("k_ld", _i64), ("v", _vp), ("v_ld", _i64),
         ("offsets", _vp), ("off_ld", _i64), ("ek", _vp), ("ev", _vp), ("e_ld", _i64),
-        ("out", _vp), ("out_ld", _i64), ("lse", _vp), ("status", _vp),
+        ("out", _vp), ("out_ld", _i64), ("lse", _vp), ("status", _vp), ("probs", _vp),
     ]
 
 
@@ -69,7 +69,7 @@ class DsaBwdIO(ctypes.Structure):
         ("out", _vp), ("out_ld", _i64), ("lse", _vp), ("dout", _vp), ("dout_ld", _i64),
         ("dq", _vp), ("dq_ld", _i64), ("dk", _vp), ("dv", _vp), ("dkv_ld", _i64),
         ("dk_acc", _vp), ("dv_acc", _vp), ("acc_ld", _i64),
-        ("doffsets", _vp), ("doff_ld", _i64), ("dek", _vp), ("dev", _vp), ("status", _vp),
+        ("doffsets", _vp), ("doff_ld", _i64), ("dek", _vp), ("dev", _vp), ("status", _vp), ("probs", _vp),
     ]
 
 

@@ -30,7 +30,7 @@ import torch.nn as nn
 from torch import Tensor
 
 from . import ops
-from ._lib import MSL_EPI_GELU, MSL_EPI_GELU_GRAD, MSL_EPI_NONE
+from ._lib import MSL_EPI_GELU, MSL_EPI_GELU_GRAD, MSL_EPI_NONE, MSL_ERR_UNSUPPORTED, MslError
 
 
 def _mm_f32(a: Tensor, b: Tensor) -> Tensor:
@@ -84,10 +84,22 @@ class DSA3DFunction(torch.autograd.Function):
             e2 = extra_kv.reshape(B * G, C).to(dt).contiguous()
             ekv = torch.addmm(torch.cat([bk, bv], 0).to(dt), e2, torch.cat([wk, wv], 0).to(dt).t())
             ek, ev = ekv[:, :C], ekv[:, C:]
-        attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev)
+        train = any(ctx.needs_input_grad)
+        probs = None
+        if train and ops.wants_probs(sh, dt):
+            # the tensor-core backward reads the forward's per-sample softmax weights
+            probs = ops.probs_buffer(sh, x2.device)
+            try:
+                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs)
+            except MslError as e:
+                if e.code != MSL_ERR_UNSUPPORTED:
+                    raise
+                probs = None
+        if probs is None:
+            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev)
         y = torch.addmm(D, attn, wo.to(dt).t())
-        if any(ctx.needs_input_grad):
-            ctx.save_for_backward(x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc)
+        if train:
+            ctx.save_for_backward(x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs)
             ctx.cfg = cfg
             ctx.in_dtype = x.dtype
             ctx.extra_dtype = extra_kv.dtype if extra_kv is not None else None
@@ -95,7 +107,7 @@ class DSA3DFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        (x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc) = ctx.saved_tensors
+        (x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs) = ctx.saved_tensors
         cfg: _Cfg = ctx.cfg
         sh: ops.DsaShape = cfg.shape
         dt = cfg.dtype
@@ -118,7 +130,7 @@ class DSA3DFunction(torch.autograd.Function):
             q, k, v = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
             _, _, _, doff, dek, dev = ops.attn_bwd(
                 sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev,
-                dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:])
+                dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs)
             # q/k/v projections
             dx += _mm_f32(dqkv, wqkv)
             g_wqkv = _mm_f32(dqkv.t(), x2)

@@ -187,7 +187,7 @@ int msl_dsa_attn_fwd(const msl_dsa_geometry* geom, const msl_dsa_fwd_io* io, voi
   P.q = io->q; P.q_ld = io->q_ld; P.k = io->k; P.k_ld = io->k_ld; P.v = io->v; P.v_ld = io->v_ld;
   P.offsets = io->offsets; P.off_ld = io->off_ld;
   P.ek = io->ek; P.ev = io->ev; P.e_ld = io->e_ld;
-  P.out = io->out; P.out_ld = io->out_ld; P.lse = io->lse; P.status = io->status;
+  P.out = io->out; P.out_ld = io->out_ld; P.lse = io->lse; P.status = io->status; P.probs = io->probs;
   if (geom->algo != MSL_ALGO_SIMT) {
     bool ok = msl::tc_supported(P);
     for (const auto& r : {std::make_pair(io->q, io->q_ld), std::make_pair(io->k, io->k_ld), std::make_pair(io->v, io->v_ld),
@@ -203,9 +203,11 @@ int msl_dsa_attn_fwd(const msl_dsa_geometry* geom, const msl_dsa_fwd_io* io, voi
       g_launches.fetch_add(1, std::memory_order_relaxed);
       return MSL_OK;
     }
-    if (geom->algo == MSL_ALGO_TC)
-      return fail(MSL_ERR_UNSUPPORTED, "tensor-core path needs bf16, head_dim %% 8 == 0 in [16,128], 16-byte aligned rows");
+    if (geom->algo == MSL_ALGO_TC || io->probs)
+      return fail(MSL_ERR_UNSUPPORTED, "tensor-core path (%s) needs bf16, head_dim %% 8 == 0 in [16,128], 16-byte aligned rows",
+                  io->probs ? "required by the probs output" : "algo = MSL_ALGO_TC");
   }
+  if (io->probs) return fail(MSL_ERR_UNSUPPORTED, "the probs output is written by the tensor-core path only (algo != SIMT)");
   int vec = 1, maxc = 1;
   rc = choose_chunking(P, {{io->q, io->q_ld}, {io->k, io->k_ld}, {io->v, io->v_ld}, {io->out, io->out_ld},
                            {P.G > 0 ? io->ek : nullptr, io->e_ld}, {P.G > 0 ? io->ev : nullptr, io->e_ld}},
@@ -261,6 +263,7 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
   P.out = const_cast<void*>(io->out); P.out_ld = io->out_ld; P.lse = const_cast<float*>(io->lse);
   P.dout = io->dout; P.dout_ld = io->dout_ld; P.dq = io->dq; P.dq_ld = io->dq_ld;
   P.doffsets = io->doffsets; P.doff_ld = io->doff_ld; P.status = io->status;
+  P.probs = const_cast<float*>(io->probs);
   if (accumulate) {
     P.dk_acc = io->dk_acc; P.dv_acc = io->dv_acc; P.acc_ld = io->acc_ld;
   } else {
@@ -273,6 +276,21 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
     P.extra_p = reinterpret_cast<float*>(ws + L.xp);
     P.dek = io->dek; P.dev = io->dev;
   }
+  // tensor-core backward: bf16, no extra keys, softmax weights saved by the forward, aligned rows
+  msl::TcLaunch TL{};
+  bool use_tc = false;
+  if (geom->algo != MSL_ALGO_SIMT && P.probs) {
+    use_tc = msl::tc_bwd_supported(P);
+    for (const auto& r : {std::make_pair(io->q, io->q_ld), std::make_pair(io->k, io->k_ld), std::make_pair(io->v, io->v_ld),
+                          std::make_pair(io->out, io->out_ld), std::make_pair(io->dout, io->dout_ld),
+                          std::make_pair(static_cast<const void*>(io->dq), io->dq_ld)})
+      if (!aligned16(r.first) || r.second % 8 != 0) use_tc = false;
+    if (!aligned16(P.dk_acc) || !aligned16(P.dv_acc) || P.acc_ld % 4 != 0) use_tc = false;
+    if (use_tc) use_tc = msl::tc_bwd_plan(P, TL, tc_smem_limit());
+  }
+  if (geom->algo == MSL_ALGO_TC && !use_tc)
+    return fail(MSL_ERR_UNSUPPORTED, "tensor-core backward needs probs from the tensor-core forward, bf16, no extra keys, "
+                                     "head_dim %% 8 == 0 in [16,128] and 16-byte aligned rows");
   int vec = 1, maxc = 1;
   rc = choose_chunking(P, {{io->q, io->q_ld}, {io->k, io->k_ld}, {io->v, io->v_ld}, {io->out, io->out_ld},
                            {io->dout, io->dout_ld}, {io->dq, io->dq_ld},
@@ -299,8 +317,13 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
     if (e == cudaSuccess) e = cudaMemsetAsync(P.dev, 0, nb, s);
     if (e != cudaSuccess) return cuda_fail(e, "clearing dek/dev");
   }
-  e = msl::launch_attn_bwd(P, vec, maxc, s);
-  if (e != cudaSuccess) return cuda_fail(e, "dsa_bwd_kernel launch");
+  if (use_tc) {
+    e = msl::launch_attn_bwd_tc(P, TL, s);
+    if (e != cudaSuccess) return cuda_fail(e, "dsa_bwd_tc_kernel launch");
+  } else {
+    e = msl::launch_attn_bwd(P, vec, maxc, s);
+    if (e != cudaSuccess) return cuda_fail(e, "dsa_bwd_kernel launch");
+  }
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (P.G > 0) {
     e = msl::launch_attn_extra_grad(P, s);

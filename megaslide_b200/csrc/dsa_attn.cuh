@@ -27,6 +27,7 @@ struct AttnParams {
   const void* ek; const void* ev; long long e_ld;
   void* out; long long out_ld;        // forward: written; backward: read
   float* lse;
+  float* probs;       // [B, nh, Nq, K] softmax weights before dropout (optional; tensor-core paths)
   const void* dout; long long dout_ld;
   void* dq; long long dq_ld;
   float* dk_acc; float* dv_acc; long long acc_ld;
@@ -48,6 +49,9 @@ struct TcLaunch {
 bool tc_supported(const AttnParams& P);
 bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit);
 cudaError_t launch_attn_fwd_tc(const AttnParams& P, const TcLaunch& L, cudaStream_t s);
+bool tc_bwd_supported(const AttnParams& P);
+bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit);
+cudaError_t launch_attn_bwd_tc(const AttnParams& P, const TcLaunch& L, cudaStream_t s);
 
 bool attn_chunking(int dtype, int d, int* vec, int* maxc);
 cudaError_t launch_attn_fwd(const AttnParams& P, int vec, int maxc, cudaStream_t s);

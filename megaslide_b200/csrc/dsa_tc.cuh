@@ -1,0 +1,335 @@
+// Building blocks shared by the tensor-core ("key envelope") kernels of the deformable gather
+// attention (forward: dsa_tc.cu, backward: dsa_tc_bwd.cu).  Both kernels run 512 threads per CTA on
+// a tile of queries of one frame, one head and one sample, walk the tile's key envelope one frame
+// ("plane") at a time in chunks of at most `maxkeys` keys, and do the dense per-chunk products with
+// mma.sync (bf16 in, fp32 accumulate) on operands staged in shared memory by cp.async.
+#pragma once
+
+#include <math.h>
+#include <stdint.h>
+
+#include "dsa_attn.cuh"
+#include "msl_common.cuh"
+
+namespace msl {
+namespace tc {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTileW = 8;               // tile columns; a 16-query row group = 2 tile rows
+constexpr int kEnvWords = 16 + 3 * 96;  // envelope ints + base-grid tables of the tile (<= 96 each)
+// Dense P~ matrices are accumulated with 32-bit integer shared-memory atomics in fixed point:
+// value * 2^24.  Entries are sums of trilinear weights (<= 1) times softmax weights whose sum is at
+// most the dropout keep scale 1/(1-p), so they stay below 2^32 for p <= 0.9 (host-checked).
+constexpr float kPtScale = 16777216.f;
+constexpr float kPtInv = 1.f / 16777216.f;
+
+// ------------------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3},{%4,%5,%6,%7},{%8,%9},{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma1688(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3},{%4,%5},{%6},{%0,%1,%2,%3};"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+               : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g));
+}
+__device__ __forceinline__ void cp_async4(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(saddr), "l"(g));
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// ------------------------------------------------------------------------------ tile geometry
+struct TileCtx {
+  int b, head, tl, tg, qh0, qw0;
+};
+
+// CTA -> (sample, local frame, tile row, tile column, head); heads vary fastest so the CTAs that run
+// together share their K/V rows in L2.
+__device__ __forceinline__ TileCtx decode_tile(const AttnParams& P, const TcLaunch& L, int tile_h) {
+  long long t = blockIdx.x;
+  TileCtx c;
+  c.head = static_cast<int>(t % P.nh);
+  t /= P.nh;
+  const int iw = static_cast<int>(t % L.tiles_w);
+  t /= L.tiles_w;
+  const int ih = static_cast<int>(t % L.tiles_h);
+  t /= L.tiles_h;
+  c.tl = static_cast<int>(t % P.q_frames);
+  c.b = static_cast<int>(t / P.q_frames);
+  c.tg = P.q_frame0 + c.tl;
+  c.qh0 = ih * tile_h;
+  c.qw0 = iw * kTileW;
+  return c;
+}
+
+// query c (0..15) of row group r: tile rows 2r, 2r+1
+__device__ __forceinline__ void query_hw(const TileCtx& T, int r, int c, int& qh, int& qw) {
+  qh = T.qh0 + 2 * r + (c >> 3);
+  qw = T.qw0 + (c & 7);
+}
+
+// Chunking of an envelope axis [lo, hi] into windows of `len` with one element of overlap.
+__device__ __forceinline__ int axis_chunks(int lo, int hi, int len) {
+  const int n = hi - lo + 1;
+  if (n <= len) return 1;
+  return 1 + (n - len + (len - 2)) / (len - 1);
+}
+__device__ __forceinline__ int axis_chunk_of(int v, int lo, int len, int nchunks) {
+  if (nchunks == 1) return 0;
+  const int i = (v - lo) / (len - 1);
+  return i < nchunks - 1 ? i : nchunks - 1;
+}
+
+struct Env {
+  int zlo, zhi, ylo, yhi, xlo, xhi;
+  int cw, R, ny, nx;  // column-chunk width, rows per chunk, chunk counts
+};
+
+// Base-grid values 2a/max(S-1,1) - 1 of the window positions a tile can reach, per axis, computed once
+// per CTA with the same float32 operations as base_grid(); tz covers frames tg - kt/2 .. tg + kt/2,
+// ty rows qh0 - kh/2 .. qh0 + tile_h - 1 + kh/2, tx columns qw0 - kw/2 .. qw0 + 7 + kw/2.
+struct Tabs {
+  const float *tz, *ty, *tx;
+};
+
+__device__ __forceinline__ void fill_tabs(const AttnParams& P, const TileCtx& T, int tile_h, float* tz, float* ty,
+                                          float* tx) {
+  for (int i = threadIdx.x; i < P.kt + P.kh + tile_h - 1 + P.kw + kTileW - 1; i += kThreads) {
+    if (i < P.kt) {
+      tz[i] = base_grid(T.tg + i - P.kt / 2, P.T);
+    } else if (i < P.kt + P.kh + tile_h - 1) {
+      const int k = i - P.kt;
+      ty[k] = base_grid(T.qh0 + k - P.kh / 2, P.H);
+    } else {
+      const int k = i - P.kt - P.kh - tile_h + 1;
+      tx[k] = base_grid(T.qw0 + k - P.kw / 2, P.W);
+    }
+  }
+}
+
+// sample_coords() with the base grid read from the tables: (qy, qx) are the query's row / column
+// inside the tile, (it, ih, iw) the window index.  Same float32 operations, same result.
+__device__ __forceinline__ void tab_coords(const AttnParams& P, const Tabs& tb, int qy, int qx, int it, int ih, int iw,
+                                           float o0, float o1, float o2, float& pt, float& ph, float& pw) {
+  float gx = tb.tx[qx + iw], gy = tb.ty[qy + ih], gz = tb.tz[it];
+  if (P.T > 1) gx = __fadd_rn(gx, __fdiv_rn(__fmul_rn(o0, P.oscale), static_cast<float>(P.T - 1)));
+  if (P.H > 1) gy = __fadd_rn(gy, __fdiv_rn(__fmul_rn(o1, P.oscale), static_cast<float>(P.H - 1)));
+  if (P.W > 1) gz = __fadd_rn(gz, __fdiv_rn(__fmul_rn(o2, P.oscale), static_cast<float>(P.W - 1)));
+  pw = unnormalize_clip(gx, P.W);
+  ph = unnormalize_clip(gy, P.H);
+  pt = unnormalize_clip(gz, P.T);
+}
+
+// Window index (it, ih, iw) of sample j, advanced by `step` samples without integer division.
+struct WinIdx {
+  int it, ih, iw;
+  __device__ __forceinline__ void init(int j, int kh, int kw) {
+    it = j / (kh * kw);
+    const int r = j - it * kh * kw;
+    ih = r / kw;
+    iw = r - ih * kw;
+  }
+  __device__ __forceinline__ void advance(int step, int kh, int kw) {
+    iw += step;
+    while (iw >= kw) {
+      iw -= kw;
+      if (++ih == kh) {
+        ih = 0;
+        ++it;
+      }
+    }
+  }
+};
+
+// ------------------------------------------------------------------------------ sample records
+// Packed per-sample record (0 = inactive sample):
+//   bits  0-11, 12-23, 24-35: fractions pt - t0, ph - h0, pw - w0 as 12-bit unorm
+//   bits 36-40: t0 - zlo + 1,  41-48: h0 - ylo,  49-56: w0 - xlo,  bit 63: active
+//   bits 57-62: free for kernel-specific flags
+__device__ __forceinline__ uint32_t quant12(float f) {
+  int u = __float2int_rn(f * 4096.f);
+  return static_cast<uint32_t>(u < 0 ? 0 : (u > 4095 ? 4095 : u));
+}
+__device__ __forceinline__ unsigned long long pack_rec(float ft, float fh, float fw, int dz, int dy, int dx) {
+  return static_cast<unsigned long long>(quant12(ft)) | (static_cast<unsigned long long>(quant12(fh)) << 12) |
+         (static_cast<unsigned long long>(quant12(fw)) << 24) | (static_cast<unsigned long long>(dz) << 36) |
+         (static_cast<unsigned long long>(dy) << 41) | (static_cast<unsigned long long>(dx) << 49) | (1ull << 63);
+}
+struct Rec {
+  float ft, fh, fw;
+  int t0, h0, w0;
+};
+__device__ __forceinline__ Rec unpack_rec(unsigned long long v, const Env& E) {
+  Rec r;
+  r.ft = static_cast<float>(v & 0xfffu) * (1.f / 4096.f);
+  r.fh = static_cast<float>((v >> 12) & 0xfffu) * (1.f / 4096.f);
+  r.fw = static_cast<float>((v >> 24) & 0xfffu) * (1.f / 4096.f);
+  r.t0 = E.zlo - 1 + static_cast<int>((v >> 36) & 0x1fu);
+  r.h0 = E.ylo + static_cast<int>((v >> 41) & 0xffu);
+  r.w0 = E.xlo + static_cast<int>((v >> 49) & 0xffu);
+  return r;
+}
+// true when the active record has a corner in plane zrel (relative frame, zlo -> 1)
+__device__ __forceinline__ bool rec_in_plane(unsigned long long v, int zrel) {
+  return (v >> 63) && static_cast<unsigned>(zrel - static_cast<int>((v >> 36) & 0x1fu)) <= 1u;
+}
+// weight factor of the lower (upper = 0) or upper corner along one axis from the fraction
+__device__ __forceinline__ float frac_weight(float f, int upper) { return upper ? f : 1.f - f; }
+
+// ------------------------------------------------------------------------------ chunk operands
+// Loads keys (z, y, x) for y in [ya, yb], x in [xa, xb] of one head into kbuf rows
+// (y - ya) * ncw + (x - xa); rows past the chunk (up to nkp) and keys outside the volume or the
+// K/V frame window are zero.  DCH = head_dim / 8 sixteen-byte chunks per key.
+template <int DCH>
+__device__ __forceinline__ void load_chunk(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
+                                           const __nv_bfloat16* base, long long ld, int z, int ya, int yb, int xa,
+                                           int xb, int nkp) {
+  const int ncw = xb - xa + 1;
+  const int nk = (yb - ya + 1) * ncw;
+  const int zl = z - P.kv_frame0;
+  const bool zok = zl >= 0 && zl < P.kv_frames;
+  const __nv_bfloat16* gb = base + static_cast<long long>(T.b) * P.Nkv * ld + T.head * P.d;
+  // one key row (ncw keys x DCH chunks) per step; row-major within the chunk
+  const int per_row = ncw * DCH;
+  for (int y = ya; y <= yb; ++y) {
+    const bool yok = zok && y >= 0 && y < P.H;
+    const int kb = (y - ya) * ncw;
+    const __nv_bfloat16* grow = gb + ((static_cast<long long>(zl) * P.H + y) * P.W) * ld;
+    for (int idx = threadIdx.x; idx < per_row; idx += kThreads) {
+      const int kx = idx / DCH, ch = idx - (idx / DCH) * DCH;  // DCH is a compile-time constant
+      const int x = xa + kx;
+      __nv_bfloat16* dst = kbuf + static_cast<size_t>(kb + kx) * rs + ch * 8;
+      if (yok && x >= 0 && x < P.W)
+        cp_async16(smem_u32(dst), grow + static_cast<long long>(x) * ld + ch * 8);
+      else
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  for (int idx = nk * DCH + threadIdx.x; idx < nkp * DCH; idx += kThreads) {  // padding keys
+    const int key = idx / DCH, ch = idx - (idx / DCH) * DCH;
+    *reinterpret_cast<uint4*>(kbuf + static_cast<size_t>(key) * rs + ch * 8) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  cp_async_wait_all();
+}
+
+// srow[16 queries][nkp keys] = A . kbuf^T for one 16-row group: A in registers (m16n8k16 A fragments
+// of the group's rows, DCH / 2 k-steps plus an m16n8k8 tail for odd DCH); the WPG warps of the group
+// split the 16-key column blocks round robin (`part` = warp index within the group).
+template <int DCH, int WPG>
+__device__ __forceinline__ void dense_scores(const __nv_bfloat16* kbuf, int rs, float* srow, int sld, int part, int nkp,
+                                             const uint32_t (&qa)[DCH / 2 > 0 ? DCH / 2 : 1][4],
+                                             const uint32_t (&qt)[2]) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int mi = lane >> 3, rr = lane & 7;
+  for (int gi = part; gi * 16 < nkp; gi += WPG) {
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    // x4 matrices: (keys +0..7, d +0..7) (keys +0..7, d +8..15) (keys +8..15, d +0..7) (keys +8..15, d +8..15)
+    const int key = gi * 16 + rr + ((mi >> 1) ? 8 : 0);
+    const __nv_bfloat16* rowp = kbuf + static_cast<size_t>(key) * rs + ((mi & 1) ? 8 : 0);
+#pragma unroll
+    for (int ks = 0; ks < DCH / 2; ++ks) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(smem_u32(rowp + ks * 16), b0, b1, b2, b3);
+      mma16816(c0, qa[ks], b0, b1);
+      mma16816(c1, qa[ks], b2, b3);
+    }
+    if constexpr (DCH & 1) {
+      const int key2 = gi * 16 + rr + ((mi & 1) ? 8 : 0);
+      uint32_t e0, e1;
+      ldsm_x2(smem_u32(kbuf + static_cast<size_t>(key2) * rs + (DCH - 1) * 8), e0, e1);
+      mma1688(c0, qt[0], qt[1], e0);
+      mma1688(c1, qt[0], qt[1], e1);
+    }
+    float* p0 = srow + static_cast<size_t>(g) * sld + gi * 16 + 2 * t4;
+    float* p1 = srow + static_cast<size_t>(g + 8) * sld + gi * 16 + 2 * t4;
+    *reinterpret_cast<float2*>(p0) = make_float2(c0[0], c0[1]);
+    *reinterpret_cast<float2*>(p1) = make_float2(c0[2], c0[3]);
+    *reinterpret_cast<float2*>(p0 + 8) = make_float2(c1[0], c1[1]);
+    *reinterpret_cast<float2*>(p1 + 8) = make_float2(c1[2], c1[3]);
+  }
+}
+
+// o[16][d tiles nt0..nt1) += A[16][nkp] . vbuf[nkp][d] for one 16-row group.  A is read from the
+// group's rows of a shared fp32 matrix (FIXED: u32 fixed point, scaled by 2^-24) and rounded to bf16
+// fragments; vbuf rows (keys) through ldmatrix.trans.  o[j] accumulates d tile nt0 + j.
+template <int DCH, int TPW, bool FIXED>
+__device__ __forceinline__ void av_product(const float* arow, int sld, const __nv_bfloat16* vbuf, int rs, int nt0,
+                                           int nt1, int nkp, float (&o)[TPW + 1][4]) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int mi = lane >> 3, rr = lane & 7;
+  for (int kk = 0; kk * 16 < nkp; ++kk) {
+    const float* a0p = arow + static_cast<size_t>(g) * sld + kk * 16 + 2 * t4;
+    const float* a1p = arow + static_cast<size_t>(g + 8) * sld + kk * 16 + 2 * t4;
+    uint32_t a[4];
+    if constexpr (FIXED) {
+      const uint2 x0 = *reinterpret_cast<const uint2*>(a0p);
+      const uint2 x1 = *reinterpret_cast<const uint2*>(a1p);
+      const uint2 x2 = *reinterpret_cast<const uint2*>(a0p + 8);
+      const uint2 x3 = *reinterpret_cast<const uint2*>(a1p + 8);
+      a[0] = pack_bf16(x0.x * kPtInv, x0.y * kPtInv);
+      a[1] = pack_bf16(x1.x * kPtInv, x1.y * kPtInv);
+      a[2] = pack_bf16(x2.x * kPtInv, x2.y * kPtInv);
+      a[3] = pack_bf16(x3.x * kPtInv, x3.y * kPtInv);
+    } else {
+      const float2 x0 = *reinterpret_cast<const float2*>(a0p);
+      const float2 x1 = *reinterpret_cast<const float2*>(a1p);
+      const float2 x2 = *reinterpret_cast<const float2*>(a0p + 8);
+      const float2 x3 = *reinterpret_cast<const float2*>(a1p + 8);
+      a[0] = pack_bf16(x0.x, x0.y);
+      a[1] = pack_bf16(x1.x, x1.y);
+      a[2] = pack_bf16(x2.x, x2.y);
+      a[3] = pack_bf16(x3.x, x3.y);
+    }
+    // x4.trans matrices: (keys +0..7, d nt) (keys +8..15, d nt) (keys +0..7, d nt+1) (keys +8..15, d nt+1)
+    const int key = kk * 16 + rr + ((mi & 1) ? 8 : 0);
+    const __nv_bfloat16* rowp = vbuf + static_cast<size_t>(key) * rs;
+#pragma unroll
+    for (int jj = 0; jj < TPW; jj += 2) {
+      const int nt = nt0 + jj;
+      if (nt + 1 < nt1) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(rowp + (nt + (mi >> 1)) * 8), b0, b1, b2, b3);
+        mma16816(o[jj], a, b0, b1);
+        mma16816(o[jj + 1], a, b2, b3);
+      } else if (nt < nt1) {
+        uint32_t b0, b1;
+        ldsm_x2_t(smem_u32(rowp + nt * 8), b0, b1);
+        mma16816(o[jj], a, b0, b1);
+      }
+    }
+  }
+}
+
+}  // namespace tc
+}  // namespace msl

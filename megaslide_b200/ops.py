@@ -123,14 +123,37 @@ class DsaShape:
             int(self.dropout_seed) & 0xFFFFFFFFFFFFFFFF, int(self.algo))
 
 
+def wants_probs(shape: DsaShape, dtype: torch.dtype) -> bool:
+    """Host-side pre-check for the tensor-core backward, which needs the forward's softmax weights
+    (``probs``): bf16, no extra keys, head_dim a multiple of 8 in [16, 128], algo not forced to the
+    CUDA-core gather.  The library makes the final decision (alignment, shared-memory plan)."""
+    return (dtype == torch.bfloat16 and shape.extra == 0 and shape.algo != _lib.MSL_ALGO_SIMT
+            and shape.head_dim % 8 == 0 and 16 <= shape.head_dim <= 128)
+
+
+def probs_buffer(shape: DsaShape, device) -> torch.Tensor:
+    """float32 [B, nh, q_rows, K] buffer for the forward's per-sample softmax weights."""
+    return torch.empty(shape.batch, shape.heads, shape.q_rows, shape.taps, device=device, dtype=torch.float32)
+
+
+def _check_probs(shape: DsaShape, probs: torch.Tensor) -> None:
+    want = (shape.batch, shape.heads, shape.q_rows, shape.taps)
+    if probs.dtype != torch.float32 or tuple(probs.shape) != want or not probs.is_contiguous():
+        raise ValueError(f"probs must be a contiguous float32 tensor of shape {want}")
+
+
 def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, offsets: torch.Tensor,
              ek: Optional[torch.Tensor] = None, ev: Optional[torch.Tensor] = None,
              out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
-             status: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+             status: Optional[torch.Tensor] = None,
+             probs: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Deformable gather attention forward.
 
     q: [B*q_rows, >=C] row view; k, v: [B*kv_rows, >=C]; offsets: float32 [B*q_rows, >=nh*K*3];
     ek, ev: [B*G, >=C] or None.  Returns (out [B*q_rows, C], lse float32 [B, nh, q_rows]).
+    probs (optional, see probs_buffer): filled with the per-sample softmax weights for the
+    tensor-core backward; the call raises MslError(MSL_ERR_UNSUPPORTED) when the tensor-core
+    forward does not apply to these operands.
     """
     _need_cuda(q, k, v, offsets, ek, ev)
     C = shape.heads * shape.head_dim
@@ -144,6 +167,10 @@ def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     io = DsaFwdIO(_ptr(q), _rows(q, "q"), _ptr(k), _rows(k, "k"), _ptr(v), _rows(v, "v"),
                   _ptr(offsets), _rows(offsets, "offsets"), _ptr(ek), _ptr(ev),
                   _rows(ek, "ek") if ek is not None else 0, _ptr(out), _rows(out, "out"), _ptr(lse), _ptr(status))
+    if probs is not None:
+        _need_cuda(probs)
+        _check_probs(shape, probs)
+        io.probs = _ptr(probs)
     g = shape.geometry(dt)
     with torch.cuda.device(q.device):
         rc = _call("msl_dsa_attn_fwd", q.device,
@@ -153,13 +180,14 @@ def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 
 def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=None, dq=None, dk=None, dv=None,
-             dk_acc=None, dv_acc=None, doffsets=None, dek=None, dev=None, workspace=None, status=None):
+             dk_acc=None, dv_acc=None, doffsets=None, dek=None, dev=None, workspace=None, status=None, probs=None):
     """Deformable gather attention backward.
 
     Without dk_acc: dK/dV are written to dk/dv (allocated if None) in q's dtype, float32
     accumulators live in ``workspace`` (allocated if None).  With dk_acc/dv_acc (float32 views):
     dK/dV are ACCUMULATED there.  Returns (dq, dk, dv, doffsets, dek, dev); dk/dv are the
-    accumulators in accumulate mode.
+    accumulators in accumulate mode.  probs: the forward's softmax weights (attn_fwd(probs=...));
+    given, the tensor-core backward runs where it applies.
     """
     _need_cuda(q, k, v, offsets, out, lse, dout, ek, ev)
     C = shape.heads * shape.head_dim
@@ -196,6 +224,10 @@ def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=N
         0 if accumulate else _rows(dk, "dk"),
         _ptr(dk_acc), _ptr(dv_acc), _rows(dk_acc, "dk_acc") if accumulate else 0,
         _ptr(doffsets), _rows(doffsets, "doffsets"), _ptr(dek), _ptr(dev), _ptr(status))
+    if probs is not None:
+        _need_cuda(probs)
+        _check_probs(shape, probs)
+        io.probs = _ptr(probs)
     with torch.cuda.device(dev_):
         rc = _call("msl_dsa_attn_bwd", dev_,
                    lambda: lib.msl_dsa_attn_bwd(ctypes.byref(g), ctypes.byref(io), _ptr(workspace) if need else None,

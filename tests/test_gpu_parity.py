@@ -363,3 +363,123 @@ def test_tc_path_rejects_float32():
     shape = ops.DsaShape(B, T, H, W, nh, d, ks, algo=2)
     with pytest.raises(msl.MslError, match="tensor-core"):
         ops.attn_fwd(shape, q, q, q, off)
+
+
+# ----------------------------------------------------------------- tensor-core backward (bf16)
+TC_BWD_CASES = [
+    # B, T, H, W, nh, d, kernel, G(=0), offset_std
+    (1, 3, 9, 11, 2, 72, (3, 7, 7), 0, 1.0),      # partial 4x8 tiles, config-2 head_dim (odd chunk count)
+    (2, 2, 16, 16, 2, 64, (3, 7, 7), 0, 0.5),
+    (1, 2, 8, 8, 1, 128, (3, 3, 3), 0, 3.0),      # largest head_dim (d-tile split over 8 warps)
+    (1, 3, 6, 7, 2, 24, (3, 3, 3), 0, 2.0),       # k8 tail in every product
+    (1, 2, 32, 32, 1, 16, (1, 3, 3), 0, 20.0),    # offsets of ~10 voxels: envelope split in chunks
+    (1, 1, 5, 5, 2, 40, (1, 3, 3), 0, 0.0),       # T=1, zero offsets (samples on grid points)
+    (1, 4, 5, 6, 1, 32, (3, 3, 3), 0, 6.0),       # many samples clamped onto the borders
+]
+
+
+def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False):
+    """Forward with the softmax weights saved (algo 2) or not (algo 1), then the backward."""
+    B, T, H, W, nh, d, ks, G, _ = case
+    q, k, v, off, ek, ev, dout = arrays
+    N = T * H * W
+    C = nh * d
+    t = lambda a: torch.from_numpy(a).to(DEV, torch.bfloat16).reshape(-1, C)  # noqa: E731
+    shape = ops.DsaShape(B, T, H, W, nh, d, ks, dropout_p=dropout_p, dropout_seed=seed, algo=algo)
+    offt = torch.from_numpy(off).to(DEV).reshape(B * N, -1)
+    qt, kt_, vt, dot = t(q), t(k), t(v), t(dout)
+    probs = ops.probs_buffer(shape, DEV) if algo == 2 else None
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out, lse = ops.attn_fwd(shape, qt, kt_, vt, offt, probs=probs, status=status)
+    kw = {}
+    if accumulate:
+        kw = dict(dk_acc=torch.full((B * N, C), 0.5, device=DEV), dv_acc=torch.full((B * N, C), -0.25, device=DEV))
+    dq, dk, dv, doff, _, _ = ops.attn_bwd(shape, qt, kt_, vt, offt, out, lse, dot, probs=probs, status=status, **kw)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    if accumulate:
+        dk, dv = dk - 0.5, dv + 0.25
+    f = lambda a: a.float().cpu().numpy().reshape(B, -1, C)  # noqa: E731
+    res = dict(out=f(out), lse=lse.cpu().numpy(), dq=f(dq), dk=f(dk), dv=f(dv), doff=doff.cpu().numpy().reshape(B, N, -1))
+    if probs is not None:
+        res["probs"] = probs.cpu().numpy()
+    return res
+
+
+def _compare_grads_bf16(got, ref, what):
+    assert rel(got["out"], ref["out"]) < RTOL_BF16, f"{what} out"
+    for key in ("dq", "dk", "dv", "doff"):
+        ef, em = fro(got[key], ref[key]), rel(got[key], ref[key])
+        assert ef < RTOL_BF16 and em < MAXREL_BF16_GRAD, f"{what} {key}: fro {ef:.3e} max {em:.3e}"
+
+
+@pytest.mark.parametrize("case", TC_BWD_CASES, ids=_tc_ids)
+def test_tc_backward_matches_oracle_and_cuda_core_path(case):
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))
+                   for i, a in enumerate(_core_inputs(case, seed=11)))
+    got = _run_tc_train(case, arrays, algo=2)
+    # the saved softmax weights are a distribution over the window of every (sample, head, query)
+    assert np.abs(got["probs"].astype(np.float64).sum(-1) - 1.0).max() < 1e-5
+    assert got["probs"].min() >= 0.0
+    ref = _oracle_core(case, arrays)
+    _compare_grads_bf16(got, ref, "tc vs oracle")
+    simt = _run_tc_train(case, arrays, algo=1)
+    _compare_grads_bf16(got, simt, "tc vs cuda-core")
+
+
+def test_tc_backward_dropout_matches_oracle_mask():
+    case = (1, 3, 8, 8, 2, 32, (3, 3, 3), 0, 1.0)
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))
+                   for i, a in enumerate(_core_inputs(case, seed=13)))
+    got = _run_tc_train(case, arrays, algo=2, dropout_p=0.3, seed=4321)
+    ref = _oracle_core(case, arrays, dropout_p=0.3, seed=4321)
+    _compare_grads_bf16(got, ref, "tc dropout vs oracle")
+
+
+def test_tc_backward_accumulate_mode():
+    case = (1, 3, 8, 8, 2, 32, (3, 3, 3), 0, 1.5)
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))
+                   for i, a in enumerate(_core_inputs(case, seed=17)))
+    got = _run_tc_train(case, arrays, algo=2, accumulate=True)
+    ref = _oracle_core(case, arrays)
+    _compare_grads_bf16(got, ref, "tc accumulate vs oracle")
+
+
+def test_tc_backward_requires_probs_when_forced():
+    case = (1, 2, 4, 4, 1, 16, (3, 3, 3), 0, 1.0)
+    B, T, H, W, nh, d, ks, G, _ = case
+    x = torch.randn(B * T * H * W, nh * d, device=DEV, dtype=torch.bfloat16)
+    off = torch.zeros(B * T * H * W, nh * 27 * 3, device=DEV)
+    shape = ops.DsaShape(B, T, H, W, nh, d, ks, algo=2)
+    out, lse = ops.attn_fwd(shape, x, x, x, off)
+    with pytest.raises(msl.MslError, match="probs"):
+        ops.attn_bwd(shape, x, x, x, off, out, lse, x)
+    # the CUDA-core forward cannot fill probs: asking for them there is an error, not silent garbage
+    simt = ops.DsaShape(B, T, H, W, nh, d, ks, algo=1)
+    with pytest.raises(msl.MslError, match="probs"):
+        ops.attn_fwd(simt, x, x, x, off, probs=ops.probs_buffer(simt, DEV))
+
+
+def test_module_bf16_training_uses_tensor_core_backward(monkeypatch):
+    """A bf16 training step of the module saves probs in the forward and hands them to the backward."""
+    from megaslide_b200.attention import DeformableSlideAttention3D
+
+    seen = []
+    real_bwd = ops.attn_bwd
+
+    def spy(*a, **kw):
+        seen.append(kw.get("probs") is not None)
+        return real_bwd(*a, **kw)
+
+    monkeypatch.setattr(ops, "attn_bwd", spy)
+    torch.manual_seed(0)
+    T, H, W, C, nh = 2, 8, 8, 64, 2
+    m = DeformableSlideAttention3D(C, nh, kernel_size=(3, 3, 3)).to(DEV, torch.bfloat16)
+    x = torch.randn(1, T * H * W, C, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    y = m(x, (T, H, W))
+    y.float().square().mean().backward()
+    torch.cuda.synchronize()
+    assert torch.isfinite(x.grad.float()).all()
+    for p in m.parameters():
+        assert p.grad is not None and torch.isfinite(p.grad.float()).all()
+    assert seen == [True]

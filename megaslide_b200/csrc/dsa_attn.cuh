@@ -74,6 +74,14 @@ cudaError_t launch_dwconv_fwd(const ConvParams& P, const void* x, long long x_ld
 cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long dy_ld, int dy_dtype,
                                 const void* x, long long x_ld, float* dw, float* db, cudaStream_t s);
 
+// Shared-memory tiled variants (dwconv_tiled.cu); cudaErrorNotSupported when the kernel width,
+// channel count, alignment or shared-memory plan is outside what they cover (nothing is launched).
+cudaError_t launch_dwconv_fwd_tiled(const ConvParams& P, const void* x, long long x_ld, const float* wt,
+                                    const float* bias, const float* bias2, int epi, const void* aux, long long aux_ld,
+                                    void* y, long long y_ld, int y_dtype, bool flip, cudaStream_t s);
+cudaError_t launch_dwconv_wgrad_tiled(const ConvParams& P, const void* dy, long long dy_ld, int dy_dtype, const void* x,
+                                      long long x_ld, float* dw, float* db, cudaStream_t s);
+
 cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, int heads, int taps,
                                   float oscale, float* out3, cudaStream_t s);
 cudaError_t launch_convert_f32(const float* src, long long src_ld, void* dst, long long dst_ld,

@@ -205,6 +205,8 @@ static cudaError_t dwconv_fwd_t(const ConvParams& P, const void* x, long long x_
 cudaError_t launch_dwconv_fwd(const ConvParams& P, const void* x, long long x_ld, const float* wt,
                               const float* bias, const float* bias2, int epi, const void* aux,
                               long long aux_ld, void* y, long long y_ld, int y_dtype, bool flip, cudaStream_t s) {
+  const cudaError_t te = launch_dwconv_fwd_tiled(P, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, y_dtype, flip, s);
+  if (te != cudaErrorNotSupported) return te;
   const size_t es = P.dtype == MSL_DTYPE_BF16 ? 2 : 4;
   const size_t ys = y_dtype == MSL_DTYPE_BF16 ? 2 : 4;
   const bool vec2 = (P.C % 2 == 0) && (x_ld % 2 == 0) && (y_ld % 2 == 0) &&
@@ -230,6 +232,8 @@ static void wgrad_t(const ConvParams& P, dim3 grid, dim3 block, const void* dy, 
 
 cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long dy_ld, int dy_dtype, const void* x,
                                 long long x_ld, float* dw, float* db, cudaStream_t s) {
+  const cudaError_t te = launch_dwconv_wgrad_tiled(P, dy, dy_ld, dy_dtype, x, x_ld, dw, db, s);
+  if (te != cudaErrorNotSupported) return te;
   const long long total_rows = static_cast<long long>(P.B) * P.out_frames * P.H;
   const int rows_per_block = max(1, 2048 / max(1, P.W));
   const dim3 grid(static_cast<unsigned>((P.C + 31) / 32),

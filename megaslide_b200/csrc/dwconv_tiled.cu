@@ -1,0 +1,503 @@
+// Shared-memory tiled depthwise 3D convolution over channels-last tokens: forward (also the input
+// gradient, as a correlation with the flipped kernel) and weight gradient.
+//
+// One CTA owns a tile of TH rows x 32 columns of the volume, one group of 32 four-byte channel words
+// (64 bf16 or 32 float32 channels) and a chunk of consecutive frames.  Input frames are staged in a
+// ring of kt + 1 shared-memory slices (tile + kh/2, kw/2 halo, zero outside the volume) with cp.async:
+// while output frame t is computed from slices t - kt/2 .. t + kt/2, slice t + kt/2 + 1 is loaded, so
+// every input frame is fetched once per chunk and the fetch overlaps the arithmetic.  A warp owns one
+// tile row and 16 consecutive columns; each lane one channel word; the kw taps of a kernel row slide
+// over 16 + kw - 1 register-resident inputs (16 * kw * channels FMAs per 16 + kw - 1 shared loads).
+//
+// Replaces nn.Conv3d(C, C, k, padding=k//2, groups=C) of dw_conv (infinity/video/attention.py:58-65,
+// 102) and offset_net[0] (attention.py:70-72, 105), forward and autograd backward.
+
+#include <math.h>
+
+#include "dsa_attn.cuh"
+#include "dsa_tc.cuh"
+#include "msl_common.cuh"
+
+namespace msl {
+namespace dwt {
+
+constexpr int kTW = 32;   // tile columns
+constexpr int kSeg = 16;  // consecutive outputs per thread along w
+
+struct Plan {
+  int th;        // tile rows (2 warps per row)
+  int fpc;       // output frames per CTA
+  int chunks, tiles_h, tiles_w, groups;
+  int sr, sc;    // slice rows / columns (tile + halo)
+  int dy_words;  // weight gradient: dy elements of one staged tile (0 for the forward)
+  size_t smem;
+  long long ctas;
+};
+
+__device__ __forceinline__ float gelu_erf(float u) { return 0.5f * u * (1.f + erff(u * 0.70710678118654752f)); }
+
+__device__ __forceinline__ float gelu_erf_grad(float u) {
+  const float cdf = 0.5f * (1.f + erff(u * 0.70710678118654752f));
+  const float pdf = 0.39894228040143268f * expf(-0.5f * u * u);
+  return fmaf(u, pdf, cdf);
+}
+
+// four-byte word -> CV channels
+template <typename T>
+struct Word;
+template <>
+struct Word<__nv_bfloat16> {
+  static constexpr int CV = 2;
+  static __device__ __forceinline__ void unpack(uint32_t w, float (&o)[2]) {
+    o[0] = bf16_lo(w);
+    o[1] = bf16_hi(w);
+  }
+};
+template <>
+struct Word<float> {
+  static constexpr int CV = 1;
+  static __device__ __forceinline__ void unpack(uint32_t w, float (&o)[1]) { o[0] = __uint_as_float(w); }
+};
+
+// CV channels of type TY at p
+template <typename TY, int CV>
+__device__ __forceinline__ void load_cv(const TY* p, float (&o)[CV]) {
+#pragma unroll
+  for (int e = 0; e < CV; ++e) o[e] = to_f32<TY>(p[e]);
+}
+template <typename TY, int CV>
+__device__ __forceinline__ void store_cv(TY* p, const float (&v)[CV]) {
+  if constexpr (CV == 2 && sizeof(TY) == 2) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v[0], v[1]);
+  } else if constexpr (CV == 2 && sizeof(TY) == 4) {
+    *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < CV; ++e) p[e] = from_f32<TY>(v[e]);
+  }
+}
+
+// Stages input frame ti (global index) of sample b: rows h0 - kh/2 .. + sr - 1, columns w0 - kw/2 ..
+// + sc - 1, channel words [c0, c0 + 32 words) as [sr][sc][32] words; zero outside the volume.
+template <typename T>
+__device__ __forceinline__ void load_slice(const ConvParams& P, const Plan& L, const T* x, long long x_ld, uint32_t* dst,
+                                           int b, int ti, int h0, int w0, int c0) {
+  const int ph = P.kh / 2, pw = P.kw / 2;
+  const T* xb = x + (static_cast<long long>(b) * P.in_frames + (ti - P.in_frame0)) * P.HW * x_ld + c0;
+  const int nchunk = L.sr * L.sc * 8;
+  for (int i = threadIdx.x; i < nchunk; i += blockDim.x) {
+    const int pos = i >> 3, ch = i & 7;
+    const int row = pos / L.sc, col = pos - (pos / L.sc) * L.sc;
+    const int h = h0 - ph + row, w = w0 - pw + col;
+    uint32_t* d = dst + pos * 32 + ch * 4;
+    if (h >= 0 && h < P.H && w >= 0 && w < P.W)
+      tc::cp_async16(tc::smem_u32(d),
+                     reinterpret_cast<const char*>(xb + (static_cast<long long>(h) * P.W + w) * x_ld) + ch * 16);
+    else
+      *reinterpret_cast<uint4*>(d) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+struct CtaPos {
+  int b, ta, tb, h0, w0, cg;
+};
+
+__device__ __forceinline__ CtaPos decode(const ConvParams& P, const Plan& L) {
+  long long id = blockIdx.x;
+  CtaPos c;
+  c.cg = static_cast<int>(id % L.groups);
+  id /= L.groups;
+  const int tw = static_cast<int>(id % L.tiles_w);
+  id /= L.tiles_w;
+  const int th = static_cast<int>(id % L.tiles_h);
+  id /= L.tiles_h;
+  const int chunk = static_cast<int>(id % L.chunks);
+  c.b = static_cast<int>(id / L.chunks);
+  c.h0 = th * L.th;
+  c.w0 = tw * kTW;
+  c.ta = P.out_frame0 + chunk * L.fpc;
+  c.tb = min(P.out_frame0 + P.out_frames, c.ta + L.fpc);
+  return c;
+}
+
+// y[p] = epi(sum_taps w[tap] x[p + tap - pad] + bias) (FLIP: w[K-1-tap], the input gradient).
+template <typename T, typename TY, int KW, bool FLIP>
+__global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvParams P, const Plan L, const T* __restrict__ x,
+                                                               long long x_ld, const float* __restrict__ wt,
+                                                               const float* __restrict__ bias,
+                                                               const float* __restrict__ bias2, int epi,
+                                                               const TY* __restrict__ aux, long long aux_ld,
+                                                               TY* __restrict__ y, long long y_ld) {
+  constexpr int CV = Word<T>::CV;
+  constexpr int NIN = kSeg + KW - 1;
+  extern __shared__ __align__(16) uint32_t ring[];
+  const CtaPos cp = decode(P, L);
+  const int pt = P.kt / 2;
+  const int nslots = P.kt + 1;
+  const int slice_words = L.sr * L.sc * 32;
+  const int base = cp.ta - pt;
+  const int c0w = cp.cg * 32;  // first channel word of the group
+  const int c0 = c0w * CV;
+  for (int ti = max(0, cp.ta - pt); ti <= min(P.T - 1, cp.ta + pt); ++ti)
+    load_slice<T>(P, L, x, x_ld, ring + ((ti - base) % nslots) * slice_words, cp.b, ti, cp.h0, cp.w0, c0);
+  tc::cp_async_wait_all();
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = warp >> 1, seg = warp & 1;
+  const int h = cp.h0 + r, ws = cp.w0 + seg * kSeg;
+  const bool active = h < P.H && ws < P.W;
+  const int c = c0 + lane * CV;
+  float bsum[CV], b2v[CV];
+#pragma unroll
+  for (int e = 0; e < CV; ++e) {
+    bsum[e] = bias ? __ldg(bias + c + e) : 0.f;
+    b2v[e] = bias2 ? __ldg(bias2 + c + e) : 0.f;
+  }
+  for (int t = cp.ta; t < cp.tb; ++t) {
+    const int tn = t + pt + 1;
+    if (t + 1 < cp.tb && tn < P.T)
+      load_slice<T>(P, L, x, x_ld, ring + ((tn - base) % nslots) * slice_words, cp.b, tn, cp.h0, cp.w0, c0);
+    if (active) {
+      float acc[kSeg][CV];
+#pragma unroll
+      for (int j = 0; j < kSeg; ++j)
+#pragma unroll
+        for (int e = 0; e < CV; ++e) acc[j][e] = 0.f;
+      for (int it = 0; it < P.kt; ++it) {
+        const int ti = t + it - pt;
+        if (ti < 0 || ti >= P.T) continue;
+        const int itw = FLIP ? P.kt - 1 - it : it;
+        const uint32_t* sl = ring + ((ti - base) % nslots) * slice_words;
+        for (int ih = 0; ih < P.kh; ++ih) {
+          const int ihw = FLIP ? P.kh - 1 - ih : ih;
+          const uint32_t* rowp = sl + ((r + ih) * L.sc + seg * kSeg) * 32 + lane;
+          float xin[NIN][CV];
+#pragma unroll
+          for (int j = 0; j < NIN; ++j) Word<T>::unpack(rowp[j * 32], xin[j]);
+          const float* wrow = wt + static_cast<long long>((itw * P.kh + ihw) * KW) * P.C + c;
+          float wv[KW][CV];
+#pragma unroll
+          for (int iw = 0; iw < KW; ++iw) {
+            const float* wp = wrow + static_cast<long long>(FLIP ? KW - 1 - iw : iw) * P.C;
+            if constexpr (CV == 2) {
+              const float2 v = __ldg(reinterpret_cast<const float2*>(wp));
+              wv[iw][0] = v.x;
+              wv[iw][CV - 1] = v.y;
+            } else {
+              wv[iw][0] = __ldg(wp);
+            }
+          }
+#pragma unroll
+          for (int iw = 0; iw < KW; ++iw)
+#pragma unroll
+            for (int j = 0; j < kSeg; ++j)
+#pragma unroll
+              for (int e = 0; e < CV; ++e) acc[j][e] = fmaf(wv[iw][e], xin[j + iw][e], acc[j][e]);
+        }
+      }
+      const long long orow0 = (static_cast<long long>(cp.b) * P.out_frames + (t - P.out_frame0)) * P.HW +
+                              static_cast<long long>(h) * P.W + ws;
+#pragma unroll
+      for (int j = 0; j < kSeg; ++j) {
+        if (ws + j >= P.W) break;
+        const long long orow = orow0 + j;
+        float av[CV];
+        if (epi == MSL_EPI_GELU_GRAD) load_cv<TY, CV>(aux + orow * aux_ld + c, av);
+        float out[CV];
+#pragma unroll
+        for (int e = 0; e < CV; ++e) {
+          float u = acc[j][e] + bsum[e];
+          if (epi == MSL_EPI_GELU)
+            u = gelu_erf(u);
+          else if (epi == MSL_EPI_GELU_GRAD)
+            u = av[e] * gelu_erf_grad(u);
+          else
+            u += b2v[e];
+          out[e] = u;
+        }
+        store_cv<TY, CV>(y + orow * y_ld + c, out);
+      }
+    }
+    tc::cp_async_wait_all();
+    __syncthreads();
+  }
+}
+
+// Weight gradient: dw[tap][c] += sum_p dy[p][c] x[p + tap - pad][c], db[c] += sum_p dy[p][c].
+// Items = (kernel row (it, ih) or the bias, 16-column segment); warp w owns items w, w + nwarps, ...
+// for the whole CTA, accumulates them in registers over the chunk's frames and tile rows, and adds
+// them to dw / db with one atomic per channel and tap at the end.
+template <typename T, typename TDY, int KW, int MAXI>
+__global__ void __launch_bounds__(256, 1) dwconv_wgrad_tiled_kernel(const ConvParams P, const Plan L,
+                                                                 const TDY* __restrict__ dy, long long dy_ld,
+                                                                 const T* __restrict__ x, long long x_ld,
+                                                                 float* __restrict__ dw, float* __restrict__ db) {
+  constexpr int CV = Word<T>::CV;
+  constexpr int NIN = kSeg + KW - 1;
+  extern __shared__ __align__(16) uint32_t ring[];
+  const CtaPos cp = decode(P, L);
+  const int pt = P.kt / 2;
+  const int nslots = P.kt + 1;
+  const int slice_words = L.sr * L.sc * 32;
+  // dy tiles in their own type, double buffered: [2][th][32 cols][32 lanes][CV]
+  TDY* dys = reinterpret_cast<TDY*>(ring + nslots * slice_words);
+  const int base = cp.ta - pt;
+  const int c0 = cp.cg * 32 * CV;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int c = c0 + lane * CV;
+  const int npairs = P.kt * P.kh;
+  const int nitems = (npairs + (db ? 1 : 0)) * 2;
+
+  // dy tile of frame t (rows h0.., columns w0..w0+31, this group's channels) with cp.async, zero
+  // outside the volume; 16-byte chunks (rows are 16-byte aligned, host-checked)
+  auto stage_dy = [&](int t, TDY* dst) {
+    constexpr int kChunks = 32 * CV * static_cast<int>(sizeof(TDY)) / 16;  // per position
+    const int n = L.th * kTW * kChunks;
+    const TDY* base_dy = dy + (static_cast<long long>(cp.b) * P.out_frames + (t - P.out_frame0)) * P.HW * dy_ld + c0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int pos = i / kChunks, ch = i - (i / kChunks) * kChunks;
+      const int row = pos / kTW, col = pos - (pos / kTW) * kTW;
+      const int hh = cp.h0 + row, ww = cp.w0 + col;
+      char* d = reinterpret_cast<char*>(dst + static_cast<size_t>(pos) * 32 * CV) + ch * 16;
+      if (hh < P.H && ww < P.W)
+        tc::cp_async16(tc::smem_u32(d),
+                       reinterpret_cast<const char*>(base_dy + (static_cast<long long>(hh) * P.W + ww) * dy_ld) + ch * 16);
+      else
+        *reinterpret_cast<uint4*>(d) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+
+  for (int ti = max(0, cp.ta - pt); ti <= min(P.T - 1, cp.ta + pt); ++ti)
+    load_slice<T>(P, L, x, x_ld, ring + ((ti - base) % nslots) * slice_words, cp.b, ti, cp.h0, cp.w0, c0);
+  stage_dy(cp.ta, dys);
+  tc::cp_async_wait_all();
+  __syncthreads();
+
+  float acc[MAXI][KW][CV];
+#pragma unroll
+  for (int s = 0; s < MAXI; ++s)
+#pragma unroll
+    for (int iw = 0; iw < KW; ++iw)
+#pragma unroll
+      for (int e = 0; e < CV; ++e) acc[s][iw][e] = 0.f;
+
+  int buf = 0;
+  for (int t = cp.ta; t < cp.tb; ++t) {
+    const int tn = t + pt + 1;
+    if (t + 1 < cp.tb && tn < P.T)
+      load_slice<T>(P, L, x, x_ld, ring + ((tn - base) % nslots) * slice_words, cp.b, tn, cp.h0, cp.w0, c0);
+    if (t + 1 < cp.tb) stage_dy(t + 1, dys + static_cast<size_t>(buf ^ 1) * L.dy_words);
+    const TDY* dyt = dys + static_cast<size_t>(buf) * L.dy_words;
+#pragma unroll
+    for (int s = 0; s < MAXI; ++s) {
+      const int item = warp + s * nwarps;
+      if (item >= nitems) break;
+      const int pair = item >> 1, seg = item & 1;
+      if (cp.w0 + seg * kSeg >= P.W) continue;
+      if (pair == npairs) {  // bias: sum of dy
+        for (int r = 0; r < L.th; ++r) {
+          const TDY* dp = dyt + (static_cast<size_t>(r * kTW + seg * kSeg) * 32 + lane) * CV;
+#pragma unroll
+          for (int j = 0; j < kSeg; ++j)
+#pragma unroll
+            for (int e = 0; e < CV; ++e) acc[s][0][e] += to_f32<TDY>(dp[j * 32 * CV + e]);
+        }
+        continue;
+      }
+      const int it = pair / P.kh, ih = pair - (pair / P.kh) * P.kh;
+      const int ti = t + it - pt;
+      if (ti < 0 || ti >= P.T) continue;
+      const uint32_t* sl = ring + ((ti - base) % nslots) * slice_words;
+      for (int r = 0; r < L.th; ++r) {
+        const uint32_t* rowp = sl + ((r + ih) * L.sc + seg * kSeg) * 32 + lane;
+        const TDY* dp = dyt + (static_cast<size_t>(r * kTW + seg * kSeg) * 32 + lane) * CV;
+        float xin[NIN][CV];
+#pragma unroll
+        for (int j = 0; j < NIN; ++j) Word<T>::unpack(rowp[j * 32], xin[j]);
+#pragma unroll
+        for (int j = 0; j < kSeg; ++j) {
+          float g[CV];
+#pragma unroll
+          for (int e = 0; e < CV; ++e) g[e] = to_f32<TDY>(dp[j * 32 * CV + e]);
+#pragma unroll
+          for (int iw = 0; iw < KW; ++iw)
+#pragma unroll
+            for (int e = 0; e < CV; ++e) acc[s][iw][e] = fmaf(g[e], xin[j + iw][e], acc[s][iw][e]);
+        }
+      }
+    }
+    tc::cp_async_wait_all();
+    __syncthreads();
+    buf ^= 1;
+  }
+#pragma unroll
+  for (int s = 0; s < MAXI; ++s) {
+    const int item = warp + s * nwarps;
+    if (item >= nitems) break;
+    const int pair = item >> 1;
+    if (pair == npairs) {
+#pragma unroll
+      for (int e = 0; e < CV; ++e) atomicAdd(db + c + e, acc[s][0][e]);
+      continue;
+    }
+    float* drow = dw + static_cast<long long>(pair * KW) * P.C + c;
+#pragma unroll
+    for (int iw = 0; iw < KW; ++iw)
+#pragma unroll
+      for (int e = 0; e < CV; ++e) atomicAdd(drow + static_cast<long long>(iw) * P.C + e, acc[s][iw][e]);
+  }
+}
+
+// ------------------------------------------------------------------------------ host side
+int smem_limit() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return 0;
+  return v - 1024;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Tile rows, frame chunking and shared memory of a launch; false when the tiled kernels do not apply.
+bool make_plan(const ConvParams& P, int cv, int dy_cv_bytes, int max_threads, Plan& L) {
+  const int kw = P.kw;
+  if (kw != 1 && kw != 3 && kw != 5 && kw != 7) return false;
+  if (P.C % (32 * cv) != 0) return false;
+  const int limit = smem_limit();
+  L.sc = kTW + kw - 1;
+  L.th = 0;
+  for (int th = max_threads / 64; th >= 1; th >>= 1) {
+    if (th > 1 && th / 2 >= P.H) continue;  // no taller than the volume needs
+    const int sr = th + P.kh - 1;
+    const size_t ring = static_cast<size_t>(P.kt + 1) * sr * L.sc * 32 * 4;
+    const size_t dyb = dy_cv_bytes ? static_cast<size_t>(2) * th * kTW * 32 * dy_cv_bytes : 0;
+    if (ring + dyb <= static_cast<size_t>(limit)) {
+      L.th = th;
+      L.sr = sr;
+      L.smem = ring + dyb;
+      L.dy_words = dy_cv_bytes ? th * kTW * 32 * cv : 0;  // elements of the dy type per buffer
+      break;
+    }
+  }
+  if (L.th == 0) return false;
+  L.tiles_h = (P.H + L.th - 1) / L.th;
+  L.tiles_w = (P.W + kTW - 1) / kTW;
+  L.groups = P.C / (32 * cv);
+  // frames per CTA: enough CTAs for ~8 waves of 148 SMs, at most 16 frames per chunk
+  const long long per_frame = static_cast<long long>(P.B) * L.tiles_h * L.tiles_w * L.groups;
+  long long want = (per_frame * P.out_frames + 148LL * 8 - 1) / (148LL * 8);
+  L.fpc = static_cast<int>(want < 1 ? 1 : (want > 16 ? 16 : want));
+  if (L.fpc > P.out_frames) L.fpc = P.out_frames;
+  L.chunks = (P.out_frames + L.fpc - 1) / L.fpc;
+  L.ctas = per_frame * L.chunks;
+  return L.ctas <= 0x7fffffffLL;
+}
+
+template <typename T, typename TY, int KW, bool FLIP>
+cudaError_t fwd_launch(const ConvParams& P, const Plan& L, const void* x, long long x_ld, const float* wt,
+                       const float* bias, const float* bias2, int epi, const void* aux, long long aux_ld, void* y,
+                       long long y_ld, cudaStream_t s) {
+  auto k = dwconv_fwd_tiled_kernel<T, TY, KW, FLIP>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem));
+  if (e != cudaSuccess) return e;
+  k<<<static_cast<unsigned>(L.ctas), L.th * 64, L.smem, s>>>(P, L, static_cast<const T*>(x), x_ld, wt, bias, bias2, epi,
+                                                            static_cast<const TY*>(aux), aux_ld, static_cast<TY*>(y),
+                                                            y_ld);
+  return cudaGetLastError();
+}
+
+template <typename T, typename TY, bool FLIP>
+cudaError_t fwd_kw(const ConvParams& P, const Plan& L, const void* x, long long x_ld, const float* wt, const float* bias,
+                   const float* bias2, int epi, const void* aux, long long aux_ld, void* y, long long y_ld,
+                   cudaStream_t s) {
+  switch (P.kw) {
+    case 1: return fwd_launch<T, TY, 1, FLIP>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+    case 3: return fwd_launch<T, TY, 3, FLIP>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+    case 5: return fwd_launch<T, TY, 5, FLIP>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+    default: return fwd_launch<T, TY, 7, FLIP>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+  }
+}
+
+template <typename T, typename TY>
+cudaError_t fwd_flip(const ConvParams& P, const Plan& L, bool flip, const void* x, long long x_ld, const float* wt,
+                     const float* bias, const float* bias2, int epi, const void* aux, long long aux_ld, void* y,
+                     long long y_ld, cudaStream_t s) {
+  if (flip) return fwd_kw<T, TY, true>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+  return fwd_kw<T, TY, false>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+}
+
+template <typename T, typename TDY, int KW, int MAXI>
+cudaError_t wgrad_launch(const ConvParams& P, const Plan& L, const void* dy, long long dy_ld, const void* x,
+                         long long x_ld, float* dw, float* db, cudaStream_t s) {
+  auto k = dwconv_wgrad_tiled_kernel<T, TDY, KW, MAXI>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem));
+  if (e != cudaSuccess) return e;
+  k<<<static_cast<unsigned>(L.ctas), L.th * 64, L.smem, s>>>(P, L, static_cast<const TDY*>(dy), dy_ld,
+                                                            static_cast<const T*>(x), x_ld, dw, db);
+  return cudaGetLastError();
+}
+
+template <typename T, typename TDY, int MAXI>
+cudaError_t wgrad_kw(const ConvParams& P, const Plan& L, const void* dy, long long dy_ld, const void* x, long long x_ld,
+                     float* dw, float* db, cudaStream_t s) {
+  switch (P.kw) {
+    case 1: return wgrad_launch<T, TDY, 1, MAXI>(P, L, dy, dy_ld, x, x_ld, dw, db, s);
+    case 3: return wgrad_launch<T, TDY, 3, MAXI>(P, L, dy, dy_ld, x, x_ld, dw, db, s);
+    case 5: return wgrad_launch<T, TDY, 5, MAXI>(P, L, dy, dy_ld, x, x_ld, dw, db, s);
+    default: return wgrad_launch<T, TDY, 7, MAXI>(P, L, dy, dy_ld, x, x_ld, dw, db, s);
+  }
+}
+
+template <typename T, typename TDY>
+cudaError_t wgrad_items(const ConvParams& P, const Plan& L, int maxi, const void* dy, long long dy_ld, const void* x,
+                        long long x_ld, float* dw, float* db, cudaStream_t s) {
+  if (maxi <= 2) return wgrad_kw<T, TDY, 2>(P, L, dy, dy_ld, x, x_ld, dw, db, s);
+  if (maxi <= 4) return wgrad_kw<T, TDY, 4>(P, L, dy, dy_ld, x, x_ld, dw, db, s);
+  return wgrad_kw<T, TDY, 6>(P, L, dy, dy_ld, x, x_ld, dw, db, s);
+}
+
+}  // namespace dwt
+
+cudaError_t launch_dwconv_fwd_tiled(const ConvParams& P, const void* x, long long x_ld, const float* wt,
+                                    const float* bias, const float* bias2, int epi, const void* aux, long long aux_ld,
+                                    void* y, long long y_ld, int y_dtype, bool flip, cudaStream_t s) {
+  const bool xb = P.dtype == MSL_DTYPE_BF16, yb = y_dtype == MSL_DTYPE_BF16;
+  const int cv = xb ? 2 : 1;
+  const size_t es = xb ? 2 : 4, ys = yb ? 2 : 4;
+  if (!dwt::aligned(x, 16) || (x_ld * es) % 16 != 0) return cudaErrorNotSupported;
+  if (!dwt::aligned(y, cv * ys) || y_ld % cv != 0 || !dwt::aligned(wt, 4 * cv)) return cudaErrorNotSupported;
+  if (epi == MSL_EPI_GELU_GRAD && (!dwt::aligned(aux, cv * ys) || aux_ld % cv != 0)) return cudaErrorNotSupported;
+  dwt::Plan L{};
+  if (!dwt::make_plan(P, cv, 0, 512, L)) return cudaErrorNotSupported;
+  if (xb) {
+    if (yb) return dwt::fwd_flip<__nv_bfloat16, __nv_bfloat16>(P, L, flip, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+    return dwt::fwd_flip<__nv_bfloat16, float>(P, L, flip, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+  }
+  if (yb) return dwt::fwd_flip<float, __nv_bfloat16>(P, L, flip, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+  return dwt::fwd_flip<float, float>(P, L, flip, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+}
+
+cudaError_t launch_dwconv_wgrad_tiled(const ConvParams& P, const void* dy, long long dy_ld, int dy_dtype, const void* x,
+                                      long long x_ld, float* dw, float* db, cudaStream_t s) {
+  const bool xb = P.dtype == MSL_DTYPE_BF16, yb = dy_dtype == MSL_DTYPE_BF16;
+  const int cv = xb ? 2 : 1;
+  const size_t es = xb ? 2 : 4, ys = yb ? 2 : 4;
+  if (!dwt::aligned(x, 16) || (x_ld * es) % 16 != 0) return cudaErrorNotSupported;
+  if (!dwt::aligned(dy, 16) || (dy_ld * ys) % 16 != 0) return cudaErrorNotSupported;
+  dwt::Plan L{};
+  if (!dwt::make_plan(P, cv, static_cast<int>(cv * ys), 256, L)) return cudaErrorNotSupported;
+  const int nwarps = L.th * 2;
+  const int nitems = (P.kt * P.kh + (db ? 1 : 0)) * 2;
+  const int maxi = (nitems + nwarps - 1) / nwarps;
+  if (maxi > 6) return cudaErrorNotSupported;
+  if (xb) {
+    if (yb) return dwt::wgrad_items<__nv_bfloat16, __nv_bfloat16>(P, L, maxi, dy, dy_ld, x, x_ld, dw, db, s);
+    return dwt::wgrad_items<__nv_bfloat16, float>(P, L, maxi, dy, dy_ld, x, x_ld, dw, db, s);
+  }
+  if (yb) return dwt::wgrad_items<float, __nv_bfloat16>(P, L, maxi, dy, dy_ld, x, x_ld, dw, db, s);
+  return dwt::wgrad_items<float, float>(P, L, maxi, dy, dy_ld, x, x_ld, dw, db, s);
+}
+
+}  // namespace msl

@@ -10,7 +10,7 @@ import torch
 
 import golden_cases as gc
 import megaslide_b200 as msl
-from megaslide_b200 import ops
+from megaslide_b200 import _lib, ops
 from oracle import dsa_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -205,6 +205,100 @@ def test_dwconv_kernels_match_oracle():
             assert rel(dx.float().cpu().numpy().reshape(B, N, C), dxo) < tol
             assert rel(gw.cpu().numpy(), gwo) < max(tol, 1e-5)
             assert rel(gb.cpu().numpy(), gbo) < max(tol, 1e-5)
+
+
+# Shapes the shared-memory tiled kernels take (channels a multiple of 64 for bf16, 32 for float32; kernel
+# widths 1/3/5/7): several 32-column tiles with a ragged last one, tile rows that do not divide H,
+# frame chunks, frame windows (time shards), mixed dtypes and the fused epilogues.
+DWCONV_TILED_CASES = [
+    # B, T, H, W, C, kernel, x dtype, y dtype, epilogue, (in_frame0, in_frames, out_frame0, out_frames)
+    (2, 5, 9, 40, 128, (3, 7, 7), torch.bfloat16, torch.bfloat16, "bias2", None),
+    (1, 6, 7, 33, 64, (3, 3, 3), torch.float32, torch.float32, "none", None),
+    (1, 4, 5, 8, 64, (1, 3, 3), torch.bfloat16, torch.float32, "gelu", None),
+    (1, 8, 6, 16, 128, (3, 5, 5), torch.bfloat16, torch.bfloat16, "none", (2, 5, 3, 3)),
+    (1, 3, 4, 5, 64, (3, 1, 1), torch.bfloat16, torch.float32, "gelu_grad", None),
+    (1, 3, 34, 12, 32, (3, 7, 7), torch.float32, torch.bfloat16, "none", (0, 3, 1, 1)),
+]
+
+
+def _gelu64(u):
+    return 0.5 * u * (1.0 + torch.erf(torch.from_numpy(u) / math.sqrt(2.0)).numpy())
+
+
+def _gelu_grad64(u):
+    t = torch.from_numpy(u)
+    return (0.5 * (1.0 + torch.erf(t / math.sqrt(2.0))) + t * torch.exp(-0.5 * t * t) / math.sqrt(2.0 * math.pi)).numpy()
+
+
+@pytest.mark.parametrize("case", DWCONV_TILED_CASES, ids=lambda c: f"T{c[1]}H{c[2]}W{c[3]}C{c[4]}k{''.join(map(str, c[5]))}{c[8]}")
+def test_dwconv_tiled_path_matches_oracle(case):
+    B, T, H, W, C, ks, xdt, ydt, epi, win = case
+    rng = np.random.default_rng(23)
+    HW, N, K = H * W, T * H * W, ks[0] * ks[1] * ks[2]
+    i0, ni, o0, no = win if win else (0, T, 0, T)
+    x = rng.normal(size=(B, T, HW, C))
+    w = rng.normal(size=(K, C)).astype(np.float32) * 0.3
+    b = rng.normal(size=(C,)).astype(np.float32)
+    b2 = rng.normal(size=(C,)).astype(np.float32)
+    dy = rng.normal(size=(B, T, HW, C))
+    aux = rng.normal(size=(B, T, HW, C))
+    if xdt == torch.bfloat16:
+        x, dy = _round_bf16(x), _round_bf16(dy)
+    if ydt == torch.bfloat16:
+        aux = _round_bf16(aux)
+    shape = ops.ConvShape(B, T, H, W, C, ks, in_frame0=i0, in_frames=ni, out_frame0=o0, out_frames=no)
+    dev_rows = lambda a, f0, nf, dt: torch.from_numpy(np.ascontiguousarray(a[:, f0:f0 + nf])).to(DEV, dt).reshape(-1, C)  # noqa: E731
+    xt = dev_rows(x, i0, ni, xdt)
+    wt, bt, b2t = (torch.from_numpy(a).to(DEV) for a in (w, b, b2))
+    kw = {}
+    if epi == "bias2":
+        kw = dict(bias=bt, bias2=b2t)
+    elif epi == "gelu":
+        kw = dict(bias=bt, epilogue=_lib.MSL_EPI_GELU)
+    elif epi == "gelu_grad":
+        kw = dict(bias=bt, epilogue=_lib.MSL_EPI_GELU_GRAD, aux=dev_rows(aux, o0, no, ydt))
+    y = ops.dwconv_fwd(shape, xt, wt, out_dtype=ydt, **kw).float().cpu().numpy().reshape(B, no, HW, C)
+    full = O.dwconv3d(x.reshape(B, N, C).astype(np.float32), w, b if epi != "none" else np.zeros(C, np.float32),
+                      (T, H, W), ks).reshape(B, T, HW, C)[:, o0:o0 + no].astype(np.float64)
+    if epi == "bias2":
+        full = full + b2
+    elif epi == "gelu":
+        full = _gelu64(full)
+    elif epi == "gelu_grad":
+        full = aux[:, o0:o0 + no] * _gelu_grad64(full)
+    tol = 2e-2 if torch.bfloat16 in (xdt, ydt) else 1e-5
+    assert rel(y, full) < tol
+    if win is not None:
+        return  # input-gradient / weight-gradient windows are covered by the time-sharded tests
+    dyt = dev_rows(dy, 0, T, xdt)
+    dx = ops.dwconv_bwd_data(shape, dyt, wt).float().cpu().numpy().reshape(B, N, C)
+    gw = torch.zeros_like(wt)
+    gb = torch.zeros_like(bt)
+    ops.dwconv_bwd_weight(shape, dyt, xt, gw, gb)
+    dxo, gwo, gbo = O.dwconv3d_backward(dy.reshape(B, N, C).astype(np.float32), x.reshape(B, N, C).astype(np.float32),
+                                        w, (T, H, W), ks)
+    tolg = 2e-2 if xdt == torch.bfloat16 else 1e-5
+    assert rel(dx, dxo) < tolg
+    assert rel(gw.cpu().numpy(), gwo) < max(tolg, 1e-5)
+    assert rel(gb.cpu().numpy(), gbo) < max(tolg, 1e-5)
+
+
+def test_dwconv_weight_grad_float32_dy_bfloat16_x():
+    """The module's offset-net branch: float32 du against bf16 x (tiled weight gradient, mixed dtypes)."""
+    B, T, H, W, C, ks = 1, 4, 6, 40, 128, (3, 3, 3)
+    rng = np.random.default_rng(29)
+    N, K = T * H * W, 27
+    x = _round_bf16(rng.normal(size=(B, N, C)))
+    dy = rng.normal(size=(B, N, C)).astype(np.float32)
+    w = rng.normal(size=(K, C)).astype(np.float32)
+    shape = ops.ConvShape(B, T, H, W, C, ks)
+    gw = torch.zeros(K, C, device=DEV)
+    gb = torch.zeros(C, device=DEV)
+    ops.dwconv_bwd_weight(shape, torch.from_numpy(dy).to(DEV).reshape(-1, C),
+                          torch.from_numpy(x).to(DEV, torch.bfloat16).reshape(-1, C), gw, gb)
+    _, gwo, gbo = O.dwconv3d_backward(dy, x.astype(np.float32), w, (T, H, W), ks)
+    assert rel(gw.cpu().numpy(), gwo) < 1e-5
+    assert rel(gb.cpu().numpy(), gbo) < 1e-5
 
 
 # ----------------------------------------------------------------- reference's structural tests

@@ -7,16 +7,24 @@
 // j with trilinear corners c and weights w_c, pv_j = p_j * keep_j / (1 - p_drop):
 //
 //   pass 1, per envelope chunk (V side):  dP = dO . V_chunk^T on the tensor cores; every sample adds
-//            dp_j  += sum_c w_c dP[q, c]                     (dp_j = dO . v_j, before dropout)
-//            g_j   += pv_j * sum_c (dw_c / dpix) dP[q, c]    (coordinate gradient, value part)
-//   then     dsq_j = softmax_scale * p_j * (keep_j dp_j / (1 - p_drop) - D)
+//            dp_j  += sum_c w_c dP[q, c]                   (dp_j = dO . v_j, before dropout)
+//            gv_j  += sum_c (dw_c / dpix) dP[q, c]         (coordinate gradient, value part / pv_j)
+//   then     dsq_j = softmax_scale * p_j * (keep_j dp_j / (1 - p_drop) - D),  g_j = pv_j gv_j
 //   pass 2, per envelope chunk (K side):  S = Q . K_chunk^T; every sample adds
-//            g_j   += dsq_j * sum_c (dw_c / dpix) S[q, c]    (coordinate gradient, key part)
-//            scatter dsq_j w_c into dS~[q, key]:  dQ += dS~ . K_chunk,  dK_chunk = dS~^T . Q
-//            scatter pv_j  w_c into P~[q, key]:   dV_chunk = P~^T . dO
+//            g_j   += dsq_j * sum_c (dw_c / dpix) S[q, c]  (coordinate gradient, key part)
+//            and scatters dsq_j w_c into dS~[q, key] and pv_j w_c into P~[q, key];
+//            dQ += dS~ . K_chunk,  dK_chunk = dS~^T . Q,  dV_chunk = P~^T . dO  (tensor cores)
 //   dK / dV chunks are added to the float32 accumulators with vector atomics (one per 4 channels of
 //   a key that received anything); g_j becomes the offset gradient through grid_sample's clip rule
 //   and the offset normalisation, with the reference's axis swap.
+//
+// Per-sample work is spread over the whole CTA: the setup sorts the active samples into one list by
+// frame (counting sort), so the samples with a corner in a plane are one contiguous range that all
+// 512 threads stride through.  The setup also records, per (plane, chunk), which 16-key tiles any
+// corner touches; loads, dense products and flushes visit only those tiles.  dS~ and P~ are
+// accumulated with 32-bit integer shared atomics in fixed point (scale 2^21 / sum_j |value_j| per
+// query, so no entry can overflow) and converted once per chunk into a transposed bf16 tile
+// [key][query] that every product reads with ldmatrix.
 //
 // Reference semantics: autograd of infinity/video/attention.py:113-186 (grid_sampler_3d_backward,
 // bmm and softmax backward, dropout).
@@ -31,21 +39,32 @@ constexpr int kGroups = 2;                  // 16-query row groups per tile
 constexpr int kWPG = kWarps / kGroups;      // warps per row group
 constexpr int kLPQ = kWPG * 32 / 16;        // lanes per query
 constexpr int kTileH = 4, kQ = kTileH * kTileW;
+constexpr int kTRow = 40;                   // bf16 per key row of a transposed dense tile (32 + 8 pad)
+constexpr int kMaxKeys = 256;               // chunk cap: 16 tiles of 16 keys (one transposition item per thread)
+constexpr int kMaxMaskChunks = 4;           // chunks per plane with their own tile masks
+constexpr float kFixRange = 2097152.f;      // 2^21: fixed-point full scale of a dense row
 
 // record flags: grid coordinate strictly inside (0, S-1) along t / h / w, dropout keep
 constexpr int kBitInT = 57, kBitInH = 58, kBitInW = 59, kBitKeep = 60;
 
 struct Smem {
-  __nv_bfloat16* kbuf;      // [maxkeys][rs]   K or V chunk (setup: staged offsets, spilling into sbuf)
-  float* sbuf;              // [32][sld]       dP / S, then dS~, then P~ (u32 fixed point)
+  __nv_bfloat16* kbuf;      // [maxkeys][rs]   K or V chunk (setup: staged offsets, spilling into sa)
+  float* sa;                // [32][sld]       dP / S (fp32), then P~ (int32), then P~^T (bf16 [key][40])
+  float* sb;                // [32][sld]       dS~ (int32), then dS~^T (bf16 [key][40])
   __nv_bfloat16* qs;        // [32][rs]        Q rows of the tile
   __nv_bfloat16* dos;       // [32][rs]        dO rows of the tile
   unsigned long long* rec;  // [32][K]         packed sample records
-  float* pp;                // [32][K]         p_j
-  float* acc;               // [32][K]         dp_j, then dsq_j
+  float* sv;                // [32][K]         dp_j, then dsq_j
   float* g3;                // [32][K][3]      coordinate gradient (t, h, w) before the clip rule
+  int* key_off;             // [maxkeys]       row of each chunk key in the K/V buffers, -1 = none
   int* env;                 // envelope + base-grid tables
   float* dd;                // [32]            D = dO . O
+  float* qsc;               // [4][32]         fixed-point scale / inverse of dS~ and P~ rows
+  long long* prow;          // [32]            row of each query's softmax weights in probs
+  int* bstart;              // [33]            hit list: first entry of each frame bucket (+ end)
+  int* bcur;                // [32]            bucket counts, then fill cursors
+  uint32_t* mask;           // [32][4]         16-key tiles touched per (plane, chunk)
+  unsigned short* hits;     // [32 * K]        sample indices q * K + j sorted by frame bucket
 };
 
 __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, const TcLaunch& L) {
@@ -53,7 +72,9 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   size_t off = 0;
   s.kbuf = reinterpret_cast<__nv_bfloat16*>(base + off);
   off += static_cast<size_t>(L.maxkeys) * L.rs * 2;
-  s.sbuf = reinterpret_cast<float*>(base + off);
+  s.sa = reinterpret_cast<float*>(base + off);
+  off += static_cast<size_t>(kQ) * L.sld * 4;
+  s.sb = reinterpret_cast<float*>(base + off);
   off += static_cast<size_t>(kQ) * L.sld * 4;
   s.qs = reinterpret_cast<__nv_bfloat16*>(base + off);
   off += static_cast<size_t>(kQ) * L.rs * 2;
@@ -61,26 +82,70 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   off += static_cast<size_t>(kQ) * L.rs * 2;
   s.rec = reinterpret_cast<unsigned long long*>(base + off);
   off += static_cast<size_t>(kQ) * P.K * 8;
-  s.pp = reinterpret_cast<float*>(base + off);
-  off += static_cast<size_t>(kQ) * P.K * 4;
-  s.acc = reinterpret_cast<float*>(base + off);
+  s.prow = reinterpret_cast<long long*>(base + off);
+  off += kQ * 8;
+  s.sv = reinterpret_cast<float*>(base + off);
   off += static_cast<size_t>(kQ) * P.K * 4;
   s.g3 = reinterpret_cast<float*>(base + off);
   off += static_cast<size_t>(kQ) * P.K * 12;
+  s.key_off = reinterpret_cast<int*>(base + off);
+  off += static_cast<size_t>(L.maxkeys) * 4;
   s.env = reinterpret_cast<int*>(base + off);
   off += kEnvWords * 4;
   s.dd = reinterpret_cast<float*>(base + off);
+  off += kQ * 4;
+  s.qsc = reinterpret_cast<float*>(base + off);
+  off += 4 * kQ * 4;
+  s.bstart = reinterpret_cast<int*>(base + off);
+  off += 36 * 4;
+  s.bcur = reinterpret_cast<int*>(base + off);
+  off += 32 * 4;
+  s.mask = reinterpret_cast<uint32_t*>(base + off);
+  off += 32 * kMaxMaskChunks * 4;
+  s.hits = reinterpret_cast<unsigned short*>(base + off);
   return s;
 }
 
-// shared memory besides the key buffer and the score rows
+// shared memory besides the key buffer, the two dense tiles and the key table
 size_t smem_fixed(const AttnParams& P, int rs) {
-  return static_cast<size_t>(kQ) * rs * 2 * 2 + static_cast<size_t>(kQ) * P.K * (8 + 4 + 4 + 12) + kEnvWords * 4 +
-         kQ * 4 + 256;
+  return static_cast<size_t>(kQ) * rs * 2 * 2 + static_cast<size_t>(kQ) * P.K * (8 + 4 + 12 + 2) + kEnvWords * 4 +
+         kQ * (8 + 4 + 16) + (36 + 32 + 32 * kMaxMaskChunks) * 4 + 256;
 }
 
-// In-plane terms of one sample in one frame from a row of per-key values (corners outside the
-// volume count as 0, like grid_sample's zero contribution of out-of-bounds corners):
+// ------------------------------------------------------------------------------ scalar helpers
+// float -> nearest int for |v| < 2^22 and back, with one add (no conversion instruction)
+__device__ __forceinline__ int fix_round(float v) { return __float_as_int(v + 12582912.f) - 0x4B400000; }
+__device__ __forceinline__ float fix_float(int v) { return __int_as_float(v + 0x4B400000) - 12582912.f; }
+
+// position of the o-th (0-based) set bit of m (which has more than o set bits)
+__device__ __forceinline__ int nth_bit(uint32_t m, int o) {
+  int base = 0;
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1) {
+    const int c = __popc(m & ((1u << w) - 1u));
+    if (o >= c) {
+      o -= c;
+      m >>= w;
+      base += w;
+    }
+  }
+  return base;
+}
+
+// record -> corner and fractions (fractions exactly q / 4096, built from the float bit pattern)
+__device__ __forceinline__ Rec decode(unsigned long long v, const Env& E) {
+  Rec r;
+  r.ft = __uint_as_float(0x3F800000u | ((static_cast<uint32_t>(v) & 0xfffu) << 11)) - 1.f;
+  r.fh = __uint_as_float(0x3F800000u | ((static_cast<uint32_t>(v >> 12) & 0xfffu) << 11)) - 1.f;
+  r.fw = __uint_as_float(0x3F800000u | ((static_cast<uint32_t>(v >> 24) & 0xfffu) << 11)) - 1.f;
+  r.t0 = E.zlo - 1 + static_cast<int>((v >> 36) & 0x1fu);
+  r.h0 = E.ylo + static_cast<int>((v >> 41) & 0xffu);
+  r.w0 = E.xlo + static_cast<int>((v >> 49) & 0xffu);
+  return r;
+}
+
+// In-plane terms of one sample from a dense row (corners outside the volume count as 0, like
+// grid_sample's zero contribution of out-of-bounds corners):
 //   bil = sum_c wy_c wx_c v_c,  dvx = d bil / d pw,  dvy = d bil / d ph.
 struct PlaneTerms {
   float bil, dvx, dvy;
@@ -94,71 +159,227 @@ __device__ __forceinline__ PlaneTerms plane_terms(const float* row, int k00, int
   const float v11 = (xok && yok) ? row[k00 + ncw + 1] : 0.f;
   const float ax0 = 1.f - c.fw, ax1 = c.fw, ay0 = 1.f - c.fh, ay1 = c.fh;
   PlaneTerms t;
-  t.bil = ay0 * (ax0 * v00 + ax1 * v01) + ay1 * (ax0 * v10 + ax1 * v11);
+  t.bil = ay0 * fmaf(ax1, v01, ax0 * v00) + ay1 * fmaf(ax1, v11, ax0 * v10);
   t.dvx = ay0 * (v01 - v00) + ay1 * (v11 - v10);
   t.dvy = ax0 * (v10 - v00) + ax1 * (v11 - v01);
   return t;
 }
 
-// accum[key][d] += A^T . X for one envelope chunk: A = the tile's 32 dense rows in sbuf (fp32, or u32
-// fixed point when FIXED), X = 32 bf16 rows (Q or dO) in shared memory.  Items (16-key tile, group of
-// 8-channel tiles) are spread over the 16 warps; each result row is added to the float32 accumulator
-// of its key with one float4 atomic per 4 channels, skipped when all four are zero.
-template <int DCH, bool FIXED>
+// adds round(value * w_c) (value already scaled) for the sample's in-volume corners to an int32 row
+__device__ __forceinline__ void scatter_fixed(int* row, int k00, int ncw, const Rec& c, float sv, int H, int W) {
+  const float ax0 = 1.f - c.fw, ax1 = c.fw, ay0 = 1.f - c.fh, ay1 = c.fh;
+  const bool xok = c.w0 + 1 < W, yok = c.h0 + 1 < H;
+  atomicAdd(row + k00, fix_round(sv * (ax0 * ay0)));
+  if (xok) atomicAdd(row + k00 + 1, fix_round(sv * (ax1 * ay0)));
+  if (yok) {
+    atomicAdd(row + k00 + ncw, fix_round(sv * (ax0 * ay1)));
+    if (xok) atomicAdd(row + k00 + ncw + 1, fix_round(sv * (ax1 * ay1)));
+  }
+}
+
+// 16-key tiles of a chunk holding the sample's corners (rows h0, h0 + 1 of the chunk)
+__device__ __forceinline__ uint32_t corner_tiles(int k00, int ncw, bool xok, bool yok) {
+  uint32_t m = (1u << (k00 >> 4)) | (xok ? 1u << ((k00 + 1) >> 4) : 0u);
+  if (yok) m |= (1u << ((k00 + ncw) >> 4)) | (xok ? 1u << ((k00 + ncw + 1) >> 4) : 0u);
+  return m;
+}
+
+// ------------------------------------------------------------------------------ chunk operands
+// Keys of the chunk (z, y in [ya, yb], x in [xa, xb]) in the 16-key tiles of mask m into kbuf rows
+// (y - ya) * ncw + (x - xa); zero past the chunk and outside the volume / K-V window; key_off[key] =
+// the key's row in the K/V buffers of the sample, -1 where there is none.
+template <int DCH>
+__device__ __forceinline__ void load_keys(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
+                                          int* key_off, const __nv_bfloat16* base, long long ld, int z, int ya, int yb,
+                                          int xa, int xb, uint32_t m) {
+  const int ncw = xb - xa + 1;
+  const int nk = (yb - ya + 1) * ncw;
+  const int zl = z - P.kv_frame0;
+  const bool zok = zl >= 0 && zl < P.kv_frames;
+  const float inv_ncw = 1.f / static_cast<float>(ncw);
+  const __nv_bfloat16* gb = base + static_cast<long long>(T.b) * P.Nkv * ld + T.head * P.d;
+  const int items = __popc(m) * 16 * DCH;
+  for (int idx = threadIdx.x; idx < items; idx += kThreads) {
+    const int o = idx / (16 * DCH), rem = idx - o * (16 * DCH);
+    const int key = nth_bit(m, o) * 16 + rem / DCH, ch = rem - (rem / DCH) * DCH;
+    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs + ch * 8;
+    // key / ncw exactly: (key + 0.5) / ncw is at least 1 / (2 ncw) away from an integer
+    const int ky = static_cast<int>((static_cast<float>(key) + 0.5f) * inv_ncw);
+    const int y = ya + ky, x = xa + (key - ky * ncw);
+    const bool ok = key < nk && zok && y >= 0 && y < P.H && x >= 0 && x < P.W;
+    const long long row = (static_cast<long long>(zl) * P.H + y) * P.W + x;
+    if (ok)
+      cp_async16(smem_u32(dst), gb + row * ld + ch * 8);
+    else
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    if (ch == 0) key_off[key] = ok ? static_cast<int>(row) : -1;
+  }
+  cp_async_wait_all();
+}
+
+// zeroes rows 0..31 of the 16-key tiles of mask m in a dense tile
+__device__ __forceinline__ void zero_tiles(float* buf, int sld, uint32_t m) {
+  const int items = __popc(m) * kQ * 4;
+  for (int i = threadIdx.x; i < items; i += kThreads) {
+    const int o = i >> 7, row = (i >> 2) & 31, c4 = i & 3;
+    *reinterpret_cast<float4*>(buf + static_cast<size_t>(row) * sld + nth_bit(m, o) * 16 + c4 * 4) =
+        make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// In-place conversion of the tiles of mask m of an int32 dense tile [32][sld] (fixed point, per-row
+// inverse scale inv[q]) into bf16 [key][kTRow].  Two phases separated by a barrier; every thread of
+// the CTA must call it.  Item = (key, half): 16 queries of one key.
+__device__ __forceinline__ void transpose_fixed(float* buf, int sld, uint32_t m, const float* inv) {
+  constexpr int kMaxIt = kMaxKeys * 2 / kThreads;
+  const int* src = reinterpret_cast<const int*>(buf);
+  const int items = __popc(m) * 32;
+  uint32_t hold[kMaxIt][8];
+#pragma unroll
+  for (int u = 0; u < kMaxIt; ++u) {
+    const int i = threadIdx.x + u * kThreads;
+    if (i < items) {
+      const int key = nth_bit(m, i >> 5) * 16 + (i & 15), half = (i >> 4) & 1;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int q = half * 16 + 2 * e;
+        const float f0 = fix_float(src[static_cast<size_t>(q) * sld + key]) * inv[q];
+        const float f1 = fix_float(src[static_cast<size_t>(q + 1) * sld + key]) * inv[q + 1];
+        hold[u][e] = pack_bf16(f0, f1);
+      }
+    }
+  }
+  __syncthreads();
+  uint32_t* dst = reinterpret_cast<uint32_t*>(buf);
+#pragma unroll
+  for (int u = 0; u < kMaxIt; ++u) {
+    const int i = threadIdx.x + u * kThreads;
+    if (i < items) {
+      const int key = nth_bit(m, i >> 5) * 16 + (i & 15), half = (i >> 4) & 1;
+      uint4* d = reinterpret_cast<uint4*>(dst + key * (kTRow / 2) + half * 8);
+      d[0] = make_uint4(hold[u][0], hold[u][1], hold[u][2], hold[u][3]);
+      d[1] = make_uint4(hold[u][4], hold[u][5], hold[u][6], hold[u][7]);
+    }
+  }
+}
+
+// S / dP for the 16 queries of a row group over the chunk's tiles of mask m: A = 16 staged bf16
+// rows xs (Q or dO, row stride rs) read with ldmatrix, kbuf rows (keys) with ldmatrix; the WPG warps
+// of the group split the tiles round robin (`part` = warp index within the group).
+template <int DCH, int WPG>
+__device__ __forceinline__ void dense_tiles(const __nv_bfloat16* kbuf, const __nv_bfloat16* xs, int rs, float* srow,
+                                            int sld, int part, uint32_t m) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int mi = lane >> 3, rr = lane & 7;
+  const int nt = __popc(m);
+  if (part >= nt) return;
+  uint32_t qa[DCH / 2 > 0 ? DCH / 2 : 1][4], qt[2] = {0u, 0u};
+  {
+    const __nv_bfloat16* ap = xs + static_cast<size_t>(lane & 15) * rs + (lane >> 4) * 8;
+#pragma unroll
+    for (int ks = 0; ks < DCH / 2; ++ks) ldsm_x4(smem_u32(ap + ks * 16), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    if constexpr (DCH & 1) ldsm_x2(smem_u32(xs + static_cast<size_t>(lane & 15) * rs + (DCH - 1) * 8), qt[0], qt[1]);
+  }
+  for (int o = part; o < nt; o += WPG) {
+    const int gi = nth_bit(m, o);
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    const int key = gi * 16 + rr + ((mi >> 1) ? 8 : 0);
+    const __nv_bfloat16* rowp = kbuf + static_cast<size_t>(key) * rs + ((mi & 1) ? 8 : 0);
+#pragma unroll
+    for (int ks = 0; ks < DCH / 2; ++ks) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(smem_u32(rowp + ks * 16), b0, b1, b2, b3);
+      mma16816(c0, qa[ks], b0, b1);
+      mma16816(c1, qa[ks], b2, b3);
+    }
+    if constexpr (DCH & 1) {
+      const int key2 = gi * 16 + rr + ((mi & 1) ? 8 : 0);
+      uint32_t e0, e1;
+      ldsm_x2(smem_u32(kbuf + static_cast<size_t>(key2) * rs + (DCH - 1) * 8), e0, e1);
+      mma1688(c0, qt[0], qt[1], e0);
+      mma1688(c1, qt[0], qt[1], e1);
+    }
+    float* p0 = srow + static_cast<size_t>(g) * sld + gi * 16 + 2 * t4;
+    float* p1 = srow + static_cast<size_t>(g + 8) * sld + gi * 16 + 2 * t4;
+    *reinterpret_cast<float2*>(p0) = make_float2(c0[0], c0[1]);
+    *reinterpret_cast<float2*>(p1) = make_float2(c0[2], c0[3]);
+    *reinterpret_cast<float2*>(p0 + 8) = make_float2(c1[0], c1[1]);
+    *reinterpret_cast<float2*>(p1 + 8) = make_float2(c1[2], c1[3]);
+  }
+}
+
+// o[16 queries of group r][channel tiles nt0..nt1) += A . kbuf over the tiles of mask m; A = rows of
+// the transposed bf16 tile tb ([key][query]) read with ldmatrix.trans, kbuf rows through
+// ldmatrix.trans.
+template <int DCH, int TPW>
+__device__ __forceinline__ void dq_product(const __nv_bfloat16* tb, int r, const __nv_bfloat16* kbuf, int rs, int nt0,
+                                           int nt1, uint32_t m, float (&o)[TPW + 1][4]) {
+  const int lane = threadIdx.x & 31;
+  const int mi = lane >> 3, rr = lane & 7;
+  for (uint32_t mm = m; mm; mm &= mm - 1u) {
+    const int kk = __ffs(mm) - 1;
+    uint32_t a[4];
+    // matrices: (queries 0-7, keys 0-7) (q 8-15, k 0-7) (q 0-7, k 8-15) (q 8-15, k 8-15) of the group
+    const __nv_bfloat16* ap = tb + static_cast<size_t>(kk * 16 + rr + ((mi >> 1) ? 8 : 0)) * kTRow + r * 16 +
+                              ((mi & 1) ? 8 : 0);
+    ldsm_x4_t(smem_u32(ap), a[0], a[1], a[2], a[3]);
+    const __nv_bfloat16* rowp = kbuf + static_cast<size_t>(kk * 16 + rr + ((mi & 1) ? 8 : 0)) * rs;
+#pragma unroll
+    for (int jj = 0; jj < TPW; jj += 2) {
+      const int nt = nt0 + jj;
+      if (nt + 1 < nt1) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(rowp + (nt + (mi >> 1)) * 8), b0, b1, b2, b3);
+        mma16816(o[jj], a, b0, b1);
+        mma16816(o[jj + 1], a, b2, b3);
+      } else if (nt < nt1) {
+        uint32_t b0, b1;
+        ldsm_x2_t(smem_u32(rowp + nt * 8), b0, b1);
+        mma16816(o[jj], a, b0, b1);
+      }
+    }
+  }
+}
+
+// accum[key][d] += A . X over the tiles of mask m: A = the transposed bf16 tile tb ([key][query], all
+// 32 queries, ldmatrix), X = 32 bf16 rows (Q or dO) in shared memory.  Items (16-key tile, group of
+// 16-channel pairs) are spread over the 16 warps; each result row is added to the float32
+// accumulator row key_off[key] with one float4 atomic per 4 channels, skipped when all four are 0.
+template <int DCH>
 __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const TileCtx& T, const TcLaunch& L,
-                                                 const float* sbuf, const __nv_bfloat16* xs, int nkp, int nk, int ncw,
-                                                 int ya, int xa, int zl, float* accum) {
+                                                 const __nv_bfloat16* tb, const __nv_bfloat16* xs, const int* key_off,
+                                                 uint32_t m, float* accum) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int mi = lane >> 3, rr = lane & 7;
-  constexpr int NP = (DCH + 1) / 2;  // 16-channel pairs of 8-channel tiles
-  const int mtiles = nkp >> 4;
+  constexpr int NP = (DCH + 1) / 2;
+  const int mtiles = __popc(m);
+  if (mtiles == 0) return;
   int ns = (kWarps + mtiles - 1) / mtiles;  // channel splits per key tile
   if (ns > NP) ns = NP;
-  const int ppi = (NP + ns - 1) / ns;  // pairs per item
+  const int ppi = (NP + ns - 1) / ns;
   const int items = mtiles * ns;
+  float* const abase = accum + static_cast<long long>(T.b) * P.Nkv * P.acc_ld + T.head * P.d;
   for (int item = warp; item < items; item += kWarps) {
-    const int mt = item / ns, sp = item - (item / ns) * ns;
+    const int mo = item / ns, sp = item - mo * ns;
+    const int mt = nth_bit(m, mo);
     const int p0 = sp * ppi, p1 = min(NP, p0 + ppi);
-    // A fragments: rows = keys mt*16 + (g, g+8), columns = queries (two k16 steps)
     uint32_t a[2][4];
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      const float* c0 = sbuf + static_cast<size_t>(kk * 16 + 2 * t4) * L.sld + mt * 16 + g;
-      const float* c1 = c0 + L.sld;
-      const float* c8 = c0 + static_cast<size_t>(8) * L.sld;
-      const float* c9 = c8 + L.sld;
-      float v[8] = {c0[0], c1[0], c0[8], c1[8], c8[0], c9[0], c8[8], c9[8]};
-      if constexpr (FIXED) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = static_cast<float>(__float_as_uint(v[i])) * kPtInv;
-      }
-      a[kk][0] = pack_bf16(v[0], v[1]);  // (key g,   queries 2t4, 2t4+1)
-      a[kk][1] = pack_bf16(v[2], v[3]);  // (key g+8, queries 2t4, 2t4+1)
-      a[kk][2] = pack_bf16(v[4], v[5]);  // (key g,   queries 2t4+8, +9)
-      a[kk][3] = pack_bf16(v[6], v[7]);  // (key g+8, queries 2t4+8, +9)
-    }
-    // destination rows of keys mt*16 + g and mt*16 + g + 8 (padding keys are skipped)
-    const int k0 = mt * 16 + g, k1 = k0 + 8;
-    float* dst0 = nullptr;
-    float* dst1 = nullptr;
-    if (k0 < nk) {
-      const int y = ya + k0 / ncw, x = xa + k0 % ncw;
-      dst0 = accum + (static_cast<long long>(T.b) * P.Nkv + (static_cast<long long>(zl) * P.H + y) * P.W + x) * P.acc_ld +
-             T.head * P.d;
-    }
-    if (k1 < nk) {
-      const int y = ya + k1 / ncw, x = xa + k1 % ncw;
-      dst1 = accum + (static_cast<long long>(T.b) * P.Nkv + (static_cast<long long>(zl) * P.H + y) * P.W + x) * P.acc_ld +
-             T.head * P.d;
-    }
+    for (int kk = 0; kk < 2; ++kk)  // rows = keys mt*16 + 0..15, columns = queries kk*16 + 0..15
+      ldsm_x4(smem_u32(tb + static_cast<size_t>(mt * 16 + (lane & 15)) * kTRow + kk * 16 + (lane >> 4) * 8), a[kk][0],
+              a[kk][1], a[kk][2], a[kk][3]);
+    const int o0 = key_off[mt * 16 + g], o1 = key_off[mt * 16 + g + 8];
+    float* dst0 = o0 >= 0 ? abase + static_cast<long long>(o0) * P.acc_ld : nullptr;
+    float* dst1 = o1 >= 0 ? abase + static_cast<long long>(o1) * P.acc_ld : nullptr;
     for (int pr = p0; pr < p1; ++pr) {
       const int nt = 2 * pr;
       float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       const bool two = nt + 1 < DCH;
 #pragma unroll
       for (int kk = 0; kk < 2; ++kk) {
-        // x4.trans matrices: (queries +0..7, ch nt) (queries +8..15, ch nt) (queries +0..7, ch nt+1) (+8..15, nt+1)
+        // x4.trans matrices: (queries +0..7, ch nt) (queries +8..15, ch nt) (+0..7, nt+1) (+8..15, nt+1)
         const __nv_bfloat16* rowp = xs + static_cast<size_t>(kk * 16 + rr + ((mi & 1) ? 8 : 0)) * L.rs;
         if (two) {
           uint32_t b0, b1, b2, b3;
@@ -175,15 +396,15 @@ __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const Tile
       for (int h = 0; h < 2; ++h) {
         if (h == 1 && !two) break;
         // lanes t4 = 0, 2 flush key g (channels 2t4..2t4+3), lanes t4 = 1, 3 key g + 8 (2t4-2..2t4+1)
-        const float o0 = __shfl_xor_sync(kFull, c[h][0], 1), o1 = __shfl_xor_sync(kFull, c[h][1], 1);
-        const float o2 = __shfl_xor_sync(kFull, c[h][2], 1), o3 = __shfl_xor_sync(kFull, c[h][3], 1);
+        const float x0 = __shfl_xor_sync(kFull, c[h][0], 1), x1 = __shfl_xor_sync(kFull, c[h][1], 1);
+        const float x2 = __shfl_xor_sync(kFull, c[h][2], 1), x3 = __shfl_xor_sync(kFull, c[h][3], 1);
         const int ch = (nt + h) * 8;
         if ((t4 & 1) == 0) {
-          const float4 v = make_float4(c[h][0], c[h][1], o0, o1);
+          const float4 v = make_float4(c[h][0], c[h][1], x0, x1);
           if (dst0 && (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f))
             atomicAdd(reinterpret_cast<float4*>(dst0 + ch + 2 * t4), v);
         } else {
-          const float4 v = make_float4(o2, o3, c[h][2], c[h][3]);
+          const float4 v = make_float4(x2, x3, c[h][2], c[h][3]);
           if (dst1 && (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f))
             atomicAdd(reinterpret_cast<float4*>(dst1 + ch + 2 * t4 - 2), v);
         }
@@ -202,19 +423,18 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   const int ll = part * 32 + lane;
   const int cq = ll / kLPQ, sub = ll - (ll / kLPQ) * kLPQ;
   const int K = P.K;
-  // the lanes of a query own contiguous window ranges (few frames per lane)
+  // setup and final stores: the lanes of a query own contiguous window ranges [js, je)
   const int jper = (K + kLPQ - 1) / kLPQ;
   const int js = min(K, sub * jper), je = min(K, js + jper);
+  const int n = je - js;       // samples of this lane
   const int qi = r * 16 + cq;  // owned query within the tile
+  const float invK = 1.f / static_cast<float>(K);
 
   int qh, qw;
   query_hw(T, r, cq, qh, qw);
   const bool qvalid = qh < P.H && qw < P.W;
   const long long qrow = (static_cast<long long>(T.tl) * P.H + qh) * P.W + qw;
-  unsigned long long* rec = S.rec + static_cast<size_t>(qi) * K;
-  float* pp = S.pp + static_cast<size_t>(qi) * K;
-  float* acc = S.acc + static_cast<size_t>(qi) * K;
-  float* g3 = S.g3 + static_cast<size_t>(qi) * K * 3;
+  const int qbase = qi * K;  // this query's samples in rec / sv / g3
 
   float* tabz = reinterpret_cast<float*>(S.env + 16);
   float* taby = tabz + 96;
@@ -223,6 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     S.env[0] = 0x7fffffff; S.env[1] = -0x7fffffff; S.env[2] = 0x7fffffff;
     S.env[3] = -0x7fffffff; S.env[4] = 0x7fffffff; S.env[5] = -0x7fffffff;
   }
+  if (threadIdx.x < 32) S.bcur[threadIdx.x] = 0;
+  if (threadIdx.x < 32 * kMaxMaskChunks) S.mask[threadIdx.x] = 0u;
+  if (sub == 0) S.prow[qi] = (static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow;
   fill_tabs(P, T, kTileH, tabz, taby, tabx);
 
   // ---- stage the tile's offsets (this head), Q and dO rows with one wave of cp.async
@@ -270,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     if (sub == 0) S.dd[qi] = dpart;
   }
 
-  // ---- sample coordinates -> envelope (raw coordinates parked in rec / acc)
+  // ---- sample coordinates -> envelope (raw coordinates parked in rec / sv)
   const int kvlo = max(P.kv_frame0, 0), kvhi = min(P.kv_frame0 + P.kv_frames, P.T) - 1;
   int zmn = 0x7fffffff, zmx = -0x7fffffff, ymn = 0x7fffffff, ymx = -0x7fffffff, xmn = 0x7fffffff, xmx = -0x7fffffff;
   bool miss = false;
@@ -281,8 +504,8 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     for (int j = js; j < je; ++j, wi.advance(1, P.kh, P.kw)) {
       float pt, ph, pw;
       tab_coords(P, tb, qy, qx, wi.it, wi.ih, wi.iw, oq[3 * j], oq[3 * j + 1], oq[3 * j + 2], pt, ph, pw);
-      rec[j] = (static_cast<unsigned long long>(__float_as_uint(ph)) << 32) | __float_as_uint(pt);
-      acc[j] = pw;
+      S.rec[qbase + j] = (static_cast<unsigned long long>(__float_as_uint(ph)) << 32) | __float_as_uint(pt);
+      S.sv[qbase + j] = pw;
       const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
       for (int dt = 0; dt < 2; ++dt) {
         const int tc = t0 + dt;
@@ -332,214 +555,246 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   // records hold t0 - zlo + 1 in 5 bits and h0 - ylo, w0 - xlo in 8 bits
   const bool overflow = any && (E.zhi - E.zlo + 2 > 31 || E.yhi - E.ylo > 255 || E.xhi - E.xlo > 255);
   if (overflow && threadIdx.x == 0 && P.status) atomicOr(P.status, MSL_STATUS_TC_RANGE);
+  const bool work = any && !overflow;
+  const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
 
-  // ---- records (with interior and keep flags), p_j, cleared accumulators
-  int zl_lo = 0x7fff, zl_hi = -1;
-  if (qvalid) {
-    const float* prob_row = P.probs + ((static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow) * K;
-    const uint64_t qglob = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
-    for (int j = js; j < je; ++j) {
-      const unsigned long long raw = rec[j];
-      const float pt = __uint_as_float(static_cast<uint32_t>(raw)), ph = __uint_as_float(static_cast<uint32_t>(raw >> 32));
-      const float pw = acc[j];
-      acc[j] = 0.f;
-      g3[3 * j] = 0.f;
-      g3[3 * j + 1] = 0.f;
-      g3[3 * j + 2] = 0.f;
-      pp[j] = __ldg(prob_row + j);
-      const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
-      if (!any || overflow || t0 + 1 < E.zlo || t0 > E.zhi) {  // no corner in a frame the K/V buffers hold
-        rec[j] = 0ull;
-        continue;
-      }
-      bool keep = true;
-      if (P.drop_thresh)
-        keep = dropout_keep(P.seed, (qglob * P.nh + T.head) * static_cast<uint64_t>(K + P.G) + j, P.drop_thresh);
-      const unsigned long long flags = (clip_grad_mult(pt, P.T) != 0.f ? 1ull << kBitInT : 0ull) |
-                                       (clip_grad_mult(ph, P.H) != 0.f ? 1ull << kBitInH : 0ull) |
-                                       (clip_grad_mult(pw, P.W) != 0.f ? 1ull << kBitInW : 0ull) |
-                                       (keep ? 1ull << kBitKeep : 0ull);
-      rec[j] = pack_rec(pt - static_cast<float>(t0), ph - static_cast<float>(h0), pw - static_cast<float>(w0),
-                        t0 - E.zlo + 1, h0 - E.ylo, w0 - E.xlo) |
-               flags;
-      zl_lo = min(zl_lo, t0 - E.zlo + 1);
-      zl_hi = max(zl_hi, t0 - E.zlo + 2);
-    }
-  }
-
-  // ---- A fragments of dO and Q (rows g and g + 8 of the row group) from the staged rows
-  const int g = lane >> 2, t4 = lane & 3;
-  uint32_t da[DCH / 2 > 0 ? DCH / 2 : 1][4], dt_[2] = {0u, 0u};
-  uint32_t qa[DCH / 2 > 0 ? DCH / 2 : 1][4], qt[2] = {0u, 0u};
+  // ---- records (interior / keep flags), frame-bucket counts and touched-tile masks
   {
-    const __nv_bfloat16* d0 = S.dos + static_cast<size_t>(r * 16 + g) * L.rs;
-    const __nv_bfloat16* d1 = S.dos + static_cast<size_t>(r * 16 + g + 8) * L.rs;
-    const __nv_bfloat16* q0 = S.qs + static_cast<size_t>(r * 16 + g) * L.rs;
-    const __nv_bfloat16* q1 = S.qs + static_cast<size_t>(r * 16 + g + 8) * L.rs;
-#pragma unroll
-    for (int ks = 0; ks < DCH / 2; ++ks) {
-      da[ks][0] = *reinterpret_cast<const uint32_t*>(d0 + ks * 16 + 2 * t4);
-      da[ks][1] = *reinterpret_cast<const uint32_t*>(d1 + ks * 16 + 2 * t4);
-      da[ks][2] = *reinterpret_cast<const uint32_t*>(d0 + ks * 16 + 8 + 2 * t4);
-      da[ks][3] = *reinterpret_cast<const uint32_t*>(d1 + ks * 16 + 8 + 2 * t4);
-      qa[ks][0] = *reinterpret_cast<const uint32_t*>(q0 + ks * 16 + 2 * t4);
-      qa[ks][1] = *reinterpret_cast<const uint32_t*>(q1 + ks * 16 + 2 * t4);
-      qa[ks][2] = *reinterpret_cast<const uint32_t*>(q0 + ks * 16 + 8 + 2 * t4);
-      qa[ks][3] = *reinterpret_cast<const uint32_t*>(q1 + ks * 16 + 8 + 2 * t4);
-    }
-    if constexpr (DCH & 1) {
-      dt_[0] = *reinterpret_cast<const uint32_t*>(d0 + (DCH - 1) * 8 + 2 * t4);
-      dt_[1] = *reinterpret_cast<const uint32_t*>(d1 + (DCH - 1) * 8 + 2 * t4);
-      qt[0] = *reinterpret_cast<const uint32_t*>(q0 + (DCH - 1) * 8 + 2 * t4);
-      qt[1] = *reinterpret_cast<const uint32_t*>(q1 + (DCH - 1) * 8 + 2 * t4);
+    const uint64_t qglob = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
+    for (int s = 0; s < jper; ++s) {  // same trip count in every lane: warp collectives inside
+      const int j = js + s;
+      int dz = -1, pa = -1, pb = -1;
+      uint32_t bits = 0u;
+      if (qvalid && s < n) {
+        const unsigned long long raw = S.rec[qbase + j];
+        const float pt = __uint_as_float(static_cast<uint32_t>(raw)), ph = __uint_as_float(static_cast<uint32_t>(raw >> 32));
+        const float pw = S.sv[qbase + j];
+        const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
+        unsigned long long v = 0ull;
+        if (work && t0 + 1 >= E.zlo && t0 <= E.zhi) {  // a corner in a frame the K/V buffers hold
+          bool keep = true;
+          if (P.drop_thresh)
+            keep = dropout_keep(P.seed, (qglob * P.nh + T.head) * static_cast<uint64_t>(K + P.G) + j, P.drop_thresh);
+          const unsigned long long flags = (clip_grad_mult(pt, P.T) != 0.f ? 1ull << kBitInT : 0ull) |
+                                           (clip_grad_mult(ph, P.H) != 0.f ? 1ull << kBitInH : 0ull) |
+                                           (clip_grad_mult(pw, P.W) != 0.f ? 1ull << kBitInW : 0ull) |
+                                           (keep ? 1ull << kBitKeep : 0ull);
+          dz = t0 - E.zlo + 1;
+          v = pack_rec(pt - static_cast<float>(t0), ph - static_cast<float>(h0), pw - static_cast<float>(w0), dz,
+                       h0 - E.ylo, w0 - E.xlo) |
+              flags;
+          if (masks) {
+            const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
+            const int ya = E.ylo + iy * (E.R - 1), xa = E.xlo + ix * (E.cw - 1);
+            const int ncw = min(xa + E.cw - 1, E.xhi) - xa + 1;
+            bits = corner_tiles((h0 - ya) * ncw + (w0 - xa), ncw, w0 + 1 < P.W, h0 + 1 < P.H);
+            const int chk = iy * E.nx + ix;
+            if (t0 >= E.zlo) pa = dz * kMaxMaskChunks + chk;           // plane z = t0 (zrel = dz)
+            if (t0 + 1 <= E.zhi) pb = (dz + 1) * kMaxMaskChunks + chk; // plane z = t0 + 1
+          }
+        }
+        S.rec[qbase + j] = v;
+      }
+      const unsigned peers = __match_any_sync(kFull, dz);
+      if (dz >= 0 && lane == __ffs(peers) - 1) atomicAdd(S.bcur + dz, __popc(peers));
+      if (pa >= 0 && (S.mask[pa] & bits) != bits) atomicOr(S.mask + pa, bits);
+      if (pb >= 0 && (S.mask[pb] & bits) != bits) atomicOr(S.mask + pb, bits);
     }
   }
-  float* grow_s = S.sbuf + static_cast<size_t>(r) * 16 * L.sld;  // the row group's 16 dense rows
-  float* srow_q = S.sbuf + static_cast<size_t>(qi) * L.sld;     // the owned query's dense row
+  __syncthreads();
+  if (warp == 0) {  // bucket starts (exclusive scan of 32 counts); the counts become fill cursors
+    const int c = S.bcur[lane];
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += t;
+    }
+    S.bstart[lane + 1] = incl;
+    if (lane == 0) S.bstart[0] = 0;
+    S.bcur[lane] = incl - c;
+  }
+  __syncthreads();
+  // hit list: every active sample once, grouped by frame bucket
+  for (int s = 0; s < jper; ++s) {
+    const int j = js + s;
+    int dz = -1;
+    if (qvalid && s < n) {
+      const unsigned long long v = S.rec[qbase + j];
+      if (v >> 63) dz = static_cast<int>((v >> 36) & 0x1fu);
+      S.sv[qbase + j] = 0.f;
+      S.g3[3 * (qbase + j)] = 0.f;
+      S.g3[3 * (qbase + j) + 1] = 0.f;
+      S.g3[3 * (qbase + j) + 2] = 0.f;
+    }
+    const unsigned peers = __match_any_sync(kFull, dz);
+    const int leader = __ffs(peers) - 1;
+    int pos = 0;
+    if (dz >= 0 && lane == leader) pos = atomicAdd(S.bcur + dz, __popc(peers));
+    pos = __shfl_sync(kFull, pos, leader) + __popc(peers & ((1u << lane) - 1u));
+    if (dz >= 0) S.hits[pos] = static_cast<unsigned short>(qbase + j);
+  }
 
-  // ---- pass 1: V side (dp_j and the value part of the coordinate gradient)
-  if (any && !overflow) {
+  const int g = lane >> 2, t4 = lane & 3;
+  float* grow_a = S.sa + static_cast<size_t>(r) * 16 * L.sld;  // the row group's 16 dense rows
+  __syncthreads();
+
+  // ---- pass 1: V side (dp_j and the value part of the coordinate gradient), hits CTA-wide
+  if (work) {
     for (int z = E.zlo; z <= E.zhi; ++z) {
       const int zrel = z - E.zlo + 1;
+      const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
       for (int iy = 0; iy < E.ny; ++iy) {
         const int ya = E.ylo + iy * (E.R - 1), yb = min(ya + E.R - 1, E.yhi);
         for (int ix = 0; ix < E.nx; ++ix) {
           const int xa = E.xlo + ix * (E.cw - 1), xb = min(xa + E.cw - 1, E.xhi);
           const int ncw = xb - xa + 1;
-          const int nkp = ((yb - ya + 1) * ncw + 15) & ~15;
+          const int ntile = (((yb - ya + 1) * ncw + 15) >> 4);
+          const uint32_t m = masks ? S.mask[zrel * kMaxMaskChunks + iy * E.nx + ix]
+                                   : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
+          if (m == 0u) continue;
           __syncthreads();
-          load_chunk<DCH>(P, T, S.kbuf, L.rs, static_cast<const __nv_bfloat16*>(P.v), P.v_ld, z, ya, yb, xa, xb, nkp);
+          load_keys<DCH>(P, T, S.kbuf, L.rs, S.key_off, static_cast<const __nv_bfloat16*>(P.v), P.v_ld, z, ya, yb, xa,
+                         xb, m);
           __syncthreads();
-          dense_scores<DCH, kWPG>(S.kbuf, L.rs, grow_s, L.sld, part, nkp, da, dt_);
+          dense_tiles<DCH, kWPG>(S.kbuf, S.dos + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, m);
           __syncthreads();
-          if (!qvalid || zrel < zl_lo || zrel > zl_hi) continue;
-          for (int j = js; j < je; ++j) {
-            const unsigned long long v = rec[j];
-            if (!rec_in_plane(v, zrel)) continue;
-            const Rec c = unpack_rec(v, E);
+          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+            const int idx = S.hits[i];
+            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+            const Rec c = decode(S.rec[idx], E);
             if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
               continue;
             const bool upper = z != c.t0;
             const float az = frac_weight(c.ft, upper);
-            const PlaneTerms pt_ = plane_terms(srow_q, (c.h0 - ya) * ncw + (c.w0 - xa), ncw, c, P.H, P.W);
-            const float pv = ((v >> kBitKeep) & 1ull) ? pp[j] * P.drop_keep_scale : 0.f;
-            acc[j] = fmaf(az, pt_.bil, acc[j]);
-            g3[3 * j + 0] = fmaf(pv, upper ? pt_.bil : -pt_.bil, g3[3 * j + 0]);
-            g3[3 * j + 1] = fmaf(pv * az, pt_.dvy, g3[3 * j + 1]);
-            g3[3 * j + 2] = fmaf(pv * az, pt_.dvx, g3[3 * j + 2]);
+            const PlaneTerms pt_ =
+                plane_terms(S.sa + static_cast<size_t>(q) * L.sld, (c.h0 - ya) * ncw + (c.w0 - xa), ncw, c, P.H, P.W);
+            S.sv[idx] = fmaf(az, pt_.bil, S.sv[idx]);
+            float* gg = S.g3 + 3 * idx;
+            gg[0] += upper ? pt_.bil : -pt_.bil;
+            gg[1] = fmaf(az, pt_.dvy, gg[1]);
+            gg[2] = fmaf(az, pt_.dvx, gg[2]);
           }
         }
       }
     }
   }
+  __syncthreads();
 
-  // ---- dsq_j = softmax_scale * p_j * (keep_j dp_j / (1 - p_drop) - D)
-  if (qvalid) {
-    const float D = S.dd[qi];
-    for (int j = js; j < je; ++j) {
-      const float kf = ((rec[j] >> kBitKeep) & 1ull) ? P.drop_keep_scale : 0.f;
-      acc[j] = pp[j] * fmaf(kf, acc[j], -D) * P.scale;
+  // ---- dsq_j = softmax_scale * p_j * (keep_j dp_j / (1 - p_drop) - D); g_j = pv_j gv_j; row scales
+  {
+    float bds = 0.f, bp = 0.f;
+    if (qvalid) {
+      const float D = S.dd[qi];
+      const float* prob_row = P.probs + S.prow[qi] * K;
+      for (int j = js; j < je; ++j) {
+        const unsigned long long v = S.rec[qbase + j];
+        if (!(v >> 63)) continue;
+        const float p = __ldg(prob_row + j);
+        const bool keep = (v >> kBitKeep) & 1ull;
+        const float pv = keep ? p * P.drop_keep_scale : 0.f;
+        const float kf = keep ? P.drop_keep_scale : 0.f;
+        const float dsq = p * fmaf(kf, S.sv[qbase + j], -D) * P.scale;
+        S.sv[qbase + j] = dsq;
+        float* gg = S.g3 + 3 * (qbase + j);
+        gg[0] *= pv;
+        gg[1] *= pv;
+        gg[2] *= pv;
+        bds += fabsf(dsq);
+        bp += pv;
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < kLPQ; o <<= 1) {
+      bds += __shfl_xor_sync(kFull, bds, o);
+      bp += __shfl_xor_sync(kFull, bp, o);
+    }
+    if (sub == 0) {
+      S.qsc[qi] = bds > 0.f ? kFixRange / bds : 1.f;
+      S.qsc[kQ + qi] = bds > 0.f ? bds / kFixRange : 0.f;
+      S.qsc[2 * kQ + qi] = bp > 0.f ? kFixRange / bp : 1.f;
+      S.qsc[3 * kQ + qi] = bp > 0.f ? bp / kFixRange : 0.f;
     }
   }
+  __syncthreads();
 
-  // ---- pass 2: K side (key part of the coordinate gradient, dQ, dK, dV)
+  // ---- pass 2: K side (key part of the coordinate gradient, dQ, dK, dV), hits CTA-wide
   constexpr int kTPW = (DCH + kWPG - 1) / kWPG;  // dQ channel tiles per warp
   const int nt0 = min(DCH, part * kTPW), nt1 = min(DCH, nt0 + kTPW);
   float oq[kTPW + 1][4];
 #pragma unroll
   for (int i = 0; i < kTPW + 1; ++i) oq[i][0] = oq[i][1] = oq[i][2] = oq[i][3] = 0.f;
-  if (any && !overflow) {
+  const __nv_bfloat16* tds = reinterpret_cast<const __nv_bfloat16*>(S.sb);  // dS~^T after the transposition
+  const __nv_bfloat16* tpp = reinterpret_cast<const __nv_bfloat16*>(S.sa);  // P~^T after the transposition
+  if (work) {
     for (int z = E.zlo; z <= E.zhi; ++z) {
       const int zrel = z - E.zlo + 1;
-      const int zl = z - P.kv_frame0;
-      const bool lane_active = qvalid && zrel >= zl_lo && zrel <= zl_hi;
+      const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
       for (int iy = 0; iy < E.ny; ++iy) {
         const int ya = E.ylo + iy * (E.R - 1), yb = min(ya + E.R - 1, E.yhi);
         for (int ix = 0; ix < E.nx; ++ix) {
           const int xa = E.xlo + ix * (E.cw - 1), xb = min(xa + E.cw - 1, E.xhi);
           const int ncw = xb - xa + 1;
-          const int nk = (yb - ya + 1) * ncw;
-          const int nkp = (nk + 15) & ~15;
+          const int ntile = (((yb - ya + 1) * ncw + 15) >> 4);
+          const uint32_t m = masks ? S.mask[zrel * kMaxMaskChunks + iy * E.nx + ix]
+                                   : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
+          if (m == 0u) continue;
           __syncthreads();
-          load_chunk<DCH>(P, T, S.kbuf, L.rs, static_cast<const __nv_bfloat16*>(P.k), P.k_ld, z, ya, yb, xa, xb, nkp);
+          load_keys<DCH>(P, T, S.kbuf, L.rs, S.key_off, static_cast<const __nv_bfloat16*>(P.k), P.k_ld, z, ya, yb, xa,
+                         xb, m);
+          zero_tiles(S.sb, L.sld, m);
           __syncthreads();
-          dense_scores<DCH, kWPG>(S.kbuf, L.rs, grow_s, L.sld, part, nkp, qa, qt);
+          dense_tiles<DCH, kWPG>(S.kbuf, S.qs + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, m);
           __syncthreads();
-          if (lane_active) {
-            for (int j = js; j < je; ++j) {
-              const unsigned long long v = rec[j];
-              if (!rec_in_plane(v, zrel)) continue;
-              const Rec c = unpack_rec(v, E);
-              if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-                continue;
-              const bool upper = z != c.t0;
-              const float az = frac_weight(c.ft, upper);
-              const PlaneTerms pt_ = plane_terms(srow_q, (c.h0 - ya) * ncw + (c.w0 - xa), ncw, c, P.H, P.W);
-              const float dsq = acc[j];
-              g3[3 * j + 0] = fmaf(dsq, upper ? pt_.bil : -pt_.bil, g3[3 * j + 0]);
-              g3[3 * j + 1] = fmaf(dsq * az, pt_.dvy, g3[3 * j + 1]);
-              g3[3 * j + 2] = fmaf(dsq * az, pt_.dvx, g3[3 * j + 2]);
-            }
+          // key part of the coordinate gradient (reads S) and the dS~ scatter (into sb)
+          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+            const int idx = S.hits[i];
+            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+            const Rec c = decode(S.rec[idx], E);
+            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
+              continue;
+            const bool upper = z != c.t0;
+            const float az = frac_weight(c.ft, upper);
+            const int k00 = (c.h0 - ya) * ncw + (c.w0 - xa);
+            const PlaneTerms pt_ = plane_terms(S.sa + static_cast<size_t>(q) * L.sld, k00, ncw, c, P.H, P.W);
+            const float dsq = S.sv[idx];
+            float* gg = S.g3 + 3 * idx;
+            gg[0] = fmaf(dsq, upper ? pt_.bil : -pt_.bil, gg[0]);
+            gg[1] = fmaf(dsq * az, pt_.dvy, gg[1]);
+            gg[2] = fmaf(dsq * az, pt_.dvx, gg[2]);
+            scatter_fixed(reinterpret_cast<int*>(S.sb) + static_cast<size_t>(q) * L.sld, k00, ncw, c,
+                          dsq * az * S.qsc[q], P.H, P.W);
           }
           __syncthreads();
-          // dS~ (float atomics: dsq is signed)
-          for (int row = warp; row < kQ; row += kWarps)
-            for (int col = lane * 4; col < nkp; col += 128)
-              *reinterpret_cast<float4*>(S.sbuf + static_cast<size_t>(row) * L.sld + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+          // dS~ -> bf16 [key][query]; S no longer needed: clear sa for P~
+          transpose_fixed(S.sb, L.sld, m, S.qsc + kQ);
+          zero_tiles(S.sa, L.sld, m);
           __syncthreads();
-          if (lane_active) {
-            for (int j = js; j < je; ++j) {
-              const unsigned long long v = rec[j];
-              if (!rec_in_plane(v, zrel)) continue;
-              const Rec c = unpack_rec(v, E);
-              if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-                continue;
-              const float dsq = acc[j] * frac_weight(c.ft, z != c.t0);
-              const int k00 = (c.h0 - ya) * ncw + (c.w0 - xa);
-              const float ax0 = 1.f - c.fw, ax1 = c.fw, ay0 = 1.f - c.fh, ay1 = c.fh;
-              atomicAdd(srow_q + k00, dsq * (ax0 * ay0));
-              if (c.w0 + 1 < P.W) atomicAdd(srow_q + k00 + 1, dsq * (ax1 * ay0));
-              if (c.h0 + 1 < P.H) {
-                atomicAdd(srow_q + k00 + ncw, dsq * (ax0 * ay1));
-                if (c.w0 + 1 < P.W) atomicAdd(srow_q + k00 + ncw + 1, dsq * (ax1 * ay1));
-              }
-            }
+          // P~ scatter (into sa), dQ += dS~ . K_chunk, dK_chunk = dS~^T . Q
+          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+            const int idx = S.hits[i];
+            const unsigned long long v = S.rec[idx];
+            if (!((v >> kBitKeep) & 1ull)) continue;
+            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+            const Rec c = decode(v, E);
+            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
+              continue;
+            const float pv = __ldg(P.probs + S.prow[q] * K + (idx - q * K)) * P.drop_keep_scale;
+            scatter_fixed(reinterpret_cast<int*>(S.sa) + static_cast<size_t>(q) * L.sld,
+                          (c.h0 - ya) * ncw + (c.w0 - xa), ncw, c,
+                          pv * frac_weight(c.ft, z != c.t0) * S.qsc[2 * kQ + q], P.H, P.W);
           }
+          dq_product<DCH, kTPW>(tds, r, S.kbuf, L.rs, nt0, nt1, m, oq);
+          kv_product_flush<DCH>(P, T, L, tds, S.qs, S.key_off, m, P.dk_acc);
           __syncthreads();
-          // dQ += dS~ . K_chunk (row group r, channel tiles [nt0, nt1)) and dK_chunk = dS~^T . Q
-          av_product<DCH, kTPW, false>(grow_s, L.sld, S.kbuf, L.rs, nt0, nt1, nkp, oq);
-          kv_product_flush<DCH, false>(P, T, L, S.sbuf, S.qs, nkp, nk, ncw, ya, xa, zl, P.dk_acc);
+          transpose_fixed(S.sa, L.sld, m, S.qsc + 3 * kQ);
           __syncthreads();
-          // P~ (fixed point, pv >= 0) -> dV_chunk = P~^T . dO
-          for (int row = warp; row < kQ; row += kWarps)
-            for (int col = lane * 4; col < nkp; col += 128)
-              *reinterpret_cast<float4*>(S.sbuf + static_cast<size_t>(row) * L.sld + col) = make_float4(0.f, 0.f, 0.f, 0.f);
-          __syncthreads();
-          if (lane_active) {
-            unsigned int* prow_u = reinterpret_cast<unsigned int*>(srow_q);
-            for (int j = js; j < je; ++j) {
-              const unsigned long long v = rec[j];
-              if (!rec_in_plane(v, zrel) || !((v >> kBitKeep) & 1ull)) continue;
-              const Rec c = unpack_rec(v, E);
-              if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-                continue;
-              const float pv = pp[j] * P.drop_keep_scale * frac_weight(c.ft, z != c.t0) * kPtScale;
-              const int k00 = (c.h0 - ya) * ncw + (c.w0 - xa);
-              const float ax0 = 1.f - c.fw, ax1 = c.fw, ay0 = 1.f - c.fh, ay1 = c.fh;
-              atomicAdd(prow_u + k00, __float2uint_rn(pv * (ax0 * ay0)));
-              if (c.w0 + 1 < P.W) atomicAdd(prow_u + k00 + 1, __float2uint_rn(pv * (ax1 * ay0)));
-              if (c.h0 + 1 < P.H) {
-                atomicAdd(prow_u + k00 + ncw, __float2uint_rn(pv * (ax0 * ay1)));
-                if (c.w0 + 1 < P.W) atomicAdd(prow_u + k00 + ncw + 1, __float2uint_rn(pv * (ax1 * ay1)));
-              }
-            }
-          }
-          __syncthreads();
-          kv_product_flush<DCH, true>(P, T, L, S.sbuf, S.dos, nkp, nk, ncw, ya, xa, zl, P.dv_acc);
+          kv_product_flush<DCH>(P, T, L, tpp, S.dos, S.key_off, m, P.dv_acc);
         }
       }
     }
   }
+  __syncthreads();
 
   // ---- dQ (bf16) and the offset gradients
   {
@@ -561,19 +816,19 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   }
   if (qvalid) {
     float* drow = P.doffsets + (static_cast<long long>(T.b) * P.Nq + qrow) * P.doff_ld + static_cast<long long>(T.head) * K3;
+    // d p / d grid = S/2 strictly inside the volume (0 on or beyond the border), times the offset
+    // normalisation: channel 0 moved grid x (W) after division by (T-1), channel 1 grid y (H) by
+    // (H-1), channel 2 grid z (T) by (W-1)
+    const float c0 = P.T > 1 ? 0.5f * static_cast<float>(P.W) * P.oscale / static_cast<float>(P.T - 1) : 0.f;
+    const float c1 = P.H > 1 ? 0.5f * static_cast<float>(P.H) * P.oscale / static_cast<float>(P.H - 1) : 0.f;
+    const float c2 = P.W > 1 ? 0.5f * static_cast<float>(P.T) * P.oscale / static_cast<float>(P.W - 1) : 0.f;
     for (int j = js; j < je; ++j) {
-      const unsigned long long v = rec[j];
-      float gt = 0.f, gh = 0.f, gw = 0.f;
-      if (v >> 63) {  // d p / d grid = S/2 strictly inside the volume, 0 on or beyond the border
-        gt = ((v >> kBitInT) & 1ull) ? g3[3 * j + 0] * (0.5f * static_cast<float>(P.T)) : 0.f;
-        gh = ((v >> kBitInH) & 1ull) ? g3[3 * j + 1] * (0.5f * static_cast<float>(P.H)) : 0.f;
-        gw = ((v >> kBitInW) & 1ull) ? g3[3 * j + 2] * (0.5f * static_cast<float>(P.W)) : 0.f;
-      }
-      // offset channel 0 moved grid x (W) after division by (T-1), channel 1 grid y (H) by (H-1),
-      // channel 2 grid z (T) by (W-1)
-      drow[3 * j + 0] = P.T > 1 ? __fdiv_rn(gw, static_cast<float>(P.T - 1)) * P.oscale : 0.f;
-      drow[3 * j + 1] = P.H > 1 ? __fdiv_rn(gh, static_cast<float>(P.H - 1)) * P.oscale : 0.f;
-      drow[3 * j + 2] = P.W > 1 ? __fdiv_rn(gt, static_cast<float>(P.W - 1)) * P.oscale : 0.f;
+      const unsigned long long v = S.rec[qbase + j];
+      const float* gg = S.g3 + 3 * (qbase + j);
+      const bool act = v >> 63;
+      drow[3 * j + 0] = (act && ((v >> kBitInW) & 1ull)) ? gg[2] * c0 : 0.f;
+      drow[3 * j + 1] = (act && ((v >> kBitInH) & 1ull)) ? gg[1] * c1 : 0.f;
+      drow[3 * j + 2] = (act && ((v >> kBitInT) & 1ull)) ? gg[0] * c2 : 0.f;
     }
   }
 }
@@ -585,6 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
 bool tc_bwd_supported(const AttnParams& P) {
   if (!tc_supported(P)) return false;
   if (P.G != 0 || P.probs == nullptr) return false;
+  if (static_cast<long long>(tc::bwd::kQ) * P.K > 65536) return false;  // hit-list entries are 16-bit
   return true;
 }
 
@@ -594,20 +850,24 @@ bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   L.tiles_h = (P.H + tc::bwd::kTileH - 1) / tc::bwd::kTileH;
   L.tiles_w = (P.W + tc::kTileW - 1) / tc::kTileW;
   const size_t fixed = tc::bwd::smem_fixed(P, L.rs);
-  const size_t per_key = static_cast<size_t>(L.rs) * 2 + static_cast<size_t>(tc::bwd::kQ) * 4;
-  const size_t slack = static_cast<size_t>(tc::bwd::kQ) * 8 * 4;  // score-row padding (sld = maxkeys + 8)
+  // per key: its K/V row, two dense fp32 columns, its key-table entry
+  const size_t per_key = static_cast<size_t>(L.rs) * 2 + 2 * static_cast<size_t>(tc::bwd::kQ) * 4 + 4;
+  const size_t slack = 2 * static_cast<size_t>(tc::bwd::kQ) * 8 * 4;  // dense-row padding (sld = maxkeys + 8)
   if (fixed + slack + per_key * 64 > static_cast<size_t>(smem_limit)) return false;
   int mk = static_cast<int>((static_cast<size_t>(smem_limit) - fixed - slack) / per_key);
   mk &= ~15;
   if (mk < 64) return false;
-  if (mk > 1024) mk = 1024;
+  if (mk > tc::bwd::kMaxKeys) mk = tc::bwd::kMaxKeys;
   L.maxkeys = mk;
   L.sld = mk + 8;  // row stride = 8 or 24 (mod 32) words: mma fragment rows hit distinct banks
-  // the setup stages 32 queries x K x 3 offsets in the key buffer + score rows
+  // a transposed bf16 tile [maxkeys][40] must fit in a dense fp32 tile [32][sld]
+  if (static_cast<size_t>(mk) * tc::bwd::kTRow * 2 > static_cast<size_t>(tc::bwd::kQ) * L.sld * 4) return false;
+  // the setup stages 32 queries x K x 3 offsets in the key buffer + the first dense tile
   if (static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::bwd::kQ) * L.sld * 4 <
       static_cast<size_t>(tc::bwd::kQ) * P.K * 12)
     return false;
-  L.smem = static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::bwd::kQ) * L.sld * 4 + fixed;
+  L.smem = static_cast<size_t>(mk) * L.rs * 2 + 2 * static_cast<size_t>(tc::bwd::kQ) * L.sld * 4 +
+           static_cast<size_t>(mk) * 4 + fixed;
   L.tiles = static_cast<long long>(P.B) * P.q_frames * L.tiles_h * L.tiles_w * P.nh;
   return L.tiles <= 0x7fffffffLL && L.smem <= static_cast<size_t>(smem_limit);
 }

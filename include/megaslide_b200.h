@@ -174,6 +174,10 @@ typedef struct msl_dwconv_geometry {
   int32_t in_frame0, in_frames;   /* frames held by the input buffer */
   int32_t out_frame0, out_frames; /* frames produced / reduced over */
   int32_t dtype;                  /* MSL_DTYPE_* of the activation buffers */
+  int32_t zero_outside;           /* 0: the input frames must hold every tap of the output frames
+                                     (frames outside the volume are zero padding); 1: frames outside
+                                     the input window also read as zero -- the adjoint of a
+                                     time-sharded forward, where dy exists only on the own frames */
 } msl_dwconv_geometry;
 
 #define MSL_EPI_NONE 0      /* y = conv(x) + bias + bias2 */

@@ -79,7 +79,7 @@ class DwconvGeometry(ctypes.Structure):
     _fields_ = [
         ("batch", _i32), ("frames", _i32), ("height", _i32), ("width", _i32), ("channels", _i32),
         ("kt", _i32), ("kh", _i32), ("kw", _i32), ("in_frame0", _i32), ("in_frames", _i32),
-        ("out_frame0", _i32), ("out_frames", _i32), ("dtype", _i32),
+        ("out_frame0", _i32), ("out_frames", _i32), ("dtype", _i32), ("zero_outside", _i32),
     ]
 
 

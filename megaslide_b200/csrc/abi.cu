@@ -141,11 +141,12 @@ int fill_conv(const msl_dwconv_geometry* g, msl::ConvParams& P) {
   if (g->in_frame0 < 0 || g->in_frames < 1 || g->in_frame0 + g->in_frames > g->frames ||
       g->out_frame0 < 0 || g->out_frames < 1 || g->out_frame0 + g->out_frames > g->frames)
     return fail(MSL_ERR_INVALID, "frame windows outside the volume");
+  if (g->zero_outside != 0 && g->zero_outside != 1) return fail(MSL_ERR_INVALID, "zero_outside must be 0 or 1");
   // every tap of every produced frame must be in the input window or outside the volume
   const int pt = g->kt / 2;
   const int need0 = g->out_frame0 - pt < 0 ? 0 : g->out_frame0 - pt;
   const int need1 = g->out_frame0 + g->out_frames + pt > g->frames ? g->frames : g->out_frame0 + g->out_frames + pt;
-  if (need0 < g->in_frame0 || need1 > g->in_frame0 + g->in_frames)
+  if (!g->zero_outside && (need0 < g->in_frame0 || need1 > g->in_frame0 + g->in_frames))
     return fail(MSL_ERR_INVALID, "input frames [%d, %d) do not cover the taps of output frames [%d, %d) (need [%d, %d))",
                 g->in_frame0, g->in_frame0 + g->in_frames, g->out_frame0, g->out_frame0 + g->out_frames, need0, need1);
   P.B = g->batch; P.T = g->frames; P.H = g->height; P.W = g->width; P.C = g->channels;

@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(256) dwconv_fwd_kernel(const ConvParams P, con
   for (int e = 0; e < CV; ++e) acc[e] = 0.f;
   for (int it = 0; it < P.kt; ++it) {
     const int ti = FLIP ? tg - it + pt : tg + it - pt;
-    if (ti < 0 || ti >= P.T) continue;
+    if (ti < P.in_frame0 || ti >= P.in_frame0 + P.in_frames) continue;  // zero outside the input frames
     const int til = ti - P.in_frame0;
     for (int ih = 0; ih < P.kh; ++ih) {
       const int hi = FLIP ? h - ih + ph : h + ih - ph;
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(512) dwconv_wgrad_kernel(const ConvParams P, c
       }
       const int ti = P.out_frame0 + tl + it - pt;
       const int hi = h + ih - ph;
-      if (ti < 0 || ti >= P.T || hi < 0 || hi >= P.H) continue;
+      if (ti < P.in_frame0 || ti >= P.in_frame0 + P.in_frames || hi < 0 || hi >= P.H) continue;
       const int til = ti - P.in_frame0;
       const T* xrow = x + ((static_cast<long long>(b) * P.in_frames + til) * P.H + hi) * P.W * x_ld + cc;
       const int wlo = max(0, pw - iw), whi = min(P.W, P.W + pw - iw);

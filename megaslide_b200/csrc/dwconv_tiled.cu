@@ -3,7 +3,8 @@
 //
 // One CTA owns a tile of TH rows x 32 columns of the volume, one group of 32 four-byte channel words
 // (64 bf16 or 32 float32 channels) and a chunk of consecutive frames.  Input frames are staged in a
-// ring of kt + 1 shared-memory slices (tile + kh/2, kw/2 halo, zero outside the volume) with cp.async:
+// ring of kt + 1 shared-memory slices (tile + kh/2, kw/2 halo, zero outside the volume; frames
+// outside the input window read as zero) with cp.async:
 // while output frame t is computed from slices t - kt/2 .. t + kt/2, slice t + kt/2 + 1 is loaded, so
 // every input frame is fetched once per chunk and the fetch overlaps the arithmetic.  A warp owns one
 // tile row and 16 consecutive columns; each lane one channel word; the kw taps of a kernel row slide
@@ -138,7 +139,7 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
   const int base = cp.ta - pt;
   const int c0w = cp.cg * 32;  // first channel word of the group
   const int c0 = c0w * CV;
-  for (int ti = max(0, cp.ta - pt); ti <= min(P.T - 1, cp.ta + pt); ++ti)
+  for (int ti = max(P.in_frame0, cp.ta - pt); ti <= min(P.in_frame0 + P.in_frames - 1, cp.ta + pt); ++ti)
     load_slice<T>(P, L, x, x_ld, ring + ((ti - base) % nslots) * slice_words, cp.b, ti, cp.h0, cp.w0, c0);
   tc::cp_async_wait_all();
   __syncthreads();
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
   }
   for (int t = cp.ta; t < cp.tb; ++t) {
     const int tn = t + pt + 1;
-    if (t + 1 < cp.tb && tn < P.T)
+    if (t + 1 < cp.tb && tn >= P.in_frame0 && tn < P.in_frame0 + P.in_frames)
       load_slice<T>(P, L, x, x_ld, ring + ((tn - base) % nslots) * slice_words, cp.b, tn, cp.h0, cp.w0, c0);
     if (active) {
       float acc[kSeg][CV];
@@ -166,7 +167,7 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
         for (int e = 0; e < CV; ++e) acc[j][e] = 0.f;
       for (int it = 0; it < P.kt; ++it) {
         const int ti = t + it - pt;
-        if (ti < 0 || ti >= P.T) continue;
+        if (ti < P.in_frame0 || ti >= P.in_frame0 + P.in_frames) continue;  // zero outside the input frames
         const int itw = FLIP ? P.kt - 1 - it : it;
         const uint32_t* sl = ring + ((ti - base) % nslots) * slice_words;
         for (int ih = 0; ih < P.kh; ++ih) {
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(256, 1) dwconv_wgrad_tiled_kernel(const ConvPa
     }
   };
 
-  for (int ti = max(0, cp.ta - pt); ti <= min(P.T - 1, cp.ta + pt); ++ti)
+  for (int ti = max(P.in_frame0, cp.ta - pt); ti <= min(P.in_frame0 + P.in_frames - 1, cp.ta + pt); ++ti)
     load_slice<T>(P, L, x, x_ld, ring + ((ti - base) % nslots) * slice_words, cp.b, ti, cp.h0, cp.w0, c0);
   stage_dy(cp.ta, dys);
   tc::cp_async_wait_all();
@@ -286,7 +287,7 @@ __global__ void __launch_bounds__(256, 1) dwconv_wgrad_tiled_kernel(const ConvPa
   int buf = 0;
   for (int t = cp.ta; t < cp.tb; ++t) {
     const int tn = t + pt + 1;
-    if (t + 1 < cp.tb && tn < P.T)
+    if (t + 1 < cp.tb && tn >= P.in_frame0 && tn < P.in_frame0 + P.in_frames)
       load_slice<T>(P, L, x, x_ld, ring + ((tn - base) % nslots) * slice_words, cp.b, tn, cp.h0, cp.w0, c0);
     if (t + 1 < cp.tb) stage_dy(t + 1, dys + static_cast<size_t>(buf ^ 1) * L.dy_words);
     const TDY* dyt = dys + static_cast<size_t>(buf) * L.dy_words;
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(256, 1) dwconv_wgrad_tiled_kernel(const ConvPa
       }
       const int it = pair / P.kh, ih = pair - (pair / P.kh) * P.kh;
       const int ti = t + it - pt;
-      if (ti < 0 || ti >= P.T) continue;
+      if (ti < P.in_frame0 || ti >= P.in_frame0 + P.in_frames) continue;
       const uint32_t* sl = ring + ((ti - base) % nslots) * slice_words;
       for (int r = 0; r < L.th; ++r) {
         const uint32_t* rowp = sl + ((r + ih) * L.sc + seg * kSeg) * 32 + lane;

@@ -252,13 +252,14 @@ class ConvShape:
     in_frames: Optional[int] = None
     out_frame0: int = 0
     out_frames: Optional[int] = None
+    zero_outside: bool = False  # input frames outside the window read as zero (sharded adjoint)
 
     def geometry(self, dtype: torch.dtype) -> DwconvGeometry:
         kt, kh, kw = self.kernel
         return DwconvGeometry(self.batch, self.frames, self.height, self.width, self.channels, kt, kh, kw,
                               self.in_frame0, self.in_frames if self.in_frames is not None else self.frames,
                               self.out_frame0, self.out_frames if self.out_frames is not None else self.frames,
-                              dtype_code(dtype))
+                              dtype_code(dtype), 1 if self.zero_outside else 0)
 
     @property
     def out_rows(self) -> int:

@@ -1,0 +1,417 @@
+"""Time-axis sharding of DeformableSlideAttention3D across ranks (one process per GPU).
+
+Rank r owns the frames [t0_r, t1_r) of a global volume of T frames (every sample of the batch); the
+coordinates of every sample use the GLOBAL T, H, W (the reference's formulas,
+infinity/video/attention.py:113-127, 194-238), so a sharded run computes exactly what one process
+computes on the whole volume.  Per forward:
+
+1. the x frames one frame beyond the own range (the 3x3x3 offset conv and the kt x kh x kw dw_conv
+   read kt//2 frames around each output frame) are exchanged with the neighbours;
+2. the offsets of the own frames are computed and the largest temporal offset is reduced over all
+   ranks (one float, MAX); from it every rank computes, for every rank, the frame range its samples
+   can reach (the bound of the trilinear corners, plus one frame of margin) -- a deterministic plan
+   that needs no further metadata exchange;
+3. the remaining x frames of that range are exchanged and K/V are projected over the whole window;
+4. the attention kernels run on the own query frames against the window (q_frame0 / kv_frame0).
+
+The backward mirrors it: every gradient that lands on a halo frame (K/V of halo frames, the
+transposed depthwise convs) is sent back to the frame's owner and added there, and the parameter
+gradients (partial sums over each rank's outputs) are summed over the ranks with one all-reduce.
+All exchanges are point-to-point (torch.distributed batch_isend_irecv: NCCL over NVLink for CUDA
+tensors); every rank issues the same collectives in the same order.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+
+from . import ops
+from ._lib import MSL_EPI_GELU, MSL_EPI_GELU_GRAD, MSL_EPI_NONE, MSL_ERR_UNSUPPORTED, MslError
+from .attention import DeformableSlideAttention3D, _mm_f32
+
+Range = Tuple[int, int]
+
+
+def shard_ranges(frames: int, world: int) -> List[Range]:
+    """Contiguous, balanced frame ranges [t0, t1) of `frames` frames over `world` ranks."""
+    if world < 1 or frames < world:
+        raise ValueError(f"cannot split {frames} frames over {world} ranks (need >= 1 frame per rank)")
+    base, rem = divmod(frames, world)
+    out, t = [], 0
+    for r in range(world):
+        n = base + (1 if r < rem else 0)
+        out.append((t, t + n))
+        t += n
+    return out
+
+
+def kv_frame_range(T: int, W: int, kt: int, own: Range, max_t_offset: float) -> Range:
+    """Frames [lo, hi) holding every trilinear corner the samples of query frames `own` can reach.
+
+    The time coordinate of window row `it` of query frame t is
+      g = 2 (t + it - kt//2) / max(T-1, 1) - 1 + o2 * offset_scale / (W-1)   (o2 = raw channel 2)
+      p = clamp(((g + 1) T - 1) / 2, 0, T-1),  corners floor(p) and floor(p) + 1
+    (the channel-2 offset moves the time axis after division by W-1: attention.py:118-127, 236).
+    `max_t_offset` = max |o2 * offset_scale| over the volume.  One frame of margin on each side
+    absorbs the float32 rounding of the kernels' arithmetic."""
+    t0, t1 = own
+    shift = (max_t_offset / (W - 1)) if W > 1 else 0.0
+    den = max(T - 1, 1)
+
+    def pix(a: int, o: float) -> float:
+        g = 2.0 * a / den - 1.0 + o
+        return min(T - 1.0, max(((g + 1.0) * T - 1.0) / 2.0, 0.0))
+
+    lo = math.floor(pix(t0 - kt // 2, -shift)) - 1
+    hi = math.floor(pix(t1 - 1 + kt // 2, shift)) + 1 + 1  # upper corner, margin
+    return max(0, lo), min(T, hi + 1)
+
+
+def conv_window(T: int, own: Range, pad: int) -> Range:
+    return max(0, own[0] - pad), min(T, own[1] + pad)
+
+
+def _overlap(a: Range, b: Range) -> Optional[Range]:
+    lo, hi = max(a[0], b[0]), min(a[1], b[1])
+    return (lo, hi) if lo < hi else None
+
+
+@dataclass
+class FramePlan:
+    """Which frames each rank owns and which window of frames each rank holds."""
+
+    owns: List[Range]
+    windows: List[Range]
+
+
+def exchange_into(buf: Tensor, buf_range: Range, local: Tensor, plan: FramePlan, fetch: Sequence[List[Range]],
+                  rank: int, group=None) -> None:
+    """Fills the frames `fetch[rank]` of `buf` (frames `buf_range`, laid out [B, frames, HW, C]) from
+    their owners; sends the own frames every other rank fetches.  `local` [B, own frames, HW, C]
+    holds this rank's frames.  fetch[s] = frame intervals rank s wants (the same list on every rank).
+    """
+    world = len(plan.owns)
+    own = plan.owns[rank]
+    ops_: list = []
+    recv_tmp = []
+    for s in range(world):
+        if s == rank:
+            continue
+        for iv in fetch[s]:  # frames rank s wants that this rank owns
+            ov = _overlap(iv, own)
+            if ov:
+                t = local[:, ov[0] - own[0]:ov[1] - own[0]].contiguous()
+                ops_.append(dist.P2POp(dist.isend, t, s, group))
+                recv_tmp.append(None)
+    for iv in fetch[rank]:
+        for r in range(world):
+            if r == rank:
+                continue
+            ov = _overlap(iv, plan.owns[r])
+            if ov:
+                t = torch.empty((buf.shape[0], ov[1] - ov[0]) + tuple(buf.shape[2:]), dtype=buf.dtype,
+                                device=buf.device)
+                ops_.append(dist.P2POp(dist.irecv, t, r, group))
+                recv_tmp.append((ov, t))
+    if ops_:
+        for req in dist.batch_isend_irecv(ops_):
+            req.wait()
+    for item in recv_tmp:
+        if item is not None:
+            ov, t = item
+            buf[:, ov[0] - buf_range[0]:ov[1] - buf_range[0]].copy_(t)
+
+
+def return_halo_grads(dwin: Tensor, plan: FramePlan, rank: int, group=None) -> Tensor:
+    """Reverse of the forward exchanges: sends the gradient rows of `dwin` ([B, window frames, HW, C],
+    frames plan.windows[rank]) that belong to other ranks to their owners, adds what the other ranks
+    send for the own frames, and returns the own frames [B, own frames, HW, C]."""
+    world = len(plan.owns)
+    win, own = plan.windows[rank], plan.owns[rank]
+    ops_: list = []
+    recvs = []
+    for r in range(world):
+        if r == rank:
+            continue
+        ov = _overlap(win, plan.owns[r])
+        if ov:
+            ops_.append(dist.P2POp(dist.isend, dwin[:, ov[0] - win[0]:ov[1] - win[0]].contiguous(), r, group))
+        ov = _overlap(plan.windows[r], own)
+        if ov:
+            t = torch.empty((dwin.shape[0], ov[1] - ov[0]) + tuple(dwin.shape[2:]), dtype=dwin.dtype,
+                            device=dwin.device)
+            ops_.append(dist.P2POp(dist.irecv, t, r, group))
+            recvs.append((ov, t))
+    if ops_:
+        for req in dist.batch_isend_irecv(ops_):
+            req.wait()
+    out = dwin[:, own[0] - win[0]:own[1] - win[0]].clone()
+    for ov, t in recvs:
+        out[:, ov[0] - own[0]:ov[1] - own[0]] += t
+    return out
+
+
+class _ShardCfg:
+    __slots__ = ("T", "H", "W", "rank", "world", "owns", "group", "heads", "head_dim", "kernel", "oscale",
+                 "dropout_p", "seed", "dtype", "param_dtypes", "G")
+
+
+class DSA3DShardedFunction(torch.autograd.Function):
+    """Forward/backward of one rank's frames of a time-sharded DeformableSlideAttention3D."""
+
+    @staticmethod
+    def forward(ctx, cfg: _ShardCfg, x, extra_kv, wq, bq, wk, bk, wv, bv, wo, bo, wd, bd, w1, b1, w2, b2):
+        T, H, W, rank = cfg.T, cfg.H, cfg.W, cfg.rank
+        HW = H * W
+        own = cfg.owns[rank]
+        nown = own[1] - own[0]
+        B, N, C = x.shape
+        dt = cfg.dtype
+        kt, kh, kw = cfg.kernel
+        nh, d, G = cfg.heads, cfg.head_dim, cfg.G
+        xl = x.to(dt).reshape(B, nown, HW, C).contiguous()
+        # 1. conv halo (the offset net's 3x3x3 conv and the dw_conv read kt//2 frames around)
+        cpad = max(1, kt // 2)
+        cwins = [conv_window(T, o, cpad) for o in cfg.owns]
+        cw = cwins[rank]
+        xc = torch.empty(B, cw[1] - cw[0], HW, C, dtype=dt, device=x.device)
+        xc[:, own[0] - cw[0]:own[1] - cw[0]].copy_(xl)
+        fetch1 = [[iv for iv in ((cwins[s][0], cfg.owns[s][0]), (cfg.owns[s][1], cwins[s][1])) if iv[0] < iv[1]]
+                  for s in range(cfg.world)]
+        exchange_into(xc, cw, xl, FramePlan(cfg.owns, cwins), fetch1, rank, cfg.group)
+        xc2 = xc.view(-1, C)
+        # 2. offsets of the own frames, then the global largest temporal offset
+        conv3 = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=cw[0], in_frames=cw[1] - cw[0],
+                              out_frame0=own[0], out_frames=nown)
+        convk = ops.ConvShape(B, T, H, W, C, (kt, kh, kw), in_frame0=cw[0], in_frames=cw[1] - cw[0],
+                              out_frame0=own[0], out_frames=nown)
+        w1_kc = ops.conv_weight_kc(w1)
+        b1f = b1.detach().float().contiguous()
+        hact = ops.dwconv_fwd(conv3, xc2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
+        w2m = w2.reshape(w2.shape[0], C)
+        off = _mm_f32(hact, w2m.to(dt).t())
+        off += b2.detach().float()
+        wd_kc = ops.conv_weight_kc(wd)
+        D = ops.dwconv_fwd(convk, xc2, wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous(),
+                           epilogue=MSL_EPI_NONE)
+        amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale)
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=cfg.group)
+        dmax = float(amax[2].item())
+        if not math.isfinite(dmax):
+            raise FloatingPointError("non-finite offsets: the K/V halo cannot be bounded")
+        # 3. K/V window of every rank (deterministic on all ranks), fetch the remaining frames
+        kwins = [kv_frame_range(T, W, kt, o, dmax) for o in cfg.owns]
+        wins = [(min(kwins[s][0], cwins[s][0]), max(kwins[s][1], cwins[s][1])) for s in range(cfg.world)]
+        win = wins[rank]
+        xw = torch.empty(B, win[1] - win[0], HW, C, dtype=dt, device=x.device)
+        xw[:, cw[0] - win[0]:cw[1] - win[0]].copy_(xc)
+        fetch2 = [[iv for iv in ((wins[s][0], cwins[s][0]), (cwins[s][1], wins[s][1])) if iv[0] < iv[1]]
+                  for s in range(cfg.world)]
+        plan = FramePlan(cfg.owns, wins)
+        exchange_into(xw, win, xl, plan, fetch2, rank, cfg.group)
+        xw2 = xw.view(-1, C)
+        xo2 = xl.view(-1, C)
+        # 4. projections: q on the own rows, k / v on the window
+        wkv = torch.cat([wk, wv], 0).to(dt)
+        q = torch.addmm(bq.to(dt), xo2, wq.to(dt).t())
+        kv = torch.addmm(torch.cat([bk, bv], 0).to(dt), xw2, wkv.t())
+        k, v = kv[:, :C], kv[:, C:]
+        ek = ev = e2 = None
+        if G:
+            e2 = extra_kv.reshape(B * G, C).to(dt).contiguous()
+            ekv = torch.addmm(torch.cat([bk, bv], 0).to(dt), e2, wkv.t())
+            ek, ev = ekv[:, :C], ekv[:, C:]
+        sh = ops.DsaShape(B, T, H, W, nh, d, (kt, kh, kw), extra=G, q_frame0=own[0], q_frames=nown,
+                          kv_frame0=win[0], kv_frames=win[1] - win[0], offset_scale=cfg.oscale,
+                          dropout_p=cfg.dropout_p, dropout_seed=cfg.seed)
+        train = any(ctx.needs_input_grad)
+        probs = None
+        if train and ops.wants_probs(sh, dt):
+            probs = ops.probs_buffer(sh, x.device)
+            try:
+                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs)
+            except MslError as e:
+                if e.code != MSL_ERR_UNSUPPORTED:
+                    raise
+                probs = None
+        if probs is None:
+            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev)
+        y = torch.addmm(D, attn, wo.to(dt).t())
+        if train:
+            ctx.save_for_backward(xw, q, kv, hact, off, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc,
+                                  probs)
+            ctx.cfg, ctx.sh, ctx.plan, ctx.cw = cfg, sh, plan, cw
+            ctx.in_dtype = x.dtype
+            ctx.extra_dtype = extra_kv.dtype if extra_kv is not None else None
+        return y.view(B, N, C)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (xw, q, kv, hact, off, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc, probs) = ctx.saved_tensors
+        cfg: _ShardCfg = ctx.cfg
+        sh: ops.DsaShape = ctx.sh
+        plan: FramePlan = ctx.plan
+        cw = ctx.cw
+        T, H, W, rank = cfg.T, cfg.H, cfg.W, cfg.rank
+        HW = H * W
+        own, win = plan.owns[rank], plan.windows[rank]
+        nown, nwin = own[1] - own[0], win[1] - win[0]
+        B = xw.shape[0]
+        C = xw.shape[-1]
+        dt = cfg.dtype
+        kt, kh, kw = cfg.kernel
+        G = cfg.G
+        xw2 = xw.view(-1, C)
+        xo2 = xw[:, own[0] - win[0]:own[1] - win[0]].reshape(-1, C)
+        with torch.autocast("cuda", enabled=False):
+            dy2 = dy.reshape(-1, C).to(dt).contiguous()
+            dattn = torch.mm(dy2, wo.to(dt))
+            g_wo = _mm_f32(dy2.t(), attn)
+            g_bo = dy2.float().sum(0)
+            dxw = torch.zeros(B, nwin, HW, C, dtype=torch.float32, device=xw.device)
+
+            def add_frames(rows: Tensor, rng: Range) -> None:
+                dxw[:, rng[0] - win[0]:rng[1] - win[0]] += rows.view(B, rng[1] - rng[0], HW, C).float()
+
+            # dw_conv term: its transposed conv spreads the own dy over the frames kt//2 around
+            pk = conv_window(T, own, kt // 2)
+            convk_t = ops.ConvShape(B, T, H, W, C, (kt, kh, kw), in_frame0=own[0], in_frames=nown,
+                                    out_frame0=pk[0], out_frames=pk[1] - pk[0], zero_outside=True)
+            add_frames(ops.dwconv_bwd_data(convk_t, dy2, wd_kc), pk)
+            convk = ops.ConvShape(B, T, H, W, C, (kt, kh, kw), in_frame0=win[0], in_frames=nwin,
+                                  out_frame0=own[0], out_frames=nown)
+            g_wd = torch.zeros_like(wd_kc)
+            g_bd = torch.zeros(C, device=xw.device, dtype=torch.float32)
+            ops.dwconv_bwd_weight(convk, dy2, xw2, g_wd, g_bd)
+            # attention core: dq on the own rows, dk / dv on the window
+            dq = torch.empty_like(q)
+            dkv = torch.empty_like(kv)
+            k, v = kv[:, :C], kv[:, C:]
+            _, _, _, doff, dek, dev = ops.attn_bwd(sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev, dq=dq,
+                                                   dk=dkv[:, :C], dv=dkv[:, C:], probs=probs)
+            add_frames(_mm_f32(dq, wq.to(dt)), own)
+            dxw += _mm_f32(dkv, wkv).view(B, nwin, HW, C)
+            g_wq = _mm_f32(dq.t(), xo2)
+            g_bq = dq.float().sum(0)
+            g_wkv = _mm_f32(dkv.t(), xw2)
+            g_bkv = dkv.float().sum(0)
+            g_wk, g_wv = g_wkv[:C], g_wkv[C:]
+            g_bk, g_bv = g_bkv[:C], g_bkv[C:]
+            d_extra = None
+            if G:
+                dekv = torch.cat([dek, dev], 1)
+                d_extra = torch.mm(dekv, wkv.float()).view(B, G, C)
+                g_ekv = torch.mm(dekv.t(), e2.float())
+                g_wk = g_wk + g_ekv[:C]
+                g_wv = g_wv + g_ekv[C:]
+                sums = dekv.sum(0)
+                g_bk = g_bk + sums[:C]
+                g_bv = g_bv + sums[C:]
+            # offset predictor
+            doff_c = doff.to(dt)
+            dh = _mm_f32(doff_c, w2m.to(dt))
+            g_w2 = _mm_f32(doff_c.t(), hact)
+            g_b2 = doff.sum(0)
+            conv3 = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=win[0], in_frames=nwin, out_frame0=own[0],
+                                  out_frames=nown)
+            du = ops.dwconv_fwd(conv3, xw2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh, out_dtype=torch.float32)
+            p3 = conv_window(T, own, 1)
+            conv3_t = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=own[0], in_frames=nown, out_frame0=p3[0],
+                                    out_frames=p3[1] - p3[0], zero_outside=True)
+            add_frames(ops.dwconv_bwd_data(conv3_t, du, w1_kc), p3)
+            g_w1 = torch.zeros_like(w1_kc)
+            g_b1 = torch.zeros(C, device=xw.device, dtype=torch.float32)
+            ops.dwconv_bwd_weight(conv3, du, xw2, g_w1, g_b1)
+            # halo gradients back to their owners; parameter gradients summed over the ranks
+            dx_own = return_halo_grads(dxw, plan, rank, cfg.group)
+            parts = [g_wq, g_bq, g_wk, g_bk, g_wv, g_bv, g_wo, g_bo, g_wd, g_bd, g_w1, g_b1, g_w2, g_b2]
+            if d_extra is not None:
+                parts.append(d_extra)
+            flat = torch.cat([p.reshape(-1).float() for p in parts])
+            dist.all_reduce(flat, group=cfg.group)
+            outs, o = [], 0
+            for p in parts:
+                outs.append(flat[o:o + p.numel()].view(p.shape))
+                o += p.numel()
+        (g_wq, g_bq, g_wk, g_bk, g_wv, g_bv, g_wo, g_bo, g_wd, g_bd, g_w1, g_b1, g_w2, g_b2) = outs[:14]
+        d_extra = outs[14] if G else None
+        pd = cfg.param_dtypes
+
+        def conv_w(gkc, k3):
+            return gkc.t().reshape(C, 1, *k3)
+
+        grads = (
+            g_wq.to(pd[0]), g_bq.to(pd[1]), g_wk.to(pd[2]), g_bk.to(pd[3]), g_wv.to(pd[4]), g_bv.to(pd[5]),
+            g_wo.to(pd[6]), g_bo.to(pd[7]), conv_w(g_wd, (kt, kh, kw)).to(pd[8]), g_bd.to(pd[9]),
+            conv_w(g_w1, (3, 3, 3)).to(pd[10]), g_b1.to(pd[11]),
+            g_w2.reshape(w2m.shape[0], C, 1, 1, 1).to(pd[12]), g_b2.to(pd[13]),
+        )
+        dx_out = dx_own.reshape(B, nown * HW, C).to(ctx.in_dtype)
+        de = d_extra.to(ctx.extra_dtype) if d_extra is not None else None
+        return (None, dx_out, de) + grads
+
+
+class TimeShardedDSA3D(nn.Module):
+    """Runs a DeformableSlideAttention3D (whose parameters it shares) on this rank's frames of a
+    volume sharded along time.
+
+    forward(x_local [B, own_frames*H*W, D], video_shape = GLOBAL (T, H, W), extra_kv=None) returns
+    the module output for the own frames; gradients w.r.t. x_local and the (replicated) parameters
+    equal those of the unsharded module (parameter gradients are summed over the ranks inside the
+    backward, so every rank ends with the full gradient).  Frame ranges: `shard_ranges(T, world)`
+    unless `frame_ranges` is given (the same list on every rank)."""
+
+    def __init__(self, module: DeformableSlideAttention3D, group=None,
+                 frame_ranges: Optional[Sequence[Range]] = None):
+        super().__init__()
+        self.module = module
+        self.group = group
+        self.frame_ranges = list(frame_ranges) if frame_ranges is not None else None
+        self._joined = False
+
+    def forward(self, x: Tensor, video_shape: Tuple[int, int, int], extra_kv: Optional[Tensor] = None) -> Tensor:
+        m = self.module
+        T, H, W = video_shape
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        owns = self.frame_ranges or shard_ranges(T, world)
+        if len(owns) != world:
+            raise ValueError("frame_ranges must have one range per rank")
+        own = owns[rank]
+        B, N, D = x.shape
+        if N != (own[1] - own[0]) * H * W:
+            raise ValueError(f"x holds {N} tokens but the own frames {own} of {H}x{W} need {(own[1] - own[0]) * H * W}")
+        if D != m.hidden_size:
+            raise ValueError(f"hidden size {D} != {m.hidden_size}")
+        if not x.is_cuda:
+            raise RuntimeError("TimeShardedDSA3D runs on CUDA tensors only (no CPU fallback)")
+        dt = x.dtype
+        if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+            dt = torch.bfloat16
+        if dt not in (torch.float32, torch.bfloat16):
+            raise TypeError(f"megaslide_b200 supports float32 and bfloat16, got {dt}")
+        if not self._joined:  # the first NCCL call of the group must involve every rank
+            dist.all_reduce(torch.zeros(1, device=x.device), group=self.group)
+            self._joined = True
+        G = extra_kv.shape[1] if extra_kv is not None else 0
+        p = m.dropout.p if m.training else 0.0
+        seed = 0
+        if p > 0:  # one seed for all ranks: the keep rule is keyed by the global softmax index
+            s = torch.randint(0, 2 ** 62, (1,), device=x.device)
+            dist.broadcast(s, src=dist.get_global_rank(self.group, 0) if self.group is not None else 0,
+                           group=self.group)
+            seed = int(s.item())
+        cfg = _ShardCfg()
+        cfg.T, cfg.H, cfg.W, cfg.rank, cfg.world, cfg.owns, cfg.group = T, H, W, rank, world, owns, self.group
+        cfg.heads, cfg.head_dim, cfg.kernel = m.num_heads, m.head_dim, (m.k_t, m.k_h, m.k_w)
+        cfg.oscale, cfg.dropout_p, cfg.seed, cfg.dtype = float(m.offset_scale), float(p), seed, dt
+        cfg.param_dtypes = tuple(t.dtype for t in m._params())
+        cfg.G = G
+        with torch.autocast("cuda", enabled=False):
+            return DSA3DShardedFunction.apply(cfg, x, extra_kv, *m._params())

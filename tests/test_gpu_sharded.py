@@ -1,0 +1,106 @@
+"""Time-sharded DeformableSlideAttention3D on 2 GPUs (NCCL) against the unsharded module.
+
+Each rank builds the same module and the same global input, runs TimeShardedDSA3D on its frames
+and the plain module on the whole volume, and compares its frames of the output and of dx and the
+(all-reduced) parameter gradients.  Offsets are made large (several frames) so the K/V halo needs
+the second exchange.  Skipped with fewer than 2 GPUs."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rel(a, b):
+    a, b = a.detach().double(), b.detach().double()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def _fro(a, b):
+    a, b = a.detach().double(), b.detach().double()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def _worker(rank, world, port, dtype_name, q):
+    import torch.distributed as dist
+
+    import megaslide_b200 as msl
+    from megaslide_b200.sharded import TimeShardedDSA3D, shard_ranges
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        dt = getattr(torch, dtype_name)
+        B, T, H, W, C, nh, ks = 1, 8, 6, 10, 64, 2, (3, 5, 5)
+        torch.manual_seed(7)
+        m = msl.DeformableSlideAttention3D(C, nh, ks, offset_scale=3.0)
+        with torch.no_grad():
+            m.offset_net[2].weight.normal_(0, 0.4)
+            m.offset_net[2].bias.normal_(0, 0.5)
+        m = m.to(dev, dt)
+        g = torch.Generator(device=dev)
+        g.manual_seed(11)
+        x = torch.randn(B, T * H * W, C, device=dev, dtype=dt, generator=g)
+        gy = torch.randn(B, T * H * W, C, device=dev, dtype=dt, generator=g)
+        # unsharded
+        xf = x.clone().requires_grad_(True)
+        yf = m(xf, (T, H, W))
+        yf.backward(gy)
+        ref_grads = [p.grad.clone() for p in m.parameters()]
+        for p in m.parameters():
+            p.grad = None
+        # sharded
+        own = shard_ranges(T, world)[rank]
+        rows = slice(own[0] * H * W, own[1] * H * W)
+        xs = x[:, rows].clone().requires_grad_(True)
+        ys = TimeShardedDSA3D(m)(xs, (T, H, W))
+        ys.backward(gy[:, rows])
+        torch.cuda.synchronize()
+        res = {"y": _rel(ys, yf[:, rows]), "dx": _fro(xs.grad, xf.grad[:, rows]),
+               "dx_max": _rel(xs.grad, xf.grad[:, rows])}
+        scale = max(float(rg.double().norm()) for rg in ref_grads)
+        for (name, p), rg in zip(m.named_parameters(), ref_grads):
+            if name == "k_proj.bias":
+                # exactly zero in exact arithmetic (a key bias shifts all scores of a query
+                # equally): both sides are rounding noise, compared with the gradient scale
+                res[name] = float((p.grad.double() - rg.double()).norm()) / scale
+            else:
+                res[name] = _fro(p.grad, rg)
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("dtype_name,tol", [("float32", 1e-4), ("bfloat16", 2e-2)])
+def test_time_sharded_matches_unsharded_on_two_gpus(dtype_name, tol):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, dtype_name, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, r in res:
+        bad = {k: v for k, v in r.items() if v >= (5e-2 if k == "dx_max" and dtype_name == "bfloat16" else tol)}
+        assert not bad, f"rank {rank}: {bad}"

@@ -190,14 +190,17 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def _alg_bytes_per_token(name, C, nh, K, es):
+def _alg_bytes_per_token(name, C, nh, K, es, probs=False):
     """Algorithmic HBM bytes per token of one launch of each entry point (operands crossing the
-    entry point once; float32 accumulators inside msl_dsa_attn_bwd are scratch, not counted)."""
+    entry point once; float32 accumulators inside msl_dsa_attn_bwd are scratch, not counted).
+    probs: the tensor-core path's saved softmax weights (float32 [nh, K] per token), written by
+    the forward and read by the backward."""
     off = 4 * nh * K * 3
-    if name == "msl_dsa_attn_bwd":  # read q k v out dout offsets lse, write dq dk dv doffsets
-        return 5 * C * es + off + 4 * nh + 3 * C * es + off
-    if name == "msl_dsa_attn_fwd":  # read q k v offsets, write out lse
-        return 3 * C * es + off + C * es + 4 * nh
+    pr = 4 * nh * K if probs else 0
+    if name == "msl_dsa_attn_bwd":  # read q k v out dout offsets lse (probs), write dq dk dv doffsets
+        return 5 * C * es + off + 4 * nh + pr + 3 * C * es + off
+    if name == "msl_dsa_attn_fwd":  # read q k v offsets, write out lse (probs)
+        return 3 * C * es + off + C * es + 4 * nh + pr
     if name == "msl_dwconv3d_bwd_weight":  # read dy, x
         return 2 * C * es
     return 2 * C * es  # read x, write y
@@ -310,14 +313,16 @@ def run_gpu(args):
     dom = max(per, key=lambda n: per[n][0])
     dom_ms = per[dom][0] / per[dom][1]
     hbm_peak, tc_peak, peak_kind = _peaks()
-    alg_bytes = _alg_bytes_per_token(dom, C, nh, K, es) * B * N
+    tc_path = dt == torch.bfloat16 and d % 8 == 0 and 16 <= d <= 128  # tensor-core kernels, probs saved
+    n_local = x.shape[1]  # this rank's tokens per sample (the kernels' launch size)
+    alg_bytes = _alg_bytes_per_token(dom, C, nh, K, es, probs=tc_path) * B * n_local
     achieved = alg_bytes / (dom_ms / 1e3) / 1e9
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
         tj = json.loads(tfile.read_text()).get(dom, {}).get(args.config)
         if tj:
-            traffic = float(tj["bytes_per_token"]) * B * N
+            traffic = float(tj["bytes_per_token"]) * B * n_local
     roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
             "traffic": traffic, "kernel": dom, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
             "algorithmic_bytes_per_launch": alg_bytes, "launch_ms": dom_ms}
@@ -325,7 +330,7 @@ def run_gpu(args):
     if fl:
         clk = clocks.get("sm_mhz") or 1965.0
         fp32_peak = 148 * 128 * 2 * clk * 1e6 / 1e12
-        ach = fl * B * N / (dom_ms / 1e3) / 1e12
+        ach = fl * B * n_local / (dom_ms / 1e3) / 1e12
         roof["fp32_cuda_core"] = {"achieved": ach, "peak": fp32_peak, "unit": "TFLOP/s", "frac": ach / fp32_peak,
                                   "peak_source": "nominal 148 SMs x 128 FMA/clk at the sampled median SM clock"}
     kernels = {n: {"ms_per_launch": v[0] / v[1], "launches": v[1], "share": v[0] / sum(t for t, _ in per.values())}

@@ -1,0 +1,413 @@
+"""CPU-master training of MegaSlide-DiT with the transformer blocks streamed through two GPU slots.
+
+Same interface as the reference's CPUMasterVideoDiT (infinity/video/trainer.py:23-650:
+`forward_and_backward(latents, timesteps, target_noise, text_embeds=None, text_mask=None) ->
+(loss, timings)`, `optimizer_step() -> grad norm`, `zero_grad()`, `get_parameters()`, `cleanup()`,
+`save_checkpoint(path)`, `load_checkpoint(path)`), same schedule (no-grad forward through the blocks
+with an activation checkpoint every `checkpoint_interval` blocks; per checkpoint segment in reverse,
+recompute then `autograd.grad` block by block; head and embeddings resident on the GPU), re-built
+around the copies:
+
+* every block's fp32 master weights live in ONE flat pinned host buffer (the CPU block's parameters
+  are views into it), next to a pinned compute-dtype (bf16) staging copy; a block moves to the GPU
+  with a single cudaMemcpyAsync from pinned memory (the reference copies parameter by parameter from
+  pageable memory, fp32);
+* the two GPU slots are flat device buffers; the slot's block module has its parameters viewing the
+  buffer.  Block l+1 is copied on a side stream while block l computes; before overwriting a slot
+  the copy waits for the event the compute stream records when it is done with the slot (the
+  reference records such events but never waits on them);
+* a slot keeps the block it holds: the recompute / backward of a segment reuses a block still
+  resident instead of copying it again;
+* a block's parameter gradients are packed into one flat device buffer and returned with one D2H
+  copy into a pinned slab; a host thread accumulates them into the block's flat fp32 gradient
+  buffer while the GPU works on the next blocks;
+* optimizer_step() computes the global gradient norm (clipping as the reference), then a host
+  thread runs AdamW on each block's flat fp32 buffers and refreshes its bf16 staging copy, block 0
+  first; the next forward copies block i as soon as block i is updated, so the host AdamW overlaps
+  the next step's GPU work.  Head / embedding parameters (GPU-resident) use torch's AdamW on the GPU.
+
+The optimizer state is per block (flat buffers), so optimizer checkpoints are not interchangeable
+with the reference's torch.optim state dict; model state dicts are.
+"""
+
+from __future__ import annotations
+
+import copy
+import math
+import queue
+import threading
+import time
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+
+def _flat_params(module: nn.Module) -> List[nn.Parameter]:
+    return [p for _, p in module.named_parameters()]
+
+
+class _HostAdamW:
+    """AdamW (decoupled weight decay, torch.optim.AdamW's update) on one flat fp32 buffer."""
+
+    def __init__(self, numel: int, lr: float, betas: Tuple[float, float], eps: float, weight_decay: float):
+        self.m = torch.zeros(numel, dtype=torch.float32)
+        self.v = torch.zeros(numel, dtype=torch.float32)
+        self.step = 0
+        self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
+
+    def update(self, p: Tensor, g: Tensor, scale: float) -> None:
+        b1, b2 = self.betas
+        self.step += 1
+        if scale != 1.0:
+            g = g * scale
+        p.mul_(1.0 - self.lr * self.wd)
+        self.m.lerp_(g, 1.0 - b1)
+        self.v.mul_(b2).addcmul_(g, g, value=1.0 - b2)
+        bc1 = 1.0 - b1 ** self.step
+        bc2 = 1.0 - b2 ** self.step
+        denom = (self.v / bc2).sqrt_().add_(self.eps)
+        p.addcdiv_(self.m, denom, value=-self.lr / bc1)
+
+    def state_dict(self):
+        return {"m": self.m, "v": self.v, "step": self.step}
+
+    def load_state_dict(self, d):
+        self.m.copy_(d["m"])
+        self.v.copy_(d["v"])
+        self.step = int(d["step"])
+
+
+class CPUMasterVideoDiT:
+    """CPU-master trainer for a MegaSlideDiT (megaslide_b200.dit or the reference's model built with
+    megaslide_b200.DeformableSlideAttention3D): fp32 master weights and AdamW on the host, blocks
+    streamed through two GPU slots."""
+
+    def __init__(self, model: nn.Module, config, force_cpu: bool = False):
+        self.model = model
+        self.config = config
+        self.force_cpu = force_cpu
+        self.use_cuda = torch.cuda.is_available() and not force_cpu and not getattr(config, "force_cpu", False)
+        if not self.use_cuda:
+            raise RuntimeError("megaslide_b200.CPUMasterVideoDiT streams to a CUDA device (no CPU mode); "
+                               "the reference's CPU-only mode stays the reference's")
+        dev = config.device
+        self.device = torch.device(f"cuda:{dev}" if isinstance(dev, int) or str(dev).isdigit() else dev)
+        self.cdtype = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}[config.dtype]
+        self.step_count = 0
+        self.model.to("cpu").float()
+        self.blocks = self.model.blocks
+        self.num_blocks = len(self.blocks)
+        self._setup_host_buffers()
+        self._setup_gpu()
+        self._worker_q: "queue.Queue" = queue.Queue()
+        self._worker_err: List[BaseException] = []
+        self._worker = threading.Thread(target=self._work_loop, daemon=True)
+        self._worker.start()
+
+    # ------------------------------------------------------------------ set-up
+    def _setup_host_buffers(self):
+        cfg = self.config
+        self.block_numel = [sum(p.numel() for p in _flat_params(b)) for b in self.blocks]
+        self.master: List[Tensor] = []
+        self.stage: List[Tensor] = []
+        self.hgrad: List[Tensor] = []
+        self.opt: List[_HostAdamW] = []
+        self.stage_ready = [threading.Event() for _ in range(self.num_blocks)]
+        for i, b in enumerate(self.blocks):
+            n = self.block_numel[i]
+            flat = torch.empty(n, dtype=torch.float32, pin_memory=True)
+            off = 0
+            for p in _flat_params(b):
+                k = p.numel()
+                flat[off:off + k].copy_(p.data.reshape(-1))
+                p.data = flat[off:off + k].view(p.shape)  # the CPU block now views the master buffer
+                off += k
+            self.master.append(flat)
+            st = torch.empty(n, dtype=self.cdtype, pin_memory=True)
+            st.copy_(flat)
+            self.stage.append(st)
+            self.hgrad.append(torch.zeros(n, dtype=torch.float32))
+            self.opt.append(_HostAdamW(n, cfg.learning_rate, (cfg.beta1, cfg.beta2), cfg.eps, cfg.weight_decay))
+            self.stage_ready[i].set()
+        self.has_grad = [False] * self.num_blocks
+
+    def _setup_gpu(self):
+        cfg = self.config
+        dev = self.device
+        self.compute_stream = torch.cuda.current_stream(dev)
+        self.weight_stream = torch.cuda.Stream(device=dev)
+        self.grad_stream = torch.cuda.Stream(device=dev)
+        nmax = max(self.block_numel)
+        self.slot_buf = [torch.empty(nmax, dtype=self.cdtype, device=dev) for _ in range(2)]
+        self.slot_block = [-1, -1]  # block held by each slot
+        self._last_slot = 1
+        self.slot_ready = [torch.cuda.Event() for _ in range(2)]
+        self.slot_free = [torch.cuda.Event() for _ in range(2)]
+        for e in self.slot_free:
+            e.record(self.compute_stream)
+        self.gpu_blocks = []
+        for s in range(2):
+            gb = copy.deepcopy(self.blocks[0]).to(dev, self.cdtype)
+            off = 0
+            for p in _flat_params(gb):
+                k = p.numel()
+                p.data = self.slot_buf[s][off:off + k].view(p.shape)
+                p.requires_grad_(False)
+                off += k
+            self.gpu_blocks.append(gb)
+        self.gflat = torch.empty(nmax, dtype=self.cdtype, device=dev)
+        self.slabs = [torch.empty(nmax, dtype=self.cdtype, pin_memory=True) for _ in range(max(2, cfg.num_grad_slabs))]
+        self.slab_free: "queue.Queue" = queue.Queue()
+        for i in range(len(self.slabs)):
+            self.slab_free.put(i)
+        self.slab_done = [torch.cuda.Event() for _ in self.slabs]
+        self.gflat_free = torch.cuda.Event()
+        self.gflat_free.record(self.compute_stream)
+        # resident head / tail (fp32 master on the GPU, torch AdamW there)
+        m = self.model
+        self.resident = [m.patch_embed, m.time_embed, m.norm_out, m.out_proj]
+        for mod in self.resident:
+            mod.to(dev)
+        m.pos_embed.data = m.pos_embed.data.to(dev)
+        self.res_params = [p for mod in self.resident for p in mod.parameters()] + [m.pos_embed]
+        self.gpu_opt = torch.optim.AdamW(self.res_params, lr=cfg.learning_rate, betas=(cfg.beta1, cfg.beta2),
+                                         eps=cfg.eps, weight_decay=cfg.weight_decay)
+
+    # ------------------------------------------------------------------ host worker
+    def _work_loop(self):
+        while True:
+            task = self._worker_q.get()
+            if task is None:
+                return
+            try:
+                task()
+            except BaseException as e:  # surfaced by the next synchronising call
+                self._worker_err.append(e)
+
+    def _worker_flush(self):
+        done = threading.Event()
+        self._worker_q.put(done.set)
+        done.wait()
+        if self._worker_err:
+            raise RuntimeError("host worker failed") from self._worker_err[0]
+
+    # ------------------------------------------------------------------ streaming
+    def _load(self, i: int) -> int:
+        """Slot holding block i, copying it in (side stream) if no slot has it; returns the slot."""
+        for s in range(2):
+            if self.slot_block[s] == i:
+                return s
+        s = 0 if self.slot_block[0] == -1 else (1 if self.slot_block[1] == -1 else None)
+        if s is None:  # the slot not used by the block computed last
+            s = 1 if self._last_slot == 0 else 0
+        if not self.stage_ready[i].wait(timeout=600.0):
+            raise RuntimeError(f"block {i}: host optimizer update did not finish")
+        n = self.block_numel[i]
+        with torch.cuda.stream(self.weight_stream):
+            self.weight_stream.wait_event(self.slot_free[s])
+            self.slot_buf[s][:n].copy_(self.stage[i], non_blocking=True)
+            self.slot_ready[s].record(self.weight_stream)
+        self.slot_block[s] = i
+        return s
+
+    def _run(self, i: int, x: Tensor, vshape, text_embeds, text_mask, prefetch: Optional[int] = None):
+        s = self._load(i)
+        self._last_slot = s
+        if prefetch is not None and 0 <= prefetch < self.num_blocks:
+            self._load(prefetch)
+        self.compute_stream.wait_event(self.slot_ready[s])
+        y = self.gpu_blocks[s](x, vshape, text_embeds, text_mask)
+        self.slot_free[s].record(self.compute_stream)
+        return y
+
+    def _return_grads(self, i: int, s: int, grads) -> None:
+        """Packs block i's parameter gradients (slot s) into one buffer and queues one D2H copy and
+        the host accumulation."""
+        n = self.block_numel[i]
+        slab_i = self.slab_free.get(timeout=600.0)
+        self.compute_stream.wait_event(self.gflat_free)
+        off = 0
+        for p, g in zip(_flat_params(self.gpu_blocks[s]), grads):
+            k = p.numel()
+            if g is None:
+                self.gflat[off:off + k].zero_()
+            else:
+                self.gflat[off:off + k].copy_(g.reshape(-1))
+            off += k
+        packed = torch.cuda.Event()
+        packed.record(self.compute_stream)
+        with torch.cuda.stream(self.grad_stream):
+            self.grad_stream.wait_event(packed)
+            self.slabs[slab_i][:n].copy_(self.gflat[:n], non_blocking=True)
+            self.slab_done[slab_i].record(self.grad_stream)
+            self.gflat_free.record(self.grad_stream)
+
+        def accumulate(i=i, slab_i=slab_i, n=n):
+            self.slab_done[slab_i].synchronize()
+            if self.has_grad[i]:
+                self.hgrad[i].add_(self.slabs[slab_i][:n])
+            else:
+                self.hgrad[i].copy_(self.slabs[slab_i][:n])
+                self.has_grad[i] = True
+            self.slab_free.put(slab_i)
+
+        self._worker_q.put(accumulate)
+
+    # ------------------------------------------------------------------ training step
+    def forward_and_backward(self, latents: Tensor, timesteps: Tensor, target_noise: Tensor,
+                             text_embeds: Optional[Tensor] = None,
+                             text_mask: Optional[Tensor] = None) -> Tuple[float, Dict[str, float]]:
+        cfg = self.config
+        dev = self.device
+        m = self.model
+        start, fwd_end, bwd_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        start.record(self.compute_stream)
+        lat = latents.to(dev, non_blocking=True)
+        tgt = target_noise.to(dev, non_blocking=True)
+        ts = timesteps.to(dev, non_blocking=True)
+        te = text_embeds.to(dev, self.cdtype) if text_embeds is not None else None
+        tm = text_mask.to(dev) if text_mask is not None else None
+        self._last_slot = 1
+        # forward: embeddings (resident, recorded for their backward), blocks without autograd
+        with torch.autocast("cuda", dtype=self.cdtype, enabled=self.cdtype != torch.float32):
+            x0, vshape = m.embed(lat, ts)
+        x0 = x0.to(self.cdtype)
+        ckpt: Dict[int, Tensor] = {}
+        x = x0.detach()
+        with torch.no_grad():
+            for i in range(self.num_blocks):
+                if i % cfg.checkpoint_interval == 0:
+                    ckpt[i] = x
+                x = self._run(i, x, vshape, te, tm, prefetch=i + 1)
+        # head and loss (resident parameters, autograd)
+        hidden = x.detach().requires_grad_(True)
+        with torch.autocast("cuda", dtype=self.cdtype, enabled=self.cdtype != torch.float32):
+            pred = m.head(hidden, tuple(lat.shape))
+        loss = nn.functional.mse_loss(pred.float(), tgt.float())
+        fwd_end.record(self.compute_stream)
+        loss.backward()
+        grad_hidden = hidden.grad.detach().to(self.cdtype)
+        # backward through the blocks, one checkpoint segment at a time (last first)
+        nseg = (self.num_blocks + cfg.checkpoint_interval - 1) // cfg.checkpoint_interval
+        for seg in range(nseg - 1, -1, -1):
+            b0 = seg * cfg.checkpoint_interval
+            b1 = min(b0 + cfg.checkpoint_interval, self.num_blocks)
+            inputs = {b0: ckpt[b0]}
+            with torch.no_grad():
+                h = ckpt[b0]
+                for j in range(b0, b1 - 1):
+                    h = self._run(j, h, vshape, te, tm, prefetch=j + 1)
+                    inputs[j + 1] = h
+            for i in range(b1 - 1, b0 - 1, -1):
+                s = self._load(i)
+                self._last_slot = s
+                # prefetch the block needed next: the previous one of this segment, or the first
+                # block of the previous segment (its recompute comes next)
+                nxt = i - 1 if i > b0 else (b0 - cfg.checkpoint_interval if seg > 0 else None)
+                if nxt is not None:
+                    self._load(nxt)
+                self.compute_stream.wait_event(self.slot_ready[s])
+                gb = self.gpu_blocks[s]
+                params = _flat_params(gb)
+                for p in params:
+                    p.requires_grad_(True)
+                inp = inputs[i].detach().requires_grad_(True)
+                out = gb(inp, vshape, te, tm)
+                grads = torch.autograd.grad(out, (inp, *params), grad_outputs=grad_hidden, allow_unused=True)
+                for p in params:
+                    p.requires_grad_(False)
+                grad_hidden = grads[0].detach()
+                self._return_grads(i, s, grads[1:])
+                self.slot_free[s].record(self.compute_stream)
+                del out, inp
+        # embeddings
+        x0.backward(grad_hidden.to(x0.dtype))
+        bwd_end.record(self.compute_stream)
+        bwd_end.synchronize()
+        self._worker_flush()
+        loss_val = float(loss.item())
+        return loss_val, {"forward": start.elapsed_time(fwd_end) / 1e3,
+                          "backward": fwd_end.elapsed_time(bwd_end) / 1e3,
+                          "total": start.elapsed_time(bwd_end) / 1e3}
+
+    def optimizer_step(self) -> float:
+        """Clips by the global gradient norm (as the reference) and applies AdamW: resident
+        parameters on the GPU now, block masters on the host in the background (block 0 first; the
+        next forward copies a block as soon as it is updated).  Returns the norm before clipping."""
+        self._worker_flush()
+        cfg = self.config
+        sq = torch.zeros((), dtype=torch.float64)
+        for i in range(self.num_blocks):
+            if self.has_grad[i]:
+                sq += self.hgrad[i].double().square().sum()
+        res_grads = [p.grad for p in self.res_params if p.grad is not None]
+        if res_grads:
+            sq += sum(g.double().square().sum() for g in res_grads).cpu()
+        norm = math.sqrt(float(sq))
+        scale = 1.0
+        if cfg.max_grad_norm > 0 and norm > cfg.max_grad_norm:
+            scale = cfg.max_grad_norm / (norm + 1e-6)
+        if res_grads:
+            if scale != 1.0:
+                for g in res_grads:
+                    g.mul_(scale)
+            self.gpu_opt.step()
+        for i in range(self.num_blocks):
+            if not self.has_grad[i]:
+                continue
+            self.stage_ready[i].clear()
+
+            def upd(i=i):
+                try:
+                    self.opt[i].update(self.master[i], self.hgrad[i], scale)
+                    self.stage[i].copy_(self.master[i])
+                finally:
+                    self.stage_ready[i].set()
+
+            self._worker_q.put(upd)
+        # the slots hold pre-update weights: force fresh copies
+        self.slot_block = [-1, -1]
+        self.step_count += 1
+        if cfg.log_interval and self.step_count % cfg.log_interval == 0:
+            print(f"  [Step {self.step_count}] Gradient norm: {norm:.4f}")
+        return norm
+
+    def zero_grad(self):
+        self._worker_flush()
+        for i in range(self.num_blocks):
+            self.has_grad[i] = False
+        self.gpu_opt.zero_grad(set_to_none=True)
+
+    def get_parameters(self):
+        self._worker_flush()
+        return list(self.model.parameters())
+
+    def cleanup(self):
+        if self._worker.is_alive():
+            self._worker_q.put(None)
+            self._worker.join(timeout=30.0)
+
+    def save_checkpoint(self, path: str):
+        self._worker_flush()
+        torch.save({"model": self.model.state_dict(), "optimizer": {"blocks": [o.state_dict() for o in self.opt],
+                                                                    "resident": self.gpu_opt.state_dict()},
+                    "step": self.step_count, "config": self.config}, path)
+
+    def load_checkpoint(self, path: str):
+        ck = torch.load(path, map_location="cpu", weights_only=False)
+        missing = [k for k in ("model", "optimizer", "step", "config") if k not in ck]
+        if missing:
+            raise ValueError(f"Invalid checkpoint: missing keys {missing}")
+        for name in ("hidden_size", "num_layers", "num_heads", "in_channels"):
+            if getattr(ck["config"], name) != getattr(self.config, name):
+                raise ValueError(f"Checkpoint config mismatch: {name}")
+        self._worker_flush()
+        self.model.load_state_dict(ck["model"])  # copies into the master views / resident params
+        for i in range(self.num_blocks):
+            self.stage[i].copy_(self.master[i])
+            self.opt[i].load_state_dict(ck["optimizer"]["blocks"][i])
+        self.gpu_opt.load_state_dict(ck["optimizer"]["resident"])
+        self.slot_block = [-1, -1]
+        self.step_count = int(ck["step"])

@@ -46,12 +46,21 @@ CPU_SAMPLE = {"c1": dict(B=1, T=8, H=16, W=16), "c2": dict(B=1, T=8, H=16, W=16)
               "c2_prof": dict(B=1, T=8, H=16, W=16)}
 
 
+# DiT step time with CPU-master streaming (the reference's MegaSlideDiT architecture:
+# additive timestep embedding, no adaLN).  Not the default workload: python bench.py --config c3
+DIT_CONFIGS = {
+    "c3": dict(frames=32, in_channels=4, height=64, width=64, patch_size=2, hidden_size=1152, num_heads=16,
+               num_layers=28, mlp_ratio=4.0, dsa_kernel_size=(3, 7, 7), learning_rate=1e-4, dtype="bfloat16",
+               checkpoint_interval=4, num_grad_slabs=4, log_interval=0),
+}
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS) + sorted(DIT_CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -389,8 +398,92 @@ def run_gpu(args):
     return 0
 
 
+def run_dit(args):
+    """DiT step time (fwd + bwd + AdamW) of the streaming CPU-master trainer on one GPU."""
+    import torch
+
+    import megaslide_b200 as msl
+    from megaslide_b200.dit import MegaSlideDiT, VideoDiTConfig
+    from megaslide_b200.stream import CPUMasterVideoDiT
+
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("--config c3 runs on one GPU (the CPU-master trainer is single-device)")
+    cfg = VideoDiTConfig(**DIT_CONFIGS[args.config], device=0)
+    torch.manual_seed(1234)
+    model = MegaSlideDiT(cfg)
+    with torch.no_grad():  # learned offsets of the size the op benchmark uses (config 2)
+        for b in model.blocks:
+            b.attn.offset_net[2].weight.normal_(0, 0.05)
+    trainer = CPUMasterVideoDiT(model, cfg)
+    g = torch.Generator().manual_seed(4321)
+    shape = (1, cfg.in_channels, cfg.frames, cfg.height, cfg.width)
+    lat = torch.randn(shape, generator=g).pin_memory()
+    noise = torch.randn(shape, generator=g).pin_memory()
+    ts = torch.randint(0, 1000, (1,), generator=g)
+
+    phases = {"fwd_bwd_wall_s": 0.0, "gpu_fwd_s": 0.0, "gpu_bwd_s": 0.0, "optimizer_call_s": 0.0}
+
+    def step(record=False):
+        trainer.zero_grad()
+        t0 = time.perf_counter()
+        loss, tm = trainer.forward_and_backward(lat, ts, noise)
+        t1 = time.perf_counter()
+        trainer.optimizer_step()
+        t2 = time.perf_counter()
+        if record:
+            phases["fwd_bwd_wall_s"] += t1 - t0
+            phases["gpu_fwd_s"] += tm["forward"]
+            phases["gpu_bwd_s"] += tm["backward"]
+            phases["optimizer_call_s"] += t2 - t1
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    trainer.get_parameters()  # host optimizer drained
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.3)
+    n0, h0, d0 = msl.launch_count(), trainer.h2d_bytes, trainer.d2h_bytes
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        loss = step(record=True)
+    t_drain = time.perf_counter()
+    trainer.get_parameters()  # the last step's host AdamW is part of the step
+    phases["final_drain_s"] = time.perf_counter() - t_drain
+    torch.cuda.synchronize()
+    sec = (time.perf_counter() - t0) / args.steps
+    clocks = sampler.stop()
+    launches = msl.launch_count() - n0
+    h2d = (trainer.h2d_bytes - h0) / args.steps
+    d2h = (trainer.d2h_bytes - d0) / args.steps
+    tokens = cfg.num_patches
+    trainer.cleanup()
+    line = {
+        "metric": "DiT step time (fwd+bwd+AdamW, CPU-master streaming)", "value": sec, "unit": "s/step",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded latents / noise; random init)",
+        "config": {"workload": f"{args.config}: MegaSlideDiT {cfg.num_layers} blocks, hidden {cfg.hidden_size}, "
+                               f"{cfg.num_heads} heads, MLP x{cfg.mlp_ratio}, latent {cfg.in_channels}x{cfg.frames}x"
+                               f"{cfg.height}x{cfg.width}, patch {cfg.patch_size} ({tokens} tokens), window "
+                               f"{tuple(cfg.dsa_kernel_size)}, checkpoint every {cfg.checkpoint_interval} blocks",
+                   "tokens_per_step": tokens, "parallelism": "single GPU, blocks streamed through 2 slots",
+                   "timing": "wall clock per step including the host AdamW (synchronised at both ends)"},
+        "e2e": {"value": sec, "unit": "s/step", "h2d_bytes_per_step": int(h2d + 2 * lat.numel() * 4 + 8),
+                "d2h_bytes_per_step": int(d2h + 4)},
+        "stream": {"weight_h2d_gbs": h2d / sec / 1e9, "grad_d2h_gbs": d2h / sec / 1e9,
+                   "weight_bytes_per_step": h2d, "grad_bytes_per_step": d2h, "loss": loss},
+        "phases_per_step": {k: v / (1 if k == "final_drain_s" else args.steps) for k, v in phases.items()},
+        "clocks": clocks, "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.config in DIT_CONFIGS:
+        return run_dit(args)
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_gpu(args)

@@ -223,6 +223,26 @@ uint64_t msl_launch_count(void);
 /* Description of the last error returned on the calling thread ("" if none). */
 const char* msl_last_error(void);
 
+/* ----------------------------------------------------------------------------------------------
+ * Host-side optimizer kernels of the CPU-master trainer (megaslide_b200/stream.py).  Plain host
+ * memory, multi-threaded (OpenMP), no GPU involvement.  They replace torch.optim.AdamW and the
+ * per-parameter gradient accumulation of the reference's CPUMasterVideoDiT
+ * (infinity/video/trainer.py:66-72, 176-221, 575-599).
+ * ---------------------------------------------------------------------------------------------- */
+
+/* dst[i] = (overwrite ? 0 : dst[i]) + src[i] for n float32 dst elements; src is float32 or bf16
+ * (src_dtype MSL_DTYPE_*).  *sumsq (optional) receives sum(dst^2) in double precision. */
+int msl_host_accumulate(float* dst, const void* src, int32_t src_dtype, int64_t n, int32_t overwrite,
+                        double* sumsq);
+
+/* One AdamW step (torch.optim.AdamW's update: decoupled weight decay, bias-corrected moments) over n
+ * float32 elements: g is scaled by grad_scale (gradient clipping) first; step = the step number
+ * after this update (>= 1).  stage (optional, MSL_DTYPE_F32 or MSL_DTYPE_BF16) receives the updated
+ * parameters in the compute dtype (bf16 rounded to nearest even) in the same pass. */
+int msl_host_adamw(float* p, float* m, float* v, const float* g, int64_t n, float lr, float beta1, float beta2,
+                   float eps, float weight_decay, int64_t step, float grad_scale, void* stage,
+                   int32_t stage_dtype);
+
 #ifdef __cplusplus
 }
 #endif

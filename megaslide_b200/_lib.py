@@ -97,6 +97,8 @@ SIGNATURES = {
                                                _vp, _vp]),
     "msl_offsets_absmax": (ctypes.c_int, [_vp, _i64, _i64, _i32, _i32, _f32, _vp, _vp]),
     "msl_convert_f32": (ctypes.c_int, [_vp, _i64, _vp, _i64, _i32, _i64, _i64, _vp]),
+    "msl_host_accumulate": (ctypes.c_int, [_vp, _vp, _i32, _i64, _i32, ctypes.POINTER(ctypes.c_double)]),
+    "msl_host_adamw": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _f32, _i64, _f32, _vp, _i32]),
     "msl_abi_version": (_i32, []),
     "msl_launch_count": (_u64, []),
     "msl_last_error": (ctypes.c_char_p, []),

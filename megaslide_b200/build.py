@@ -28,7 +28,7 @@ NVCC_FLAGS = [
     "-std=c++17",
     "-lineinfo",
     "-Xcompiler",
-    "-fPIC,-O3",
+    "-fPIC,-O3,-fopenmp",
     "--expt-relaxed-constexpr",
     "-Xptxas",
     "-warn-spills",
@@ -69,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         subprocess.run(cmd, check=True)
     out = lib_path()
     if force or not out.exists() or out.stat().st_mtime < max(o.stat().st_mtime for o in objs):
-        cmd = [nvcc, *ARCH_FLAGS, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(out)]
+        cmd = [nvcc, *ARCH_FLAGS, "-shared", "-Xcompiler", "-fPIC,-fopenmp", *map(str, objs), "-o", str(out), "-lgomp"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

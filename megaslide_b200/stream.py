@@ -33,6 +33,7 @@ with the reference's torch.optim state dict; model state dicts are.
 from __future__ import annotations
 
 import copy
+import ctypes
 import math
 import queue
 import threading
@@ -43,13 +44,16 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
+from . import _lib
+
 
 def _flat_params(module: nn.Module) -> List[nn.Parameter]:
     return [p for _, p in module.named_parameters()]
 
 
 class _HostAdamW:
-    """AdamW (decoupled weight decay, torch.optim.AdamW's update) on one flat fp32 buffer."""
+    """AdamW state of one flat float32 buffer; the update is msl_host_adamw (one multi-threaded pass
+    over parameters, moments and gradient that also writes the compute-dtype staging copy)."""
 
     def __init__(self, numel: int, lr: float, betas: Tuple[float, float], eps: float, weight_decay: float):
         self.m = torch.zeros(numel, dtype=torch.float32)
@@ -57,18 +61,17 @@ class _HostAdamW:
         self.step = 0
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
 
-    def update(self, p: Tensor, g: Tensor, scale: float) -> None:
-        b1, b2 = self.betas
+    def update(self, p: Tensor, g: Tensor, scale: float, stage: Optional[Tensor] = None) -> None:
+        for t in (p, g, self.m, self.v):
+            if t.dtype != torch.float32 or not t.is_contiguous() or t.device.type != "cpu":
+                raise TypeError("host AdamW buffers must be contiguous float32 host tensors")
+        sdt = 0
+        if stage is not None:
+            sdt = {torch.float32: _lib.MSL_DTYPE_F32, torch.bfloat16: _lib.MSL_DTYPE_BF16}[stage.dtype]
         self.step += 1
-        if scale != 1.0:
-            g = g * scale
-        p.mul_(1.0 - self.lr * self.wd)
-        self.m.lerp_(g, 1.0 - b1)
-        self.v.mul_(b2).addcmul_(g, g, value=1.0 - b2)
-        bc1 = 1.0 - b1 ** self.step
-        bc2 = 1.0 - b2 ** self.step
-        denom = (self.v / bc2).sqrt_().add_(self.eps)
-        p.addcdiv_(self.m, denom, value=-self.lr / bc1)
+        _lib.check("msl_host_adamw", _lib.load().msl_host_adamw(
+            p.data_ptr(), self.m.data_ptr(), self.v.data_ptr(), g.data_ptr(), p.numel(), self.lr, self.betas[0],
+            self.betas[1], self.eps, self.wd, self.step, scale, stage.data_ptr() if stage is not None else None, sdt))
 
     def state_dict(self):
         return {"m": self.m, "v": self.v, "step": self.step}
@@ -77,6 +80,15 @@ class _HostAdamW:
         self.m.copy_(d["m"])
         self.v.copy_(d["v"])
         self.step = int(d["step"])
+
+
+def _accumulate(dst: Tensor, src: Tensor, overwrite: bool) -> float:
+    """dst (float32) = [dst +] src (float32 or bf16) on the host; returns sum(dst^2)."""
+    sq = ctypes.c_double(0.0)
+    code = {torch.float32: _lib.MSL_DTYPE_F32, torch.bfloat16: _lib.MSL_DTYPE_BF16}[src.dtype]
+    _lib.check("msl_host_accumulate", _lib.load().msl_host_accumulate(
+        dst.data_ptr(), src.data_ptr(), code, dst.numel(), 1 if overwrite else 0, ctypes.byref(sq)))
+    return float(sq.value)
 
 
 class CPUMasterVideoDiT:
@@ -96,6 +108,8 @@ class CPUMasterVideoDiT:
         self.device = torch.device(f"cuda:{dev}" if isinstance(dev, int) or str(dev).isdigit() else dev)
         self.cdtype = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}[config.dtype]
         self.step_count = 0
+        self.h2d_bytes = 0  # block weights copied to the GPU (counters for measurement)
+        self.d2h_bytes = 0  # block gradients copied back
         self.model.to("cpu").float()
         self.blocks = self.model.blocks
         self.num_blocks = len(self.blocks)
@@ -132,6 +146,7 @@ class CPUMasterVideoDiT:
             self.opt.append(_HostAdamW(n, cfg.learning_rate, (cfg.beta1, cfg.beta2), cfg.eps, cfg.weight_decay))
             self.stage_ready[i].set()
         self.has_grad = [False] * self.num_blocks
+        self.sumsq = [0.0] * self.num_blocks  # sum of squares of each block's gradient
 
     def _setup_gpu(self):
         cfg = self.config
@@ -210,6 +225,7 @@ class CPUMasterVideoDiT:
             self.slot_buf[s][:n].copy_(self.stage[i], non_blocking=True)
             self.slot_ready[s].record(self.weight_stream)
         self.slot_block[s] = i
+        self.h2d_bytes += n * self.stage[i].element_size()
         return s
 
     def _run(self, i: int, x: Tensor, vshape, text_embeds, text_mask, prefetch: Optional[int] = None):
@@ -238,6 +254,7 @@ class CPUMasterVideoDiT:
             off += k
         packed = torch.cuda.Event()
         packed.record(self.compute_stream)
+        self.d2h_bytes += n * self.gflat.element_size()
         with torch.cuda.stream(self.grad_stream):
             self.grad_stream.wait_event(packed)
             self.slabs[slab_i][:n].copy_(self.gflat[:n], non_blocking=True)
@@ -246,11 +263,8 @@ class CPUMasterVideoDiT:
 
         def accumulate(i=i, slab_i=slab_i, n=n):
             self.slab_done[slab_i].synchronize()
-            if self.has_grad[i]:
-                self.hgrad[i].add_(self.slabs[slab_i][:n])
-            else:
-                self.hgrad[i].copy_(self.slabs[slab_i][:n])
-                self.has_grad[i] = True
+            self.sumsq[i] = _accumulate(self.hgrad[i], self.slabs[slab_i][:n], overwrite=not self.has_grad[i])
+            self.has_grad[i] = True
             self.slab_free.put(slab_i)
 
         self._worker_q.put(accumulate)
@@ -338,14 +352,11 @@ class CPUMasterVideoDiT:
         next forward copies a block as soon as it is updated).  Returns the norm before clipping."""
         self._worker_flush()
         cfg = self.config
-        sq = torch.zeros((), dtype=torch.float64)
-        for i in range(self.num_blocks):
-            if self.has_grad[i]:
-                sq += self.hgrad[i].double().square().sum()
+        sq = sum(self.sumsq[i] for i in range(self.num_blocks) if self.has_grad[i])
         res_grads = [p.grad for p in self.res_params if p.grad is not None]
         if res_grads:
-            sq += sum(g.double().square().sum() for g in res_grads).cpu()
-        norm = math.sqrt(float(sq))
+            sq += float(torch.stack([g.float().square().sum() for g in res_grads]).sum())
+        norm = math.sqrt(sq)
         scale = 1.0
         if cfg.max_grad_norm > 0 and norm > cfg.max_grad_norm:
             scale = cfg.max_grad_norm / (norm + 1e-6)
@@ -361,8 +372,7 @@ class CPUMasterVideoDiT:
 
             def upd(i=i):
                 try:
-                    self.opt[i].update(self.master[i], self.hgrad[i], scale)
-                    self.stage[i].copy_(self.master[i])
+                    self.opt[i].update(self.master[i], self.hgrad[i], scale, stage=self.stage[i])
                 finally:
                     self.stage_ready[i].set()
 

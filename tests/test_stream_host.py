@@ -15,19 +15,39 @@ REF = Path("/root/reference")
 
 
 def test_host_adamw_matches_torch_adamw():
+    """msl_host_adamw (native, one pass) against torch.optim.AdamW, with clipping scale and the bf16
+    staging copy written in the same pass."""
     torch.manual_seed(0)
-    p0 = torch.randn(1000)
+    n = 100_003
+    p0 = torch.randn(n)
     p_ref = torch.nn.Parameter(p0.clone())
     opt = torch.optim.AdamW([p_ref], lr=1e-3, betas=(0.9, 0.99), eps=1e-8, weight_decay=0.05)
     p = p0.clone()
-    host = _HostAdamW(1000, 1e-3, (0.9, 0.99), 1e-8, 0.05)
+    stage = torch.empty(n, dtype=torch.bfloat16)
+    host = _HostAdamW(n, 1e-3, (0.9, 0.99), 1e-8, 0.05)
     for step in range(5):
-        g = torch.randn(1000)
+        g = torch.randn(n)
         scale = 0.5 if step == 2 else 1.0
         p_ref.grad = g * scale
         opt.step()
-        host.update(p, g.clone(), scale)
-        assert torch.allclose(p, p_ref.detach(), rtol=1e-6, atol=1e-7), step
+        host.update(p, g.clone(), scale, stage=stage)
+        assert torch.allclose(p, p_ref.detach(), rtol=1e-5, atol=1e-7), step
+        assert torch.equal(stage, p.to(torch.bfloat16)), step
+
+
+def test_host_accumulate_and_sum_of_squares():
+    from megaslide_b200.stream import _accumulate
+
+    torch.manual_seed(1)
+    a = torch.randn(50_001).to(torch.bfloat16)
+    b = torch.randn(50_001)
+    dst = torch.full((50_001,), 7.0)
+    sq = _accumulate(dst, a, overwrite=True)
+    assert torch.equal(dst, a.float())
+    assert abs(sq - float(a.double().square().sum())) <= 1e-9 * sq
+    sq = _accumulate(dst, b, overwrite=False)
+    assert torch.allclose(dst, a.float() + b)
+    assert abs(sq - float(dst.double().square().sum())) <= 1e-9 * sq
 
 
 def test_config_validation():

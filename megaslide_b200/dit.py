@@ -50,6 +50,7 @@ class VideoDiTConfig:
     device: Union[int, str] = 0
     force_cpu: bool = False
     log_interval: int = 10
+    resident_blocks: Optional[bool] = None  # CPU-master trainer: None = decide from device memory
 
     @property
     def num_patches(self) -> int:

@@ -26,6 +26,12 @@ around the copies:
   first; the next forward copies block i as soon as block i is updated, so the host AdamW overlaps
   the next step's GPU work.  Head / embedding parameters (GPU-resident) use torch's AdamW on the GPU.
 
+Resident mode (chosen when every block's bf16 weights and autograd activations fit in 60% of the
+free HBM -- config 3 on a 180 GB B200 -- or forced with config.resident_blocks): each block keeps its
+own device weight buffer, refreshed by one H2D copy after its host update, and the step is one
+forward with autograd plus one backward (no recompute).  The streaming mode above is the one for
+models whose weights do not fit.
+
 The optimizer state is per block (flat buffers), so optimizer checkpoints are not interchangeable
 with the reference's torch.optim state dict; model state dicts are.
 """
@@ -115,6 +121,7 @@ class CPUMasterVideoDiT:
         self.num_blocks = len(self.blocks)
         self._setup_host_buffers()
         self._setup_gpu()
+        self.resident: Optional[bool] = None  # decided at the first step (needs the token count)
         self._worker_q: "queue.Queue" = queue.Queue()
         self._worker_err: List[BaseException] = []
         self._worker = threading.Thread(target=self._work_loop, daemon=True)
@@ -190,6 +197,80 @@ class CPUMasterVideoDiT:
         self.gpu_opt = torch.optim.AdamW(self.res_params, lr=cfg.learning_rate, betas=(cfg.beta1, cfg.beta2),
                                          eps=cfg.eps, weight_decay=cfg.weight_decay)
 
+    # ------------------------------------------------------------------ resident mode
+    def _decide_resident(self, tokens: int) -> bool:
+        """Resident mode when every block's compute-dtype weights and autograd activations fit in 60%
+        of the free device memory (B200: 180 GB); the estimate per block and token is the hidden state
+        in ~24 copies (projections, norms, MLP) plus the attention's float32 offsets and softmax weights.
+        config.resident_blocks (True / False) overrides."""
+        forced = getattr(self.config, "resident_blocks", None)
+        if forced is not None:
+            return bool(forced)
+        cfg = self.config
+        es = torch.tensor([], dtype=self.cdtype).element_size()
+        K = cfg.dsa_kernel_size[0] * cfg.dsa_kernel_size[1] * cfg.dsa_kernel_size[2]
+        weights = sum(self.block_numel) * es
+        acts = tokens * (cfg.hidden_size * es * 24 + cfg.num_heads * K * 16) * self.num_blocks
+        free, _ = torch.cuda.mem_get_info(self.device)
+        return weights + acts <= 0.6 * free
+
+    def _setup_resident(self):
+        dev = self.device
+        self.res_buf = [torch.empty(n, dtype=self.cdtype, device=dev) for n in self.block_numel]
+        self.res_blocks = []
+        for i, b in enumerate(self.blocks):
+            gb = copy.deepcopy(b).to(dev, self.cdtype)
+            off = 0
+            for p in _flat_params(gb):
+                k = p.numel()
+                p.data = self.res_buf[i][off:off + k].view(p.shape)
+                p.requires_grad_(False)
+                off += k
+            self.res_blocks.append(gb)
+        self.res_dirty = [True] * self.num_blocks
+        self.res_ready = [torch.cuda.Event() for _ in range(self.num_blocks)]
+
+    def _upload(self, i: int) -> None:
+        """Copies block i's updated staging weights to its resident buffer (side stream)."""
+        if not self.res_dirty[i]:
+            return
+        if not self.stage_ready[i].wait(timeout=600.0):
+            raise RuntimeError(f"block {i}: host optimizer update did not finish")
+        with torch.cuda.stream(self.weight_stream):
+            self.res_buf[i].copy_(self.stage[i], non_blocking=True)
+            self.res_ready[i].record(self.weight_stream)
+        self.res_dirty[i] = False
+        self.h2d_bytes += self.block_numel[i] * self.stage[i].element_size()
+
+    def _blocks_resident(self, x: Tensor, vshape, te, tm, head_fn) -> Tuple[Tensor, Tensor, Tensor]:
+        """One forward with autograd through all blocks (graphs kept), the head, then one backward
+        block by block; returns (loss, gradient w.r.t. the block input, the fwd-end event)."""
+        saved = []
+        for i in range(self.num_blocks):
+            self._upload(i)
+            if i + 1 < self.num_blocks:
+                self._upload(i + 1)
+            self.compute_stream.wait_event(self.res_ready[i])
+            blk = self.res_blocks[i]
+            for p in _flat_params(blk):
+                p.requires_grad_(True)
+            inp = x.detach().requires_grad_(True)
+            out = blk(inp, vshape, te, tm)
+            saved.append((inp, out))
+            x = out.detach()
+        loss, grad_hidden, fwd_end = head_fn(x)
+        for i in range(self.num_blocks - 1, -1, -1):
+            inp, out = saved[i]
+            params = _flat_params(self.res_blocks[i])
+            grads = torch.autograd.grad(out, (inp, *params), grad_outputs=grad_hidden, allow_unused=True)
+            for p in params:
+                p.requires_grad_(False)
+            grad_hidden = grads[0].detach()
+            self._return_grads(i, params, grads[1:])
+            saved[i] = None
+            del inp, out
+        return loss, grad_hidden, fwd_end
+
     # ------------------------------------------------------------------ host worker
     def _work_loop(self):
         while True:
@@ -238,14 +319,14 @@ class CPUMasterVideoDiT:
         self.slot_free[s].record(self.compute_stream)
         return y
 
-    def _return_grads(self, i: int, s: int, grads) -> None:
-        """Packs block i's parameter gradients (slot s) into one buffer and queues one D2H copy and
-        the host accumulation."""
+    def _return_grads(self, i: int, params, grads) -> None:
+        """Packs block i's parameter gradients into one buffer and queues one D2H copy and the host
+        accumulation."""
         n = self.block_numel[i]
         slab_i = self.slab_free.get(timeout=600.0)
         self.compute_stream.wait_event(self.gflat_free)
         off = 0
-        for p, g in zip(_flat_params(self.gpu_blocks[s]), grads):
+        for p, g in zip(params, grads):
             k = p.numel()
             if g is None:
                 self.gflat[off:off + k].zero_()
@@ -288,6 +369,29 @@ class CPUMasterVideoDiT:
         with torch.autocast("cuda", dtype=self.cdtype, enabled=self.cdtype != torch.float32):
             x0, vshape = m.embed(lat, ts)
         x0 = x0.to(self.cdtype)
+        if self.resident is None:
+            self.resident = self._decide_resident(x0.shape[0] * x0.shape[1])
+            if self.resident:
+                self._setup_resident()
+        if self.resident:
+
+            def head_fn(xb):
+                hidden = xb.detach().requires_grad_(True)
+                with torch.autocast("cuda", dtype=self.cdtype, enabled=self.cdtype != torch.float32):
+                    pred = m.head(hidden, tuple(lat.shape))
+                loss_ = nn.functional.mse_loss(pred.float(), tgt.float())
+                fwd_end.record(self.compute_stream)
+                loss_.backward()
+                return loss_, hidden.grad.detach().to(self.cdtype), fwd_end
+
+            loss, grad_hidden, _ = self._blocks_resident(x0.detach(), vshape, te, tm, head_fn)
+            x0.backward(grad_hidden.to(x0.dtype))
+            bwd_end.record(self.compute_stream)
+            bwd_end.synchronize()
+            self._worker_flush()
+            return float(loss.item()), {"forward": start.elapsed_time(fwd_end) / 1e3,
+                                        "backward": fwd_end.elapsed_time(bwd_end) / 1e3,
+                                        "total": start.elapsed_time(bwd_end) / 1e3}
         ckpt: Dict[int, Tensor] = {}
         x = x0.detach()
         with torch.no_grad():
@@ -333,7 +437,7 @@ class CPUMasterVideoDiT:
                 for p in params:
                     p.requires_grad_(False)
                 grad_hidden = grads[0].detach()
-                self._return_grads(i, s, grads[1:])
+                self._return_grads(i, params, grads[1:])
                 self.slot_free[s].record(self.compute_stream)
                 del out, inp
         # embeddings
@@ -377,8 +481,10 @@ class CPUMasterVideoDiT:
                     self.stage_ready[i].set()
 
             self._worker_q.put(upd)
-        # the slots hold pre-update weights: force fresh copies
+        # the slots / resident buffers hold pre-update weights: force fresh copies
         self.slot_block = [-1, -1]
+        if self.resident:
+            self.res_dirty = [True] * self.num_blocks
         self.step_count += 1
         if cfg.log_interval and self.step_count % cfg.log_interval == 0:
             print(f"  [Step {self.step_count}] Gradient norm: {norm:.4f}")
@@ -420,4 +526,6 @@ class CPUMasterVideoDiT:
             self.opt[i].load_state_dict(ck["optimizer"]["blocks"][i])
         self.gpu_opt.load_state_dict(ck["optimizer"]["resident"])
         self.slot_block = [-1, -1]
+        if self.resident:
+            self.res_dirty = [True] * self.num_blocks
         self.step_count = int(ck["step"])

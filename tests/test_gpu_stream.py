@@ -1,5 +1,5 @@
 """CPU-master streaming trainer on the GPU: two training steps of CPUMasterVideoDiT (blocks streamed
-through two slots, host AdamW) against the same model trained in place on the GPU with plain
+through two slots or resident, host AdamW) against the same model trained in place on the GPU with plain
 autograd, gradient clipping and torch.optim.AdamW.  float32 end to end, so losses, gradient norms
 and updated parameters agree to rounding."""
 
@@ -29,10 +29,12 @@ def _batch(cfg, seed):
     return lat, ts, noise
 
 
+@pytest.mark.parametrize("resident", [False, True], ids=["streamed", "resident"])
 @pytest.mark.parametrize("dtype,tol", [("float32", 1e-4), ("bfloat16", 3e-2)])
-def test_streamed_steps_match_in_place_training(dtype, tol):
+def test_streamed_steps_match_in_place_training(dtype, tol, resident):
     torch.manual_seed(3)
     cfg = _cfg(dtype)
+    cfg.resident_blocks = resident
     model = MegaSlideDiT(cfg)
     with torch.no_grad():  # non-zero offsets so the attention gradients reach every parameter
         for b in model.blocks:

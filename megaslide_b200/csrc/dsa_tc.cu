@@ -1,26 +1,27 @@
 // Tensor-core ("key envelope") formulation of the deformable gather attention forward, bf16.
 //
-// One CTA owns a tile of 8 x 8 queries of one frame, one head and one sample (64 queries, 16 warps:
-// four per 16-query row group; 8 lanes per query share its per-sample work).
-// Every trilinear corner any of the tile's 64 x K samples can touch lies in the tile's key
-// envelope: frames [zlo, zhi] x rows [ylo, yhi] x columns [xlo, xhi].  The CTA walks that
-// envelope one frame ("plane") at a time, in chunks of at most `maxkeys` keys (rows and columns
-// split with a one-row / one-column overlap so that the four corners a sample has in a plane
-// always fall in one chunk):
+// One CTA owns a tile of 4 x 8 queries of one frame, one head and one sample (32 queries = two
+// 16-query row groups; 16 warps, 8 per group; 16 lanes per query for the per-query work).
+// Every trilinear corner any of the tile's samples can touch lies in the tile's key envelope:
+// frames [zlo, zhi] x rows [ylo, yhi] x columns [xlo, xhi].  The CTA walks it one frame ("plane")
+// at a time, in chunks of at most `maxkeys` keys (rows and columns split with one row / column of
+// overlap so that the four corners a sample has in a plane always fall in one chunk):
 //
-//   pass 1, per chunk:  S = Q . K_chunk^T on the tensor cores (mma.sync m16n8k16 bf16 -> fp32,
-//                       one 16-query row group per warp pair), kept in shared memory; every sample
-//                       with corners in the chunk adds  sum_corners w_c * S[q, corner]  to its score.
+//   pass 1, per chunk:  S = Q . K_chunk^T on the tensor cores (mma.sync bf16 -> fp32) over the
+//                       16-key tiles any corner touches; every sample with corners in the chunk adds
+//                       sum_corners w_c * S[q, corner] to its score.
 //   softmax:            per query over its K samples (+ G extra keys, scored the same way).
-//   pass 2, per chunk:  every sample scatters p * w_c into a dense P~[q, key] (shared memory), then
-//                       O += P~ . V_chunk on the tensor cores (ldmatrix.trans for V).
+//   pass 2, per chunk:  every sample scatters p * w_c into a dense P~[q, key] (32-bit fixed point,
+//                       per-query scale), converted once to bf16 [key][query]; O += P~ . V_chunk on
+//                       the tensor cores (ldmatrix.trans for both operands).
 //
-// The dense products are redundant (the envelope holds more keys than the samples' corners), but
-// they run on the tensor cores and replace 8 * d scalar FMAs and 8 gathered d-vectors per sample
-// by 8 shared-memory reads of scalars.  Sample coordinates come from the offsets with the same float32
-// arithmetic as the CUDA-core kernels (msl_common.cuh), so corner choices are identical; each sample's
-// corner and trilinear fractions are computed once per tile and kept as a packed 8-byte record
-// (fractions quantised to 12 bits: interpolation weights within 1.2e-4 - this path is bf16 only).
+// The setup sorts the tile's active samples into one list by frame (counting sort), so the samples
+// with a corner in a plane are one contiguous range that all 512 threads stride through, and records
+// per (plane, chunk) which 16-key tiles any corner touches: loads, products and the conversion visit
+// only those.  Sample coordinates come from the offsets with the same float32 arithmetic as the
+// CUDA-core kernels (msl_common.cuh), so corner choices are identical; each sample's corner and
+// trilinear fractions are kept as a packed 8-byte record (fractions quantised to 12 bits:
+// interpolation weights within 1.2e-4 - this path is bf16 only).
 // Reference semantics: infinity/video/attention.py:113-186 (grid, grid_sample, softmax, dropout,
 // value sum) and :159-173 (extra keys).
 
@@ -28,20 +29,23 @@
 
 namespace msl {
 namespace tc {
+namespace fwd {
 
-constexpr int kWPG = kWarps / 4;      // warps per 16-query row group
-constexpr int kLPQ = kWPG * 32 / 16;  // lanes per query for the per-sample work
-constexpr int kTileH = 8, kQ = kTileH * kTileW;
+using namespace t32;
 
-// Shared-memory layout, sized by the host (TcLaunch).
 struct Smem {
-  __nv_bfloat16* kbuf;  // [maxkeys][rs]
-  float* sbuf;          // [4][16][sld]
-  float* sacc;          // [64][K + G]
-  unsigned long long* rec;  // [64][K] packed sample records (see pack_rec)
-  int* env;             // [16] envelope, then base-grid tables (float) from env + 16
-  float* mrow;          // [64]
-  float* lrow;          // [64]
+  __nv_bfloat16* kbuf;      // [maxkeys][rs]   K or V chunk (setup: staged offsets, spilling into sbuf)
+  float* sbuf;              // [32][sld]       S (fp32), then P~ (int32), then P~^T (bf16 [key][40])
+  __nv_bfloat16* qs;        // [32][rs]        Q rows of the tile
+  unsigned long long* rec;  // [32][K]         packed sample records
+  float* sacc;              // [32][K + G]     scores, then unnormalised dropout-applied weights
+  int* env;                 // envelope + base-grid tables
+  float* lrow;              // [32]            softmax sums
+  float* qsc;               // [2][32]         P~ fixed-point scale / inverse per query
+  int* bstart;              // [36]            hit list: first entry of each frame bucket (+ end)
+  int* bcur;                // [32]            bucket counts, then fill cursors
+  uint32_t* mask;           // [32][4]         16-key tiles touched per (plane, chunk)
+  unsigned short* hits;     // [32 * K]        sample indices q * K + j sorted by frame bucket
 };
 
 __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, const TcLaunch& L) {
@@ -50,17 +54,51 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   s.kbuf = reinterpret_cast<__nv_bfloat16*>(base + off);
   off += static_cast<size_t>(L.maxkeys) * L.rs * 2;
   s.sbuf = reinterpret_cast<float*>(base + off);
-  off += static_cast<size_t>(4) * 16 * L.sld * 4;
+  off += static_cast<size_t>(kQ) * L.sld * 4;
+  s.qs = reinterpret_cast<__nv_bfloat16*>(base + off);
+  off += static_cast<size_t>(kQ) * L.rs * 2;
   s.rec = reinterpret_cast<unsigned long long*>(base + off);
   off += static_cast<size_t>(kQ) * P.K * 8;
   s.sacc = reinterpret_cast<float*>(base + off);
   off += static_cast<size_t>(kQ) * (P.K + P.G) * 4;
   s.env = reinterpret_cast<int*>(base + off);
   off += kEnvWords * 4;
-  s.mrow = reinterpret_cast<float*>(base + off);
-  off += kQ * 4;
   s.lrow = reinterpret_cast<float*>(base + off);
+  off += kQ * 4;
+  s.qsc = reinterpret_cast<float*>(base + off);
+  off += 2 * kQ * 4;
+  s.bstart = reinterpret_cast<int*>(base + off);
+  off += 36 * 4;
+  s.bcur = reinterpret_cast<int*>(base + off);
+  off += 32 * 4;
+  s.mask = reinterpret_cast<uint32_t*>(base + off);
+  off += 32 * kMaxMaskChunks * 4;
+  s.hits = reinterpret_cast<unsigned short*>(base + off);
   return s;
+}
+
+// shared memory besides the key buffer and the dense tile
+size_t smem_fixed(const AttnParams& P, int rs) {
+  return static_cast<size_t>(kQ) * rs * 2 + static_cast<size_t>(kQ) * P.K * (8 + 2) +
+         static_cast<size_t>(kQ) * (P.K + P.G) * 4 + kEnvWords * 4 + kQ * 4 * 3 + (36 + 32 + 32 * kMaxMaskChunks) * 4 +
+         256;
+}
+
+// loads G extra keys / values of this head into kbuf rows 0..G-1 (zero up to gp)
+template <int DCH>
+__device__ __forceinline__ void load_extra(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
+                                           const void* src, int gp) {
+  const __nv_bfloat16* eb = static_cast<const __nv_bfloat16*>(src) + static_cast<long long>(T.b) * P.G * P.e_ld +
+                            T.head * P.d;
+  for (int idx = threadIdx.x; idx < gp * DCH; idx += kThreads) {
+    const int key = idx / DCH, ch = idx - (idx / DCH) * DCH;
+    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs + ch * 8;
+    if (key < P.G)
+      cp_async16(smem_u32(dst), eb + static_cast<long long>(key) * P.e_ld + ch * 8);
+    else
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  cp_async_wait_all();
 }
 
 template <int DCH>
@@ -70,23 +108,22 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   const TileCtx T = decode_tile(P, L, kTileH);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = warp / kWPG, part = warp - (warp / kWPG) * kWPG;
-  const int ll = part * 32 + lane;           // 0..127 within the row group
-  const int cq = ll / kLPQ, sub = ll - (ll / kLPQ) * kLPQ;  // owned query (0..15) and lane of that query
+  const int ll = part * 32 + lane;
+  const int cq = ll / kLPQ, sub = ll - (ll / kLPQ) * kLPQ;
   const int K = P.K, KG = P.K + P.G;
-  // the kLPQ lanes of a query own contiguous window ranges, so a lane's samples touch few frames and
-  // whole lanes skip the frames they cannot reach
+  // setup: the lanes of a query own contiguous window ranges [js, je)
   const int jper = (K + kLPQ - 1) / kLPQ;
   const int js = min(K, sub * jper), je = min(K, js + jper);
-  const SampleGeom sg{P.T, P.H, P.W, P.kt, P.kh, P.kw, P.oscale};
+  const int n = je - js;
+  const int qi = r * 16 + cq;
+  const float invK = 1.f / static_cast<float>(K);
 
   int qh, qw;
   query_hw(T, r, cq, qh, qw);
   const bool qvalid = qh < P.H && qw < P.W;
   const long long qrow = (static_cast<long long>(T.tl) * P.H + qh) * P.W + qw;
-  const float* orow = P.offsets + (static_cast<long long>(T.b) * P.Nq + qrow) * P.off_ld +
-                      static_cast<long long>(T.head) * K * 3;
-  float* sacc = S.sacc + static_cast<size_t>(r * 16 + cq) * KG;
-  unsigned long long* rec = S.rec + static_cast<size_t>(r * 16 + cq) * K;
+  const int qbase = qi * K;  // this query's records
+  float* sacc = S.sacc + static_cast<size_t>(qi) * KG;
 
   float* tabz = reinterpret_cast<float*>(S.env + 16);
   float* taby = tabz + 96;
@@ -95,48 +132,48 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     S.env[0] = 0x7fffffff; S.env[1] = -0x7fffffff; S.env[2] = 0x7fffffff;
     S.env[3] = -0x7fffffff; S.env[4] = 0x7fffffff; S.env[5] = -0x7fffffff;
   }
+  if (threadIdx.x < 32) S.bcur[threadIdx.x] = 0;
+  if (threadIdx.x < 32 * kMaxMaskChunks) S.mask[threadIdx.x] = 0u;
   fill_tabs(P, T, kTileH, tabz, taby, tabx);
+
+  // ---- stage the tile's offsets (this head) and Q rows with one wave of cp.async
+  const int K3 = 3 * K;
+  float* ostage = reinterpret_cast<float*>(S.kbuf);
+  for (int q2 = warp; q2 < kQ; q2 += kWarps) {
+    int sqh, sqw;
+    query_hw(T, q2 >> 4, q2 & 15, sqh, sqw);
+    const bool ok = sqh < P.H && sqw < P.W;
+    const long long grow = static_cast<long long>(T.b) * P.Nq + (static_cast<long long>(T.tl) * P.H + sqh) * P.W + sqw;
+    if (ok) {
+      const float* src = P.offsets + grow * P.off_ld + static_cast<long long>(T.head) * K3;
+      float* dst = ostage + static_cast<size_t>(q2) * K3;
+      for (int k = lane; k < K3; k += 32) cp_async4(smem_u32(dst + k), src + k);
+    }
+    for (int ch = lane; ch < DCH; ch += 32) {
+      __nv_bfloat16* dq_ = S.qs + static_cast<size_t>(q2) * L.rs + ch * 8;
+      if (ok)
+        cp_async16(smem_u32(dq_), static_cast<const __nv_bfloat16*>(P.q) + grow * P.q_ld + T.head * P.d + ch * 8);
+      else
+        *reinterpret_cast<uint4*>(dq_) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  cp_async_wait_all();
   __syncthreads();
   const Tabs tb{tabz, taby, tabx};
   const int qy = qh - T.qh0, qx = qw - T.qw0;
 
-  // ---- setup: sample coordinates.  This head's offsets of the tile are staged in the key / score
-  // buffers (unused until pass 1) with one wave of cp.async per round of 32 queries (row groups 0-1,
-  // then 2-3), so the coordinate pass reads shared memory instead of a dependent global round trip
-  // per sample.  Raw coordinates are kept in rec / sacc until the envelope is known.
-  const int K3 = 3 * K;
-  float* ostage = reinterpret_cast<float*>(S.kbuf);
+  // ---- sample coordinates -> envelope (raw coordinates parked in rec / sacc)
   const int kvlo = max(P.kv_frame0, 0), kvhi = min(P.kv_frame0 + P.kv_frames, P.T) - 1;
   int zmn = 0x7fffffff, zmx = -0x7fffffff, ymn = 0x7fffffff, ymx = -0x7fffffff, xmn = 0x7fffffff, xmx = -0x7fffffff;
   bool miss = false;
-  for (int round = 0; round < 2; ++round) {
-    __syncthreads();
-    for (int qi = round * 32 + warp; qi < round * 32 + 32; qi += kWarps) {
-      int sqh, sqw;
-      query_hw(T, qi >> 4, qi & 15, sqh, sqw);
-      if (sqh >= P.H || sqw >= P.W) continue;
-      const float* src = P.offsets +
-                         (static_cast<long long>(T.b) * P.Nq + (static_cast<long long>(T.tl) * P.H + sqh) * P.W + sqw) * P.off_ld +
-                         static_cast<long long>(T.head) * K3;
-      float* dst = ostage + static_cast<size_t>(qi - round * 32) * K3;
-      for (int k = lane; k < K3; k += 32) cp_async4(smem_u32(dst + k), src + k);
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    if ((r >> 1) != round) continue;
-    const float* oq = ostage + static_cast<size_t>(r * 16 + cq - round * 32) * K3;
+  if (qvalid) {
+    const float* oq = ostage + static_cast<size_t>(qi) * K3;
     WinIdx wi;
     wi.init(js, P.kh, P.kw);
-#pragma unroll 2
     for (int j = js; j < je; ++j, wi.advance(1, P.kh, P.kw)) {
-      if (!qvalid) {
-        rec[j] = 0ull;
-        sacc[j] = 0.f;
-        continue;
-      }
       float pt, ph, pw;
       tab_coords(P, tb, qy, qx, wi.it, wi.ih, wi.iw, oq[3 * j], oq[3 * j + 1], oq[3 * j + 2], pt, ph, pw);
-      rec[j] = (static_cast<unsigned long long>(__float_as_uint(ph)) << 32) | __float_as_uint(pt);
+      S.rec[qbase + j] = (static_cast<unsigned long long>(__float_as_uint(ph)) << 32) | __float_as_uint(pt);
       sacc[j] = pw;
       const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
       for (int dt = 0; dt < 2; ++dt) {
@@ -155,7 +192,6 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
       xmx = max(xmx, w0 + 1 < P.W ? w0 + 1 : w0);
     }
   }
-  for (int j = K + sub; j < KG; j += kLPQ) sacc[j] = 0.f;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     zmn = min(zmn, __shfl_xor_sync(kFull, zmn, o));
@@ -186,106 +222,116 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   }
   const bool split = E.ny * E.nx > 1;
   // records hold t0 - zlo + 1 in 5 bits and h0 - ylo, w0 - xlo in 8 bits
-  const bool chunk_overflow = any && (E.zhi - E.zlo + 2 > 31 || E.yhi - E.ylo > 255 || E.xhi - E.xlo > 255);
-  if (chunk_overflow && threadIdx.x == 0 && P.status) atomicOr(P.status, MSL_STATUS_TC_RANGE);
+  const bool overflow = any && (E.zhi - E.zlo + 2 > 31 || E.yhi - E.ylo > 255 || E.xhi - E.xlo > 255);
+  if (overflow && threadIdx.x == 0 && P.status) atomicOr(P.status, MSL_STATUS_TC_RANGE);
+  const bool work = any && !overflow;
+  const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
 
-  // pack the per-sample records now that the envelope is known; the lane's frame range [zl_lo, zl_hi]
-  // (relative, as zrel) bounds the frames its samples touch
-  int zl_lo = 0x7fff, zl_hi = -1;
-  for (int j = js; j < je; ++j) {
-    if (!qvalid) continue;
-    const unsigned long long raw = rec[j];
-    const float pt = __uint_as_float(static_cast<uint32_t>(raw)), ph = __uint_as_float(static_cast<uint32_t>(raw >> 32));
-    const float pw = sacc[j];
-    sacc[j] = 0.f;
-    const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
-    if (!any || chunk_overflow || t0 + 1 < E.zlo || t0 > E.zhi) {  // no corner in a frame the K/V buffers hold
-      rec[j] = 0ull;
-      continue;
+  // ---- records, frame-bucket counts and touched-tile masks; scores start at 0
+  for (int s = 0; s < jper; ++s) {  // same trip count in every lane: warp collectives inside
+    const int j = js + s;
+    int dz = -1, pa = -1, pb = -1;
+    uint32_t bits = 0u;
+    if (qvalid && s < n) {
+      const unsigned long long raw = S.rec[qbase + j];
+      const float pt = __uint_as_float(static_cast<uint32_t>(raw)), ph = __uint_as_float(static_cast<uint32_t>(raw >> 32));
+      const float pw = sacc[j];
+      sacc[j] = 0.f;
+      const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
+      unsigned long long v = 0ull;
+      if (work && t0 + 1 >= E.zlo && t0 <= E.zhi) {  // a corner in a frame the K/V buffers hold
+        dz = t0 - E.zlo + 1;
+        v = pack_rec(pt - static_cast<float>(t0), ph - static_cast<float>(h0), pw - static_cast<float>(w0), dz,
+                     h0 - E.ylo, w0 - E.xlo);
+        if (masks) {
+          const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
+          const int ya = E.ylo + iy * (E.R - 1), xa = E.xlo + ix * (E.cw - 1);
+          const int ncw = min(xa + E.cw - 1, E.xhi) - xa + 1;
+          bits = corner_tiles((h0 - ya) * ncw + (w0 - xa), ncw, w0 + 1 < P.W, h0 + 1 < P.H);
+          const int chk = iy * E.nx + ix;
+          if (t0 >= E.zlo) pa = dz * kMaxMaskChunks + chk;
+          if (t0 + 1 <= E.zhi) pb = (dz + 1) * kMaxMaskChunks + chk;
+        }
+      }
+      S.rec[qbase + j] = v;
     }
-    rec[j] = pack_rec(pt - static_cast<float>(t0), ph - static_cast<float>(h0), pw - static_cast<float>(w0),
-                      t0 - E.zlo + 1, h0 - E.ylo, w0 - E.xlo);
-    zl_lo = min(zl_lo, t0 - E.zlo + 1);
-    zl_hi = max(zl_hi, t0 - E.zlo + 2);
+    const unsigned peers = __match_any_sync(kFull, dz);
+    if (dz >= 0 && lane == __ffs(peers) - 1) atomicAdd(S.bcur + dz, __popc(peers));
+    if (pa >= 0 && (S.mask[pa] & bits) != bits) atomicOr(S.mask + pa, bits);
+    if (pb >= 0 && (S.mask[pb] & bits) != bits) atomicOr(S.mask + pb, bits);
   }
-
-  // ---- Q fragments (rows g and g + 8 of the group)
-  const int g = lane >> 2, t4 = lane & 3;
-  uint32_t qa[DCH / 2 > 0 ? DCH / 2 : 1][4];
-  uint32_t qt[2] = {0u, 0u};
-  {
-    int qh0_, qw0_, qh1_, qw1_;
-    query_hw(T, r, g, qh0_, qw0_);
-    query_hw(T, r, g + 8, qh1_, qw1_);
-    const bool v0 = qh0_ < P.H && qw0_ < P.W, v1 = qh1_ < P.H && qw1_ < P.W;
-    const __nv_bfloat16* q0 = static_cast<const __nv_bfloat16*>(P.q) +
-        (static_cast<long long>(T.b) * P.Nq + (static_cast<long long>(T.tl) * P.H + qh0_) * P.W + qw0_) * P.q_ld + T.head * P.d;
-    const __nv_bfloat16* q1 = static_cast<const __nv_bfloat16*>(P.q) +
-        (static_cast<long long>(T.b) * P.Nq + (static_cast<long long>(T.tl) * P.H + qh1_) * P.W + qw1_) * P.q_ld + T.head * P.d;
+  if (qvalid)
+    for (int e = K + sub; e < KG; e += kLPQ) sacc[e] = 0.f;
+  __syncthreads();
+  if (warp == 0) {  // bucket starts (exclusive scan of 32 counts); the counts become fill cursors
+    const int c = S.bcur[lane];
+    int incl = c;
 #pragma unroll
-    for (int ks = 0; ks < DCH / 2; ++ks) {
-      qa[ks][0] = v0 ? __ldg(reinterpret_cast<const unsigned int*>(q0 + ks * 16 + 2 * t4)) : 0u;
-      qa[ks][1] = v1 ? __ldg(reinterpret_cast<const unsigned int*>(q1 + ks * 16 + 2 * t4)) : 0u;
-      qa[ks][2] = v0 ? __ldg(reinterpret_cast<const unsigned int*>(q0 + ks * 16 + 8 + 2 * t4)) : 0u;
-      qa[ks][3] = v1 ? __ldg(reinterpret_cast<const unsigned int*>(q1 + ks * 16 + 8 + 2 * t4)) : 0u;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += t;
     }
-    if constexpr (DCH & 1) {
-      qt[0] = v0 ? __ldg(reinterpret_cast<const unsigned int*>(q0 + (DCH - 1) * 8 + 2 * t4)) : 0u;
-      qt[1] = v1 ? __ldg(reinterpret_cast<const unsigned int*>(q1 + (DCH - 1) * 8 + 2 * t4)) : 0u;
-    }
+    S.bstart[lane + 1] = incl;
+    if (lane == 0) S.bstart[0] = 0;
+    S.bcur[lane] = incl - c;
   }
-  const float* srow_q = S.sbuf + (static_cast<size_t>(r) * 16 + cq) * L.sld;  // scores of the owned query
+  __syncthreads();
+  for (int s = 0; s < jper; ++s) {  // hit list: every active sample once, grouped by frame bucket
+    const int j = js + s;
+    int dz = -1;
+    if (qvalid && s < n) {
+      const unsigned long long v = S.rec[qbase + j];
+      if (v >> 63) dz = static_cast<int>((v >> 36) & 0x1fu);
+    }
+    const unsigned peers = __match_any_sync(kFull, dz);
+    const int leader = __ffs(peers) - 1;
+    int pos = 0;
+    if (dz >= 0 && lane == leader) pos = atomicAdd(S.bcur + dz, __popc(peers));
+    pos = __shfl_sync(kFull, pos, leader) + __popc(peers & ((1u << lane) - 1u));
+    if (dz >= 0) S.hits[pos] = static_cast<unsigned short>(qbase + j);
+  }
+  const int g = lane >> 2, t4 = lane & 3;
+  float* grow_s = S.sbuf + static_cast<size_t>(r) * 16 * L.sld;  // the row group's 16 dense rows
+  const __nv_bfloat16* qgrp = S.qs + static_cast<size_t>(r) * 16 * L.rs;
+  __syncthreads();
 
-  // ---- pass 1: scores
-  if (any && !chunk_overflow) {
+  // ---- pass 1: scores (hits CTA-wide)
+  if (work) {
     for (int z = E.zlo; z <= E.zhi; ++z) {
       const int zrel = z - E.zlo + 1;
+      const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
       for (int iy = 0; iy < E.ny; ++iy) {
         const int ya = E.ylo + iy * (E.R - 1), yb = min(ya + E.R - 1, E.yhi);
         for (int ix = 0; ix < E.nx; ++ix) {
           const int xa = E.xlo + ix * (E.cw - 1), xb = min(xa + E.cw - 1, E.xhi);
           const int ncw = xb - xa + 1;
-          const int nkp = ((yb - ya + 1) * ncw + 15) & ~15;
+          const int ntile = (((yb - ya + 1) * ncw + 15) >> 4);
+          const uint32_t m = masks ? S.mask[zrel * kMaxMaskChunks + iy * E.nx + ix]
+                                   : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
+          if (m == 0u) continue;
           __syncthreads();
-          load_chunk<DCH>(P, T, S.kbuf, L.rs, static_cast<const __nv_bfloat16*>(P.k), P.k_ld, z, ya, yb, xa, xb, nkp);
+          load_keys<DCH>(P, T, S.kbuf, L.rs, nullptr, static_cast<const __nv_bfloat16*>(P.k), P.k_ld, z, ya, yb, xa, xb,
+                         m);
           __syncthreads();
-          dense_scores<DCH, kWPG>(S.kbuf, L.rs, S.sbuf + static_cast<size_t>(r) * 16 * L.sld, L.sld, part, nkp, qa, qt);
+          dense_tiles<DCH, kWPG>(S.kbuf, qgrp, L.rs, grow_s, L.sld, part, m);
           __syncthreads();
-          if (!qvalid || zrel < zl_lo || zrel > zl_hi) continue;
-          for (int j0 = js; j0 < je; j0 += 4) {
-            unsigned long long vv[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) vv[u] = (j0 + u < je) ? rec[j0 + u] : 0ull;
-            bool hit[4];
-            bool anyhit = false;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              hit[u] = (vv[u] >> 63) && static_cast<unsigned>(zrel - static_cast<int>((vv[u] >> 36) & 0x1fu)) <= 1u;
-              anyhit |= hit[u];
-            }
-            if (!anyhit) continue;
-            float acc[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const Rec c = unpack_rec(vv[u], E);
-              if (split && hit[u])
-                hit[u] = axis_chunk_of(c.h0, E.ylo, E.R, E.ny) == iy && axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) == ix;
-              const float az = hit[u] ? frac_weight(c.ft, z != c.t0) : 0.f;
-              const float ay0 = c.h0 < P.H ? 1.f - c.fh : 0.f, ay1 = c.h0 + 1 < P.H ? c.fh : 0.f;
-              const float ax0 = c.w0 < P.W ? 1.f - c.fw : 0.f, ax1 = c.w0 + 1 < P.W ? c.fw : 0.f;
-              // clamp the corner indices into the chunk so masked-out corners read a valid address
-              const int k00 = hit[u] ? (c.h0 - ya) * ncw + (c.w0 - xa) : 0;
-              const int k01 = (hit[u] && ax1 != 0.f) ? k00 + 1 : k00;
-              const int k10 = (hit[u] && ay1 != 0.f) ? k00 + ncw : k00;
-              const int k11 = (hit[u] && ax1 != 0.f && ay1 != 0.f) ? k00 + ncw + 1 : k00;
-              float a = (ax0 * ay0) * az * srow_q[k00];
-              a = fmaf((ax1 * ay0) * az, srow_q[k01], a);
-              a = fmaf((ax0 * ay1) * az, srow_q[k10], a);
-              acc[u] = fmaf((ax1 * ay1) * az, srow_q[k11], a);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              if (hit[u]) sacc[j0 + u] += acc[u];
+          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+            const int idx = S.hits[i];
+            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+            const Rec c = decode_rec(S.rec[idx], E);
+            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
+              continue;
+            const float* row = S.sbuf + static_cast<size_t>(q) * L.sld;
+            const int k00 = (c.h0 - ya) * ncw + (c.w0 - xa);
+            const bool xok = c.w0 + 1 < P.W, yok = c.h0 + 1 < P.H;
+            const float v00 = row[k00];
+            const float v01 = xok ? row[k00 + 1] : 0.f;
+            const float v10 = yok ? row[k00 + ncw] : 0.f;
+            const float v11 = (xok && yok) ? row[k00 + ncw + 1] : 0.f;
+            const float ax0 = 1.f - c.fw, ax1 = c.fw;
+            const float bil = (1.f - c.fh) * fmaf(ax1, v01, ax0 * v00) + c.fh * fmaf(ax1, v11, ax0 * v10);
+            float* sp = S.sacc + static_cast<size_t>(q) * KG + (idx - q * K);
+            *sp = fmaf(frac_weight(c.ft, z != c.t0), bil, *sp);
           }
         }
       }
@@ -293,28 +339,20 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   }
 
   // ---- extra keys: S_extra = Q . EK^T (all G keys in one chunk of the key buffer)
+  const int gp = (P.G + 15) & ~15;
+  const uint32_t gmask = gp >= 512 ? 0xffffffffu : (1u << (gp >> 4)) - 1u;
   if (P.G > 0) {
-    const int gp = (P.G + 15) & ~15;
     __syncthreads();
-    {
-      const __nv_bfloat16* eb = static_cast<const __nv_bfloat16*>(P.ek) + static_cast<long long>(T.b) * P.G * P.e_ld + T.head * P.d;
-      for (int idx = threadIdx.x; idx < gp * DCH; idx += kThreads) {
-        const int key = idx / DCH, ch = idx - (idx / DCH) * DCH;
-        __nv_bfloat16* dst = S.kbuf + static_cast<size_t>(key) * L.rs + ch * 8;
-        if (key < P.G)
-          cp_async16(smem_u32(dst), eb + static_cast<long long>(key) * P.e_ld + ch * 8);
-        else
-          *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-      }
-      cp_async_wait_all();
-    }
+    load_extra<DCH>(P, T, S.kbuf, L.rs, P.ek, gp);
     __syncthreads();
-    dense_scores<DCH, kWPG>(S.kbuf, L.rs, S.sbuf + static_cast<size_t>(r) * 16 * L.sld, L.sld, part, gp, qa, qt);
+    dense_tiles<DCH, kWPG>(S.kbuf, qgrp, L.rs, grow_s, L.sld, part, gmask);
     __syncthreads();
-    for (int e = sub; e < P.G; e += kLPQ) sacc[K + e] = srow_q[e];
+    if (qvalid)
+      for (int e = sub; e < P.G; e += kLPQ) sacc[K + e] = S.sbuf[static_cast<size_t>(qi) * L.sld + e];
   }
+  __syncthreads();
 
-  // ---- softmax over the K (+G) scores of each query (4 lanes per query)
+  // ---- softmax over the K (+G) scores of each query; optional saved probabilities; P~ row scales
   float m = -INFINITY;
   if (qvalid)
     for (int j = sub; j < KG; j += kLPQ) m = fmaxf(m, sacc[j] * P.scale_log2);
@@ -325,120 +363,92 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     for (int j = sub; j < KG; j += kLPQ) l += exp2f(sacc[j] * P.scale_log2 - m);
 #pragma unroll
   for (int o = 1; o < kLPQ; o <<= 1) l += __shfl_xor_sync(kFull, l, o);
+  float bp = 0.f;
   if (qvalid) {
-    // optional per-sample softmax weights (normalised, before dropout) for the tensor-core backward
     float* prob_row = P.probs ? P.probs + ((static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow) * K : nullptr;
     const float inv_l = 1.f / l;
+    const uint64_t qg = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
     for (int j = sub; j < KG; j += kLPQ) {
       const float p = exp2f(sacc[j] * P.scale_log2 - m);
       if (prob_row && j < K) prob_row[j] = p * inv_l;
       float pv = p;
-      if (P.drop_thresh) {
-        const uint64_t q = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
-        const uint64_t idx = (q * P.nh + T.head) * static_cast<uint64_t>(KG) + j;
-        pv = dropout_keep(P.seed, idx, P.drop_thresh) ? p * P.drop_keep_scale : 0.f;
-      }
+      if (P.drop_thresh)
+        pv = dropout_keep(P.seed, (qg * P.nh + T.head) * static_cast<uint64_t>(KG) + j, P.drop_thresh)
+                 ? p * P.drop_keep_scale : 0.f;
       sacc[j] = pv;  // unnormalised, dropout applied
+      bp += pv;
     }
   }
+#pragma unroll
+  for (int o = 1; o < kLPQ; o <<= 1) bp += __shfl_xor_sync(kFull, bp, o);
   if (sub == 0) {
-    S.mrow[r * 16 + cq] = m;
-    S.lrow[r * 16 + cq] = l;
+    S.lrow[qi] = l;
+    S.qsc[qi] = bp > 0.f ? kFixRange / bp : 1.f;
+    S.qsc[kQ + qi] = bp > 0.f ? bp / kFixRange : 0.f;
     if (qvalid) P.lse[(static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow] = m + log2f(l);
   }
+  __syncthreads();
 
-  // ---- pass 2: O = P~ . V
-  constexpr int NT = DCH;  // n8 tiles of the head dimension, split over the group's warps
-  constexpr int kTPW = (NT + kWPG - 1) / kWPG;
-  const int nt0 = min(NT, part * kTPW), nt1 = min(NT, nt0 + kTPW);
-  float o[kTPW + 1][4];  // o[j] accumulates d tile nt0 + j
+  // ---- pass 2: O = P~ . V (hits CTA-wide)
+  constexpr int kTPW = (DCH + kWPG - 1) / kWPG;  // channel tiles per warp
+  const int nt0 = min(DCH, part * kTPW), nt1 = min(DCH, nt0 + kTPW);
+  float o[kTPW + 1][4];
 #pragma unroll
   for (int i = 0; i < kTPW + 1; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float* prow = S.sbuf + static_cast<size_t>(r) * 16 * L.sld;
-  float* prow_q = S.sbuf + (static_cast<size_t>(r) * 16 + cq) * L.sld;
-  if (any && !chunk_overflow) {
+  const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(S.sbuf);  // P~^T after the transposition
+  if (work) {
     for (int z = E.zlo; z <= E.zhi; ++z) {
       const int zrel = z - E.zlo + 1;
+      const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
       for (int iy = 0; iy < E.ny; ++iy) {
         const int ya = E.ylo + iy * (E.R - 1), yb = min(ya + E.R - 1, E.yhi);
         for (int ix = 0; ix < E.nx; ++ix) {
           const int xa = E.xlo + ix * (E.cw - 1), xb = min(xa + E.cw - 1, E.xhi);
           const int ncw = xb - xa + 1;
-          const int nkp = ((yb - ya + 1) * ncw + 15) & ~15;
+          const int ntile = (((yb - ya + 1) * ncw + 15) >> 4);
+          const uint32_t mk = masks ? S.mask[zrel * kMaxMaskChunks + iy * E.nx + ix]
+                                    : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
+          if (mk == 0u) continue;
           __syncthreads();
-          load_chunk<DCH>(P, T, S.kbuf, L.rs, static_cast<const __nv_bfloat16*>(P.v), P.v_ld, z, ya, yb, xa, xb, nkp);
-          // zero P~ of the row group (16 rows x nkp), the group's warps split the rows
-          for (int rrow = part * (16 / kWPG); rrow < (part + 1) * (16 / kWPG); ++rrow)
-            for (int col = lane * 4; col < nkp; col += 128)
-              *reinterpret_cast<float4*>(prow + static_cast<size_t>(rrow) * L.sld + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+          load_keys<DCH>(P, T, S.kbuf, L.rs, nullptr, static_cast<const __nv_bfloat16*>(P.v), P.v_ld, z, ya, yb, xa,
+                         xb, mk);
+          zero_tiles<kQ>(S.sbuf, L.sld, mk);
           __syncthreads();
-          if (qvalid && zrel >= zl_lo && zrel <= zl_hi) {
-            unsigned int* prow_u = reinterpret_cast<unsigned int*>(prow_q);
-            for (int j0 = js; j0 < je; j0 += 4) {
-              unsigned long long vv[4];
-#pragma unroll
-              for (int u = 0; u < 4; ++u) vv[u] = (j0 + u < je) ? rec[j0 + u] : 0ull;
-              bool hit[4];
-              bool anyhit = false;
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                hit[u] = (vv[u] >> 63) && static_cast<unsigned>(zrel - static_cast<int>((vv[u] >> 36) & 0x1fu)) <= 1u;
-                anyhit |= hit[u];
-              }
-              if (!anyhit) continue;
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                if (!hit[u]) continue;
-                const Rec c = unpack_rec(vv[u], E);
-                if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-                  continue;
-                const float pv = sacc[j0 + u] * kPtScale;
-                if (pv == 0.f) continue;
-                const float az = frac_weight(c.ft, z != c.t0);
-                const int k00 = (c.h0 - ya) * ncw + (c.w0 - xa);
-                const float ay0 = 1.f - c.fh, ay1 = c.fh, ax0 = 1.f - c.fw, ax1 = c.fw;
-                atomicAdd(prow_u + k00, __float2uint_rn(pv * ((ax0 * ay0) * az)));
-                if (c.w0 + 1 < P.W) atomicAdd(prow_u + k00 + 1, __float2uint_rn(pv * ((ax1 * ay0) * az)));
-                if (c.h0 + 1 < P.H) {
-                  atomicAdd(prow_u + k00 + ncw, __float2uint_rn(pv * ((ax0 * ay1) * az)));
-                  if (c.w0 + 1 < P.W) atomicAdd(prow_u + k00 + ncw + 1, __float2uint_rn(pv * ((ax1 * ay1) * az)));
-                }
-              }
-            }
+          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+            const int idx = S.hits[i];
+            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+            const float pv = S.sacc[static_cast<size_t>(q) * KG + (idx - q * K)];
+            if (pv == 0.f) continue;
+            const Rec c = decode_rec(S.rec[idx], E);
+            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
+              continue;
+            scatter_fixed_row(reinterpret_cast<int*>(S.sbuf) + static_cast<size_t>(q) * L.sld,
+                              (c.h0 - ya) * ncw + (c.w0 - xa), ncw, c,
+                              pv * frac_weight(c.ft, z != c.t0) * S.qsc[q], P.H, P.W);
           }
           __syncthreads();
-          av_product<DCH, kTPW, true>(prow, L.sld, S.kbuf, L.rs, nt0, nt1, nkp, o);
+          transpose_fixed(S.sbuf, L.sld, mk, S.qsc + kQ);
+          __syncthreads();
+          dq_product<DCH, kTPW>(tp, r, S.kbuf, L.rs, nt0, nt1, mk, o);
         }
       }
     }
   }
-  if (P.G > 0) {
-    const int gp = (P.G + 15) & ~15;
+  if (P.G > 0) {  // extra values: their weights straight into the fixed-point rows
     __syncthreads();
-    {
-      const __nv_bfloat16* eb = static_cast<const __nv_bfloat16*>(P.ev) + static_cast<long long>(T.b) * P.G * P.e_ld + T.head * P.d;
-      for (int idx = threadIdx.x; idx < gp * DCH; idx += kThreads) {
-        const int key = idx / DCH, ch = idx - (idx / DCH) * DCH;
-        __nv_bfloat16* dst = S.kbuf + static_cast<size_t>(key) * L.rs + ch * 8;
-        if (key < P.G)
-          cp_async16(smem_u32(dst), eb + static_cast<long long>(key) * P.e_ld + ch * 8);
-        else
-          *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-      }
-      cp_async_wait_all();
-    }
-    for (int rrow = part * (16 / kWPG); rrow < (part + 1) * (16 / kWPG); ++rrow)
-      for (int col = lane * 4; col < gp; col += 128)
-        *reinterpret_cast<float4*>(prow + static_cast<size_t>(rrow) * L.sld + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+    load_extra<DCH>(P, T, S.kbuf, L.rs, P.ev, gp);
+    zero_tiles<kQ>(S.sbuf, L.sld, gmask);
     __syncthreads();
-    for (int e = sub; e < P.G; e += kLPQ)
-      reinterpret_cast<unsigned int*>(prow_q)[e] = qvalid ? __float2uint_rn(sacc[K + e] * kPtScale) : 0u;
+    if (qvalid)
+      for (int e = sub; e < P.G; e += kLPQ)
+        reinterpret_cast<int*>(S.sbuf)[static_cast<size_t>(qi) * L.sld + e] = fix_round(sacc[K + e] * S.qsc[qi]);
     __syncthreads();
-    av_product<DCH, kTPW, true>(prow, L.sld, S.kbuf, L.rs, nt0, nt1, gp, o);
+    transpose_fixed(S.sbuf, L.sld, gmask, S.qsc + kQ);
+    __syncthreads();
+    dq_product<DCH, kTPW>(tp, r, S.kbuf, L.rs, nt0, nt1, gmask, o);
   }
 
   // ---- normalise and store
-  __syncthreads();  // lrow written by the sample lanes of other warps
   {
     int qh0_, qw0_, qh1_, qw1_;
     query_hw(T, r, g, qh0_, qw0_);
@@ -460,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   }
 }
 
+}  // namespace fwd
 }  // namespace tc
 
 // ------------------------------------------------------------------------------ host side
@@ -467,42 +478,46 @@ bool tc_supported(const AttnParams& P) {
   if (P.dtype != MSL_DTYPE_BF16) return false;
   if (P.d % 8 != 0 || P.d < 16 || P.d > 128) return false;
   if (P.T > 65535 || P.K > 2048 || P.G > 256) return false;
-  if (P.drop_thresh && P.drop_keep_scale > 10.f) return false;  // fixed-point P~ range (dropout p <= 0.9)
+  if (static_cast<long long>(tc::t32::kQ) * P.K > 65536) return false;  // hit-list entries are 16-bit
   // base-grid tables hold at most 96 positions per axis
-  if (P.kt > 96 || P.kh + tc::kTileH - 1 > 96 || P.kw + tc::kTileW - 1 > 96) return false;
+  if (P.kt > 96 || P.kh + tc::t32::kTileH - 1 > 96 || P.kw + tc::kTileW - 1 > 96) return false;
   return true;
 }
 
 bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   const int dch = P.d / 8;
   L.rs = (dch & 1) ? P.d : P.d + 8;  // odd number of 16-byte chunks per row: conflict-free ldmatrix
-  L.tiles_h = (P.H + tc::kTileH - 1) / tc::kTileH;
+  L.tiles_h = (P.H + tc::t32::kTileH - 1) / tc::t32::kTileH;
   L.tiles_w = (P.W + tc::kTileW - 1) / tc::kTileW;
-  const size_t fixed = static_cast<size_t>(tc::kQ) * (P.K + P.G) * 4 + static_cast<size_t>(tc::kQ) * P.K * 8 +
-                       tc::kEnvWords * 4 + 2 * tc::kQ * 4 + 256;
-  const size_t per_key = static_cast<size_t>(L.rs) * 2 + 4 * 16 * 4;
-  if (fixed + per_key * 64 > static_cast<size_t>(smem_limit)) return false;
-  int mk = static_cast<int>((static_cast<size_t>(smem_limit) - fixed - 4 * 16 * 8 * 4) / per_key);
+  const size_t fixed = tc::fwd::smem_fixed(P, L.rs);
+  const size_t per_key = static_cast<size_t>(L.rs) * 2 + static_cast<size_t>(tc::t32::kQ) * 4;
+  const size_t slack = static_cast<size_t>(tc::t32::kQ) * 8 * 4;  // dense-row padding (sld = maxkeys + 8)
+  if (fixed + slack + per_key * 64 > static_cast<size_t>(smem_limit)) return false;
+  int mk = static_cast<int>((static_cast<size_t>(smem_limit) - fixed - slack) / per_key);
   mk &= ~15;
   const int gp = (P.G + 15) & ~15;
-  if (mk < 64 || mk < gp) return false;
-  if (mk > 1024) mk = 1024;
+  if (mk < 64) return false;
+  if (mk > tc::t32::kMaxKeys) mk = tc::t32::kMaxKeys;
+  if (mk < gp) return false;
   L.maxkeys = mk;
-  L.sld = mk + 8;
-  // the setup stages 32 queries x K x 3 offsets in the key + score buffers
-  if (static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(4) * 16 * L.sld * 4 < static_cast<size_t>(32) * P.K * 12)
-    return false;  // row stride = 8 or 24 (mod 32) words: mma fragment rows hit distinct banks
-  L.smem = static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(4) * 16 * L.sld * 4 + fixed;
+  L.sld = mk + 8;  // row stride = 8 or 24 (mod 32) words: mma fragment rows hit distinct banks
+  // a transposed bf16 tile [maxkeys][40] must fit in the dense fp32 tile [32][sld]
+  if (static_cast<size_t>(mk) * tc::t32::kTRow * 2 > static_cast<size_t>(tc::t32::kQ) * L.sld * 4) return false;
+  // the setup stages 32 queries x K x 3 offsets in the key buffer + the dense tile
+  if (static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4 <
+      static_cast<size_t>(tc::t32::kQ) * P.K * 12)
+    return false;
+  L.smem = static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4 + fixed;
   L.tiles = static_cast<long long>(P.B) * P.q_frames * L.tiles_h * L.tiles_w * P.nh;
-  return L.tiles <= 0x7fffffffLL;
+  return L.tiles <= 0x7fffffffLL && L.smem <= static_cast<size_t>(smem_limit);
 }
 
 template <int DCH>
 static cudaError_t launch_fwd_tc_t(const AttnParams& P, const TcLaunch& L, cudaStream_t s) {
-  cudaError_t e = cudaFuncSetAttribute(tc::dsa_fwd_tc_kernel<DCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(tc::fwd::dsa_fwd_tc_kernel<DCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
-  tc::dsa_fwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L);
+  tc::fwd::dsa_fwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L);
   return cudaGetLastError();
 }
 

@@ -331,5 +331,232 @@ __device__ __forceinline__ void av_product(const float* arow, int sld, const __n
   }
 }
 
+// ------------------------------------------------------------------------------ masked chunks
+// ------------------------------------------------------------------------------ scalar helpers
+// float -> nearest int for |v| < 2^22 and back, with one add (no conversion instruction)
+__device__ __forceinline__ int fix_round(float v) { return __float_as_int(v + 12582912.f) - 0x4B400000; }
+__device__ __forceinline__ float fix_float(int v) { return __int_as_float(v + 0x4B400000) - 12582912.f; }
+
+// position of the o-th (0-based) set bit of m (which has more than o set bits)
+__device__ __forceinline__ int nth_bit(uint32_t m, int o) {
+  int base = 0;
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1) {
+    const int c = __popc(m & ((1u << w) - 1u));
+    if (o >= c) {
+      o -= c;
+      m >>= w;
+      base += w;
+    }
+  }
+  return base;
+}
+
+// record -> corner and fractions (fractions exactly q / 4096, built from the float bit pattern)
+__device__ __forceinline__ Rec decode_rec(unsigned long long v, const Env& E) {
+  Rec r;
+  r.ft = __uint_as_float(0x3F800000u | ((static_cast<uint32_t>(v) & 0xfffu) << 11)) - 1.f;
+  r.fh = __uint_as_float(0x3F800000u | ((static_cast<uint32_t>(v >> 12) & 0xfffu) << 11)) - 1.f;
+  r.fw = __uint_as_float(0x3F800000u | ((static_cast<uint32_t>(v >> 24) & 0xfffu) << 11)) - 1.f;
+  r.t0 = E.zlo - 1 + static_cast<int>((v >> 36) & 0x1fu);
+  r.h0 = E.ylo + static_cast<int>((v >> 41) & 0xffu);
+  r.w0 = E.xlo + static_cast<int>((v >> 49) & 0xffu);
+  return r;
+}
+
+// adds round(value * w_c) (value already scaled) for the sample's in-volume corners to an int32 row
+__device__ __forceinline__ void scatter_fixed_row(int* row, int k00, int ncw, const Rec& c, float sv, int H, int W) {
+  const float ax0 = 1.f - c.fw, ax1 = c.fw, ay0 = 1.f - c.fh, ay1 = c.fh;
+  const bool xok = c.w0 + 1 < W, yok = c.h0 + 1 < H;
+  atomicAdd(row + k00, fix_round(sv * (ax0 * ay0)));
+  if (xok) atomicAdd(row + k00 + 1, fix_round(sv * (ax1 * ay0)));
+  if (yok) {
+    atomicAdd(row + k00 + ncw, fix_round(sv * (ax0 * ay1)));
+    if (xok) atomicAdd(row + k00 + ncw + 1, fix_round(sv * (ax1 * ay1)));
+  }
+}
+
+// 16-key tiles of a chunk holding the sample's corners (rows h0, h0 + 1 of the chunk)
+__device__ __forceinline__ uint32_t corner_tiles(int k00, int ncw, bool xok, bool yok) {
+  uint32_t m = (1u << (k00 >> 4)) | (xok ? 1u << ((k00 + 1) >> 4) : 0u);
+  if (yok) m |= (1u << ((k00 + ncw) >> 4)) | (xok ? 1u << ((k00 + ncw + 1) >> 4) : 0u);
+  return m;
+}
+
+// Keys of the chunk (z, y in [ya, yb], x in [xa, xb]) in the 16-key tiles of mask m into kbuf rows
+// (y - ya) * ncw + (x - xa); zero past the chunk and outside the volume / K-V window; key_off[key] =
+// the key's row in the K/V buffers of the sample, -1 where there is none (key_off may be null).
+template <int DCH>
+__device__ __forceinline__ void load_keys(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
+                                          int* key_off, const __nv_bfloat16* base, long long ld, int z, int ya, int yb,
+                                          int xa, int xb, uint32_t m) {
+  const int ncw = xb - xa + 1;
+  const int nk = (yb - ya + 1) * ncw;
+  const int zl = z - P.kv_frame0;
+  const bool zok = zl >= 0 && zl < P.kv_frames;
+  const float inv_ncw = 1.f / static_cast<float>(ncw);
+  const __nv_bfloat16* gb = base + static_cast<long long>(T.b) * P.Nkv * ld + T.head * P.d;
+  const int items = __popc(m) * 16 * DCH;
+  for (int idx = threadIdx.x; idx < items; idx += kThreads) {
+    const int o = idx / (16 * DCH), rem = idx - o * (16 * DCH);
+    const int key = nth_bit(m, o) * 16 + rem / DCH, ch = rem - (rem / DCH) * DCH;
+    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs + ch * 8;
+    // key / ncw exactly: (key + 0.5) / ncw is at least 1 / (2 ncw) away from an integer
+    const int ky = static_cast<int>((static_cast<float>(key) + 0.5f) * inv_ncw);
+    const int y = ya + ky, x = xa + (key - ky * ncw);
+    const bool ok = key < nk && zok && y >= 0 && y < P.H && x >= 0 && x < P.W;
+    const long long row = (static_cast<long long>(zl) * P.H + y) * P.W + x;
+    if (ok)
+      cp_async16(smem_u32(dst), gb + row * ld + ch * 8);
+    else
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    if (key_off && ch == 0) key_off[key] = ok ? static_cast<int>(row) : -1;
+  }
+  cp_async_wait_all();
+}
+
+// zeroes rows 0..ROWS-1 of the 16-key tiles of mask m in a dense fp32 / int32 tile
+template <int ROWS>
+__device__ __forceinline__ void zero_tiles(float* buf, int sld, uint32_t m) {
+  const int items = __popc(m) * ROWS * 4;
+  for (int i = threadIdx.x; i < items; i += kThreads) {
+    const int o = i / (ROWS * 4), row = (i >> 2) % ROWS, c4 = i & 3;
+    *reinterpret_cast<float4*>(buf + static_cast<size_t>(row) * sld + nth_bit(m, o) * 16 + c4 * 4) =
+        make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// S / dP for the 16 queries of a row group over the chunk's tiles of mask m: A = 16 staged bf16
+// rows xs (Q or dO, row stride rs) read with ldmatrix, kbuf rows (keys) with ldmatrix; the WPG warps
+// of the group split the tiles round robin (`part` = warp index within the group).
+template <int DCH, int WPG>
+__device__ __forceinline__ void dense_tiles(const __nv_bfloat16* kbuf, const __nv_bfloat16* xs, int rs, float* srow,
+                                            int sld, int part, uint32_t m) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int mi = lane >> 3, rr = lane & 7;
+  const int nt = __popc(m);
+  if (part >= nt) return;
+  uint32_t qa[DCH / 2 > 0 ? DCH / 2 : 1][4], qt[2] = {0u, 0u};
+  {
+    const __nv_bfloat16* ap = xs + static_cast<size_t>(lane & 15) * rs + (lane >> 4) * 8;
+#pragma unroll
+    for (int ks = 0; ks < DCH / 2; ++ks) ldsm_x4(smem_u32(ap + ks * 16), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    if constexpr (DCH & 1) ldsm_x2(smem_u32(xs + static_cast<size_t>(lane & 15) * rs + (DCH - 1) * 8), qt[0], qt[1]);
+  }
+  for (int o = part; o < nt; o += WPG) {
+    const int gi = nth_bit(m, o);
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    const int key = gi * 16 + rr + ((mi >> 1) ? 8 : 0);
+    const __nv_bfloat16* rowp = kbuf + static_cast<size_t>(key) * rs + ((mi & 1) ? 8 : 0);
+#pragma unroll
+    for (int ks = 0; ks < DCH / 2; ++ks) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(smem_u32(rowp + ks * 16), b0, b1, b2, b3);
+      mma16816(c0, qa[ks], b0, b1);
+      mma16816(c1, qa[ks], b2, b3);
+    }
+    if constexpr (DCH & 1) {
+      const int key2 = gi * 16 + rr + ((mi & 1) ? 8 : 0);
+      uint32_t e0, e1;
+      ldsm_x2(smem_u32(kbuf + static_cast<size_t>(key2) * rs + (DCH - 1) * 8), e0, e1);
+      mma1688(c0, qt[0], qt[1], e0);
+      mma1688(c1, qt[0], qt[1], e1);
+    }
+    float* p0 = srow + static_cast<size_t>(g) * sld + gi * 16 + 2 * t4;
+    float* p1 = srow + static_cast<size_t>(g + 8) * sld + gi * 16 + 2 * t4;
+    *reinterpret_cast<float2*>(p0) = make_float2(c0[0], c0[1]);
+    *reinterpret_cast<float2*>(p1) = make_float2(c0[2], c0[3]);
+    *reinterpret_cast<float2*>(p0 + 8) = make_float2(c1[0], c1[1]);
+    *reinterpret_cast<float2*>(p1 + 8) = make_float2(c1[2], c1[3]);
+  }
+}
+
+// ------------------------------------------------------------------------------ 32-query tiles
+// Geometry shared by the kernels that use 4 x 8 query tiles (two 16-query row groups, 8 warps each,
+// 16 lanes per query for the per-sample work).
+namespace t32 {
+constexpr int kGroups = 2;                  // 16-query row groups per tile
+constexpr int kWPG = kWarps / kGroups;      // warps per row group
+constexpr int kLPQ = kWPG * 32 / 16;        // lanes per query
+constexpr int kTileH = 4, kQ = kTileH * kTileW;
+constexpr int kTRow = 40;                   // bf16 per key row of a transposed dense tile (32 + 8 pad)
+constexpr int kMaxKeys = 256;               // chunk cap: 16 tiles of 16 keys (one transposition item per thread)
+constexpr int kMaxMaskChunks = 4;           // chunks per plane with their own tile masks
+constexpr float kFixRange = 2097152.f;      // 2^21: fixed-point full scale of a dense row
+
+
+
+// In-place conversion of the tiles of mask m of an int32 dense tile [32][sld] (fixed point, per-row
+// inverse scale inv[q]) into bf16 [key][kTRow].  Two phases separated by a barrier; every thread of
+// the CTA must call it.  Item = (key, half): 16 queries of one key.
+__device__ __forceinline__ void transpose_fixed(float* buf, int sld, uint32_t m, const float* inv) {
+  constexpr int kMaxIt = kMaxKeys * 2 / kThreads;
+  const int* src = reinterpret_cast<const int*>(buf);
+  const int items = __popc(m) * 32;
+  uint32_t hold[kMaxIt][8];
+#pragma unroll
+  for (int u = 0; u < kMaxIt; ++u) {
+    const int i = threadIdx.x + u * kThreads;
+    if (i < items) {
+      const int key = nth_bit(m, i >> 5) * 16 + (i & 15), half = (i >> 4) & 1;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int q = half * 16 + 2 * e;
+        const float f0 = fix_float(src[static_cast<size_t>(q) * sld + key]) * inv[q];
+        const float f1 = fix_float(src[static_cast<size_t>(q + 1) * sld + key]) * inv[q + 1];
+        hold[u][e] = pack_bf16(f0, f1);
+      }
+    }
+  }
+  __syncthreads();
+  uint32_t* dst = reinterpret_cast<uint32_t*>(buf);
+#pragma unroll
+  for (int u = 0; u < kMaxIt; ++u) {
+    const int i = threadIdx.x + u * kThreads;
+    if (i < items) {
+      const int key = nth_bit(m, i >> 5) * 16 + (i & 15), half = (i >> 4) & 1;
+      uint4* d = reinterpret_cast<uint4*>(dst + key * (kTRow / 2) + half * 8);
+      d[0] = make_uint4(hold[u][0], hold[u][1], hold[u][2], hold[u][3]);
+      d[1] = make_uint4(hold[u][4], hold[u][5], hold[u][6], hold[u][7]);
+    }
+  }
+}
+
+// o[16 queries of group r][channel tiles nt0..nt1) += A . kbuf over the tiles of mask m; A = rows of
+// the transposed bf16 tile tb ([key][query]) read with ldmatrix.trans, kbuf rows through
+// ldmatrix.trans.
+template <int DCH, int TPW>
+__device__ __forceinline__ void dq_product(const __nv_bfloat16* tb, int r, const __nv_bfloat16* kbuf, int rs, int nt0,
+                                           int nt1, uint32_t m, float (&o)[TPW + 1][4]) {
+  const int lane = threadIdx.x & 31;
+  const int mi = lane >> 3, rr = lane & 7;
+  for (uint32_t mm = m; mm; mm &= mm - 1u) {
+    const int kk = __ffs(mm) - 1;
+    uint32_t a[4];
+    // matrices: (queries 0-7, keys 0-7) (q 8-15, k 0-7) (q 0-7, k 8-15) (q 8-15, k 8-15) of the group
+    const __nv_bfloat16* ap = tb + static_cast<size_t>(kk * 16 + rr + ((mi >> 1) ? 8 : 0)) * kTRow + r * 16 +
+                              ((mi & 1) ? 8 : 0);
+    ldsm_x4_t(smem_u32(ap), a[0], a[1], a[2], a[3]);
+    const __nv_bfloat16* rowp = kbuf + static_cast<size_t>(kk * 16 + rr + ((mi & 1) ? 8 : 0)) * rs;
+#pragma unroll
+    for (int jj = 0; jj < TPW; jj += 2) {
+      const int nt = nt0 + jj;
+      if (nt + 1 < nt1) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(rowp + (nt + (mi >> 1)) * 8), b0, b1, b2, b3);
+        mma16816(o[jj], a, b0, b1);
+        mma16816(o[jj + 1], a, b2, b3);
+      } else if (nt < nt1) {
+        uint32_t b0, b1;
+        ldsm_x2_t(smem_u32(rowp + nt * 8), b0, b1);
+        mma16816(o[jj], a, b0, b1);
+      }
+    }
+  }
+}
+
+}  // namespace t32
+
 }  // namespace tc
 }  // namespace msl

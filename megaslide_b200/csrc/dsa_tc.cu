@@ -295,45 +295,40 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   const __nv_bfloat16* qgrp = S.qs + static_cast<size_t>(r) * 16 * L.rs;
   __syncthreads();
 
-  // ---- pass 1: scores (hits CTA-wide)
-  if (work) {
-    for (int z = E.zlo; z <= E.zhi; ++z) {
-      const int zrel = z - E.zlo + 1;
+  // ---- pass 1: scores (hits CTA-wide); the next chunk's keys load while this chunk's samples combine
+  const int nch = work ? (E.zhi - E.zlo + 1) * E.ny * E.nx : 0;
+  {
+    const __nv_bfloat16* kg = static_cast<const __nv_bfloat16*>(P.k);
+    int c = next_chunk(E, S.mask, masks, 0, nch);
+    if (c < nch) issue_keys<DCH>(P, T, S.kbuf, L.rs, kg, P.k_ld, chunk_at(E, S.mask, masks, c));
+    while (c < nch) {
+      const Chunk k = chunk_at(E, S.mask, masks, c);
+      const int ncw = k.xb - k.xa + 1;
+      const int zrel = k.z - E.zlo + 1;
       const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
-      for (int iy = 0; iy < E.ny; ++iy) {
-        const int ya = E.ylo + iy * (E.R - 1), yb = min(ya + E.R - 1, E.yhi);
-        for (int ix = 0; ix < E.nx; ++ix) {
-          const int xa = E.xlo + ix * (E.cw - 1), xb = min(xa + E.cw - 1, E.xhi);
-          const int ncw = xb - xa + 1;
-          const int ntile = (((yb - ya + 1) * ncw + 15) >> 4);
-          const uint32_t m = masks ? S.mask[zrel * kMaxMaskChunks + iy * E.nx + ix]
-                                   : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
-          if (m == 0u) continue;
-          __syncthreads();
-          load_keys<DCH>(P, T, S.kbuf, L.rs, nullptr, static_cast<const __nv_bfloat16*>(P.k), P.k_ld, z, ya, yb, xa, xb,
-                         m);
-          __syncthreads();
-          dense_tiles<DCH, kWPG>(S.kbuf, qgrp, L.rs, grow_s, L.sld, part, m);
-          __syncthreads();
-          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
-            const int idx = S.hits[i];
-            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
-            const Rec c = decode_rec(S.rec[idx], E);
-            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-              continue;
-            const float* row = S.sbuf + static_cast<size_t>(q) * L.sld;
-            const int k00 = (c.h0 - ya) * ncw + (c.w0 - xa);
-            const bool xok = c.w0 + 1 < P.W, yok = c.h0 + 1 < P.H;
-            const float v00 = row[k00];
-            const float v01 = xok ? row[k00 + 1] : 0.f;
-            const float v10 = yok ? row[k00 + ncw] : 0.f;
-            const float v11 = (xok && yok) ? row[k00 + ncw + 1] : 0.f;
-            const float ax0 = 1.f - c.fw, ax1 = c.fw;
-            const float bil = (1.f - c.fh) * fmaf(ax1, v01, ax0 * v00) + c.fh * fmaf(ax1, v11, ax0 * v10);
-            float* sp = S.sacc + static_cast<size_t>(q) * KG + (idx - q * K);
-            *sp = fmaf(frac_weight(c.ft, z != c.t0), bil, *sp);
-          }
-        }
+      cp_async_wait_all();
+      __syncthreads();
+      dense_tiles<DCH, kWPG>(S.kbuf, qgrp, L.rs, grow_s, L.sld, part, k.m);
+      __syncthreads();
+      c = next_chunk(E, S.mask, masks, c + 1, nch);
+      if (c < nch) issue_keys<DCH>(P, T, S.kbuf, L.rs, kg, P.k_ld, chunk_at(E, S.mask, masks, c));
+      for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+        const int idx = S.hits[i];
+        const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+        const Rec rc = decode_rec(S.rec[idx], E);
+        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
+          continue;
+        const float* row = S.sbuf + static_cast<size_t>(q) * L.sld;
+        const int k00 = (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa);
+        const bool xok = rc.w0 + 1 < P.W, yok = rc.h0 + 1 < P.H;
+        const float v00 = row[k00];
+        const float v01 = xok ? row[k00 + 1] : 0.f;
+        const float v10 = yok ? row[k00 + ncw] : 0.f;
+        const float v11 = (xok && yok) ? row[k00 + ncw + 1] : 0.f;
+        const float ax0 = 1.f - rc.fw, ax1 = rc.fw;
+        const float bil = (1.f - rc.fh) * fmaf(ax1, v01, ax0 * v00) + rc.fh * fmaf(ax1, v11, ax0 * v10);
+        float* sp = S.sacc + static_cast<size_t>(q) * KG + (idx - q * K);
+        *sp = fmaf(frac_weight(rc.ft, k.z != rc.t0), bil, *sp);
       }
     }
   }
@@ -396,42 +391,35 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
 #pragma unroll
   for (int i = 0; i < kTPW + 1; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(S.sbuf);  // P~^T after the transposition
-  if (work) {
-    for (int z = E.zlo; z <= E.zhi; ++z) {
-      const int zrel = z - E.zlo + 1;
+  {
+    const __nv_bfloat16* vg = static_cast<const __nv_bfloat16*>(P.v);
+    for (int c = next_chunk(E, S.mask, masks, 0, nch); c < nch; c = next_chunk(E, S.mask, masks, c + 1, nch)) {
+      const Chunk k = chunk_at(E, S.mask, masks, c);
+      const int ncw = k.xb - k.xa + 1;
+      const int zrel = k.z - E.zlo + 1;
       const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
-      for (int iy = 0; iy < E.ny; ++iy) {
-        const int ya = E.ylo + iy * (E.R - 1), yb = min(ya + E.R - 1, E.yhi);
-        for (int ix = 0; ix < E.nx; ++ix) {
-          const int xa = E.xlo + ix * (E.cw - 1), xb = min(xa + E.cw - 1, E.xhi);
-          const int ncw = xb - xa + 1;
-          const int ntile = (((yb - ya + 1) * ncw + 15) >> 4);
-          const uint32_t mk = masks ? S.mask[zrel * kMaxMaskChunks + iy * E.nx + ix]
-                                    : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
-          if (mk == 0u) continue;
-          __syncthreads();
-          load_keys<DCH>(P, T, S.kbuf, L.rs, nullptr, static_cast<const __nv_bfloat16*>(P.v), P.v_ld, z, ya, yb, xa,
-                         xb, mk);
-          zero_tiles<kQ>(S.sbuf, L.sld, mk);
-          __syncthreads();
-          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
-            const int idx = S.hits[i];
-            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
-            const float pv = S.sacc[static_cast<size_t>(q) * KG + (idx - q * K)];
-            if (pv == 0.f) continue;
-            const Rec c = decode_rec(S.rec[idx], E);
-            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-              continue;
-            scatter_fixed_row(reinterpret_cast<int*>(S.sbuf) + static_cast<size_t>(q) * L.sld,
-                              (c.h0 - ya) * ncw + (c.w0 - xa), ncw, c,
-                              pv * frac_weight(c.ft, z != c.t0) * S.qsc[q], P.H, P.W);
-          }
-          __syncthreads();
-          transpose_fixed(S.sbuf, L.sld, mk, S.qsc + kQ);
-          __syncthreads();
-          dq_product<DCH, kTPW>(tp, r, S.kbuf, L.rs, nt0, nt1, mk, o);
-        }
+      __syncthreads();  // the previous chunk's product is done with the key buffer and the dense tile
+      // the values land while the weights are scattered and converted
+      issue_keys<DCH>(P, T, S.kbuf, L.rs, vg, P.v_ld, k);
+      zero_tiles<kQ>(S.sbuf, L.sld, k.m);
+      __syncthreads();
+      for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+        const int idx = S.hits[i];
+        const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+        const float pv = S.sacc[static_cast<size_t>(q) * KG + (idx - q * K)];
+        if (pv == 0.f) continue;
+        const Rec rc = decode_rec(S.rec[idx], E);
+        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
+          continue;
+        scatter_fixed_row(reinterpret_cast<int*>(S.sbuf) + static_cast<size_t>(q) * L.sld,
+                          (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa), ncw, rc,
+                          pv * frac_weight(rc.ft, k.z != rc.t0) * S.qsc[q], P.H, P.W);
       }
+      __syncthreads();
+      transpose_fixed(S.sbuf, L.sld, k.m, S.qsc + kQ);
+      cp_async_wait_all();
+      __syncthreads();
+      dq_product<DCH, kTPW>(tp, r, S.kbuf, L.rs, nt0, nt1, k.m, o);
     }
   }
   if (P.G > 0) {  // extra values: their weights straight into the fixed-point rows
@@ -478,6 +466,7 @@ bool tc_supported(const AttnParams& P) {
   if (P.dtype != MSL_DTYPE_BF16) return false;
   if (P.d % 8 != 0 || P.d < 16 || P.d > 128) return false;
   if (P.T > 65535 || P.K > 2048 || P.G > 256) return false;
+  if (static_cast<long long>(P.kv_frames) * P.H * P.W > 0x7fffffffLL) return false;  // 32-bit key rows
   if (static_cast<long long>(tc::t32::kQ) * P.K > 65536) return false;  // hit-list entries are 16-bit
   // base-grid tables hold at most 96 positions per axis
   if (P.kt > 96 || P.kh + tc::t32::kTileH - 1 > 96 || P.kw + tc::kTileW - 1 > 96) return false;

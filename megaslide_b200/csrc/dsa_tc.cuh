@@ -383,36 +383,77 @@ __device__ __forceinline__ uint32_t corner_tiles(int k00, int ncw, bool xok, boo
   return m;
 }
 
-// Keys of the chunk (z, y in [ya, yb], x in [xa, xb]) in the 16-key tiles of mask m into kbuf rows
-// (y - ya) * ncw + (x - xa); zero past the chunk and outside the volume / K-V window; key_off[key] =
-// the key's row in the K/V buffers of the sample, -1 where there is none (key_off may be null).
-template <int DCH>
-__device__ __forceinline__ void load_keys(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
-                                          int* key_off, const __nv_bfloat16* base, long long ld, int z, int ya, int yb,
-                                          int xa, int xb, uint32_t m) {
-  const int ncw = xb - xa + 1;
-  const int nk = (yb - ya + 1) * ncw;
-  const int zl = z - P.kv_frame0;
-  const bool zok = zl >= 0 && zl < P.kv_frames;
-  const float inv_ncw = 1.f / static_cast<float>(ncw);
-  const __nv_bfloat16* gb = base + static_cast<long long>(T.b) * P.Nkv * ld + T.head * P.d;
-  const int items = __popc(m) * 16 * DCH;
-  for (int idx = threadIdx.x; idx < items; idx += kThreads) {
-    const int o = idx / (16 * DCH), rem = idx - o * (16 * DCH);
-    const int key = nth_bit(m, o) * 16 + rem / DCH, ch = rem - (rem / DCH) * DCH;
-    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs + ch * 8;
-    // key / ncw exactly: (key + 0.5) / ncw is at least 1 / (2 ncw) away from an integer
-    const int ky = static_cast<int>((static_cast<float>(key) + 0.5f) * inv_ncw);
-    const int y = ya + ky, x = xa + (key - ky * ncw);
-    const bool ok = key < nk && zok && y >= 0 && y < P.H && x >= 0 && x < P.W;
-    const long long row = (static_cast<long long>(zl) * P.H + y) * P.W + x;
-    if (ok)
-      cp_async16(smem_u32(dst), gb + row * ld + ch * 8);
-    else
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-    if (key_off && ch == 0) key_off[key] = ok ? static_cast<int>(row) : -1;
+// The envelope walk: chunk c = ((z - zlo) * ny + iy) * nx + ix covers frame z, rows [ya, yb] and
+// columns [xa, xb]; its keys are numbered (y - ya) * ncw + (x - xa) and m marks the 16-key tiles any
+// sample of the tile touches (every tile of the chunk when the masks are not kept).  Tile masks are
+// kept per plane for up to kMaskChunks chunks.
+constexpr int kMaskChunks = 4;
+
+struct Chunk {
+  int z, iy, ix, ya, yb, xa, xb;
+  uint32_t m;
+};
+
+__device__ __forceinline__ Chunk chunk_at(const Env& E, const uint32_t* mask, bool masks, int c) {
+  Chunk k;
+  const int per_z = E.ny * E.nx;
+  const int zr = c / per_z, rem = c - zr * per_z;
+  k.iy = rem / E.nx;
+  k.ix = rem - k.iy * E.nx;
+  k.z = E.zlo + zr;
+  k.ya = E.ylo + k.iy * (E.R - 1);
+  k.yb = min(k.ya + E.R - 1, E.yhi);
+  k.xa = E.xlo + k.ix * (E.cw - 1);
+  k.xb = min(k.xa + E.cw - 1, E.xhi);
+  const int ntile = ((k.yb - k.ya + 1) * (k.xb - k.xa + 1) + 15) >> 4;
+  k.m = masks ? mask[(zr + 1) * kMaskChunks + rem] : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
+  return k;
+}
+
+// the first chunk at or after c with a touched tile, nch when there is none
+__device__ __forceinline__ int next_chunk(const Env& E, const uint32_t* mask, bool masks, int c, int nch) {
+  if (!masks) return c;
+  const int per_z = E.ny * E.nx;
+  for (; c < nch; ++c) {
+    const int zr = c / per_z;
+    if (mask[(zr + 1) * kMaskChunks + (c - zr * per_z)]) break;
   }
-  cp_async_wait_all();
+  return c;
+}
+
+// Row of chunk key `key` in the K/V buffers of the sample, -1 past the chunk and outside the volume /
+// K-V window.
+__device__ __forceinline__ int chunk_key_row(const AttnParams& P, const Chunk& k, int key) {
+  const int ncw = k.xb - k.xa + 1;
+  // key / ncw exactly: (key + 0.5) / ncw is at least 1 / (2 ncw) away from an integer
+  const int ky = static_cast<int>((static_cast<float>(key) + 0.5f) * (1.f / static_cast<float>(ncw)));
+  const int y = k.ya + ky, x = k.xa + (key - ky * ncw);
+  const int zl = k.z - P.kv_frame0;
+  const bool ok = y <= k.yb && zl >= 0 && zl < P.kv_frames && y >= 0 && y < P.H && x >= 0 && x < P.W;
+  return ok ? (zl * P.H + y) * P.W + x : -1;
+}
+
+// Starts the copy of the chunk's keys in the 16-key tiles of k.m into kbuf rows (one thread per key
+// row, one 16-byte cp.async per 8 channels); rows without a key are zeroed with plain stores.  The
+// copies land at the caller's cp_async_wait_all().
+template <int DCH>
+__device__ __forceinline__ void issue_keys(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
+                                           const __nv_bfloat16* base, long long ld, const Chunk& k) {
+  const __nv_bfloat16* gb = base + static_cast<long long>(T.b) * P.Nkv * ld + T.head * P.d;
+  const int nkeys = __popc(k.m) * 16;
+  for (int i = threadIdx.x; i < nkeys; i += kThreads) {
+    const int key = nth_bit(k.m, i >> 4) * 16 + (i & 15);
+    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs;
+    const int row = chunk_key_row(P, k, key);
+    if (row >= 0) {
+      const __nv_bfloat16* src = gb + static_cast<long long>(row) * ld;
+#pragma unroll
+      for (int ch = 0; ch < DCH; ++ch) cp_async16(smem_u32(dst + ch * 8), src + ch * 8);
+    } else {
+#pragma unroll
+      for (int ch = 0; ch < DCH; ++ch) *reinterpret_cast<uint4*>(dst + ch * 8) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
 }
 
 // zeroes rows 0..ROWS-1 of the 16-key tiles of mask m in a dense fp32 / int32 tile
@@ -482,7 +523,7 @@ constexpr int kLPQ = kWPG * 32 / 16;        // lanes per query
 constexpr int kTileH = 4, kQ = kTileH * kTileW;
 constexpr int kTRow = 40;                   // bf16 per key row of a transposed dense tile (32 + 8 pad)
 constexpr int kMaxKeys = 256;               // chunk cap: 16 tiles of 16 keys (one transposition item per thread)
-constexpr int kMaxMaskChunks = 4;           // chunks per plane with their own tile masks
+constexpr int kMaxMaskChunks = kMaskChunks;  // chunks per plane with their own tile masks
 constexpr float kFixRange = 2097152.f;      // 2^21: fixed-point full scale of a dense row
 
 

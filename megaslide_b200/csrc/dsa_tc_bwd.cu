@@ -431,43 +431,44 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   float* grow_a = S.sa + static_cast<size_t>(r) * 16 * L.sld;  // the row group's 16 dense rows
   __syncthreads();
 
-  // ---- pass 1: V side (dp_j and the value part of the coordinate gradient), hits CTA-wide
-  if (work) {
-    for (int z = E.zlo; z <= E.zhi; ++z) {
-      const int zrel = z - E.zlo + 1;
+  // ---- pass 1: V side (dp_j and the value part of the coordinate gradient), hits CTA-wide; the next
+  // chunk's values load while this chunk's samples run, and after the last one pass 2's first keys
+  const int nch = work ? (E.zhi - E.zlo + 1) * E.ny * E.nx : 0;
+  const __nv_bfloat16* kg = static_cast<const __nv_bfloat16*>(P.k);
+  const __nv_bfloat16* vg = static_cast<const __nv_bfloat16*>(P.v);
+  const int c_first = next_chunk(E, S.mask, masks, 0, nch);
+  {
+    int c = c_first;
+    if (c < nch) issue_keys<DCH>(P, T, S.kbuf, L.rs, vg, P.v_ld, chunk_at(E, S.mask, masks, c));
+    while (c < nch) {
+      const Chunk k = chunk_at(E, S.mask, masks, c);
+      const int ncw = k.xb - k.xa + 1;
+      const int zrel = k.z - E.zlo + 1;
       const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
-      for (int iy = 0; iy < E.ny; ++iy) {
-        const int ya = E.ylo + iy * (E.R - 1), yb = min(ya + E.R - 1, E.yhi);
-        for (int ix = 0; ix < E.nx; ++ix) {
-          const int xa = E.xlo + ix * (E.cw - 1), xb = min(xa + E.cw - 1, E.xhi);
-          const int ncw = xb - xa + 1;
-          const int ntile = (((yb - ya + 1) * ncw + 15) >> 4);
-          const uint32_t m = masks ? S.mask[zrel * kMaxMaskChunks + iy * E.nx + ix]
-                                   : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
-          if (m == 0u) continue;
-          __syncthreads();
-          load_keys<DCH>(P, T, S.kbuf, L.rs, S.key_off, static_cast<const __nv_bfloat16*>(P.v), P.v_ld, z, ya, yb, xa,
-                         xb, m);
-          __syncthreads();
-          dense_tiles<DCH, kWPG>(S.kbuf, S.dos + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, m);
-          __syncthreads();
-          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
-            const int idx = S.hits[i];
-            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
-            const Rec c = decode_rec(S.rec[idx], E);
-            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-              continue;
-            const bool upper = z != c.t0;
-            const float az = frac_weight(c.ft, upper);
-            const PlaneTerms pt_ =
-                plane_terms(S.sa + static_cast<size_t>(q) * L.sld, (c.h0 - ya) * ncw + (c.w0 - xa), ncw, c, P.H, P.W);
-            S.sv[idx] = fmaf(az, pt_.bil, S.sv[idx]);
-            float* gg = S.g3 + 3 * idx;
-            gg[0] += upper ? pt_.bil : -pt_.bil;
-            gg[1] = fmaf(az, pt_.dvy, gg[1]);
-            gg[2] = fmaf(az, pt_.dvx, gg[2]);
-          }
-        }
+      cp_async_wait_all();
+      __syncthreads();
+      dense_tiles<DCH, kWPG>(S.kbuf, S.dos + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, k.m);
+      __syncthreads();
+      c = next_chunk(E, S.mask, masks, c + 1, nch);
+      if (c < nch)
+        issue_keys<DCH>(P, T, S.kbuf, L.rs, vg, P.v_ld, chunk_at(E, S.mask, masks, c));
+      else
+        issue_keys<DCH>(P, T, S.kbuf, L.rs, kg, P.k_ld, chunk_at(E, S.mask, masks, c_first));
+      for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+        const int idx = S.hits[i];
+        const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+        const Rec rc = decode_rec(S.rec[idx], E);
+        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
+          continue;
+        const bool upper = k.z != rc.t0;
+        const float az = frac_weight(rc.ft, upper);
+        const PlaneTerms pt_ = plane_terms(S.sa + static_cast<size_t>(q) * L.sld, (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa),
+                                           ncw, rc, P.H, P.W);
+        S.sv[idx] = fmaf(az, pt_.bil, S.sv[idx]);
+        float* gg = S.g3 + 3 * idx;
+        gg[0] += upper ? pt_.bil : -pt_.bil;
+        gg[1] = fmaf(az, pt_.dvy, gg[1]);
+        gg[2] = fmaf(az, pt_.dvx, gg[2]);
       }
     }
   }
@@ -518,73 +519,68 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   for (int i = 0; i < kTPW + 1; ++i) oq[i][0] = oq[i][1] = oq[i][2] = oq[i][3] = 0.f;
   const __nv_bfloat16* tds = reinterpret_cast<const __nv_bfloat16*>(S.sb);  // dS~^T after the transposition
   const __nv_bfloat16* tpp = reinterpret_cast<const __nv_bfloat16*>(S.sa);  // P~^T after the transposition
-  if (work) {
-    for (int z = E.zlo; z <= E.zhi; ++z) {
-      const int zrel = z - E.zlo + 1;
-      const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
-      for (int iy = 0; iy < E.ny; ++iy) {
-        const int ya = E.ylo + iy * (E.R - 1), yb = min(ya + E.R - 1, E.yhi);
-        for (int ix = 0; ix < E.nx; ++ix) {
-          const int xa = E.xlo + ix * (E.cw - 1), xb = min(xa + E.cw - 1, E.xhi);
-          const int ncw = xb - xa + 1;
-          const int ntile = (((yb - ya + 1) * ncw + 15) >> 4);
-          const uint32_t m = masks ? S.mask[zrel * kMaxMaskChunks + iy * E.nx + ix]
-                                   : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
-          if (m == 0u) continue;
-          __syncthreads();
-          load_keys<DCH>(P, T, S.kbuf, L.rs, S.key_off, static_cast<const __nv_bfloat16*>(P.k), P.k_ld, z, ya, yb, xa,
-                         xb, m);
-          zero_tiles<kQ>(S.sb, L.sld, m);
-          __syncthreads();
-          dense_tiles<DCH, kWPG>(S.kbuf, S.qs + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, m);
-          __syncthreads();
-          // key part of the coordinate gradient (reads S) and the dS~ scatter (into sb)
-          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
-            const int idx = S.hits[i];
-            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
-            const Rec c = decode_rec(S.rec[idx], E);
-            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-              continue;
-            const bool upper = z != c.t0;
-            const float az = frac_weight(c.ft, upper);
-            const int k00 = (c.h0 - ya) * ncw + (c.w0 - xa);
-            const PlaneTerms pt_ = plane_terms(S.sa + static_cast<size_t>(q) * L.sld, k00, ncw, c, P.H, P.W);
-            const float dsq = S.sv[idx];
-            float* gg = S.g3 + 3 * idx;
-            gg[0] = fmaf(dsq, upper ? pt_.bil : -pt_.bil, gg[0]);
-            gg[1] = fmaf(dsq * az, pt_.dvy, gg[1]);
-            gg[2] = fmaf(dsq * az, pt_.dvx, gg[2]);
-            scatter_fixed_row(reinterpret_cast<int*>(S.sb) + static_cast<size_t>(q) * L.sld, k00, ncw, c,
-                          dsq * az * S.qsc[q], P.H, P.W);
-          }
-          __syncthreads();
-          // dS~ -> bf16 [key][query]; S no longer needed: clear sa for P~
-          transpose_fixed(S.sb, L.sld, m, S.qsc + kQ);
-          zero_tiles<kQ>(S.sa, L.sld, m);
-          __syncthreads();
-          // P~ scatter (into sa), dQ += dS~ . K_chunk, dK_chunk = dS~^T . Q
-          for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
-            const int idx = S.hits[i];
-            const unsigned long long v = S.rec[idx];
-            if (!((v >> kBitKeep) & 1ull)) continue;
-            const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
-            const Rec c = decode_rec(v, E);
-            if (split && (axis_chunk_of(c.h0, E.ylo, E.R, E.ny) != iy || axis_chunk_of(c.w0, E.xlo, E.cw, E.nx) != ix))
-              continue;
-            const float pv = __ldg(P.probs + S.prow[q] * K + (idx - q * K)) * P.drop_keep_scale;
-            scatter_fixed_row(reinterpret_cast<int*>(S.sa) + static_cast<size_t>(q) * L.sld,
-                          (c.h0 - ya) * ncw + (c.w0 - xa), ncw, c,
-                          pv * frac_weight(c.ft, z != c.t0) * S.qsc[2 * kQ + q], P.H, P.W);
-          }
-          dq_product<DCH, kTPW>(tds, r, S.kbuf, L.rs, nt0, nt1, m, oq);
-          kv_product_flush<DCH>(P, T, L, tds, S.qs, S.key_off, m, P.dk_acc);
-          __syncthreads();
-          transpose_fixed(S.sa, L.sld, m, S.qsc + 3 * kQ);
-          __syncthreads();
-          kv_product_flush<DCH>(P, T, L, tpp, S.dos, S.key_off, m, P.dv_acc);
-        }
-      }
+  // (the first chunk's keys were issued at the end of pass 1; each later chunk's keys load while the
+  // previous chunk's P~ is converted and its dV flushed)
+  for (int c = c_first; c < nch;) {
+    const Chunk k = chunk_at(E, S.mask, masks, c);
+    const int ncw = k.xb - k.xa + 1;
+    const int zrel = k.z - E.zlo + 1;
+    const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
+    cp_async_wait_all();
+    __syncthreads();  // keys landed; the previous chunk's dV flush is done with key_off and sa
+    for (int i = threadIdx.x; i < __popc(k.m) * 16; i += kThreads) {
+      const int key = nth_bit(k.m, i >> 4) * 16 + (i & 15);
+      S.key_off[key] = chunk_key_row(P, k, key);
     }
+    zero_tiles<kQ>(S.sb, L.sld, k.m);
+    dense_tiles<DCH, kWPG>(S.kbuf, S.qs + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, k.m);
+    __syncthreads();
+    // key part of the coordinate gradient (reads S) and the dS~ scatter (into sb)
+    for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+      const int idx = S.hits[i];
+      const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+      const Rec rc = decode_rec(S.rec[idx], E);
+      if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
+        continue;
+      const bool upper = k.z != rc.t0;
+      const float az = frac_weight(rc.ft, upper);
+      const int k00 = (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa);
+      const PlaneTerms pt_ = plane_terms(S.sa + static_cast<size_t>(q) * L.sld, k00, ncw, rc, P.H, P.W);
+      const float dsq = S.sv[idx];
+      float* gg = S.g3 + 3 * idx;
+      gg[0] = fmaf(dsq, upper ? pt_.bil : -pt_.bil, gg[0]);
+      gg[1] = fmaf(dsq * az, pt_.dvy, gg[1]);
+      gg[2] = fmaf(dsq * az, pt_.dvx, gg[2]);
+      scatter_fixed_row(reinterpret_cast<int*>(S.sb) + static_cast<size_t>(q) * L.sld, k00, ncw, rc,
+                        dsq * az * S.qsc[q], P.H, P.W);
+    }
+    __syncthreads();
+    // dS~ -> bf16 [key][query]; S no longer needed: clear sa for P~
+    transpose_fixed(S.sb, L.sld, k.m, S.qsc + kQ);
+    zero_tiles<kQ>(S.sa, L.sld, k.m);
+    __syncthreads();
+    // P~ scatter (into sa), dQ += dS~ . K_chunk, dK_chunk = dS~^T . Q
+    for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+      const int idx = S.hits[i];
+      const unsigned long long v = S.rec[idx];
+      if (!((v >> kBitKeep) & 1ull)) continue;
+      const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+      const Rec rc = decode_rec(v, E);
+      if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
+        continue;
+      const float pv = __ldg(P.probs + S.prow[q] * K + (idx - q * K)) * P.drop_keep_scale;
+      scatter_fixed_row(reinterpret_cast<int*>(S.sa) + static_cast<size_t>(q) * L.sld,
+                        (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa), ncw, rc,
+                        pv * frac_weight(rc.ft, k.z != rc.t0) * S.qsc[2 * kQ + q], P.H, P.W);
+    }
+    dq_product<DCH, kTPW>(tds, r, S.kbuf, L.rs, nt0, nt1, k.m, oq);
+    kv_product_flush<DCH>(P, T, L, tds, S.qs, S.key_off, k.m, P.dk_acc);
+    __syncthreads();  // the key buffer is free
+    c = next_chunk(E, S.mask, masks, c + 1, nch);
+    if (c < nch) issue_keys<DCH>(P, T, S.kbuf, L.rs, kg, P.k_ld, chunk_at(E, S.mask, masks, c));
+    transpose_fixed(S.sa, L.sld, k.m, S.qsc + 3 * kQ);
+    __syncthreads();
+    kv_product_flush<DCH>(P, T, L, tpp, S.dos, S.key_off, k.m, P.dv_acc);
   }
   __syncthreads();
 

@@ -48,6 +48,8 @@ extern "C" {
 #define MSL_STATUS_TC_RANGE 2u   /* tensor-core path: a tile's key envelope needed more than 255
                                     chunks per axis (offsets of hundreds of voxels); its results are
                                     not valid - rerun with MSL_ALGO_SIMT */
+#define MSL_STATUS_TIMEOUT 4u    /* tensor-core path: a CTA's TMA copies did not complete within a second;
+                                    it stopped waiting and its results are not valid */
 
 /* kernel family */
 #define MSL_ALGO_AUTO 0 /* tensor-core envelope kernels when supported (bf16, head_dim % 8 == 0, <= 128) */

@@ -23,6 +23,7 @@ MSL_DTYPE_F32 = 0
 MSL_DTYPE_BF16 = 1
 MSL_STATUS_HALO_MISS = 1
 MSL_STATUS_TC_RANGE = 2
+MSL_STATUS_TIMEOUT = 4
 MSL_ALGO_AUTO = 0
 MSL_ALGO_SIMT = 1
 MSL_ALGO_TC = 2

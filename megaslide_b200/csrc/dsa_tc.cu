@@ -27,6 +27,10 @@
 
 #include "dsa_tc.cuh"
 
+#include <cudaTypedefs.h>
+#include <stdlib.h>
+#include <string.h>
+
 namespace msl {
 namespace tc {
 namespace fwd {
@@ -46,6 +50,8 @@ struct Smem {
   int* bcur;                // [32]            bucket counts, then fill cursors
   uint32_t* mask;           // [32][4]         16-key tiles touched per (plane, chunk)
   unsigned short* hits;     // [32 * K]        sample indices q * K + j sorted by frame bucket
+  unsigned long long* kbar; // mbarrier of the key buffer's TMA copies
+  int* dead;                // set when a TMA wait gave up
 };
 
 __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, const TcLaunch& L) {
@@ -74,6 +80,11 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   s.mask = reinterpret_cast<uint32_t*>(base + off);
   off += 32 * kMaxMaskChunks * 4;
   s.hits = reinterpret_cast<unsigned short*>(base + off);
+  off += static_cast<size_t>(kQ) * P.K * 2;
+  // last: the setup's offset staging spills from the key buffer into the regions after it
+  off = (off + 7) & ~static_cast<size_t>(7);
+  s.kbar = reinterpret_cast<unsigned long long*>(base + off);
+  s.dead = reinterpret_cast<int*>(base + off + 8);
   return s;
 }
 
@@ -81,7 +92,7 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
 size_t smem_fixed(const AttnParams& P, int rs) {
   return static_cast<size_t>(kQ) * rs * 2 + static_cast<size_t>(kQ) * P.K * (8 + 2) +
          static_cast<size_t>(kQ) * (P.K + P.G) * 4 + kEnvWords * 4 + kQ * 4 * 3 + (36 + 32 + 32 * kMaxMaskChunks) * 4 +
-         256;
+         24 + 256;
 }
 
 // loads G extra keys / values of this head into kbuf rows 0..G-1 (zero up to gp)
@@ -102,8 +113,10 @@ __device__ __forceinline__ void load_extra(const AttnParams& P, const TileCtx& T
 }
 
 template <int DCH>
-__global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParams P, const TcLaunch L) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParams P, const TcLaunch L,
+                                                                  const __grid_constant__ CUtensorMap kmap,
+                                                                  const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   const Smem S = carve(smem_raw, P, L);
   const TileCtx T = decode_tile(P, L, kTileH);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -134,6 +147,17 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   }
   if (threadIdx.x < 32) S.bcur[threadIdx.x] = 0;
   if (threadIdx.x < 32 * kMaxMaskChunks) S.mask[threadIdx.x] = 0u;
+  // TMA destinations are 128-byte aligned: boxes start at multiples of 8 keys x rs (rs % 8 == 0) bf16
+  const bool tma = L.tma && (smem_u32(S.kbuf) & 127u) == 0u;
+  const uint32_t kbar = smem_u32(S.kbar);
+  if (threadIdx.x == 0) {
+    *S.dead = 0;
+    if (tma) {
+      mbar_init(kbar, 1);
+      fence_mbar_init();
+    }
+  }
+  uint32_t kphase = 0;
   fill_tabs(P, T, kTileH, tabz, taby, tabx);
 
   // ---- stage the tile's offsets (this head) and Q rows with one wave of cp.async
@@ -212,13 +236,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   E.zlo = S.env[0]; E.zhi = S.env[1]; E.ylo = S.env[2]; E.yhi = S.env[3]; E.xlo = S.env[4]; E.xhi = S.env[5];
   const bool any = E.zlo <= E.zhi && E.ylo <= E.yhi && E.xlo <= E.xhi;
   if (any) {
-    const int nxk = E.xhi - E.xlo + 1;
-    E.cw = nxk <= L.maxkeys / 2 ? nxk : L.maxkeys / 2;
-    E.R = L.maxkeys / E.cw;
-    E.ny = axis_chunks(E.ylo, E.yhi, E.R);
-    E.nx = axis_chunks(E.xlo, E.xhi, E.cw);
+    chunk_shape(E, L.maxkeys);
   } else {
     E.cw = E.R = E.ny = E.nx = 1;
+    E.kst = 8;
   }
   const bool split = E.ny * E.nx > 1;
   // records hold t0 - zlo + 1 in 5 bits and h0 - ylo, w0 - xlo in 8 bits
@@ -246,8 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         if (masks) {
           const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
           const int ya = E.ylo + iy * (E.R - 1), xa = E.xlo + ix * (E.cw - 1);
-          const int ncw = min(xa + E.cw - 1, E.xhi) - xa + 1;
-          bits = corner_tiles((h0 - ya) * ncw + (w0 - xa), ncw, w0 + 1 < P.W, h0 + 1 < P.H);
+          bits = corner_tiles((h0 - ya) * E.kst + (w0 - xa), E.kst, w0 + 1 < P.W, h0 + 1 < P.H);
           const int chk = iy * E.nx + ix;
           if (t0 >= E.zlo) pa = dz * kMaxMaskChunks + chk;
           if (t0 + 1 <= E.zhi) pb = (dz + 1) * kMaxMaskChunks + chk;
@@ -296,39 +316,58 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   __syncthreads();
 
   // ---- pass 1: scores (hits CTA-wide); the next chunk's keys load while this chunk's samples combine
-  const int nch = work ? (E.zhi - E.zlo + 1) * E.ny * E.nx : 0;
+  const int nz = work ? E.zhi - E.zlo + 1 : 0;
+  const __nv_bfloat16* kg = static_cast<const __nv_bfloat16*>(P.k);
+  const __nv_bfloat16* vg = static_cast<const __nv_bfloat16*>(P.v);
+  const int kst = E.kst;
   {
-    const __nv_bfloat16* kg = static_cast<const __nv_bfloat16*>(P.k);
-    int c = next_chunk(E, S.mask, masks, 0, nch);
-    if (c < nch) issue_keys<DCH>(P, T, S.kbuf, L.rs, kg, P.k_ld, chunk_at(E, S.mask, masks, c));
-    while (c < nch) {
-      const Chunk k = chunk_at(E, S.mask, masks, c);
-      const int ncw = k.xb - k.xa + 1;
-      const int zrel = k.z - E.zlo + 1;
-      const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
-      cp_async_wait_all();
+    Chunk k;
+    bool have = chunk_first(E, S.mask, masks, nz, k);
+    if (have) {
+      if (tma) {
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &kmap, kbar);
+      } else {
+        issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, kg, P.k_ld);
+      }
+    }
+    while (have) {
+      const Chunk cur = k;
+      if (tma) {
+        wait_keys(kbar, kphase, S.dead, P.status);
+        kphase ^= 1u;
+      } else {
+        cp_async_wait_all();
+      }
       __syncthreads();
-      dense_tiles<DCH, kWPG>(S.kbuf, qgrp, L.rs, grow_s, L.sld, part, k.m);
+      dense_tiles<DCH, kWPG>(S.kbuf, qgrp, L.rs, grow_s, L.sld, part, cur.m);
       __syncthreads();
-      c = next_chunk(E, S.mask, masks, c + 1, nch);
-      if (c < nch) issue_keys<DCH>(P, T, S.kbuf, L.rs, kg, P.k_ld, chunk_at(E, S.mask, masks, c));
+      have = chunk_next(E, S.mask, masks, nz, k);
+      if (have) {
+        if (tma) {
+          if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &kmap, kbar);
+        } else {
+          issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, kg, P.k_ld);
+        }
+      }
+      const int z = E.zlo + cur.zr, ya = chunk_ya(E, cur), xa = chunk_xa(E, cur);
+      const int hlo = S.bstart[cur.zr], hhi = S.bstart[cur.zr + 2];
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
         const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
         const Rec rc = decode_rec(S.rec[idx], E);
-        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
+        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
           continue;
         const float* row = S.sbuf + static_cast<size_t>(q) * L.sld;
-        const int k00 = (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa);
+        const int k00 = (rc.h0 - ya) * kst + (rc.w0 - xa);
         const bool xok = rc.w0 + 1 < P.W, yok = rc.h0 + 1 < P.H;
         const float v00 = row[k00];
         const float v01 = xok ? row[k00 + 1] : 0.f;
-        const float v10 = yok ? row[k00 + ncw] : 0.f;
-        const float v11 = (xok && yok) ? row[k00 + ncw + 1] : 0.f;
+        const float v10 = yok ? row[k00 + kst] : 0.f;
+        const float v11 = (xok && yok) ? row[k00 + kst + 1] : 0.f;
         const float ax0 = 1.f - rc.fw, ax1 = rc.fw;
         const float bil = (1.f - rc.fh) * fmaf(ax1, v01, ax0 * v00) + rc.fh * fmaf(ax1, v11, ax0 * v10);
         float* sp = S.sacc + static_cast<size_t>(q) * KG + (idx - q * K);
-        *sp = fmaf(frac_weight(rc.ft, k.z != rc.t0), bil, *sp);
+        *sp = fmaf(frac_weight(rc.ft, z != rc.t0), bil, *sp);
       }
     }
   }
@@ -392,16 +431,18 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   for (int i = 0; i < kTPW + 1; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(S.sbuf);  // P~^T after the transposition
   {
-    const __nv_bfloat16* vg = static_cast<const __nv_bfloat16*>(P.v);
-    for (int c = next_chunk(E, S.mask, masks, 0, nch); c < nch; c = next_chunk(E, S.mask, masks, c + 1, nch)) {
-      const Chunk k = chunk_at(E, S.mask, masks, c);
-      const int ncw = k.xb - k.xa + 1;
-      const int zrel = k.z - E.zlo + 1;
-      const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
+    Chunk k;
+    for (bool have = chunk_first(E, S.mask, masks, nz, k); have; have = chunk_next(E, S.mask, masks, nz, k)) {
       __syncthreads();  // the previous chunk's product is done with the key buffer and the dense tile
       // the values land while the weights are scattered and converted
-      issue_keys<DCH>(P, T, S.kbuf, L.rs, vg, P.v_ld, k);
+      if (tma) {
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &vmap, kbar);
+      } else {
+        issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, vg, P.v_ld);
+      }
       zero_tiles<kQ>(S.sbuf, L.sld, k.m);
+      const int z = E.zlo + k.zr, ya = chunk_ya(E, k), xa = chunk_xa(E, k);
+      const int hlo = S.bstart[k.zr], hhi = S.bstart[k.zr + 2];
       __syncthreads();
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
@@ -412,12 +453,17 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
           continue;
         scatter_fixed_row(reinterpret_cast<int*>(S.sbuf) + static_cast<size_t>(q) * L.sld,
-                          (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa), ncw, rc,
-                          pv * frac_weight(rc.ft, k.z != rc.t0) * S.qsc[q], P.H, P.W);
+                          (rc.h0 - ya) * kst + (rc.w0 - xa), kst, rc,
+                          pv * frac_weight(rc.ft, z != rc.t0) * S.qsc[q], P.H, P.W);
       }
       __syncthreads();
       transpose_fixed(S.sbuf, L.sld, k.m, S.qsc + kQ);
-      cp_async_wait_all();
+      if (tma) {
+        wait_keys(kbar, kphase, S.dead, P.status);
+        kphase ^= 1u;
+      } else {
+        cp_async_wait_all();
+      }
       __syncthreads();
       dq_product<DCH, kTPW>(tp, r, S.kbuf, L.rs, nt0, nt1, k.m, o);
     }
@@ -502,31 +548,66 @@ bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
 }
 
 template <int DCH>
-static cudaError_t launch_fwd_tc_t(const AttnParams& P, const TcLaunch& L, cudaStream_t s) {
+static cudaError_t launch_fwd_tc_t(const AttnParams& P, const TcLaunch& L, const CUtensorMap& km,
+                                   const CUtensorMap& vm, cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(tc::fwd::dsa_fwd_tc_kernel<DCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
-  tc::fwd::dsa_fwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L);
+  tc::fwd::dsa_fwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L, km, vm);
   return cudaGetLastError();
 }
 
-cudaError_t launch_attn_fwd_tc(const AttnParams& P, const TcLaunch& L, cudaStream_t s) {
+bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base, long long ld, int rs) {
+  // MSL_TC_LOADS=cpasync selects the cp.async loads (both paths compute the same results)
+  const char* sel = getenv("MSL_TC_LOADS");
+  const bool off = sel && strcmp(sel, "cpasync") == 0;
+  using Encode = PFN_cuTensorMapEncodeTiled_v12000;
+  static const Encode encode = []() -> Encode {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<Encode>(fn);
+  }();
+  memset(map, 0, sizeof(*map));
+  if (off || !encode || !base) return false;
+  // 16-byte aligned base and row stride; the box (rs channels x 8 columns) within the tensor's extents
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 2) & 15) || (rs * 2) % 16 != 0 || rs > 256) return false;
+  if (static_cast<long long>(P.nh) * P.d < rs || P.W < 8 || ld < static_cast<long long>(P.nh) * P.d) return false;
+  const cuuint64_t dims[5] = {static_cast<cuuint64_t>(P.nh) * P.d, static_cast<cuuint64_t>(P.W),
+                              static_cast<cuuint64_t>(P.H), static_cast<cuuint64_t>(P.kv_frames),
+                              static_cast<cuuint64_t>(P.B)};
+  const cuuint64_t row = static_cast<cuuint64_t>(ld) * 2;
+  const cuuint64_t strides[4] = {row, row * P.W, row * P.W * P.H, row * static_cast<cuuint64_t>(P.Nkv)};
+  const cuuint32_t box[5] = {static_cast<cuuint32_t>(rs), 8, 1, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  if (strides[3] >= (1ull << 40)) return false;
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_attn_fwd_tc(const AttnParams& P, const TcLaunch& L0, cudaStream_t s) {
+  TcLaunch L = L0;
+  CUtensorMap km, vm;
+  L.tma = make_key_map(&km, P, P.k, P.k_ld, L.rs) && make_key_map(&vm, P, P.v, P.v_ld, L.rs);
   switch (P.d / 8) {
-    case 2: return launch_fwd_tc_t<2>(P, L, s);
-    case 3: return launch_fwd_tc_t<3>(P, L, s);
-    case 4: return launch_fwd_tc_t<4>(P, L, s);
-    case 5: return launch_fwd_tc_t<5>(P, L, s);
-    case 6: return launch_fwd_tc_t<6>(P, L, s);
-    case 7: return launch_fwd_tc_t<7>(P, L, s);
-    case 8: return launch_fwd_tc_t<8>(P, L, s);
-    case 9: return launch_fwd_tc_t<9>(P, L, s);
-    case 10: return launch_fwd_tc_t<10>(P, L, s);
-    case 11: return launch_fwd_tc_t<11>(P, L, s);
-    case 12: return launch_fwd_tc_t<12>(P, L, s);
-    case 13: return launch_fwd_tc_t<13>(P, L, s);
-    case 14: return launch_fwd_tc_t<14>(P, L, s);
-    case 15: return launch_fwd_tc_t<15>(P, L, s);
-    case 16: return launch_fwd_tc_t<16>(P, L, s);
+    case 2: return launch_fwd_tc_t<2>(P, L, km, vm, s);
+    case 3: return launch_fwd_tc_t<3>(P, L, km, vm, s);
+    case 4: return launch_fwd_tc_t<4>(P, L, km, vm, s);
+    case 5: return launch_fwd_tc_t<5>(P, L, km, vm, s);
+    case 6: return launch_fwd_tc_t<6>(P, L, km, vm, s);
+    case 7: return launch_fwd_tc_t<7>(P, L, km, vm, s);
+    case 8: return launch_fwd_tc_t<8>(P, L, km, vm, s);
+    case 9: return launch_fwd_tc_t<9>(P, L, km, vm, s);
+    case 10: return launch_fwd_tc_t<10>(P, L, km, vm, s);
+    case 11: return launch_fwd_tc_t<11>(P, L, km, vm, s);
+    case 12: return launch_fwd_tc_t<12>(P, L, km, vm, s);
+    case 13: return launch_fwd_tc_t<13>(P, L, km, vm, s);
+    case 14: return launch_fwd_tc_t<14>(P, L, km, vm, s);
+    case 15: return launch_fwd_tc_t<15>(P, L, km, vm, s);
+    case 16: return launch_fwd_tc_t<16>(P, L, km, vm, s);
     default: return cudaErrorInvalidValue;
   }
 }

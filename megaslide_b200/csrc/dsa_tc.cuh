@@ -2,8 +2,12 @@
 // attention (forward: dsa_tc.cu, backward: dsa_tc_bwd.cu).  Both kernels run 512 threads per CTA on
 // a tile of queries of one frame, one head and one sample, walk the tile's key envelope one frame
 // ("plane") at a time in chunks of at most `maxkeys` keys, and do the dense per-chunk products with
-// mma.sync (bf16 in, fp32 accumulate) on operands staged in shared memory by cp.async.
+// mma.sync (bf16 in, fp32 accumulate) on operands in shared memory.  Key / value chunks arrive by TMA
+// tensor copies (one 8-key box per chunk row segment, completing on an mbarrier) when the K / V
+// buffers meet TMA's alignment rules, else by cp.async.
 #pragma once
+
+#include <cuda.h>
 
 #include <math.h>
 #include <stdint.h>
@@ -66,6 +70,38 @@ __device__ __forceinline__ void cp_async4(uint32_t saddr, const void* g) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+// orders this thread's earlier generic-proxy shared-memory accesses before its later TMA writes
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// 5-d tiled tensor copy global -> this CTA's shared memory, completing on mbarrier `bar` (no multicast)
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], "
+      "[%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 // ------------------------------------------------------------------------------ tile geometry
 struct TileCtx {
@@ -112,7 +148,19 @@ __device__ __forceinline__ int axis_chunk_of(int v, int lo, int len, int nchunks
 struct Env {
   int zlo, zhi, ylo, yhi, xlo, xhi;
   int cw, R, ny, nx;  // column-chunk width, rows per chunk, chunk counts
+  int kst;            // key row stride in a chunk: cw rounded up to 8 (chunk key = (y - ya) * kst + x - xa)
 };
+
+// Chunk shape for an envelope [ylo, yhi] x [xlo, xhi] and `maxkeys` keys per chunk: columns split into
+// windows of at most maxkeys / 2, rows into windows of maxkeys / kst (>= 2, as maxkeys % 16 == 0).
+__device__ __forceinline__ void chunk_shape(Env& E, int maxkeys) {
+  const int nxk = E.xhi - E.xlo + 1;
+  E.cw = nxk <= maxkeys / 2 ? nxk : maxkeys / 2;
+  E.kst = (E.cw + 7) & ~7;
+  E.R = maxkeys / E.kst;
+  E.ny = axis_chunks(E.ylo, E.yhi, E.R);
+  E.nx = axis_chunks(E.xlo, E.xhi, E.cw);
+}
 
 // Base-grid values 2a/max(S-1,1) - 1 of the window positions a tile can reach, per axis, computed once
 // per CTA with the same float32 operations as base_grid(); tz covers frames tg - kt/2 .. tg + kt/2,
@@ -383,75 +431,137 @@ __device__ __forceinline__ uint32_t corner_tiles(int k00, int ncw, bool xok, boo
   return m;
 }
 
-// The envelope walk: chunk c = ((z - zlo) * ny + iy) * nx + ix covers frame z, rows [ya, yb] and
-// columns [xa, xb]; its keys are numbered (y - ya) * ncw + (x - xa) and m marks the 16-key tiles any
-// sample of the tile touches (every tile of the chunk when the masks are not kept).  Tile masks are
-// kept per plane for up to kMaskChunks chunks.
+// The envelope walk: chunk (zr, iy, ix) covers frame z = zlo + zr, rows [ya, yb] and columns
+// [xa, xb] (windows of R rows / cw columns with one row / column of overlap, so that the four corners
+// a sample has in a plane fall in one chunk).  Its keys are numbered (y - ya) * kst + (x - xa); m marks
+// the 16-key tiles any sample of the tile touches (every tile of the chunk when no masks are kept).
+// Tile masks are kept per plane for up to kMaskChunks chunks.
 constexpr int kMaskChunks = 4;
 
 struct Chunk {
-  int z, iy, ix, ya, yb, xa, xb;
+  int zr, iy, ix;
   uint32_t m;
 };
 
-__device__ __forceinline__ Chunk chunk_at(const Env& E, const uint32_t* mask, bool masks, int c) {
-  Chunk k;
-  const int per_z = E.ny * E.nx;
-  const int zr = c / per_z, rem = c - zr * per_z;
-  k.iy = rem / E.nx;
-  k.ix = rem - k.iy * E.nx;
-  k.z = E.zlo + zr;
-  k.ya = E.ylo + k.iy * (E.R - 1);
-  k.yb = min(k.ya + E.R - 1, E.yhi);
-  k.xa = E.xlo + k.ix * (E.cw - 1);
-  k.xb = min(k.xa + E.cw - 1, E.xhi);
-  const int ntile = ((k.yb - k.ya + 1) * (k.xb - k.xa + 1) + 15) >> 4;
-  k.m = masks ? mask[(zr + 1) * kMaskChunks + rem] : (ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u);
-  return k;
+__device__ __forceinline__ int chunk_ya(const Env& E, const Chunk& k) { return E.ylo + k.iy * (E.R - 1); }
+__device__ __forceinline__ int chunk_yb(const Env& E, const Chunk& k) { return min(chunk_ya(E, k) + E.R - 1, E.yhi); }
+__device__ __forceinline__ int chunk_xa(const Env& E, const Chunk& k) { return E.xlo + k.ix * (E.cw - 1); }
+__device__ __forceinline__ int chunk_xb(const Env& E, const Chunk& k) { return min(chunk_xa(E, k) + E.cw - 1, E.xhi); }
+
+// the chunk's tile mask; 0 = nothing to do
+__device__ __forceinline__ uint32_t chunk_mask(const Env& E, const uint32_t* mask, bool masks, const Chunk& k) {
+  if (masks) return mask[(k.zr + 1) * kMaskChunks + k.iy * E.nx + k.ix];
+  const int ntile = ((chunk_yb(E, k) - chunk_ya(E, k) + 1) * E.kst + 15) >> 4;
+  return ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u;
 }
 
-// the first chunk at or after c with a touched tile, nch when there is none
-__device__ __forceinline__ int next_chunk(const Env& E, const uint32_t* mask, bool masks, int c, int nch) {
-  if (!masks) return c;
-  const int per_z = E.ny * E.nx;
-  for (; c < nch; ++c) {
-    const int zr = c / per_z;
-    if (mask[(zr + 1) * kMaskChunks + (c - zr * per_z)]) break;
+// moves k to the first chunk at or after it with a touched tile; false when the walk is over
+__device__ __forceinline__ bool chunk_seek(const Env& E, const uint32_t* mask, bool masks, int nz, Chunk& k) {
+  while (k.zr < nz) {
+    k.m = chunk_mask(E, mask, masks, k);
+    if (k.m) return true;
+    if (++k.ix == E.nx) {
+      k.ix = 0;
+      if (++k.iy == E.ny) {
+        k.iy = 0;
+        ++k.zr;
+      }
+    }
   }
-  return c;
+  return false;
+}
+__device__ __forceinline__ bool chunk_first(const Env& E, const uint32_t* mask, bool masks, int nz, Chunk& k) {
+  k.zr = k.iy = k.ix = 0;
+  return chunk_seek(E, mask, masks, nz, k);
+}
+__device__ __forceinline__ bool chunk_next(const Env& E, const uint32_t* mask, bool masks, int nz, Chunk& k) {
+  if (++k.ix == E.nx) {
+    k.ix = 0;
+    if (++k.iy == E.ny) {
+      k.iy = 0;
+      ++k.zr;
+    }
+  }
+  return chunk_seek(E, mask, masks, nz, k);
 }
 
 // Row of chunk key `key` in the K/V buffers of the sample, -1 past the chunk and outside the volume /
 // K-V window.
-__device__ __forceinline__ int chunk_key_row(const AttnParams& P, const Chunk& k, int key) {
-  const int ncw = k.xb - k.xa + 1;
-  // key / ncw exactly: (key + 0.5) / ncw is at least 1 / (2 ncw) away from an integer
-  const int ky = static_cast<int>((static_cast<float>(key) + 0.5f) * (1.f / static_cast<float>(ncw)));
-  const int y = k.ya + ky, x = k.xa + (key - ky * ncw);
-  const int zl = k.z - P.kv_frame0;
-  const bool ok = y <= k.yb && zl >= 0 && zl < P.kv_frames && y >= 0 && y < P.H && x >= 0 && x < P.W;
+__device__ __forceinline__ int chunk_key_row(const AttnParams& P, const Env& E, const Chunk& k, int key) {
+  // key / kst exactly: (key + 0.5) / kst is at least 1 / (2 kst) away from an integer
+  const int ky = static_cast<int>((static_cast<float>(key) + 0.5f) * (1.f / static_cast<float>(E.kst)));
+  const int y = chunk_ya(E, k) + ky, x = chunk_xa(E, k) + (key - ky * E.kst);
+  const int zl = E.zlo + k.zr - P.kv_frame0;
+  const bool ok = y <= chunk_yb(E, k) && x <= chunk_xb(E, k) && zl >= 0 && zl < P.kv_frames && y >= 0 && y < P.H &&
+                  x >= 0 && x < P.W;
   return ok ? (zl * P.H + y) * P.W + x : -1;
 }
 
-// Starts the copy of the chunk's keys in the 16-key tiles of k.m into kbuf rows (one thread per key
-// row, one 16-byte cp.async per 8 channels); rows without a key are zeroed with plain stores.  The
-// copies land at the caller's cp_async_wait_all().
+// cp.async path: starts the copy of the chunk's keys in the tiles of k.m into kbuf rows (lanes along
+// the 16-byte pieces of a row); rows without a key are zeroed.  The copies land at the caller's
+// cp_async_wait_all().
 template <int DCH>
-__device__ __forceinline__ void issue_keys(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
-                                           const __nv_bfloat16* base, long long ld, const Chunk& k) {
+__device__ __forceinline__ void issue_keys(const AttnParams& P, const TileCtx& T, const Env& E, const Chunk& k,
+                                           __nv_bfloat16* kbuf, int rs, const __nv_bfloat16* base, long long ld) {
   const __nv_bfloat16* gb = base + static_cast<long long>(T.b) * P.Nkv * ld + T.head * P.d;
-  const int nkeys = __popc(k.m) * 16;
-  for (int i = threadIdx.x; i < nkeys; i += kThreads) {
-    const int key = nth_bit(k.m, i >> 4) * 16 + (i & 15);
-    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs;
-    const int row = chunk_key_row(P, k, key);
-    if (row >= 0) {
-      const __nv_bfloat16* src = gb + static_cast<long long>(row) * ld;
-#pragma unroll
-      for (int ch = 0; ch < DCH; ++ch) cp_async16(smem_u32(dst + ch * 8), src + ch * 8);
-    } else {
-#pragma unroll
-      for (int ch = 0; ch < DCH; ++ch) *reinterpret_cast<uint4*>(dst + ch * 8) = make_uint4(0u, 0u, 0u, 0u);
+  const int items = __popc(k.m) * 16 * DCH;
+  for (int idx = threadIdx.x; idx < items; idx += kThreads) {
+    const int slot = idx / DCH, ch = idx - slot * DCH;  // DCH is a constant: multiply-shift
+    const int key = nth_bit(k.m, slot >> 4) * 16 + (slot & 15);
+    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs + ch * 8;
+    const int row = chunk_key_row(P, E, k, key);
+    if (row >= 0)
+      cp_async16(smem_u32(dst), gb + static_cast<long long>(row) * ld + ch * 8);
+    else
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// TMA path: warp 0 copies the chunk's 8-key boxes (box i = keys 8i .. 8i+7 = one row segment; only
+// boxes in touched tiles) with tensor map `map` (dims: channel, x, y, frame, sample; box rs x 8); the
+// copies complete on mbarrier `bar`.  Coordinates outside the volume / K-V window read as zeros.  The
+// half tile past the last box, when the chunk ends inside a touched tile, is zeroed by warps 1-3.
+__device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCtx& T, const Env& E, const Chunk& k,
+                                               __nv_bfloat16* kbuf, int rs, const CUtensorMap* map, uint32_t bar) {
+  const int gpr = E.kst >> 3;  // boxes per chunk row
+  const int nbox = (chunk_yb(E, k) - chunk_ya(E, k) + 1) * gpr;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    if (lane == 0) {
+      // boxes in touched tiles: two per tile, one for a last tile cut in half (nbox / 2 <= 16)
+      const int full = nbox >> 1;
+      const uint32_t below = full >= 32 ? 0xffffffffu : (1u << full) - 1u;
+      const int cnt = 2 * __popc(k.m & below) + ((nbox & 1) ? static_cast<int>((k.m >> full) & 1u) : 0);
+      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(cnt) * 16u * static_cast<uint32_t>(rs));
+    }
+    __syncwarp();
+    fence_proxy_async();
+    const int ya = chunk_ya(E, k), xa = chunk_xa(E, k), zl = E.zlo + k.zr - P.kv_frame0;
+    const uint32_t dst0 = smem_u32(kbuf);
+    for (int i = lane; i < nbox; i += 32) {
+      if (!((k.m >> (i >> 1)) & 1u)) continue;
+      const int row = i / gpr, g = i - row * gpr;
+      tma_load_5d(dst0 + static_cast<uint32_t>(i) * 16u * static_cast<uint32_t>(rs), map, bar, T.head * P.d,
+                  xa + g * 8, ya + row, zl, T.b);
+    }
+  } else if ((nbox & 1) && ((k.m >> (nbox >> 1)) & 1u)) {
+    const int words = rs;  // 8 keys x rs bf16 = rs 16-byte words
+    uint4* tail = reinterpret_cast<uint4*>(kbuf + static_cast<size_t>(nbox) * 8 * rs);
+    for (int i = threadIdx.x - 32; i < words; i += kThreads - 32) tail[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// Waits for the TMA copies of phase `parity` on mbarrier bar.  Bounded: after about a second the CTA
+// stops waiting and issuing (flag *dead, status MSL_STATUS_TIMEOUT); its results are then invalid.
+__device__ __forceinline__ void wait_keys(uint32_t bar, uint32_t parity, volatile int* dead, uint32_t* status) {
+  if (mbar_try_wait(bar, parity) || *dead) return;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*dead) return;
+    if (global_ns() - t0 > 1000000000ull) {
+      *dead = 1;
+      if (status) atomicOr(status, MSL_STATUS_TIMEOUT);
+      return;
     }
   }
 }

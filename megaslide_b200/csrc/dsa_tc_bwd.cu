@@ -59,6 +59,8 @@ struct Smem {
   int* bcur;                // [32]            bucket counts, then fill cursors
   uint32_t* mask;           // [32][4]         16-key tiles touched per (plane, chunk)
   unsigned short* hits;     // [32 * K]        sample indices q * K + j sorted by frame bucket
+  unsigned long long* kbar; // mbarrier of the key buffer's TMA copies
+  int* dead;                // set when a TMA wait gave up
 };
 
 __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, const TcLaunch& L) {
@@ -97,13 +99,18 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   s.mask = reinterpret_cast<uint32_t*>(base + off);
   off += 32 * kMaxMaskChunks * 4;
   s.hits = reinterpret_cast<unsigned short*>(base + off);
+  off += static_cast<size_t>(kQ) * P.K * 2;
+  // last: the setup's offset staging spills from the key buffer into the regions after it
+  off = (off + 7) & ~static_cast<size_t>(7);
+  s.kbar = reinterpret_cast<unsigned long long*>(base + off);
+  s.dead = reinterpret_cast<int*>(base + off + 8);
   return s;
 }
 
 // shared memory besides the key buffer, the two dense tiles and the key table
 size_t smem_fixed(const AttnParams& P, int rs) {
   return static_cast<size_t>(kQ) * rs * 2 * 2 + static_cast<size_t>(kQ) * P.K * (8 + 4 + 12 + 2) + kEnvWords * 4 +
-         kQ * (8 + 4 + 16) + (36 + 32 + 32 * kMaxMaskChunks) * 4 + 256;
+         kQ * (8 + 4 + 16) + (36 + 32 + 32 * kMaxMaskChunks) * 4 + 24 + 256;
 }
 
 // In-plane terms of one sample from a dense row (corners outside the volume count as 0, like
@@ -206,8 +213,10 @@ __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const Tile
 }
 
 template <int DCH>
-__global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParams P, const TcLaunch L) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParams P, const TcLaunch L,
+                                                                  const __grid_constant__ CUtensorMap kmap,
+                                                                  const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   const Smem S = carve(smem_raw, P, L);
   const TileCtx T = decode_tile(P, L, kTileH);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -238,6 +247,17 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   if (threadIdx.x < 32) S.bcur[threadIdx.x] = 0;
   if (threadIdx.x < 32 * kMaxMaskChunks) S.mask[threadIdx.x] = 0u;
   if (sub == 0) S.prow[qi] = (static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow;
+  // TMA destinations are 128-byte aligned: boxes start at multiples of 8 keys x rs (rs % 8 == 0) bf16
+  const bool tma = L.tma && (smem_u32(S.kbuf) & 127u) == 0u;
+  const uint32_t kbar = smem_u32(S.kbar);
+  if (threadIdx.x == 0) {
+    *S.dead = 0;
+    if (tma) {
+      mbar_init(kbar, 1);
+      fence_mbar_init();
+    }
+  }
+  uint32_t kphase = 0;
   fill_tabs(P, T, kTileH, tabz, taby, tabx);
 
   // ---- stage the tile's offsets (this head), Q and dO rows with one wave of cp.async
@@ -335,13 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   E.zlo = S.env[0]; E.zhi = S.env[1]; E.ylo = S.env[2]; E.yhi = S.env[3]; E.xlo = S.env[4]; E.xhi = S.env[5];
   const bool any = E.zlo <= E.zhi && E.ylo <= E.yhi && E.xlo <= E.xhi;
   if (any) {
-    const int nxk = E.xhi - E.xlo + 1;
-    E.cw = nxk <= L.maxkeys / 2 ? nxk : L.maxkeys / 2;
-    E.R = L.maxkeys / E.cw;
-    E.ny = axis_chunks(E.ylo, E.yhi, E.R);
-    E.nx = axis_chunks(E.xlo, E.xhi, E.cw);
+    chunk_shape(E, L.maxkeys);
   } else {
     E.cw = E.R = E.ny = E.nx = 1;
+    E.kst = 8;
   }
   const bool split = E.ny * E.nx > 1;
   // records hold t0 - zlo + 1 in 5 bits and h0 - ylo, w0 - xlo in 8 bits
@@ -378,8 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
           if (masks) {
             const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
             const int ya = E.ylo + iy * (E.R - 1), xa = E.xlo + ix * (E.cw - 1);
-            const int ncw = min(xa + E.cw - 1, E.xhi) - xa + 1;
-            bits = corner_tiles((h0 - ya) * ncw + (w0 - xa), ncw, w0 + 1 < P.W, h0 + 1 < P.H);
+            bits = corner_tiles((h0 - ya) * E.kst + (w0 - xa), E.kst, w0 + 1 < P.W, h0 + 1 < P.H);
             const int chk = iy * E.nx + ix;
             if (t0 >= E.zlo) pa = dz * kMaxMaskChunks + chk;           // plane z = t0 (zrel = dz)
             if (t0 + 1 <= E.zhi) pb = (dz + 1) * kMaxMaskChunks + chk; // plane z = t0 + 1
@@ -433,37 +449,53 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
 
   // ---- pass 1: V side (dp_j and the value part of the coordinate gradient), hits CTA-wide; the next
   // chunk's values load while this chunk's samples run, and after the last one pass 2's first keys
-  const int nch = work ? (E.zhi - E.zlo + 1) * E.ny * E.nx : 0;
+  const int nz = work ? E.zhi - E.zlo + 1 : 0;
   const __nv_bfloat16* kg = static_cast<const __nv_bfloat16*>(P.k);
   const __nv_bfloat16* vg = static_cast<const __nv_bfloat16*>(P.v);
-  const int c_first = next_chunk(E, S.mask, masks, 0, nch);
+  const int kst = E.kst;
+  Chunk k2;  // pass 2's first chunk
+  const bool have2 = chunk_first(E, S.mask, masks, nz, k2);
   {
-    int c = c_first;
-    if (c < nch) issue_keys<DCH>(P, T, S.kbuf, L.rs, vg, P.v_ld, chunk_at(E, S.mask, masks, c));
-    while (c < nch) {
-      const Chunk k = chunk_at(E, S.mask, masks, c);
-      const int ncw = k.xb - k.xa + 1;
-      const int zrel = k.z - E.zlo + 1;
-      const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
-      cp_async_wait_all();
+    Chunk k = k2;
+    bool have = have2;
+    if (have) {
+      if (tma) {
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &vmap, kbar);
+      } else {
+        issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, vg, P.v_ld);
+      }
+    }
+    while (have) {
+      const Chunk cur = k;
+      if (tma) {
+        wait_keys(kbar, kphase, S.dead, P.status);
+        kphase ^= 1u;
+      } else {
+        cp_async_wait_all();
+      }
       __syncthreads();
-      dense_tiles<DCH, kWPG>(S.kbuf, S.dos + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, k.m);
+      dense_tiles<DCH, kWPG>(S.kbuf, S.dos + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, cur.m);
       __syncthreads();
-      c = next_chunk(E, S.mask, masks, c + 1, nch);
-      if (c < nch)
-        issue_keys<DCH>(P, T, S.kbuf, L.rs, vg, P.v_ld, chunk_at(E, S.mask, masks, c));
-      else
-        issue_keys<DCH>(P, T, S.kbuf, L.rs, kg, P.k_ld, chunk_at(E, S.mask, masks, c_first));
+      have = chunk_next(E, S.mask, masks, nz, k);
+      const bool v = have;
+      if (!have) k = k2;
+      if (tma) {
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, v ? &vmap : &kmap, kbar);
+      } else {
+        issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, v ? vg : kg, v ? P.v_ld : P.k_ld);
+      }
+      const int z = E.zlo + cur.zr, ya = chunk_ya(E, cur), xa = chunk_xa(E, cur);
+      const int hlo = S.bstart[cur.zr], hhi = S.bstart[cur.zr + 2];
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
         const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
         const Rec rc = decode_rec(S.rec[idx], E);
-        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
+        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
           continue;
-        const bool upper = k.z != rc.t0;
+        const bool upper = z != rc.t0;
         const float az = frac_weight(rc.ft, upper);
-        const PlaneTerms pt_ = plane_terms(S.sa + static_cast<size_t>(q) * L.sld, (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa),
-                                           ncw, rc, P.H, P.W);
+        const PlaneTerms pt_ =
+            plane_terms(S.sa + static_cast<size_t>(q) * L.sld, (rc.h0 - ya) * kst + (rc.w0 - xa), kst, rc, P.H, P.W);
         S.sv[idx] = fmaf(az, pt_.bil, S.sv[idx]);
         float* gg = S.g3 + 3 * idx;
         gg[0] += upper ? pt_.bil : -pt_.bil;
@@ -521,66 +553,80 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   const __nv_bfloat16* tpp = reinterpret_cast<const __nv_bfloat16*>(S.sa);  // P~^T after the transposition
   // (the first chunk's keys were issued at the end of pass 1; each later chunk's keys load while the
   // previous chunk's P~ is converted and its dV flushed)
-  for (int c = c_first; c < nch;) {
-    const Chunk k = chunk_at(E, S.mask, masks, c);
-    const int ncw = k.xb - k.xa + 1;
-    const int zrel = k.z - E.zlo + 1;
-    const int hlo = S.bstart[zrel - 1], hhi = S.bstart[zrel + 1];
-    cp_async_wait_all();
-    __syncthreads();  // keys landed; the previous chunk's dV flush is done with key_off and sa
-    for (int i = threadIdx.x; i < __popc(k.m) * 16; i += kThreads) {
-      const int key = nth_bit(k.m, i >> 4) * 16 + (i & 15);
-      S.key_off[key] = chunk_key_row(P, k, key);
+  {
+    Chunk k = k2;
+    bool have = have2;
+    while (have) {
+      const Chunk cur = k;
+      const int z = E.zlo + cur.zr, ya = chunk_ya(E, cur), xa = chunk_xa(E, cur);
+      const int hlo = S.bstart[cur.zr], hhi = S.bstart[cur.zr + 2];
+      if (tma) {
+        wait_keys(kbar, kphase, S.dead, P.status);
+        kphase ^= 1u;
+      } else {
+        cp_async_wait_all();
+      }
+      __syncthreads();  // keys landed; the previous chunk's dV flush is done with key_off and sa
+      for (int i = threadIdx.x; i < __popc(cur.m) * 16; i += kThreads) {
+        const int key = nth_bit(cur.m, i >> 4) * 16 + (i & 15);
+        S.key_off[key] = chunk_key_row(P, E, cur, key);
+      }
+      zero_tiles<kQ>(S.sb, L.sld, cur.m);
+      dense_tiles<DCH, kWPG>(S.kbuf, S.qs + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, cur.m);
+      __syncthreads();
+      // key part of the coordinate gradient (reads S) and the dS~ scatter (into sb)
+      for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+        const int idx = S.hits[i];
+        const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+        const Rec rc = decode_rec(S.rec[idx], E);
+        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
+          continue;
+        const bool upper = z != rc.t0;
+        const float az = frac_weight(rc.ft, upper);
+        const int k00 = (rc.h0 - ya) * kst + (rc.w0 - xa);
+        const PlaneTerms pt_ = plane_terms(S.sa + static_cast<size_t>(q) * L.sld, k00, kst, rc, P.H, P.W);
+        const float dsq = S.sv[idx];
+        float* gg = S.g3 + 3 * idx;
+        gg[0] = fmaf(dsq, upper ? pt_.bil : -pt_.bil, gg[0]);
+        gg[1] = fmaf(dsq * az, pt_.dvy, gg[1]);
+        gg[2] = fmaf(dsq * az, pt_.dvx, gg[2]);
+        scatter_fixed_row(reinterpret_cast<int*>(S.sb) + static_cast<size_t>(q) * L.sld, k00, kst, rc,
+                          dsq * az * S.qsc[q], P.H, P.W);
+      }
+      __syncthreads();
+      // dS~ -> bf16 [key][query]; S no longer needed: clear sa for P~
+      transpose_fixed(S.sb, L.sld, cur.m, S.qsc + kQ);
+      zero_tiles<kQ>(S.sa, L.sld, cur.m);
+      __syncthreads();
+      // P~ scatter (into sa), dQ += dS~ . K_chunk, dK_chunk = dS~^T . Q
+      for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
+        const int idx = S.hits[i];
+        const unsigned long long v = S.rec[idx];
+        if (!((v >> kBitKeep) & 1ull)) continue;
+        const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
+        const Rec rc = decode_rec(v, E);
+        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
+          continue;
+        const float pv = __ldg(P.probs + S.prow[q] * K + (idx - q * K)) * P.drop_keep_scale;
+        scatter_fixed_row(reinterpret_cast<int*>(S.sa) + static_cast<size_t>(q) * L.sld,
+                          (rc.h0 - ya) * kst + (rc.w0 - xa), kst, rc,
+                          pv * frac_weight(rc.ft, z != rc.t0) * S.qsc[2 * kQ + q], P.H, P.W);
+      }
+      dq_product<DCH, kTPW>(tds, r, S.kbuf, L.rs, nt0, nt1, cur.m, oq);
+      kv_product_flush<DCH>(P, T, L, tds, S.qs, S.key_off, cur.m, P.dk_acc);
+      __syncthreads();  // the key buffer is free
+      have = chunk_next(E, S.mask, masks, nz, k);
+      if (have) {
+        if (tma) {
+          if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &kmap, kbar);
+        } else {
+          issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, kg, P.k_ld);
+        }
+      }
+      transpose_fixed(S.sa, L.sld, cur.m, S.qsc + 3 * kQ);
+      __syncthreads();
+      kv_product_flush<DCH>(P, T, L, tpp, S.dos, S.key_off, cur.m, P.dv_acc);
     }
-    zero_tiles<kQ>(S.sb, L.sld, k.m);
-    dense_tiles<DCH, kWPG>(S.kbuf, S.qs + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, k.m);
-    __syncthreads();
-    // key part of the coordinate gradient (reads S) and the dS~ scatter (into sb)
-    for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
-      const int idx = S.hits[i];
-      const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
-      const Rec rc = decode_rec(S.rec[idx], E);
-      if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
-        continue;
-      const bool upper = k.z != rc.t0;
-      const float az = frac_weight(rc.ft, upper);
-      const int k00 = (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa);
-      const PlaneTerms pt_ = plane_terms(S.sa + static_cast<size_t>(q) * L.sld, k00, ncw, rc, P.H, P.W);
-      const float dsq = S.sv[idx];
-      float* gg = S.g3 + 3 * idx;
-      gg[0] = fmaf(dsq, upper ? pt_.bil : -pt_.bil, gg[0]);
-      gg[1] = fmaf(dsq * az, pt_.dvy, gg[1]);
-      gg[2] = fmaf(dsq * az, pt_.dvx, gg[2]);
-      scatter_fixed_row(reinterpret_cast<int*>(S.sb) + static_cast<size_t>(q) * L.sld, k00, ncw, rc,
-                        dsq * az * S.qsc[q], P.H, P.W);
-    }
-    __syncthreads();
-    // dS~ -> bf16 [key][query]; S no longer needed: clear sa for P~
-    transpose_fixed(S.sb, L.sld, k.m, S.qsc + kQ);
-    zero_tiles<kQ>(S.sa, L.sld, k.m);
-    __syncthreads();
-    // P~ scatter (into sa), dQ += dS~ . K_chunk, dK_chunk = dS~^T . Q
-    for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
-      const int idx = S.hits[i];
-      const unsigned long long v = S.rec[idx];
-      if (!((v >> kBitKeep) & 1ull)) continue;
-      const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
-      const Rec rc = decode_rec(v, E);
-      if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
-        continue;
-      const float pv = __ldg(P.probs + S.prow[q] * K + (idx - q * K)) * P.drop_keep_scale;
-      scatter_fixed_row(reinterpret_cast<int*>(S.sa) + static_cast<size_t>(q) * L.sld,
-                        (rc.h0 - k.ya) * ncw + (rc.w0 - k.xa), ncw, rc,
-                        pv * frac_weight(rc.ft, k.z != rc.t0) * S.qsc[2 * kQ + q], P.H, P.W);
-    }
-    dq_product<DCH, kTPW>(tds, r, S.kbuf, L.rs, nt0, nt1, k.m, oq);
-    kv_product_flush<DCH>(P, T, L, tds, S.qs, S.key_off, k.m, P.dk_acc);
-    __syncthreads();  // the key buffer is free
-    c = next_chunk(E, S.mask, masks, c + 1, nch);
-    if (c < nch) issue_keys<DCH>(P, T, S.kbuf, L.rs, kg, P.k_ld, chunk_at(E, S.mask, masks, c));
-    transpose_fixed(S.sa, L.sld, k.m, S.qsc + 3 * kQ);
-    __syncthreads();
-    kv_product_flush<DCH>(P, T, L, tpp, S.dos, S.key_off, k.m, P.dv_acc);
   }
   __syncthreads();
 
@@ -661,31 +707,35 @@ bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
 }
 
 template <int DCH>
-static cudaError_t launch_bwd_tc_t(const AttnParams& P, const TcLaunch& L, cudaStream_t s) {
+static cudaError_t launch_bwd_tc_t(const AttnParams& P, const TcLaunch& L, const CUtensorMap& km,
+                                   const CUtensorMap& vm, cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(tc::bwd::dsa_bwd_tc_kernel<DCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
-  tc::bwd::dsa_bwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L);
+  tc::bwd::dsa_bwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L, km, vm);
   return cudaGetLastError();
 }
 
-cudaError_t launch_attn_bwd_tc(const AttnParams& P, const TcLaunch& L, cudaStream_t s) {
+cudaError_t launch_attn_bwd_tc(const AttnParams& P, const TcLaunch& L0, cudaStream_t s) {
+  TcLaunch L = L0;
+  CUtensorMap km, vm;
+  L.tma = make_key_map(&km, P, P.k, P.k_ld, L.rs) && make_key_map(&vm, P, P.v, P.v_ld, L.rs);
   switch (P.d / 8) {
-    case 2: return launch_bwd_tc_t<2>(P, L, s);
-    case 3: return launch_bwd_tc_t<3>(P, L, s);
-    case 4: return launch_bwd_tc_t<4>(P, L, s);
-    case 5: return launch_bwd_tc_t<5>(P, L, s);
-    case 6: return launch_bwd_tc_t<6>(P, L, s);
-    case 7: return launch_bwd_tc_t<7>(P, L, s);
-    case 8: return launch_bwd_tc_t<8>(P, L, s);
-    case 9: return launch_bwd_tc_t<9>(P, L, s);
-    case 10: return launch_bwd_tc_t<10>(P, L, s);
-    case 11: return launch_bwd_tc_t<11>(P, L, s);
-    case 12: return launch_bwd_tc_t<12>(P, L, s);
-    case 13: return launch_bwd_tc_t<13>(P, L, s);
-    case 14: return launch_bwd_tc_t<14>(P, L, s);
-    case 15: return launch_bwd_tc_t<15>(P, L, s);
-    case 16: return launch_bwd_tc_t<16>(P, L, s);
+    case 2: return launch_bwd_tc_t<2>(P, L, km, vm, s);
+    case 3: return launch_bwd_tc_t<3>(P, L, km, vm, s);
+    case 4: return launch_bwd_tc_t<4>(P, L, km, vm, s);
+    case 5: return launch_bwd_tc_t<5>(P, L, km, vm, s);
+    case 6: return launch_bwd_tc_t<6>(P, L, km, vm, s);
+    case 7: return launch_bwd_tc_t<7>(P, L, km, vm, s);
+    case 8: return launch_bwd_tc_t<8>(P, L, km, vm, s);
+    case 9: return launch_bwd_tc_t<9>(P, L, km, vm, s);
+    case 10: return launch_bwd_tc_t<10>(P, L, km, vm, s);
+    case 11: return launch_bwd_tc_t<11>(P, L, km, vm, s);
+    case 12: return launch_bwd_tc_t<12>(P, L, km, vm, s);
+    case 13: return launch_bwd_tc_t<13>(P, L, km, vm, s);
+    case 14: return launch_bwd_tc_t<14>(P, L, km, vm, s);
+    case 15: return launch_bwd_tc_t<15>(P, L, km, vm, s);
+    case 16: return launch_bwd_tc_t<16>(P, L, km, vm, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -521,6 +521,31 @@ def test_tc_backward_matches_oracle_and_cuda_core_path(case):
     _compare_grads_bf16(got, simt, "tc vs cuda-core")
 
 
+LOAD_PATH_CASES = [
+    (1, 3, 9, 11, 2, 72, (3, 7, 7), 0, 1.0),
+    (2, 2, 16, 16, 2, 64, (3, 7, 7), 0, 0.5),     # even chunk count: boxes read 8 channels of the next head
+    (1, 2, 32, 32, 2, 32, (1, 3, 3), 0, 20.0),    # envelope split in chunks
+    (1, 4, 12, 20, 1, 72, (3, 5, 5), 0, 6.0),     # boxes past the volume's borders (zero fill)
+]
+
+
+@pytest.mark.parametrize("case", LOAD_PATH_CASES, ids=_tc_ids)
+def test_tc_tma_and_cp_async_loads_agree_bitwise(case, monkeypatch):
+    """The chunk loads by TMA tensor copies (default) and by cp.async (MSL_TC_LOADS=cpasync) fill
+    every key the products use with the same values: forward, dQ and the offset gradient agree bit
+    for bit; dK / dV are sums of float atomics from many CTAs (order-dependent rounding)."""
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))
+                   for i, a in enumerate(_core_inputs(case, seed=23)))
+    monkeypatch.delenv("MSL_TC_LOADS", raising=False)
+    tma = _run_tc_train(case, arrays, algo=2)
+    monkeypatch.setenv("MSL_TC_LOADS", "cpasync")
+    cpa = _run_tc_train(case, arrays, algo=2)
+    for key in ("out", "lse", "probs", "dq", "doff"):
+        assert np.array_equal(tma[key], cpa[key]), key
+    for key in ("dk", "dv"):
+        assert fro(tma[key], cpa[key]) < 1e-3, key
+
+
 def test_tc_backward_dropout_matches_oracle_mask():
     case = (1, 3, 8, 8, 2, 32, (3, 3, 3), 0, 1.0)
     arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))

@@ -50,11 +50,6 @@ struct TcLaunch {
   size_t smem;
 };
 bool tc_supported(const AttnParams& P);
-// Tensor map over the K or V rows of head-sliced [B, Nkv, ld] bf16 buffers for the tensor-core kernels:
-// dims (channel, x, y, frame, sample), box (rs channels, 8 columns, 1, 1, 1), zero fill outside.  False
-// (and the kernels load with cp.async) when the base / row stride are not 16-byte aligned or the
-// driver's encoder is unavailable.
-bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base, long long ld, int rs);
 bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit);
 cudaError_t launch_attn_fwd_tc(const AttnParams& P, const TcLaunch& L, cudaStream_t s);
 bool tc_bwd_supported(const AttnParams& P);

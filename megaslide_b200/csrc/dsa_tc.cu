@@ -46,8 +46,8 @@ struct Smem {
   int* env;                 // envelope + base-grid tables
   float* lrow;              // [32]            softmax sums
   float* qsc;               // [2][32]         P~ fixed-point scale / inverse per query
-  int* bstart;              // [36]            hit list: first entry of each frame bucket (+ end)
-  int* bcur;                // [32]            bucket counts, then fill cursors
+  int* bstart;              // [132]           hit list: first entry of each (chunk, frame) bucket (+ end)
+  int* bcur;                // [128]           bucket counts, then fill cursors
   uint32_t* mask;           // [32][4]         16-key tiles touched per (plane, chunk)
   unsigned short* hits;     // [32 * K]        sample indices q * K + j sorted by frame bucket
   unsigned long long* kbar; // mbarrier of the key buffer's TMA copies
@@ -74,9 +74,9 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   s.qsc = reinterpret_cast<float*>(base + off);
   off += 2 * kQ * 4;
   s.bstart = reinterpret_cast<int*>(base + off);
-  off += 36 * 4;
+  off += (kBuckets + 4) * 4;
   s.bcur = reinterpret_cast<int*>(base + off);
-  off += 32 * 4;
+  off += kBuckets * 4;
   s.mask = reinterpret_cast<uint32_t*>(base + off);
   off += 32 * kMaxMaskChunks * 4;
   s.hits = reinterpret_cast<unsigned short*>(base + off);
@@ -91,7 +91,7 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
 // shared memory besides the key buffer and the dense tile
 size_t smem_fixed(const AttnParams& P, int rs) {
   return static_cast<size_t>(kQ) * rs * 2 + static_cast<size_t>(kQ) * P.K * (8 + 2) +
-         static_cast<size_t>(kQ) * (P.K + P.G) * 4 + kEnvWords * 4 + kQ * 4 * 3 + (36 + 32 + 32 * kMaxMaskChunks) * 4 +
+         static_cast<size_t>(kQ) * (P.K + P.G) * 4 + kEnvWords * 4 + kQ * 4 * 3 + (2 * kBuckets + 4 + 32 * kMaxMaskChunks) * 4 +
          24 + 256;
 }
 
@@ -114,8 +114,7 @@ __device__ __forceinline__ void load_extra(const AttnParams& P, const TileCtx& T
 
 template <int DCH>
 __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParams P, const TcLaunch L,
-                                                                  const __grid_constant__ CUtensorMap kmap,
-                                                                  const __grid_constant__ CUtensorMap vmap) {
+                                                                  const __grid_constant__ KeyMaps maps) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const Smem S = carve(smem_raw, P, L);
   const TileCtx T = decode_tile(P, L, kTileH);
@@ -145,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     S.env[0] = 0x7fffffff; S.env[1] = -0x7fffffff; S.env[2] = 0x7fffffff;
     S.env[3] = -0x7fffffff; S.env[4] = 0x7fffffff; S.env[5] = -0x7fffffff;
   }
-  if (threadIdx.x < 32) S.bcur[threadIdx.x] = 0;
+  if (threadIdx.x < kBuckets) S.bcur[threadIdx.x] = 0;
   if (threadIdx.x < 32 * kMaxMaskChunks) S.mask[threadIdx.x] = 0u;
   // TMA destinations are 128-byte aligned: boxes start at multiples of 8 keys x rs (rs % 8 == 0) bf16
   const bool tma = L.tma && (smem_u32(S.kbuf) & 127u) == 0u;
@@ -247,11 +246,12 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   if (overflow && threadIdx.x == 0 && P.status) atomicOr(P.status, MSL_STATUS_TC_RANGE);
   const bool work = any && !overflow;
   const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
+  const bool fsplit = split && !masks;  // chunks of a plane share one hit bucket: filter the hits
 
   // ---- records, frame-bucket counts and touched-tile masks; scores start at 0
   for (int s = 0; s < jper; ++s) {  // same trip count in every lane: warp collectives inside
     const int j = js + s;
-    int dz = -1, pa = -1, pb = -1;
+    int bk = -1, pa = -1, pb = -1;
     uint32_t bits = 0u;
     if (qvalid && s < n) {
       const unsigned long long raw = S.rec[qbase + j];
@@ -261,9 +261,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
       const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
       unsigned long long v = 0ull;
       if (work && t0 + 1 >= E.zlo && t0 <= E.zhi) {  // a corner in a frame the K/V buffers hold
-        dz = t0 - E.zlo + 1;
+        const int dz = t0 - E.zlo + 1;
         v = pack_rec(pt - static_cast<float>(t0), ph - static_cast<float>(h0), pw - static_cast<float>(w0), dz,
                      h0 - E.ylo, w0 - E.xlo);
+        bk = dz;
         if (masks) {
           const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
           const int ya = E.ylo + iy * (E.R - 1), xa = E.xlo + ix * (E.cw - 1);
@@ -271,44 +272,35 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
           const int chk = iy * E.nx + ix;
           if (t0 >= E.zlo) pa = dz * kMaxMaskChunks + chk;
           if (t0 + 1 <= E.zhi) pb = (dz + 1) * kMaxMaskChunks + chk;
+          v |= static_cast<unsigned long long>(chk) << kBitChunk;
+          bk += chk * 32;
         }
       }
       S.rec[qbase + j] = v;
     }
-    const unsigned peers = __match_any_sync(kFull, dz);
-    if (dz >= 0 && lane == __ffs(peers) - 1) atomicAdd(S.bcur + dz, __popc(peers));
+    const unsigned peers = __match_any_sync(kFull, bk);
+    if (bk >= 0 && lane == __ffs(peers) - 1) atomicAdd(S.bcur + bk, __popc(peers));
     if (pa >= 0 && (S.mask[pa] & bits) != bits) atomicOr(S.mask + pa, bits);
     if (pb >= 0 && (S.mask[pb] & bits) != bits) atomicOr(S.mask + pb, bits);
   }
   if (qvalid)
     for (int e = K + sub; e < KG; e += kLPQ) sacc[e] = 0.f;
   __syncthreads();
-  if (warp == 0) {  // bucket starts (exclusive scan of 32 counts); the counts become fill cursors
-    const int c = S.bcur[lane];
-    int incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(kFull, incl, o);
-      if (lane >= o) incl += t;
-    }
-    S.bstart[lane + 1] = incl;
-    if (lane == 0) S.bstart[0] = 0;
-    S.bcur[lane] = incl - c;
-  }
+  if (warp == 0) scan_buckets(S.bcur, S.bstart);
   __syncthreads();
-  for (int s = 0; s < jper; ++s) {  // hit list: every active sample once, grouped by frame bucket
+  for (int s = 0; s < jper; ++s) {  // hit list: every active sample once, grouped by (chunk, frame) bucket
     const int j = js + s;
-    int dz = -1;
+    int bk = -1;
     if (qvalid && s < n) {
       const unsigned long long v = S.rec[qbase + j];
-      if (v >> 63) dz = static_cast<int>((v >> 36) & 0x1fu);
+      if (v >> 63) bk = rec_bucket(v);
     }
-    const unsigned peers = __match_any_sync(kFull, dz);
+    const unsigned peers = __match_any_sync(kFull, bk);
     const int leader = __ffs(peers) - 1;
     int pos = 0;
-    if (dz >= 0 && lane == leader) pos = atomicAdd(S.bcur + dz, __popc(peers));
+    if (bk >= 0 && lane == leader) pos = atomicAdd(S.bcur + bk, __popc(peers));
     pos = __shfl_sync(kFull, pos, leader) + __popc(peers & ((1u << lane) - 1u));
-    if (dz >= 0) S.hits[pos] = static_cast<unsigned short>(qbase + j);
+    if (bk >= 0) S.hits[pos] = static_cast<unsigned short>(qbase + j);
   }
   const int g = lane >> 2, t4 = lane & 3;
   float* grow_s = S.sbuf + static_cast<size_t>(r) * 16 * L.sld;  // the row group's 16 dense rows
@@ -325,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     bool have = chunk_first(E, S.mask, masks, nz, k);
     if (have) {
       if (tma) {
-        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &kmap, kbar);
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.k, maps.have, kbar, true);
       } else {
         issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, kg, P.k_ld);
       }
@@ -344,18 +336,19 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
       have = chunk_next(E, S.mask, masks, nz, k);
       if (have) {
         if (tma) {
-          if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &kmap, kbar);
+          if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.k, maps.have, kbar, false);
         } else {
           issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, kg, P.k_ld);
         }
       }
       const int z = E.zlo + cur.zr, ya = chunk_ya(E, cur), xa = chunk_xa(E, cur);
-      const int hlo = S.bstart[cur.zr], hhi = S.bstart[cur.zr + 2];
+      const int hb = (masks ? cur.iy * E.nx + cur.ix : 0) * 32 + cur.zr;
+      const int hlo = S.bstart[hb], hhi = S.bstart[hb + 2];
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
         const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
         const Rec rc = decode_rec(S.rec[idx], E);
-        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
+        if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
           continue;
         const float* row = S.sbuf + static_cast<size_t>(q) * L.sld;
         const int k00 = (rc.h0 - ya) * kst + (rc.w0 - xa);
@@ -424,8 +417,13 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   __syncthreads();
 
   // ---- pass 2: O = P~ . V (hits CTA-wide)
-  constexpr int kTPW = (DCH + kWPG - 1) / kWPG;  // channel tiles per warp
-  const int nt0 = min(DCH, part * kTPW), nt1 = min(DCH, nt0 + kTPW);
+  // the 8 warps of a row group: 4 channel ranges (sizes differ by at most one tile) x 2 halves of the
+  // touched tiles (every other one), so that every warp runs two short accumulation chains; the
+  // halves are added once at the end
+  constexpr int kCB = DCH / 4, kCX = DCH % 4;
+  constexpr int kTPW = kCB + (kCX ? 1 : 0);  // channel tiles per warp (at most)
+  const int cpart = part & 3, kpar = part >> 2;
+  const int nt0 = cpart * kCB + min(cpart, kCX), nt1 = nt0 + kCB + (cpart < kCX ? 1 : 0);
   float o[kTPW + 1][4];
 #pragma unroll
   for (int i = 0; i < kTPW + 1; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -436,13 +434,14 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
       __syncthreads();  // the previous chunk's product is done with the key buffer and the dense tile
       // the values land while the weights are scattered and converted
       if (tma) {
-        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &vmap, kbar);
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.v, maps.have, kbar, P.G > 0);
       } else {
         issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, vg, P.v_ld);
       }
       zero_tiles<kQ>(S.sbuf, L.sld, k.m);
       const int z = E.zlo + k.zr, ya = chunk_ya(E, k), xa = chunk_xa(E, k);
-      const int hlo = S.bstart[k.zr], hhi = S.bstart[k.zr + 2];
+      const int hb = (masks ? k.iy * E.nx + k.ix : 0) * 32 + k.zr;
+      const int hlo = S.bstart[hb], hhi = S.bstart[hb + 2];
       __syncthreads();
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
@@ -450,14 +449,14 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         const float pv = S.sacc[static_cast<size_t>(q) * KG + (idx - q * K)];
         if (pv == 0.f) continue;
         const Rec rc = decode_rec(S.rec[idx], E);
-        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
+        if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
           continue;
         scatter_fixed_row(reinterpret_cast<int*>(S.sbuf) + static_cast<size_t>(q) * L.sld,
                           (rc.h0 - ya) * kst + (rc.w0 - xa), kst, rc,
                           pv * frac_weight(rc.ft, z != rc.t0) * S.qsc[q], P.H, P.W);
       }
       __syncthreads();
-      transpose_fixed(S.sbuf, L.sld, k.m, S.qsc + kQ);
+      transpose_fixed<kMaxKeysFwd>(S.sbuf, L.sld, k.m, S.qsc + kQ);
       if (tma) {
         wait_keys(kbar, kphase, S.dead, P.status);
         kphase ^= 1u;
@@ -465,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         cp_async_wait_all();
       }
       __syncthreads();
-      dq_product<DCH, kTPW>(tp, r, S.kbuf, L.rs, nt0, nt1, k.m, o);
+      dq_product<DCH, kTPW, 2>(tp, r, S.kbuf, L.rs, nt0, nt1, k.m, o, kpar);
     }
   }
   if (P.G > 0) {  // extra values: their weights straight into the fixed-point rows
@@ -477,13 +476,36 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
       for (int e = sub; e < P.G; e += kLPQ)
         reinterpret_cast<int*>(S.sbuf)[static_cast<size_t>(qi) * L.sld + e] = fix_round(sacc[K + e] * S.qsc[qi]);
     __syncthreads();
-    transpose_fixed(S.sbuf, L.sld, gmask, S.qsc + kQ);
+    transpose_fixed<kMaxKeysFwd>(S.sbuf, L.sld, gmask, S.qsc + kQ);
     __syncthreads();
-    dq_product<DCH, kTPW>(tp, r, S.kbuf, L.rs, nt0, nt1, gmask, o);
+    dq_product<DCH, kTPW, 2>(tp, r, S.kbuf, L.rs, nt0, nt1, gmask, o, kpar);
   }
 
-  // ---- normalise and store
+  // ---- the warps of the second half of the tiles hand their partial sums to the first half
   {
+    __syncthreads();  // every product is done with the dense tile
+    float4* red = reinterpret_cast<float4*>(S.sbuf) + ((r * 4 + cpart) * kTPW) * 32 + lane;  // [2][4][kTPW][32]
+    if (kpar == 1) {
+#pragma unroll
+      for (int j = 0; j < kTPW; ++j)
+        if (nt0 + j < nt1) red[j * 32] = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
+    }
+    __syncthreads();
+    if (kpar == 0) {
+#pragma unroll
+      for (int j = 0; j < kTPW; ++j) {
+        if (nt0 + j >= nt1) continue;
+        const float4 t = red[j * 32];
+        o[j][0] += t.x;
+        o[j][1] += t.y;
+        o[j][2] += t.z;
+        o[j][3] += t.w;
+      }
+    }
+  }
+
+  // ---- normalise and store (first-half warps)
+  if (kpar == 0) {
     int qh0_, qw0_, qh1_, qw1_;
     query_hw(T, r, g, qh0_, qw0_);
     query_hw(T, r, g + 8, qh1_, qw1_);
@@ -532,12 +554,14 @@ bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   mk &= ~15;
   const int gp = (P.G + 15) & ~15;
   if (mk < 64) return false;
-  if (mk > tc::t32::kMaxKeys) mk = tc::t32::kMaxKeys;
+  if (mk > tc::t32::kMaxKeysFwd) mk = tc::t32::kMaxKeysFwd;
   if (mk < gp) return false;
   L.maxkeys = mk;
   L.sld = mk + 8;  // row stride = 8 or 24 (mod 32) words: mma fragment rows hit distinct banks
   // a transposed bf16 tile [maxkeys][40] must fit in the dense fp32 tile [32][sld]
   if (static_cast<size_t>(mk) * tc::t32::kTRow * 2 > static_cast<size_t>(tc::t32::kQ) * L.sld * 4) return false;
+  // so must the output partial sums handed between the warp halves ([2][4][(dch + 3) / 4][32] float4)
+  if (static_cast<size_t>(4096) * ((dch + 3) / 4) > static_cast<size_t>(tc::t32::kQ) * L.sld * 4) return false;
   // the setup stages 32 queries x K x 3 offsets in the key buffer + the dense tile
   if (static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4 <
       static_cast<size_t>(tc::t32::kQ) * P.K * 12)
@@ -548,19 +572,20 @@ bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
 }
 
 template <int DCH>
-static cudaError_t launch_fwd_tc_t(const AttnParams& P, const TcLaunch& L, const CUtensorMap& km,
-                                   const CUtensorMap& vm, cudaStream_t s) {
+static cudaError_t launch_fwd_tc_t(const AttnParams& P, const TcLaunch& L, const tc::KeyMaps& maps,
+                                   cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(tc::fwd::dsa_fwd_tc_kernel<DCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
-  tc::fwd::dsa_fwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L, km, vm);
+  tc::fwd::dsa_fwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L, maps);
   return cudaGetLastError();
 }
 
-bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base, long long ld, int rs) {
-  // MSL_TC_LOADS=cpasync selects the cp.async loads (both paths compute the same results)
-  const char* sel = getenv("MSL_TC_LOADS");
-  const bool off = sel && strcmp(sel, "cpasync") == 0;
+namespace tc {
+
+// One tensor map over head-sliced [B, Nkv, ld] bf16 rows: dims (channel, x, y, frame, sample), box
+// (rs channels, bw columns, 1, 1, 1), zero fill outside.
+static bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base, long long ld, int rs, int bw) {
   using Encode = PFN_cuTensorMapEncodeTiled_v12000;
   static const Encode encode = []() -> Encode {
     void* fn = nullptr;
@@ -570,17 +595,16 @@ bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base, long 
       return nullptr;
     return reinterpret_cast<Encode>(fn);
   }();
-  memset(map, 0, sizeof(*map));
-  if (off || !encode || !base) return false;
-  // 16-byte aligned base and row stride; the box (rs channels x 8 columns) within the tensor's extents
+  if (!encode || !base) return false;
+  // 16-byte aligned base and row stride; the box within the tensor's extents
   if ((reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 2) & 15) || (rs * 2) % 16 != 0 || rs > 256) return false;
-  if (static_cast<long long>(P.nh) * P.d < rs || P.W < 8 || ld < static_cast<long long>(P.nh) * P.d) return false;
+  if (static_cast<long long>(P.nh) * P.d < rs || P.W < bw || ld < static_cast<long long>(P.nh) * P.d) return false;
   const cuuint64_t dims[5] = {static_cast<cuuint64_t>(P.nh) * P.d, static_cast<cuuint64_t>(P.W),
                               static_cast<cuuint64_t>(P.H), static_cast<cuuint64_t>(P.kv_frames),
                               static_cast<cuuint64_t>(P.B)};
   const cuuint64_t row = static_cast<cuuint64_t>(ld) * 2;
   const cuuint64_t strides[4] = {row, row * P.W, row * P.W * P.H, row * static_cast<cuuint64_t>(P.Nkv)};
-  const cuuint32_t box[5] = {static_cast<cuuint32_t>(rs), 8, 1, 1, 1};
+  const cuuint32_t box[5] = {static_cast<cuuint32_t>(rs), static_cast<cuuint32_t>(bw), 1, 1, 1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   if (strides[3] >= (1ull << 40)) return false;
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
@@ -588,26 +612,40 @@ bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base, long 
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_key_maps(KeyMaps* maps, const AttnParams& P, int rs) {
+  memset(maps, 0, sizeof(*maps));
+  // MSL_TC_LOADS=cpasync selects the cp.async loads (both paths compute the same results)
+  const char* sel = getenv("MSL_TC_LOADS");
+  if (sel && strcmp(sel, "cpasync") == 0) return false;
+  for (int j = 0; j < 4; ++j)
+    if (make_key_map(&maps->k[j], P, P.k, P.k_ld, rs, 8 * (j + 1)) &&
+        make_key_map(&maps->v[j], P, P.v, P.v_ld, rs, 8 * (j + 1)))
+      maps->have |= 1 << j;
+  return maps->have & 1;  // the 8-column boxes serve every chunk width
+}
+
+}  // namespace tc
+
 cudaError_t launch_attn_fwd_tc(const AttnParams& P, const TcLaunch& L0, cudaStream_t s) {
   TcLaunch L = L0;
-  CUtensorMap km, vm;
-  L.tma = make_key_map(&km, P, P.k, P.k_ld, L.rs) && make_key_map(&vm, P, P.v, P.v_ld, L.rs);
+  tc::KeyMaps maps;
+  L.tma = tc::make_key_maps(&maps, P, L.rs);
   switch (P.d / 8) {
-    case 2: return launch_fwd_tc_t<2>(P, L, km, vm, s);
-    case 3: return launch_fwd_tc_t<3>(P, L, km, vm, s);
-    case 4: return launch_fwd_tc_t<4>(P, L, km, vm, s);
-    case 5: return launch_fwd_tc_t<5>(P, L, km, vm, s);
-    case 6: return launch_fwd_tc_t<6>(P, L, km, vm, s);
-    case 7: return launch_fwd_tc_t<7>(P, L, km, vm, s);
-    case 8: return launch_fwd_tc_t<8>(P, L, km, vm, s);
-    case 9: return launch_fwd_tc_t<9>(P, L, km, vm, s);
-    case 10: return launch_fwd_tc_t<10>(P, L, km, vm, s);
-    case 11: return launch_fwd_tc_t<11>(P, L, km, vm, s);
-    case 12: return launch_fwd_tc_t<12>(P, L, km, vm, s);
-    case 13: return launch_fwd_tc_t<13>(P, L, km, vm, s);
-    case 14: return launch_fwd_tc_t<14>(P, L, km, vm, s);
-    case 15: return launch_fwd_tc_t<15>(P, L, km, vm, s);
-    case 16: return launch_fwd_tc_t<16>(P, L, km, vm, s);
+    case 2: return launch_fwd_tc_t<2>(P, L, maps, s);
+    case 3: return launch_fwd_tc_t<3>(P, L, maps, s);
+    case 4: return launch_fwd_tc_t<4>(P, L, maps, s);
+    case 5: return launch_fwd_tc_t<5>(P, L, maps, s);
+    case 6: return launch_fwd_tc_t<6>(P, L, maps, s);
+    case 7: return launch_fwd_tc_t<7>(P, L, maps, s);
+    case 8: return launch_fwd_tc_t<8>(P, L, maps, s);
+    case 9: return launch_fwd_tc_t<9>(P, L, maps, s);
+    case 10: return launch_fwd_tc_t<10>(P, L, maps, s);
+    case 11: return launch_fwd_tc_t<11>(P, L, maps, s);
+    case 12: return launch_fwd_tc_t<12>(P, L, maps, s);
+    case 13: return launch_fwd_tc_t<13>(P, L, maps, s);
+    case 14: return launch_fwd_tc_t<14>(P, L, maps, s);
+    case 15: return launch_fwd_tc_t<15>(P, L, maps, s);
+    case 16: return launch_fwd_tc_t<16>(P, L, maps, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -152,10 +152,10 @@ struct Env {
 };
 
 // Chunk shape for an envelope [ylo, yhi] x [xlo, xhi] and `maxkeys` keys per chunk: columns split into
-// windows of at most maxkeys / 2, rows into windows of maxkeys / kst (>= 2, as maxkeys % 16 == 0).
+// windows of at most min(maxkeys / 2, 32), rows into windows of maxkeys / kst (>= 2, as maxkeys % 16 == 0).
 __device__ __forceinline__ void chunk_shape(Env& E, int maxkeys) {
   const int nxk = E.xhi - E.xlo + 1;
-  E.cw = nxk <= maxkeys / 2 ? nxk : maxkeys / 2;
+  E.cw = min(nxk, min(maxkeys / 2, 32));  // at most 32 columns: one TMA box per chunk row
   E.kst = (E.cw + 7) & ~7;
   E.R = maxkeys / E.kst;
   E.ny = axis_chunks(E.ylo, E.yhi, E.R);
@@ -412,6 +412,33 @@ __device__ __forceinline__ Rec decode_rec(unsigned long long v, const Env& E) {
   return r;
 }
 
+// Hit lists are bucketed by (chunk, frame): record bits 61-62 hold the sample's chunk within its planes
+// (iy * nx + ix, when tile masks are kept, else 0); bucket = chunk * 32 + (t0 - zlo + 1).  The hits of
+// chunk c in plane zr are the buckets c * 32 + zr (upper corner there) and c * 32 + zr + 1 (lower):
+// one contiguous range [bstart[c * 32 + zr], bstart[c * 32 + zr + 2]).
+constexpr int kBitChunk = 61;
+constexpr int kBuckets = 128;
+__device__ __forceinline__ int rec_bucket(unsigned long long v) {
+  return static_cast<int>((v >> kBitChunk) & 3u) * 32 + static_cast<int>((v >> 36) & 0x1fu);
+}
+// exclusive scan of the kBuckets counts in bcur by warp 0: bucket starts in bstart[0 .. kBuckets], the
+// counts become fill cursors
+__device__ __forceinline__ void scan_buckets(int* bcur, int* bstart) {
+  const int lane = threadIdx.x & 31;
+  const int4 c = reinterpret_cast<const int4*>(bcur)[lane];
+  const int s = c.x + c.y + c.z + c.w;
+  int incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const int e0 = incl - s, e1 = e0 + c.x, e2 = e1 + c.y, e3 = e2 + c.z;
+  reinterpret_cast<int4*>(bstart)[lane] = make_int4(e0, e1, e2, e3);
+  reinterpret_cast<int4*>(bcur)[lane] = make_int4(e0, e1, e2, e3);
+  if (lane == 31) bstart[kBuckets] = incl;
+}
+
 // adds round(value * w_c) (value already scaled) for the sample's in-volume corners to an int32 row
 __device__ __forceinline__ void scatter_fixed_row(int* row, int k00, int ncw, const Rec& c, float sv, int H, int W) {
   const float ax0 = 1.f - c.fw, ax1 = c.fw, ay0 = 1.f - c.fh, ay1 = c.fh;
@@ -517,38 +544,70 @@ __device__ __forceinline__ void issue_keys(const AttnParams& P, const TileCtx& T
   }
 }
 
-// TMA path: warp 0 copies the chunk's 8-key boxes (box i = keys 8i .. 8i+7 = one row segment; only
-// boxes in touched tiles) with tensor map `map` (dims: channel, x, y, frame, sample; box rs x 8); the
-// copies complete on mbarrier `bar`.  Coordinates outside the volume / K-V window read as zeros.  The
-// half tile past the last box, when the chunk ends inside a touched tile, is zeroed by warps 1-3.
+// Tensor maps of one launch: K and V, box widths 8, 16, 24 and 32 keys (index kst / 8 - 1); bit j of
+// `have` set when map j of both exists.
+struct alignas(64) KeyMaps {
+  CUtensorMap k[4], v[4];
+  int have;
+};
+
+// Fills the launch's tensor maps (widths whose box fits the volume; 16-byte aligned K / V base and row
+// stride).  False when TMA cannot serve the launch (the kernels then load with cp.async).
+bool make_key_maps(KeyMaps* maps, const AttnParams& P, int rs);
+
+// TMA path: warps 0-3 copy the chunk's rows [ya, yb] x columns [xa, xa + kst) into kbuf rows
+// (y - ya) * kst + x - xa, one box per chunk row (lane i: row i; box width kst) when the launch has
+// that map, else one 8-key box per row segment (lane i: keys 8i .. 8i+7).  Boxes whose keys are all in
+// untouched tiles are skipped; coordinates outside the volume / K-V window read as zeros, and the
+// half tile past the last key, when the chunk ends inside a touched tile, is filled by one more 8-key
+// box placed wholly outside the volume (zeros).  The copies complete on mbarrier `bar`.  In TMA mode
+// the key buffer is written only by TMA, and its earlier generic reads are ordered by the CTA barrier
+// before the call; `first` adds the proxy fence for the setup's generic use of the buffer.
+// (boxes <= maxkeys / 8 <= 64: two per lane)
 __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCtx& T, const Env& E, const Chunk& k,
-                                               __nv_bfloat16* kbuf, int rs, const CUtensorMap* map, uint32_t bar) {
-  const int gpr = E.kst >> 3;  // boxes per chunk row
-  const int nbox = (chunk_yb(E, k) - chunk_ya(E, k) + 1) * gpr;
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    if (lane == 0) {
-      // boxes in touched tiles: two per tile, one for a last tile cut in half (nbox / 2 <= 16)
-      const int full = nbox >> 1;
-      const uint32_t below = full >= 32 ? 0xffffffffu : (1u << full) - 1u;
-      const int cnt = 2 * __popc(k.m & below) + ((nbox & 1) ? static_cast<int>((k.m >> full) & 1u) : 0);
-      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(cnt) * 16u * static_cast<uint32_t>(rs));
+                                               __nv_bfloat16* kbuf, int rs, const CUtensorMap* maps, int have,
+                                               uint32_t bar, bool first) {
+  // box b is issued by warp b % 4: a warp's copies issue one lane after another, so four warps
+  // shorten the issue (measured: 4 ~ 8 warps > 16 > 1)
+  constexpr int kIW = 4;
+  if (threadIdx.x >= 32 * kIW) return;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nkeys = (chunk_yb(E, k) - chunk_ya(E, k) + 1) * E.kst;
+  const int mi = (E.kst >> 3) - 1;
+  const bool wide = mi < 4 && ((have >> mi) & 1);
+  const int bw = wide ? E.kst : 8;  // keys per box
+  const int nbox = nkeys / bw;      // <= 64
+  // boxes b = lane and lane + 32; a box is issued when any of its keys lies in a touched tile
+  bool on[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int b = lane + 32 * u;
+    on[u] = false;
+    if (b < nbox) {
+      const int t0 = (b * bw) >> 4, t1 = (b * bw + bw - 1) >> 4;
+      on[u] = ((k.m >> t0) & ((2u << (t1 - t0)) - 1u)) != 0u;
     }
-    __syncwarp();
-    fence_proxy_async();
-    const int ya = chunk_ya(E, k), xa = chunk_xa(E, k), zl = E.zlo + k.zr - P.kv_frame0;
-    const uint32_t dst0 = smem_u32(kbuf);
-    for (int i = lane; i < nbox; i += 32) {
-      if (!((k.m >> (i >> 1)) & 1u)) continue;
-      const int row = i / gpr, g = i - row * gpr;
-      tma_load_5d(dst0 + static_cast<uint32_t>(i) * 16u * static_cast<uint32_t>(rs), map, bar, T.head * P.d,
-                  xa + g * 8, ya + row, zl, T.b);
-    }
-  } else if ((nbox & 1) && ((k.m >> (nbox >> 1)) & 1u)) {
-    const int words = rs;  // 8 keys x rs bf16 = rs 16-byte words
-    uint4* tail = reinterpret_cast<uint4*>(kbuf + static_cast<size_t>(nbox) * 8 * rs);
-    for (int i = threadIdx.x - 32; i < words; i += kThreads - 32) tail[i] = make_uint4(0u, 0u, 0u, 0u);
   }
+  const bool tail = (nkeys & 15) && ((k.m >> (nkeys >> 4)) & 1u);
+  const int cnt = __popc(__ballot_sync(0xffffffffu, on[0])) + __popc(__ballot_sync(0xffffffffu, on[1]));
+  if (threadIdx.x == 0) {
+    if (first) fence_proxy_async();
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>((cnt * bw + (tail ? 8 : 0)) * rs * 2));
+  }
+  __syncwarp();
+  const int zl = E.zlo + k.zr - P.kv_frame0;
+  if (first && (on[0] || on[1])) fence_proxy_async();
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    if (!on[u] || (lane + 32 * u) % kIW != wid) continue;
+    const int b = lane + 32 * u;
+    const int row = wide ? b : b / (E.kst >> 3);
+    const int col = wide ? 0 : (b - row * (E.kst >> 3)) * 8;
+    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>(b * bw * rs * 2), wide ? maps + mi : maps, bar, T.head * P.d,
+                chunk_xa(E, k) + col, chunk_ya(E, k) + row, zl, T.b);
+  }
+  if (tail && threadIdx.x == 0)  // columns W .. W+7: all outside the volume
+    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>(nkeys * rs * 2), maps, bar, T.head * P.d, P.W, 0, 0, T.b);
 }
 
 // Waits for the TMA copies of phase `parity` on mbarrier bar.  Bounded: after about a second the CTA
@@ -632,7 +691,8 @@ constexpr int kWPG = kWarps / kGroups;      // warps per row group
 constexpr int kLPQ = kWPG * 32 / 16;        // lanes per query
 constexpr int kTileH = 4, kQ = kTileH * kTileW;
 constexpr int kTRow = 40;                   // bf16 per key row of a transposed dense tile (32 + 8 pad)
-constexpr int kMaxKeys = 256;               // chunk cap: 16 tiles of 16 keys (one transposition item per thread)
+constexpr int kMaxKeys = 256;               // backward chunk cap: 16 tiles of 16 keys
+constexpr int kMaxKeysFwd = 512;            // forward chunk cap: 32 tiles (the whole tile mask)
 constexpr int kMaxMaskChunks = kMaskChunks;  // chunks per plane with their own tile masks
 constexpr float kFixRange = 2097152.f;      // 2^21: fixed-point full scale of a dense row
 
@@ -640,9 +700,10 @@ constexpr float kFixRange = 2097152.f;      // 2^21: fixed-point full scale of a
 
 // In-place conversion of the tiles of mask m of an int32 dense tile [32][sld] (fixed point, per-row
 // inverse scale inv[q]) into bf16 [key][kTRow].  Two phases separated by a barrier; every thread of
-// the CTA must call it.  Item = (key, half): 16 queries of one key.
+// the CTA must call it.  Item = (key, half): 16 queries of one key; MAXKEYS = the launch's key cap.
+template <int MAXKEYS>
 __device__ __forceinline__ void transpose_fixed(float* buf, int sld, uint32_t m, const float* inv) {
-  constexpr int kMaxIt = kMaxKeys * 2 / kThreads;
+  constexpr int kMaxIt = MAXKEYS * 2 / kThreads;
   const int* src = reinterpret_cast<const int*>(buf);
   const int items = __popc(m) * 32;
   uint32_t hold[kMaxIt][8];
@@ -677,11 +738,20 @@ __device__ __forceinline__ void transpose_fixed(float* buf, int sld, uint32_t m,
 // o[16 queries of group r][channel tiles nt0..nt1) += A . kbuf over the tiles of mask m; A = rows of
 // the transposed bf16 tile tb ([key][query]) read with ldmatrix.trans, kbuf rows through
 // ldmatrix.trans.
-template <int DCH, int TPW>
+// With KSPLIT > 1 the warp takes every KSPLIT-th touched tile from the kpar-th on (the partial sums
+// of the KSPLIT warps that share channels are added by the caller).
+template <int DCH, int TPW, int KSPLIT = 1>
 __device__ __forceinline__ void dq_product(const __nv_bfloat16* tb, int r, const __nv_bfloat16* kbuf, int rs, int nt0,
-                                           int nt1, uint32_t m, float (&o)[TPW + 1][4]) {
+                                           int nt1, uint32_t m, float (&o)[TPW + 1][4], int kpar = 0) {
   const int lane = threadIdx.x & 31;
   const int mi = lane >> 3, rr = lane & 7;
+  if (KSPLIT > 1) {  // drop the touched tiles of the other warps: keep ordinals kpar, kpar + KSPLIT, ...
+    uint32_t keep = 0u;
+    int ord = 0;
+    for (uint32_t mm = m; mm; mm &= mm - 1u, ++ord)
+      if (ord % KSPLIT == kpar) keep |= mm & (~mm + 1u);
+    m = keep;
+  }
   for (uint32_t mm = m; mm; mm &= mm - 1u) {
     const int kk = __ffs(mm) - 1;
     uint32_t a[4];

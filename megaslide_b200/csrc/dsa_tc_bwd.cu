@@ -55,8 +55,8 @@ struct Smem {
   float* dd;                // [32]            D = dO . O
   float* qsc;               // [4][32]         fixed-point scale / inverse of dS~ and P~ rows
   long long* prow;          // [32]            row of each query's softmax weights in probs
-  int* bstart;              // [33]            hit list: first entry of each frame bucket (+ end)
-  int* bcur;                // [32]            bucket counts, then fill cursors
+  int* bstart;              // [132]           hit list: first entry of each (chunk, frame) bucket (+ end)
+  int* bcur;                // [128]           bucket counts, then fill cursors
   uint32_t* mask;           // [32][4]         16-key tiles touched per (plane, chunk)
   unsigned short* hits;     // [32 * K]        sample indices q * K + j sorted by frame bucket
   unsigned long long* kbar; // mbarrier of the key buffer's TMA copies
@@ -93,9 +93,9 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   s.qsc = reinterpret_cast<float*>(base + off);
   off += 4 * kQ * 4;
   s.bstart = reinterpret_cast<int*>(base + off);
-  off += 36 * 4;
+  off += (kBuckets + 4) * 4;
   s.bcur = reinterpret_cast<int*>(base + off);
-  off += 32 * 4;
+  off += kBuckets * 4;
   s.mask = reinterpret_cast<uint32_t*>(base + off);
   off += 32 * kMaxMaskChunks * 4;
   s.hits = reinterpret_cast<unsigned short*>(base + off);
@@ -110,7 +110,7 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
 // shared memory besides the key buffer, the two dense tiles and the key table
 size_t smem_fixed(const AttnParams& P, int rs) {
   return static_cast<size_t>(kQ) * rs * 2 * 2 + static_cast<size_t>(kQ) * P.K * (8 + 4 + 12 + 2) + kEnvWords * 4 +
-         kQ * (8 + 4 + 16) + (36 + 32 + 32 * kMaxMaskChunks) * 4 + 24 + 256;
+         kQ * (8 + 4 + 16) + (2 * kBuckets + 4 + 32 * kMaxMaskChunks) * 4 + 24 + 256;
 }
 
 // In-plane terms of one sample from a dense row (corners outside the volume count as 0, like
@@ -214,8 +214,7 @@ __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const Tile
 
 template <int DCH>
 __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParams P, const TcLaunch L,
-                                                                  const __grid_constant__ CUtensorMap kmap,
-                                                                  const __grid_constant__ CUtensorMap vmap) {
+                                                                  const __grid_constant__ KeyMaps maps) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const Smem S = carve(smem_raw, P, L);
   const TileCtx T = decode_tile(P, L, kTileH);
@@ -244,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     S.env[0] = 0x7fffffff; S.env[1] = -0x7fffffff; S.env[2] = 0x7fffffff;
     S.env[3] = -0x7fffffff; S.env[4] = 0x7fffffff; S.env[5] = -0x7fffffff;
   }
-  if (threadIdx.x < 32) S.bcur[threadIdx.x] = 0;
+  if (threadIdx.x < kBuckets) S.bcur[threadIdx.x] = 0;
   if (threadIdx.x < 32 * kMaxMaskChunks) S.mask[threadIdx.x] = 0u;
   if (sub == 0) S.prow[qi] = (static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow;
   // TMA destinations are 128-byte aligned: boxes start at multiples of 8 keys x rs (rs % 8 == 0) bf16
@@ -366,13 +365,14 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   if (overflow && threadIdx.x == 0 && P.status) atomicOr(P.status, MSL_STATUS_TC_RANGE);
   const bool work = any && !overflow;
   const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
+  const bool fsplit = split && !masks;  // chunks of a plane share one hit bucket: filter the hits
 
   // ---- records (interior / keep flags), frame-bucket counts and touched-tile masks
   {
     const uint64_t qglob = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
     for (int s = 0; s < jper; ++s) {  // same trip count in every lane: warp collectives inside
       const int j = js + s;
-      int dz = -1, pa = -1, pb = -1;
+      int bk = -1, pa = -1, pb = -1;
       uint32_t bits = 0u;
       if (qvalid && s < n) {
         const unsigned long long raw = S.rec[qbase + j];
@@ -388,10 +388,11 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
                                            (clip_grad_mult(ph, P.H) != 0.f ? 1ull << kBitInH : 0ull) |
                                            (clip_grad_mult(pw, P.W) != 0.f ? 1ull << kBitInW : 0ull) |
                                            (keep ? 1ull << kBitKeep : 0ull);
-          dz = t0 - E.zlo + 1;
+          const int dz = t0 - E.zlo + 1;
           v = pack_rec(pt - static_cast<float>(t0), ph - static_cast<float>(h0), pw - static_cast<float>(w0), dz,
                        h0 - E.ylo, w0 - E.xlo) |
               flags;
+          bk = dz;
           if (masks) {
             const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
             const int ya = E.ylo + iy * (E.R - 1), xa = E.xlo + ix * (E.cw - 1);
@@ -399,48 +400,39 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
             const int chk = iy * E.nx + ix;
             if (t0 >= E.zlo) pa = dz * kMaxMaskChunks + chk;           // plane z = t0 (zrel = dz)
             if (t0 + 1 <= E.zhi) pb = (dz + 1) * kMaxMaskChunks + chk; // plane z = t0 + 1
+            v |= static_cast<unsigned long long>(chk) << kBitChunk;
+            bk += chk * 32;
           }
         }
         S.rec[qbase + j] = v;
       }
-      const unsigned peers = __match_any_sync(kFull, dz);
-      if (dz >= 0 && lane == __ffs(peers) - 1) atomicAdd(S.bcur + dz, __popc(peers));
+      const unsigned peers = __match_any_sync(kFull, bk);
+      if (bk >= 0 && lane == __ffs(peers) - 1) atomicAdd(S.bcur + bk, __popc(peers));
       if (pa >= 0 && (S.mask[pa] & bits) != bits) atomicOr(S.mask + pa, bits);
       if (pb >= 0 && (S.mask[pb] & bits) != bits) atomicOr(S.mask + pb, bits);
     }
   }
   __syncthreads();
-  if (warp == 0) {  // bucket starts (exclusive scan of 32 counts); the counts become fill cursors
-    const int c = S.bcur[lane];
-    int incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(kFull, incl, o);
-      if (lane >= o) incl += t;
-    }
-    S.bstart[lane + 1] = incl;
-    if (lane == 0) S.bstart[0] = 0;
-    S.bcur[lane] = incl - c;
-  }
+  if (warp == 0) scan_buckets(S.bcur, S.bstart);
   __syncthreads();
-  // hit list: every active sample once, grouped by frame bucket
+  // hit list: every active sample once, grouped by (chunk, frame) bucket
   for (int s = 0; s < jper; ++s) {
     const int j = js + s;
-    int dz = -1;
+    int bk = -1;
     if (qvalid && s < n) {
       const unsigned long long v = S.rec[qbase + j];
-      if (v >> 63) dz = static_cast<int>((v >> 36) & 0x1fu);
+      if (v >> 63) bk = rec_bucket(v);
       S.sv[qbase + j] = 0.f;
       S.g3[3 * (qbase + j)] = 0.f;
       S.g3[3 * (qbase + j) + 1] = 0.f;
       S.g3[3 * (qbase + j) + 2] = 0.f;
     }
-    const unsigned peers = __match_any_sync(kFull, dz);
+    const unsigned peers = __match_any_sync(kFull, bk);
     const int leader = __ffs(peers) - 1;
     int pos = 0;
-    if (dz >= 0 && lane == leader) pos = atomicAdd(S.bcur + dz, __popc(peers));
+    if (bk >= 0 && lane == leader) pos = atomicAdd(S.bcur + bk, __popc(peers));
     pos = __shfl_sync(kFull, pos, leader) + __popc(peers & ((1u << lane) - 1u));
-    if (dz >= 0) S.hits[pos] = static_cast<unsigned short>(qbase + j);
+    if (bk >= 0) S.hits[pos] = static_cast<unsigned short>(qbase + j);
   }
 
   const int g = lane >> 2, t4 = lane & 3;
@@ -460,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     bool have = have2;
     if (have) {
       if (tma) {
-        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &vmap, kbar);
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.v, maps.have, kbar, true);
       } else {
         issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, vg, P.v_ld);
       }
@@ -480,17 +472,18 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
       const bool v = have;
       if (!have) k = k2;
       if (tma) {
-        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, v ? &vmap : &kmap, kbar);
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, v ? maps.v : maps.k, maps.have, kbar, false);
       } else {
         issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, v ? vg : kg, v ? P.v_ld : P.k_ld);
       }
       const int z = E.zlo + cur.zr, ya = chunk_ya(E, cur), xa = chunk_xa(E, cur);
-      const int hlo = S.bstart[cur.zr], hhi = S.bstart[cur.zr + 2];
+      const int hb = (masks ? cur.iy * E.nx + cur.ix : 0) * 32 + cur.zr;
+      const int hlo = S.bstart[hb], hhi = S.bstart[hb + 2];
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
         const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
         const Rec rc = decode_rec(S.rec[idx], E);
-        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
+        if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
           continue;
         const bool upper = z != rc.t0;
         const float az = frac_weight(rc.ft, upper);
@@ -559,7 +552,8 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     while (have) {
       const Chunk cur = k;
       const int z = E.zlo + cur.zr, ya = chunk_ya(E, cur), xa = chunk_xa(E, cur);
-      const int hlo = S.bstart[cur.zr], hhi = S.bstart[cur.zr + 2];
+      const int hb = (masks ? cur.iy * E.nx + cur.ix : 0) * 32 + cur.zr;
+      const int hlo = S.bstart[hb], hhi = S.bstart[hb + 2];
       if (tma) {
         wait_keys(kbar, kphase, S.dead, P.status);
         kphase ^= 1u;
@@ -579,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
         const int idx = S.hits[i];
         const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
         const Rec rc = decode_rec(S.rec[idx], E);
-        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
+        if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
           continue;
         const bool upper = z != rc.t0;
         const float az = frac_weight(rc.ft, upper);
@@ -595,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
       }
       __syncthreads();
       // dS~ -> bf16 [key][query]; S no longer needed: clear sa for P~
-      transpose_fixed(S.sb, L.sld, cur.m, S.qsc + kQ);
+      transpose_fixed<kMaxKeys>(S.sb, L.sld, cur.m, S.qsc + kQ);
       zero_tiles<kQ>(S.sa, L.sld, cur.m);
       __syncthreads();
       // P~ scatter (into sa), dQ += dS~ . K_chunk, dK_chunk = dS~^T . Q
@@ -605,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
         if (!((v >> kBitKeep) & 1ull)) continue;
         const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
         const Rec rc = decode_rec(v, E);
-        if (split && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
+        if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
           continue;
         const float pv = __ldg(P.probs + S.prow[q] * K + (idx - q * K)) * P.drop_keep_scale;
         scatter_fixed_row(reinterpret_cast<int*>(S.sa) + static_cast<size_t>(q) * L.sld,
@@ -618,12 +612,12 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
       have = chunk_next(E, S.mask, masks, nz, k);
       if (have) {
         if (tma) {
-          if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, &kmap, kbar);
+          if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.k, maps.have, kbar, false);
         } else {
           issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, kg, P.k_ld);
         }
       }
-      transpose_fixed(S.sa, L.sld, cur.m, S.qsc + 3 * kQ);
+      transpose_fixed<kMaxKeys>(S.sa, L.sld, cur.m, S.qsc + 3 * kQ);
       __syncthreads();
       kv_product_flush<DCH>(P, T, L, tpp, S.dos, S.key_off, cur.m, P.dv_acc);
     }
@@ -707,35 +701,35 @@ bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
 }
 
 template <int DCH>
-static cudaError_t launch_bwd_tc_t(const AttnParams& P, const TcLaunch& L, const CUtensorMap& km,
-                                   const CUtensorMap& vm, cudaStream_t s) {
+static cudaError_t launch_bwd_tc_t(const AttnParams& P, const TcLaunch& L, const tc::KeyMaps& maps,
+                                   cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(tc::bwd::dsa_bwd_tc_kernel<DCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
-  tc::bwd::dsa_bwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L, km, vm);
+  tc::bwd::dsa_bwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L, maps);
   return cudaGetLastError();
 }
 
 cudaError_t launch_attn_bwd_tc(const AttnParams& P, const TcLaunch& L0, cudaStream_t s) {
   TcLaunch L = L0;
-  CUtensorMap km, vm;
-  L.tma = make_key_map(&km, P, P.k, P.k_ld, L.rs) && make_key_map(&vm, P, P.v, P.v_ld, L.rs);
+  tc::KeyMaps maps;
+  L.tma = tc::make_key_maps(&maps, P, L.rs);
   switch (P.d / 8) {
-    case 2: return launch_bwd_tc_t<2>(P, L, km, vm, s);
-    case 3: return launch_bwd_tc_t<3>(P, L, km, vm, s);
-    case 4: return launch_bwd_tc_t<4>(P, L, km, vm, s);
-    case 5: return launch_bwd_tc_t<5>(P, L, km, vm, s);
-    case 6: return launch_bwd_tc_t<6>(P, L, km, vm, s);
-    case 7: return launch_bwd_tc_t<7>(P, L, km, vm, s);
-    case 8: return launch_bwd_tc_t<8>(P, L, km, vm, s);
-    case 9: return launch_bwd_tc_t<9>(P, L, km, vm, s);
-    case 10: return launch_bwd_tc_t<10>(P, L, km, vm, s);
-    case 11: return launch_bwd_tc_t<11>(P, L, km, vm, s);
-    case 12: return launch_bwd_tc_t<12>(P, L, km, vm, s);
-    case 13: return launch_bwd_tc_t<13>(P, L, km, vm, s);
-    case 14: return launch_bwd_tc_t<14>(P, L, km, vm, s);
-    case 15: return launch_bwd_tc_t<15>(P, L, km, vm, s);
-    case 16: return launch_bwd_tc_t<16>(P, L, km, vm, s);
+    case 2: return launch_bwd_tc_t<2>(P, L, maps, s);
+    case 3: return launch_bwd_tc_t<3>(P, L, maps, s);
+    case 4: return launch_bwd_tc_t<4>(P, L, maps, s);
+    case 5: return launch_bwd_tc_t<5>(P, L, maps, s);
+    case 6: return launch_bwd_tc_t<6>(P, L, maps, s);
+    case 7: return launch_bwd_tc_t<7>(P, L, maps, s);
+    case 8: return launch_bwd_tc_t<8>(P, L, maps, s);
+    case 9: return launch_bwd_tc_t<9>(P, L, maps, s);
+    case 10: return launch_bwd_tc_t<10>(P, L, maps, s);
+    case 11: return launch_bwd_tc_t<11>(P, L, maps, s);
+    case 12: return launch_bwd_tc_t<12>(P, L, maps, s);
+    case 13: return launch_bwd_tc_t<13>(P, L, maps, s);
+    case 14: return launch_bwd_tc_t<14>(P, L, maps, s);
+    case 15: return launch_bwd_tc_t<15>(P, L, maps, s);
+    case 16: return launch_bwd_tc_t<16>(P, L, maps, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -137,77 +137,60 @@ __device__ __forceinline__ PlaneTerms plane_terms(const float* row, int k00, int
 
 // ------------------------------------------------------------------------------ chunk operands
 // accum[key][d] += A . X over the tiles of mask m: A = the transposed bf16 tile tb ([key][query], all
-// 32 queries, ldmatrix), X = 32 bf16 rows (Q or dO) in shared memory.  Items = (16-key tile, pair of
-// 8-channel tiles), round robin over the 16 warps, two items in flight per warp so their ldmatrix /
-// mma / store latencies overlap; each result row is added to the float32 accumulator row
-// key_off[key] with one float4 atomic per 4 channels, skipped when all four are 0.
+// 32 queries, ldmatrix), X = 32 bf16 rows (Q or dO) in shared memory.  Items = (16-key tile, group of
+// 3 channel tiles), round robin over the 16 warps: one A fragment serves three independent
+// accumulator chains.  Each lane adds its fragment pairs to the float32 accumulator rows key_off[key]
+// with float2 atomics (no shuffles or zero tests: fewer instructions measured faster).
 template <int DCH>
 __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const TileCtx& T, const TcLaunch& L,
                                                  const __nv_bfloat16* tb, const __nv_bfloat16* xs, const int* key_off,
                                                  uint32_t m, float* accum) {
-  constexpr int NP = (DCH + 1) / 2;  // channel pairs (the last one single when DCH is odd)
-  constexpr int U = 2;               // items in flight per warp
+  constexpr int NG = 3;                     // channel tiles per item
+  constexpr int NCG = (DCH + NG - 1) / NG;  // channel groups
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int mi = lane >> 3, rr = lane & 7;
-  const int items = __popc(m) * NP;
-  float* const abase = accum + static_cast<long long>(T.b) * P.Nkv * P.acc_ld + T.head * P.d;
-  for (int base = warp; base < items; base += kWarps * U) {
-    float c[U][2][4];
-    int tile[U], pr[U];
+  const int items = __popc(m) * NCG;
+  float* const abase = accum + static_cast<long long>(T.b) * P.Nkv * P.acc_ld + T.head * P.d + 2 * t4;
+  for (int item = warp; item < items; item += kWarps) {
+    const int mo = item / NCG, cg = item - mo * NCG;
+    const int tile = nth_bit(m, mo);
+    const int nt0 = cg * NG;
+    float c[NG][4];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int item = base + u * kWarps;
+    for (int j = 0; j < NG; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) c[u][h][0] = c[u][h][1] = c[u][h][2] = c[u][h][3] = 0.f;
-      tile[u] = -1;
-      pr[u] = 0;
-      if (item < items) {
-        const int mo = item / NP;
-        pr[u] = item - mo * NP;
-        tile[u] = nth_bit(m, mo);
-        const int nt = 2 * pr[u];
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          uint32_t a[4];  // rows = keys tile*16 + 0..15, columns = queries kk*16 + 0..15
-          ldsm_x4(smem_u32(tb + static_cast<size_t>(tile[u] * 16 + (lane & 15)) * kTRow + kk * 16 + (lane >> 4) * 8),
-                  a[0], a[1], a[2], a[3]);
-          // x4.trans matrices: (queries +0..7, ch nt) (queries +8..15, ch nt) (+0..7, nt+1) (+8..15, nt+1)
-          const __nv_bfloat16* rowp = xs + static_cast<size_t>(kk * 16 + rr + ((mi & 1) ? 8 : 0)) * L.rs;
-          if (nt + 1 < DCH) {
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(smem_u32(rowp + (nt + (mi >> 1)) * 8), b0, b1, b2, b3);
-            mma16816(c[u][0], a, b0, b1);
-            mma16816(c[u][1], a, b2, b3);
-          } else {
-            uint32_t b0, b1;
-            ldsm_x2_t(smem_u32(rowp + nt * 8), b0, b1);
-            mma16816(c[u][0], a, b0, b1);
-          }
-        }
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t a[4];  // rows = keys tile*16 + 0..15, columns = queries kk*16 + 0..15
+      ldsm_x4(smem_u32(tb + static_cast<size_t>(tile * 16 + (lane & 15)) * kTRow + kk * 16 + (lane >> 4) * 8), a[0], a[1],
+              a[2], a[3]);
+      // x4.trans matrices: (queries +0..7, ch nt) (queries +8..15, ch nt) (+0..7, nt+1) (+8..15, nt+1)
+      const __nv_bfloat16* rowp = xs + static_cast<size_t>(kk * 16 + rr + ((mi & 1) ? 8 : 0)) * L.rs;
+      if (nt0 + 1 < DCH) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(rowp + (nt0 + (mi >> 1)) * 8), b0, b1, b2, b3);
+        mma16816(c[0], a, b0, b1);
+        mma16816(c[1], a, b2, b3);
+      } else {
+        uint32_t b0, b1;
+        ldsm_x2_t(smem_u32(rowp + nt0 * 8), b0, b1);
+        mma16816(c[0], a, b0, b1);
+      }
+      if (nt0 + 2 < DCH) {
+        uint32_t b0, b1;
+        ldsm_x2_t(smem_u32(rowp + (nt0 + 2) * 8), b0, b1);
+        mma16816(c[2], a, b0, b1);
       }
     }
+    const int o0 = key_off[tile * 16 + g], o1 = key_off[tile * 16 + g + 8];
+    float* const a0 = abase + static_cast<long long>(max(o0, 0)) * P.acc_ld + nt0 * 8;
+    float* const a1 = abase + static_cast<long long>(max(o1, 0)) * P.acc_ld + nt0 * 8;
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (tile[u] < 0) break;  // warp-uniform
-      const int o0 = key_off[tile[u] * 16 + g], o1 = key_off[tile[u] * 16 + g + 8];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int ch = (2 * pr[u] + h) * 8;
-        if (ch >= DCH * 8) break;  // warp-uniform
-        // lanes t4 = 0, 2 flush key g (channels 2t4..2t4+3), lanes t4 = 1, 3 key g + 8 (2t4-2..2t4+1)
-        const float x0 = __shfl_xor_sync(kFull, c[u][h][0], 1), x1 = __shfl_xor_sync(kFull, c[u][h][1], 1);
-        const float x2 = __shfl_xor_sync(kFull, c[u][h][2], 1), x3 = __shfl_xor_sync(kFull, c[u][h][3], 1);
-        if ((t4 & 1) == 0) {
-          const float4 v = make_float4(c[u][h][0], c[u][h][1], x0, x1);
-          if (o0 >= 0 && (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f))
-            atomicAdd(reinterpret_cast<float4*>(abase + static_cast<long long>(o0) * P.acc_ld + ch + 2 * t4), v);
-        } else {
-          const float4 v = make_float4(x2, x3, c[u][h][2], c[u][h][3]);
-          if (o1 >= 0 && (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f))
-            atomicAdd(reinterpret_cast<float4*>(abase + static_cast<long long>(o1) * P.acc_ld + ch + 2 * t4 - 2), v);
-        }
-      }
+    for (int j = 0; j < NG; ++j) {
+      if (nt0 + j >= DCH) break;  // warp-uniform
+      // the fragment's own pairs: key g (c0, c1) and key g + 8 (c2, c3), channels 8 (nt0 + j) + 2t4, +1
+      if (o0 >= 0) atomicAdd(reinterpret_cast<float2*>(a0 + j * 8), make_float2(c[j][0], c[j][1]));
+      if (o1 >= 0) atomicAdd(reinterpret_cast<float2*>(a1 + j * 8), make_float2(c[j][2], c[j][3]));
     }
   }
 }

@@ -488,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     if (qvalid) {
       const float D = S.dd[qi];
       const float* prob_row = P.probs + S.prow[qi] * K;
-      for (int j = js; j < je; ++j) {
+      for (int j = sub; j < K; j += kLPQ) {  // lanes of the query read consecutive weights
         const unsigned long long v = S.rec[qbase + j];
         if (!(v >> 63)) continue;
         const float p = __ldg(prob_row + j);
@@ -633,13 +633,14 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     const float c0 = P.T > 1 ? 0.5f * static_cast<float>(P.W) * P.oscale / static_cast<float>(P.T - 1) : 0.f;
     const float c1 = P.H > 1 ? 0.5f * static_cast<float>(P.H) * P.oscale / static_cast<float>(P.H - 1) : 0.f;
     const float c2 = P.W > 1 ? 0.5f * static_cast<float>(P.T) * P.oscale / static_cast<float>(P.W - 1) : 0.f;
-    for (int j = js; j < je; ++j) {
+    // element e = 3j + c of the row (the 16 lanes of the query store consecutive floats): channel c
+    // takes coordinate gradient component 2 - c (w, h, t) and the interior flag of that axis
+    for (int e = sub; e < K3; e += kLPQ) {
+      const int j = e / 3, c = e - 3 * j;
       const unsigned long long v = S.rec[qbase + j];
-      const float* gg = S.g3 + 3 * (qbase + j);
-      const bool act = v >> 63;
-      drow[3 * j + 0] = (act && ((v >> kBitInW) & 1ull)) ? gg[2] * c0 : 0.f;
-      drow[3 * j + 1] = (act && ((v >> kBitInH) & 1ull)) ? gg[1] * c1 : 0.f;
-      drow[3 * j + 2] = (act && ((v >> kBitInT) & 1ull)) ? gg[0] * c2 : 0.f;
+      const float cc = c == 0 ? c0 : (c == 1 ? c1 : c2);
+      const bool on = (v >> 63) && ((v >> (kBitInW - c)) & 1ull);
+      drow[e] = on ? S.g3[3 * (qbase + j) + 2 - c] * cc : 0.f;
     }
   }
 }

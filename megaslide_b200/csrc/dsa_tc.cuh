@@ -628,11 +628,15 @@ __device__ __forceinline__ void wait_keys(uint32_t bar, uint32_t parity, volatil
 // zeroes rows 0..ROWS-1 of the 16-key tiles of mask m in a dense fp32 / int32 tile
 template <int ROWS>
 __device__ __forceinline__ void zero_tiles(float* buf, int sld, uint32_t m) {
-  const int items = __popc(m) * ROWS * 4;
-  for (int i = threadIdx.x; i < items; i += kThreads) {
-    const int o = i / (ROWS * 4), row = (i >> 2) % ROWS, c4 = i & 3;
-    *reinterpret_cast<float4*>(buf + static_cast<size_t>(row) * sld + nth_bit(m, o) * 16 + c4 * 4) =
-        make_float4(0.f, 0.f, 0.f, 0.f);
+  // one warp per 16-key tile (one bit search per warp and tile); a store instruction covers 8 rows x
+  // 64 bytes: 4 wavefronts, the minimum for 512 bytes
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = __popc(m);
+  for (int o = warp; o < nt; o += kWarps) {
+    float* const col = buf + nth_bit(m, o) * 16 + (lane & 3) * 4;
+#pragma unroll
+    for (int row = lane >> 2; row < ROWS; row += 8)
+      *reinterpret_cast<float4*>(col + static_cast<size_t>(row) * sld) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
@@ -707,11 +711,14 @@ __device__ __forceinline__ void transpose_fixed(float* buf, int sld, uint32_t m,
   const int* src = reinterpret_cast<const int*>(buf);
   const int items = __popc(m) * 32;
   uint32_t hold[kMaxIt][8];
+  int keyv[kMaxIt];  // the item's key, found once (bit search) for both phases
 #pragma unroll
   for (int u = 0; u < kMaxIt; ++u) {
     const int i = threadIdx.x + u * kThreads;
+    keyv[u] = 0;
     if (i < items) {
       const int key = nth_bit(m, i >> 5) * 16 + (i & 15), half = (i >> 4) & 1;
+      keyv[u] = key;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int q = half * 16 + 2 * e;
@@ -727,7 +734,7 @@ __device__ __forceinline__ void transpose_fixed(float* buf, int sld, uint32_t m,
   for (int u = 0; u < kMaxIt; ++u) {
     const int i = threadIdx.x + u * kThreads;
     if (i < items) {
-      const int key = nth_bit(m, i >> 5) * 16 + (i & 15), half = (i >> 4) & 1;
+      const int key = keyv[u], half = (i >> 4) & 1;
       uint4* d = reinterpret_cast<uint4*>(dst + key * (kTRow / 2) + half * 8);
       d[0] = make_uint4(hold[u][0], hold[u][1], hold[u][2], hold[u][3]);
       d[1] = make_uint4(hold[u][4], hold[u][5], hold[u][6], hold[u][7]);

@@ -488,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     if (qvalid) {
       const float D = S.dd[qi];
       const float* prob_row = P.probs + S.prow[qi] * K;
-      for (int j = sub; j < K; j += kLPQ) {  // lanes of the query read consecutive weights
+      for (int j = js; j < je; ++j) {
         const unsigned long long v = S.rec[qbase + j];
         if (!(v >> 63)) continue;
         const float p = __ldg(prob_row + j);

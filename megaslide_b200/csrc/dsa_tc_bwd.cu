@@ -152,9 +152,10 @@ __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const Tile
   const int mi = lane >> 3, rr = lane & 7;
   const int items = __popc(m) * NCG;
   float* const abase = accum + static_cast<long long>(T.b) * P.Nkv * P.acc_ld + T.head * P.d + 2 * t4;
+  const int tl = nth_bit(m, lane);  // lane o: the o-th touched tile (one bit search per warp)
   for (int item = warp; item < items; item += kWarps) {
     const int mo = item / NCG, cg = item - mo * NCG;
-    const int tile = nth_bit(m, mo);
+    const int tile = __shfl_sync(kFull, tl, mo);
     const int nt0 = cg * NG;
     float c[NG][4];
 #pragma unroll

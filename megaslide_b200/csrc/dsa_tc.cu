@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   const bool work = any && !overflow;
   const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
   const bool fsplit = split && !masks;  // chunks of a plane share one hit bucket: filter the hits
+  if (masks) chunk_pair_planes(E, L.maxkeys);
 
   // ---- records, frame-bucket counts and touched-tile masks; scores start at 0
   for (int s = 0; s < jper; ++s) {  // same trip count in every lane: warp collectives inside
@@ -341,26 +342,22 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
           issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, kg, P.k_ld);
         }
       }
-      const int z = E.zlo + cur.zr, ya = chunk_ya(E, cur), xa = chunk_xa(E, cur);
-      const int hb = (masks ? cur.iy * E.nx + cur.ix : 0) * 32 + cur.zr;
-      const int hlo = S.bstart[hb], hhi = S.bstart[hb + 2];
+      const int zb = E.zlo + cur.zr * E.pg, ya = chunk_ya(E, cur), xa = chunk_xa(E, cur);
+      // hits with a corner in the chunk's planes: buckets t0 - zlo + 1 = zb - zlo .. zb - zlo + pg
+      const int hb = (masks ? cur.iy * E.nx + cur.ix : 0) * 32 + cur.zr * E.pg;
+      const int hlo = S.bstart[hb], hhi = S.bstart[hb + E.pg + 1];
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
         const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
         const Rec rc = decode_rec(S.rec[idx], E);
         if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
           continue;
-        const float* row = S.sbuf + static_cast<size_t>(q) * L.sld;
-        const int k00 = (rc.h0 - ya) * kst + (rc.w0 - xa);
-        const bool xok = rc.w0 + 1 < P.W, yok = rc.h0 + 1 < P.H;
-        const float v00 = row[k00];
-        const float v01 = xok ? row[k00 + 1] : 0.f;
-        const float v10 = yok ? row[k00 + kst] : 0.f;
-        const float v11 = (xok && yok) ? row[k00 + kst + 1] : 0.f;
-        const float ax0 = 1.f - rc.fw, ax1 = rc.fw;
-        const float bil = (1.f - rc.fh) * fmaf(ax1, v01, ax0 * v00) + rc.fh * fmaf(ax1, v11, ax0 * v10);
+        const float* row = S.sbuf + static_cast<size_t>(q) * L.sld + (rc.h0 - ya) * kst + (rc.w0 - xa);
         float* sp = S.sacc + static_cast<size_t>(q) * KG + (idx - q * K);
-        *sp = fmaf(frac_weight(rc.ft, z != rc.t0), bil, *sp);
+        const int pa = rc.t0 - zb;  // chunk plane of the lower corner: -1 .. pg - 1
+        if (pa >= 0) *sp = fmaf(frac_weight(rc.ft, false), plane_bil(row + pa * E.kpp, kst, rc, P.H, P.W), *sp);
+        if (pa + 1 < E.pg)
+          *sp = fmaf(frac_weight(rc.ft, true), plane_bil(row + (pa + 1) * E.kpp, kst, rc, P.H, P.W), *sp);
       }
     }
   }
@@ -439,9 +436,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, vg, P.v_ld);
       }
       zero_tiles<kQ>(S.sbuf, L.sld, k.m);
-      const int z = E.zlo + k.zr, ya = chunk_ya(E, k), xa = chunk_xa(E, k);
-      const int hb = (masks ? k.iy * E.nx + k.ix : 0) * 32 + k.zr;
-      const int hlo = S.bstart[hb], hhi = S.bstart[hb + 2];
+      const int zb = E.zlo + k.zr * E.pg, ya = chunk_ya(E, k), xa = chunk_xa(E, k);
+      const int hb = (masks ? k.iy * E.nx + k.ix : 0) * 32 + k.zr * E.pg;
+      const int hlo = S.bstart[hb], hhi = S.bstart[hb + E.pg + 1];
       __syncthreads();
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
@@ -451,9 +448,13 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         const Rec rc = decode_rec(S.rec[idx], E);
         if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != k.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != k.ix))
           continue;
-        scatter_fixed_row(reinterpret_cast<int*>(S.sbuf) + static_cast<size_t>(q) * L.sld,
-                          (rc.h0 - ya) * kst + (rc.w0 - xa), kst, rc,
-                          pv * frac_weight(rc.ft, z != rc.t0) * S.qsc[q], P.H, P.W);
+        int* row = reinterpret_cast<int*>(S.sbuf) + static_cast<size_t>(q) * L.sld;
+        const int k00 = (rc.h0 - ya) * kst + (rc.w0 - xa);
+        const float ps = pv * S.qsc[q];
+        const int pa = rc.t0 - zb;  // chunk plane of the lower corner: -1 .. pg - 1
+        if (pa >= 0) scatter_fixed_row(row + pa * E.kpp, k00, kst, rc, ps * frac_weight(rc.ft, false), P.H, P.W);
+        if (pa + 1 < E.pg)
+          scatter_fixed_row(row + (pa + 1) * E.kpp, k00, kst, rc, ps * frac_weight(rc.ft, true), P.H, P.W);
       }
       __syncthreads();
       transpose_fixed<kMaxKeysFwd>(S.sbuf, L.sld, k.m, S.qsc + kQ);

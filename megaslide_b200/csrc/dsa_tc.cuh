@@ -149,6 +149,8 @@ struct Env {
   int zlo, zhi, ylo, yhi, xlo, xhi;
   int cw, R, ny, nx;  // column-chunk width, rows per chunk, chunk counts
   int kst;            // key row stride in a chunk: cw rounded up to 8 (chunk key = (y - ya) * kst + x - xa)
+  int pg;             // planes per chunk (1, or 2 when two planes' keys fit one chunk)
+  int kpp;            // key offset of a chunk's second plane (multiple of 16; pg == 2)
 };
 
 // Chunk shape for an envelope [ylo, yhi] x [xlo, xhi] and `maxkeys` keys per chunk: columns split into
@@ -160,6 +162,18 @@ __device__ __forceinline__ void chunk_shape(Env& E, int maxkeys) {
   E.R = maxkeys / E.kst;
   E.ny = axis_chunks(E.ylo, E.yhi, E.R);
   E.nx = axis_chunks(E.xlo, E.xhi, E.cw);
+  E.pg = 1;
+  E.kpp = 0;
+}
+
+// Two planes per chunk when one chunk holds a whole plane and two planes' keys (each padded to whole
+// 16-key tiles) fit `maxkeys`: a sample whose two trilinear planes share the chunk is visited once.
+__device__ __forceinline__ void chunk_pair_planes(Env& E, int maxkeys) {
+  const int kp = ((E.yhi - E.ylo + 1) * E.kst + 15) & ~15;
+  if (E.ny == 1 && E.nx == 1 && E.zhi > E.zlo && 2 * kp <= maxkeys) {
+    E.pg = 2;
+    E.kpp = kp;
+  }
 }
 
 // Base-grid values 2a/max(S-1,1) - 1 of the window positions a tile can reach, per axis, computed once
@@ -439,6 +453,18 @@ __device__ __forceinline__ void scan_buckets(int* bcur, int* bstart) {
   if (lane == 31) bstart[kBuckets] = incl;
 }
 
+// bilinear combination of the sample's in-plane corners from a dense row (row points at the corner
+// (h0, w0); corners outside the volume count as 0)
+__device__ __forceinline__ float plane_bil(const float* row, int kst, const Rec& c, int H, int W) {
+  const bool xok = c.w0 + 1 < W, yok = c.h0 + 1 < H;
+  const float v00 = row[0];
+  const float v01 = xok ? row[1] : 0.f;
+  const float v10 = yok ? row[kst] : 0.f;
+  const float v11 = (xok && yok) ? row[kst + 1] : 0.f;
+  const float ax0 = 1.f - c.fw, ax1 = c.fw;
+  return (1.f - c.fh) * fmaf(ax1, v01, ax0 * v00) + c.fh * fmaf(ax1, v11, ax0 * v10);
+}
+
 // adds round(value * w_c) (value already scaled) for the sample's in-volume corners to an int32 row
 __device__ __forceinline__ void scatter_fixed_row(int* row, int k00, int ncw, const Rec& c, float sv, int H, int W) {
   const float ax0 = 1.f - c.fw, ax1 = c.fw, ay0 = 1.f - c.fh, ay1 = c.fh;
@@ -458,11 +484,12 @@ __device__ __forceinline__ uint32_t corner_tiles(int k00, int ncw, bool xok, boo
   return m;
 }
 
-// The envelope walk: chunk (zr, iy, ix) covers frame z = zlo + zr, rows [ya, yb] and columns
-// [xa, xb] (windows of R rows / cw columns with one row / column of overlap, so that the four corners
-// a sample has in a plane fall in one chunk).  Its keys are numbered (y - ya) * kst + (x - xa); m marks
-// the 16-key tiles any sample of the tile touches (every tile of the chunk when no masks are kept).
-// Tile masks are kept per plane for up to kMaskChunks chunks.
+// The envelope walk: chunk (zr, iy, ix) covers frames zlo + zr * pg .. + pg - 1 (those up to zhi),
+// rows [ya, yb] and columns [xa, xb] (windows of R rows / cw columns with one row / column of overlap,
+// so that the four corners a sample has in a plane fall in one chunk).  Its keys are numbered
+// pl * kpp + (y - ya) * kst + (x - xa) for chunk plane pl; m marks the 16-key tiles any sample of the
+// tile touches (every tile of the chunk when no masks are kept; pg == 2 only with masks).  Tile masks
+// are kept per plane for up to kMaskChunks chunks.
 constexpr int kMaskChunks = 4;
 
 struct Chunk {
@@ -477,14 +504,21 @@ __device__ __forceinline__ int chunk_xb(const Env& E, const Chunk& k) { return m
 
 // the chunk's tile mask; 0 = nothing to do
 __device__ __forceinline__ uint32_t chunk_mask(const Env& E, const uint32_t* mask, bool masks, const Chunk& k) {
-  if (masks) return mask[(k.zr + 1) * kMaskChunks + k.iy * E.nx + k.ix];
+  if (masks) {
+    const int c = k.iy * E.nx + k.ix, z0 = k.zr * E.pg;
+    uint32_t m = mask[(z0 + 1) * kMaskChunks + c];
+    if (E.pg == 2 && E.zlo + z0 + 1 <= E.zhi) m |= mask[(z0 + 2) * kMaskChunks + c] << (E.kpp >> 4);
+    return m;
+  }
   const int ntile = ((chunk_yb(E, k) - chunk_ya(E, k) + 1) * E.kst + 15) >> 4;
   return ntile >= 32 ? 0xffffffffu : (1u << ntile) - 1u;
 }
 
 // moves k to the first chunk at or after it with a touched tile; false when the walk is over
+// (nz = frames of the envelope, 0 when the tile has no work)
 __device__ __forceinline__ bool chunk_seek(const Env& E, const uint32_t* mask, bool masks, int nz, Chunk& k) {
-  while (k.zr < nz) {
+  const int ng = E.pg == 2 ? (nz + 1) >> 1 : nz;  // chunk rows along z
+  while (k.zr < ng) {
     k.m = chunk_mask(E, mask, masks, k);
     if (k.m) return true;
     if (++k.ix == E.nx) {
@@ -515,12 +549,14 @@ __device__ __forceinline__ bool chunk_next(const Env& E, const uint32_t* mask, b
 // Row of chunk key `key` in the K/V buffers of the sample, -1 past the chunk and outside the volume /
 // K-V window.
 __device__ __forceinline__ int chunk_key_row(const AttnParams& P, const Env& E, const Chunk& k, int key) {
+  const int pl = (E.pg == 2 && key >= E.kpp) ? 1 : 0;
+  key -= pl * E.kpp;
   // key / kst exactly: (key + 0.5) / kst is at least 1 / (2 kst) away from an integer
   const int ky = static_cast<int>((static_cast<float>(key) + 0.5f) * (1.f / static_cast<float>(E.kst)));
   const int y = chunk_ya(E, k) + ky, x = chunk_xa(E, k) + (key - ky * E.kst);
-  const int zl = E.zlo + k.zr - P.kv_frame0;
-  const bool ok = y <= chunk_yb(E, k) && x <= chunk_xb(E, k) && zl >= 0 && zl < P.kv_frames && y >= 0 && y < P.H &&
-                  x >= 0 && x < P.W;
+  const int z = E.zlo + k.zr * E.pg + pl, zl = z - P.kv_frame0;
+  const bool ok = y <= chunk_yb(E, k) && x <= chunk_xb(E, k) && z <= E.zhi && zl >= 0 && zl < P.kv_frames && y >= 0 &&
+                  y < P.H && x >= 0 && x < P.W;
   return ok ? (zl * P.H + y) * P.W + x : -1;
 }
 
@@ -555,15 +591,14 @@ struct alignas(64) KeyMaps {
 // stride).  False when TMA cannot serve the launch (the kernels then load with cp.async).
 bool make_key_maps(KeyMaps* maps, const AttnParams& P, int rs);
 
-// TMA path: warps 0-3 copy the chunk's rows [ya, yb] x columns [xa, xa + kst) into kbuf rows
-// (y - ya) * kst + x - xa, one box per chunk row (lane i: row i; box width kst) when the launch has
-// that map, else one 8-key box per row segment (lane i: keys 8i .. 8i+7).  Boxes whose keys are all in
-// untouched tiles are skipped; coordinates outside the volume / K-V window read as zeros, and the
-// half tile past the last key, when the chunk ends inside a touched tile, is filled by one more 8-key
-// box placed wholly outside the volume (zeros).  The copies complete on mbarrier `bar`.  In TMA mode
-// the key buffer is written only by TMA, and its earlier generic reads are ordered by the CTA barrier
-// before the call; `first` adds the proxy fence for the setup's generic use of the buffer.
-// (boxes <= maxkeys / 8 <= 64: two per lane)
+// TMA path: warps 0-3 copy, for each chunk plane pl, rows [ya, yb] x columns [xa, xa + kst) into kbuf
+// rows pl * kpp + (y - ya) * kst + x - xa: one box per chunk row (box width kst) when the launch has that
+// map, else one 8-key box per row segment.  Boxes whose keys are all in untouched tiles are skipped;
+// coordinates outside the volume / K-V window read as zeros, and the half tile past a plane's last key,
+// when the plane ends inside a touched tile, is filled by one more 8-key box placed wholly outside the
+// volume (zeros).  The copies complete on mbarrier `bar`.  In TMA mode the key buffer is written only
+// by TMA, and its earlier generic reads are ordered by the CTA barrier before the call; `first` adds
+// the proxy fence for the setup's generic use of the buffer.  (boxes <= maxkeys / 8 <= 64: two per lane)
 __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCtx& T, const Env& E, const Chunk& k,
                                                __nv_bfloat16* kbuf, int rs, const CUtensorMap* maps, int have,
                                                uint32_t bar, bool first) {
@@ -572,42 +607,52 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
   constexpr int kIW = 4;
   if (threadIdx.x >= 32 * kIW) return;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int nkeys = (chunk_yb(E, k) - chunk_ya(E, k) + 1) * E.kst;
+  const int nkeys = (chunk_yb(E, k) - chunk_ya(E, k) + 1) * E.kst;  // keys of one plane
   const int mi = (E.kst >> 3) - 1;
   const bool wide = mi < 4 && ((have >> mi) & 1);
   const int bw = wide ? E.kst : 8;  // keys per box
-  const int nbox = nkeys / bw;      // <= 64
-  // boxes b = lane and lane + 32; a box is issued when any of its keys lies in a touched tile
+  const int nbp = nkeys / bw;       // boxes per plane
+  const int np = E.pg == 2 && E.zlo + k.zr * 2 + 1 <= E.zhi ? 2 : 1;
+  // boxes b = lane and lane + 32 (plane b / nbp); a box is issued when any of its keys lies in a touched tile
   bool on[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const int b = lane + 32 * u;
     on[u] = false;
-    if (b < nbox) {
-      const int t0 = (b * bw) >> 4, t1 = (b * bw + bw - 1) >> 4;
+    if (b < np * nbp) {
+      const int pl = b >= nbp ? 1 : 0;
+      const int key0 = pl * E.kpp + (b - pl * nbp) * bw;
+      const int t0 = key0 >> 4, t1 = (key0 + bw - 1) >> 4;
       on[u] = ((k.m >> t0) & ((2u << (t1 - t0)) - 1u)) != 0u;
     }
   }
-  const bool tail = (nkeys & 15) && ((k.m >> (nkeys >> 4)) & 1u);
+  // plane pl's tail: keys pl * kpp + nkeys .. +7 when that tile is touched
+  bool tail[2];
+#pragma unroll
+  for (int pl = 0; pl < 2; ++pl) {
+    const int kt = pl * E.kpp + nkeys;
+    tail[pl] = pl < np && (nkeys & 15) && ((k.m >> (kt >> 4)) & 1u);
+  }
   const int cnt = __popc(__ballot_sync(0xffffffffu, on[0])) + __popc(__ballot_sync(0xffffffffu, on[1]));
   if (threadIdx.x == 0) {
     if (first) fence_proxy_async();
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>((cnt * bw + (tail ? 8 : 0)) * rs * 2));
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>((cnt * bw + ((tail[0] ? 8 : 0) + (tail[1] ? 8 : 0))) * rs * 2));
   }
   __syncwarp();
-  const int zl = E.zlo + k.zr - P.kv_frame0;
   if (first && (on[0] || on[1])) fence_proxy_async();
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     if (!on[u] || (lane + 32 * u) % kIW != wid) continue;
     const int b = lane + 32 * u;
-    const int row = wide ? b : b / (E.kst >> 3);
-    const int col = wide ? 0 : (b - row * (E.kst >> 3)) * 8;
-    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>(b * bw * rs * 2), wide ? maps + mi : maps, bar, T.head * P.d,
-                chunk_xa(E, k) + col, chunk_ya(E, k) + row, zl, T.b);
+    const int pl = b >= nbp ? 1 : 0, lb = b - pl * nbp;
+    const int row = wide ? lb : lb / (E.kst >> 3);
+    const int col = wide ? 0 : (lb - row * (E.kst >> 3)) * 8;
+    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((pl * E.kpp + lb * bw) * rs * 2), wide ? maps + mi : maps, bar,
+                T.head * P.d, chunk_xa(E, k) + col, chunk_ya(E, k) + row, E.zlo + k.zr * E.pg + pl - P.kv_frame0, T.b);
   }
-  if (tail && threadIdx.x == 0)  // columns W .. W+7: all outside the volume
-    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>(nkeys * rs * 2), maps, bar, T.head * P.d, P.W, 0, 0, T.b);
+  if (threadIdx.x < 2 && tail[threadIdx.x])  // columns W .. W+7: all outside the volume
+    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((threadIdx.x * E.kpp + nkeys) * rs * 2), maps, bar, T.head * P.d,
+                P.W, 0, 0, T.b);
 }
 
 // Waits for the TMA copies of phase `parity` on mbarrier bar.  Bounded: after about a second the CTA

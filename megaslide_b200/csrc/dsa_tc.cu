@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   if (masks) chunk_pair_planes(E, L.maxkeys);
 
   // ---- records, frame-bucket counts and touched-tile masks; scores start at 0
-  for (int s = 0; s < jper; ++s) {  // same trip count in every lane: warp collectives inside
+  for (int s = 0; s < jper; ++s) {
     const int j = js + s;
     int bk = -1, pa = -1, pb = -1;
     uint32_t bits = 0u;
@@ -279,8 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
       }
       S.rec[qbase + j] = v;
     }
-    const unsigned peers = __match_any_sync(kFull, bk);
-    if (bk >= 0 && lane == __ffs(peers) - 1) atomicAdd(S.bcur + bk, __popc(peers));
+    if (bk >= 0) atomicAdd(S.bcur + bk, 1);  // plain shared atomics: faster than warp-matched ones here
     if (pa >= 0 && (S.mask[pa] & bits) != bits) atomicOr(S.mask + pa, bits);
     if (pb >= 0 && (S.mask[pb] & bits) != bits) atomicOr(S.mask + pb, bits);
   }
@@ -296,12 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
       const unsigned long long v = S.rec[qbase + j];
       if (v >> 63) bk = rec_bucket(v);
     }
-    const unsigned peers = __match_any_sync(kFull, bk);
-    const int leader = __ffs(peers) - 1;
-    int pos = 0;
-    if (bk >= 0 && lane == leader) pos = atomicAdd(S.bcur + bk, __popc(peers));
-    pos = __shfl_sync(kFull, pos, leader) + __popc(peers & ((1u << lane) - 1u));
-    if (bk >= 0) S.hits[pos] = static_cast<unsigned short>(qbase + j);
+    if (bk >= 0) S.hits[atomicAdd(S.bcur + bk, 1)] = static_cast<unsigned short>(qbase + j);
   }
   const int g = lane >> 2, t4 = lane & 3;
   float* grow_s = S.sbuf + static_cast<size_t>(r) * 16 * L.sld;  // the row group's 16 dense rows

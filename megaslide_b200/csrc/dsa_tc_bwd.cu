@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   // ---- records (interior / keep flags), frame-bucket counts and touched-tile masks
   {
     const uint64_t qglob = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
-    for (int s = 0; s < jper; ++s) {  // same trip count in every lane: warp collectives inside
+    for (int s = 0; s < jper; ++s) {
       const int j = js + s;
       int bk = -1, pa = -1, pb = -1;
       uint32_t bits = 0u;
@@ -390,8 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
         }
         S.rec[qbase + j] = v;
       }
-      const unsigned peers = __match_any_sync(kFull, bk);
-      if (bk >= 0 && lane == __ffs(peers) - 1) atomicAdd(S.bcur + bk, __popc(peers));
+      if (bk >= 0) atomicAdd(S.bcur + bk, 1);  // plain shared atomics: faster than warp-matched ones here
       if (pa >= 0 && (S.mask[pa] & bits) != bits) atomicOr(S.mask + pa, bits);
       if (pb >= 0 && (S.mask[pb] & bits) != bits) atomicOr(S.mask + pb, bits);
     }
@@ -411,12 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
       S.g3[3 * (qbase + j) + 1] = 0.f;
       S.g3[3 * (qbase + j) + 2] = 0.f;
     }
-    const unsigned peers = __match_any_sync(kFull, bk);
-    const int leader = __ffs(peers) - 1;
-    int pos = 0;
-    if (bk >= 0 && lane == leader) pos = atomicAdd(S.bcur + bk, __popc(peers));
-    pos = __shfl_sync(kFull, pos, leader) + __popc(peers & ((1u << lane) - 1u));
-    if (bk >= 0) S.hits[pos] = static_cast<unsigned short>(qbase + j);
+    if (bk >= 0) S.hits[atomicAdd(S.bcur + bk, 1)] = static_cast<unsigned short>(qbase + j);
   }
 
   const int g = lane >> 2, t4 = lane & 3;

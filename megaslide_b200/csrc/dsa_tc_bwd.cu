@@ -137,15 +137,16 @@ __device__ __forceinline__ PlaneTerms plane_terms(const float* row, int k00, int
 
 // ------------------------------------------------------------------------------ chunk operands
 // accum[key][d] += A . X over the tiles of mask m: A = the transposed bf16 tile tb ([key][query], all
-// 32 queries, ldmatrix), X = 32 bf16 rows (Q or dO) in shared memory.  Items = (16-key tile, group of
-// 3 channel tiles), round robin over the 16 warps: one A fragment serves three independent
-// accumulator chains.  Each lane adds its fragment pairs to the float32 accumulator rows key_off[key]
+// 32 queries, ldmatrix), X = 32 bf16 rows (Q or dO) in shared memory.  Items = (16-key tile, the
+// head's channel tiles, or half of them for even counts and head_dim > 72: registers), round robin
+// over the 16 warps: one A fragment serves every accumulator chain of the item (measured at
+// head_dim 72: whole-head items beat 3 or 5 channel tiles).  Each lane adds its fragment pairs to the float32 accumulator rows key_off[key]
 // with float2 atomics (no shuffles or zero tests: fewer instructions measured faster).
 template <int DCH>
 __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const TileCtx& T, const TcLaunch& L,
                                                  const __nv_bfloat16* tb, const __nv_bfloat16* xs, const int* key_off,
                                                  uint32_t m, float* accum) {
-  constexpr int NG = 3;                     // channel tiles per item
+  constexpr int NG = (DCH & 1) && DCH <= 9 ? DCH : (DCH + 1) / 2;  // channel tiles per item (head or half)
   constexpr int NCG = (DCH + NG - 1) / NG;  // channel groups
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
@@ -167,20 +168,18 @@ __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const Tile
               a[2], a[3]);
       // x4.trans matrices: (queries +0..7, ch nt) (queries +8..15, ch nt) (+0..7, nt+1) (+8..15, nt+1)
       const __nv_bfloat16* rowp = xs + static_cast<size_t>(kk * 16 + rr + ((mi & 1) ? 8 : 0)) * L.rs;
-      if (nt0 + 1 < DCH) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(rowp + (nt0 + (mi >> 1)) * 8), b0, b1, b2, b3);
-        mma16816(c[0], a, b0, b1);
-        mma16816(c[1], a, b2, b3);
-      } else {
-        uint32_t b0, b1;
-        ldsm_x2_t(smem_u32(rowp + nt0 * 8), b0, b1);
-        mma16816(c[0], a, b0, b1);
-      }
-      if (nt0 + 2 < DCH) {
-        uint32_t b0, b1;
-        ldsm_x2_t(smem_u32(rowp + (nt0 + 2) * 8), b0, b1);
-        mma16816(c[2], a, b0, b1);
+#pragma unroll
+      for (int j = 0; j < NG; j += 2) {
+        if (nt0 + j + 1 < DCH && j + 1 < NG) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_u32(rowp + (nt0 + j + (mi >> 1)) * 8), b0, b1, b2, b3);
+          mma16816(c[j], a, b0, b1);
+          mma16816(c[j + 1], a, b2, b3);
+        } else if (nt0 + j < DCH) {
+          uint32_t b0, b1;
+          ldsm_x2_t(smem_u32(rowp + (nt0 + j) * 8), b0, b1);
+          mma16816(c[j], a, b0, b1);
+        }
       }
     }
     const int o0 = key_off[tile * 16 + g], o1 = key_off[tile * 16 + g + 8];

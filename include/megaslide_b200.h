@@ -89,7 +89,11 @@ typedef struct msl_dsa_geometry {
  * the backward pass); status: optional device word OR-ed with MSL_STATUS_* bits;
  * probs: optional float32 [B, nh, q rows, kt*kh*kw], the softmax weight of every window sample
  * before dropout (extra keys excluded), written only by the tensor-core path (MSL_ALGO_TC, or
- * MSL_ALGO_AUTO when it applies) and consumed by the tensor-core backward; NULL = not saved. */
+ * MSL_ALGO_AUTO when it applies) and consumed by the tensor-core backward; NULL = not saved.
+ * saved: optional msl_dsa_saved_bytes(geom) bytes (16-byte aligned): the tensor-core forward's
+ * per-sample records (trilinear corner, fractions, interior and dropout flags) and per-tile key
+ * envelopes, which the tensor-core backward reads instead of recomputing the sample coordinates
+ * from the offsets; written only by the tensor-core path.  NULL = not saved. */
 typedef struct msl_dsa_fwd_io {
   const void* q;   int64_t q_ld;
   const void* k;   int64_t k_ld;
@@ -100,6 +104,7 @@ typedef struct msl_dsa_fwd_io {
   float* lse;
   uint32_t* status;
   float* probs;
+  void* saved;
 } msl_dsa_fwd_io;
 
 /* Backward operands.  Inputs as in the forward plus out/lse from it and dout = dL/d out.
@@ -112,8 +117,9 @@ typedef struct msl_dsa_fwd_io {
  *   dk_acc != NULL: float32 dk_acc, dv_acc [B, kv rows, >=nh*d] (row stride acc_ld) are
  *                   ACCUMULATED into (not cleared), dk / dv are not touched.  Used by the
  *                   time-sharded path, which reduces halo rows across ranks before converting.
- * probs: the forward's optional softmax weights (see msl_dsa_fwd_io).  When given (bf16, no extra
- * keys) the tensor-core backward runs; NULL selects the CUDA-core backward. */
+ * probs, saved: the tensor-core forward's optional outputs (see msl_dsa_fwd_io), from the forward of
+ * the same operands.  When both are given (bf16, no extra keys) the tensor-core backward runs;
+ * otherwise the CUDA-core backward. */
 typedef struct msl_dsa_bwd_io {
   const void* q;   int64_t q_ld;
   const void* k;   int64_t k_ld;
@@ -130,7 +136,12 @@ typedef struct msl_dsa_bwd_io {
   float* dek;      float* dev;
   uint32_t* status;
   const float* probs;
+  const void* saved;
 } msl_dsa_bwd_io;
+
+/* Size in bytes of the `saved` buffer of msl_dsa_fwd_io / msl_dsa_bwd_io for this geometry
+ * (0 for an invalid geometry). */
+size_t msl_dsa_saved_bytes(const msl_dsa_geometry* geom);
 
 /* Forward of the deformable gather attention: for every query, head and window sample, the
  * trilinear border-clamped sample of K and V at the offset grid position (reference

@@ -57,7 +57,7 @@ class DsaFwdIO(ctypes.Structure):
     _fields_ = [
         ("q", _vp), ("q_ld", _i64), ("k", _vp), ("k_ld", _i64), ("v", _vp), ("v_ld", _i64),
         ("offsets", _vp), ("off_ld", _i64), ("ek", _vp), ("ev", _vp), ("e_ld", _i64),
-        ("out", _vp), ("out_ld", _i64), ("lse", _vp), ("status", _vp), ("probs", _vp),
+        ("out", _vp), ("out_ld", _i64), ("lse", _vp), ("status", _vp), ("probs", _vp), ("saved", _vp),
     ]
 
 
@@ -71,6 +71,7 @@ class DsaBwdIO(ctypes.Structure):
         ("dq", _vp), ("dq_ld", _i64), ("dk", _vp), ("dv", _vp), ("dkv_ld", _i64),
         ("dk_acc", _vp), ("dv_acc", _vp), ("acc_ld", _i64),
         ("doffsets", _vp), ("doff_ld", _i64), ("dek", _vp), ("dev", _vp), ("status", _vp), ("probs", _vp),
+        ("saved", _vp),
     ]
 
 
@@ -88,6 +89,7 @@ class DwconvGeometry(ctypes.Structure):
 SIGNATURES = {
     "msl_dsa_attn_fwd": (ctypes.c_int, [ctypes.POINTER(DsaGeometry), ctypes.POINTER(DsaFwdIO), _vp]),
     "msl_dsa_attn_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(DsaGeometry), _i32]),
+    "msl_dsa_saved_bytes": (ctypes.c_size_t, [ctypes.POINTER(DsaGeometry)]),
     "msl_dsa_attn_bwd": (ctypes.c_int, [ctypes.POINTER(DsaGeometry), ctypes.POINTER(DsaBwdIO), _vp,
                                         ctypes.c_size_t, _vp]),
     "msl_dsa_attn_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(DsaGeometry), ctypes.POINTER(DsaBwdIO), _vp]),

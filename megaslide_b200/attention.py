@@ -85,21 +85,22 @@ class DSA3DFunction(torch.autograd.Function):
             ekv = torch.addmm(torch.cat([bk, bv], 0).to(dt), e2, torch.cat([wk, wv], 0).to(dt).t())
             ek, ev = ekv[:, :C], ekv[:, C:]
         train = any(ctx.needs_input_grad)
-        probs = None
+        probs = saved = None
         if train and ops.wants_probs(sh, dt):
-            # the tensor-core backward reads the forward's per-sample softmax weights
-            probs = ops.probs_buffer(sh, x2.device)
+            # the tensor-core backward reads the forward's per-sample softmax weights and records
+            probs, saved = ops.saved_buffers(sh, dt, x2.device)
             try:
-                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs)
+                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved)
             except MslError as e:
                 if e.code != MSL_ERR_UNSUPPORTED:
                     raise
-                probs = None
+                probs = saved = None
         if probs is None:
             attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev)
         y = torch.addmm(D, attn, wo.to(dt).t())
         if train:
-            ctx.save_for_backward(x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs)
+            ctx.save_for_backward(x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
+                                  saved)
             ctx.cfg = cfg
             ctx.in_dtype = x.dtype
             ctx.extra_dtype = extra_kv.dtype if extra_kv is not None else None
@@ -107,7 +108,7 @@ class DSA3DFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        (x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs) = ctx.saved_tensors
+        (x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs, saved) = ctx.saved_tensors
         cfg: _Cfg = ctx.cfg
         sh: ops.DsaShape = cfg.shape
         dt = cfg.dtype
@@ -130,7 +131,7 @@ class DSA3DFunction(torch.autograd.Function):
             q, k, v = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
             _, _, _, doff, dek, dev = ops.attn_bwd(
                 sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev,
-                dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs)
+                dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs, saved=saved)
             # q/k/v projections
             dx += _mm_f32(dqkv, wqkv)
             g_wqkv = _mm_f32(dqkv.t(), x2)

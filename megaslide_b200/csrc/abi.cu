@@ -189,6 +189,8 @@ int msl_dsa_attn_fwd(const msl_dsa_geometry* geom, const msl_dsa_fwd_io* io, voi
   P.offsets = io->offsets; P.off_ld = io->off_ld;
   P.ek = io->ek; P.ev = io->ev; P.e_ld = io->e_ld;
   P.out = io->out; P.out_ld = io->out_ld; P.lse = io->lse; P.status = io->status; P.probs = io->probs;
+  P.saved = io->saved;
+  if (io->saved && !aligned16(io->saved)) return fail(MSL_ERR_INVALID, "saved must be 16-byte aligned");
   if (geom->algo != MSL_ALGO_SIMT) {
     bool ok = msl::tc_supported(P);
     for (const auto& r : {std::make_pair(io->q, io->q_ld), std::make_pair(io->k, io->k_ld), std::make_pair(io->v, io->v_ld),
@@ -204,11 +206,12 @@ int msl_dsa_attn_fwd(const msl_dsa_geometry* geom, const msl_dsa_fwd_io* io, voi
       g_launches.fetch_add(1, std::memory_order_relaxed);
       return MSL_OK;
     }
-    if (geom->algo == MSL_ALGO_TC || io->probs)
+    if (geom->algo == MSL_ALGO_TC || io->probs || io->saved)
       return fail(MSL_ERR_UNSUPPORTED, "tensor-core path (%s) needs bf16, head_dim %% 8 == 0 in [16,128], 16-byte aligned rows",
-                  io->probs ? "required by the probs output" : "algo = MSL_ALGO_TC");
+                  (io->probs || io->saved) ? "required by the probs / saved outputs" : "algo = MSL_ALGO_TC");
   }
-  if (io->probs) return fail(MSL_ERR_UNSUPPORTED, "the probs output is written by the tensor-core path only (algo != SIMT)");
+  if (io->probs || io->saved)
+    return fail(MSL_ERR_UNSUPPORTED, "the probs / saved outputs are written by the tensor-core path only (algo != SIMT)");
   int vec = 1, maxc = 1;
   rc = choose_chunking(P, {{io->q, io->q_ld}, {io->k, io->k_ld}, {io->v, io->v_ld}, {io->out, io->out_ld},
                            {P.G > 0 ? io->ek : nullptr, io->e_ld}, {P.G > 0 ? io->ev : nullptr, io->e_ld}},
@@ -218,6 +221,12 @@ int msl_dsa_attn_fwd(const msl_dsa_geometry* geom, const msl_dsa_fwd_io* io, voi
   if (e != cudaSuccess) return cuda_fail(e, "dsa_fwd_kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return MSL_OK;
+}
+
+size_t msl_dsa_saved_bytes(const msl_dsa_geometry* geom) {
+  msl::AttnParams P;
+  if (fill_geometry(geom, P)) return 0;
+  return static_cast<size_t>(msl::saved_bytes(P));
 }
 
 size_t msl_dsa_attn_bwd_workspace_bytes(const msl_dsa_geometry* geom, int32_t accumulate_mode) {
@@ -265,6 +274,8 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
   P.dout = io->dout; P.dout_ld = io->dout_ld; P.dq = io->dq; P.dq_ld = io->dq_ld;
   P.doffsets = io->doffsets; P.doff_ld = io->doff_ld; P.status = io->status;
   P.probs = const_cast<float*>(io->probs);
+  P.saved = const_cast<void*>(io->saved);
+  if (io->saved && !aligned16(io->saved)) return fail(MSL_ERR_INVALID, "saved must be 16-byte aligned");
   if (accumulate) {
     P.dk_acc = io->dk_acc; P.dv_acc = io->dv_acc; P.acc_ld = io->acc_ld;
   } else {
@@ -280,7 +291,7 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
   // tensor-core backward: bf16, no extra keys, softmax weights saved by the forward, aligned rows
   msl::TcLaunch TL{};
   bool use_tc = false;
-  if (geom->algo != MSL_ALGO_SIMT && P.probs) {
+  if (geom->algo != MSL_ALGO_SIMT && P.probs && P.saved) {
     use_tc = msl::tc_bwd_supported(P);
     for (const auto& r : {std::make_pair(io->q, io->q_ld), std::make_pair(io->k, io->k_ld), std::make_pair(io->v, io->v_ld),
                           std::make_pair(io->out, io->out_ld), std::make_pair(io->dout, io->dout_ld),
@@ -290,7 +301,7 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
     if (use_tc) use_tc = msl::tc_bwd_plan(P, TL, tc_smem_limit());
   }
   if (geom->algo == MSL_ALGO_TC && !use_tc)
-    return fail(MSL_ERR_UNSUPPORTED, "tensor-core backward needs probs from the tensor-core forward, bf16, no extra keys, "
+    return fail(MSL_ERR_UNSUPPORTED, "tensor-core backward needs probs and saved from the tensor-core forward, bf16, no extra keys, "
                                      "head_dim %% 8 == 0 in [16,128] and 16-byte aligned rows");
   int vec = 1, maxc = 1;
   rc = choose_chunking(P, {{io->q, io->q_ld}, {io->k, io->k_ld}, {io->v, io->v_ld}, {io->out, io->out_ld},

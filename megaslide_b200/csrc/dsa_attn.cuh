@@ -30,6 +30,7 @@ struct AttnParams {
   void* out; long long out_ld;        // forward: written; backward: read
   float* lse;
   float* probs;       // [B, nh, Nq, K] softmax weights before dropout (optional; tensor-core paths)
+  void* saved;        // tensor-core forward -> backward: per-sample records + tile envelopes (optional)
   const void* dout; long long dout_ld;
   void* dq; long long dq_ld;
   float* dk_acc; float* dv_acc; long long acc_ld;
@@ -49,6 +50,13 @@ struct TcLaunch {
   long long tiles;
   size_t smem;
 };
+// Layout of `saved` (msl_dsa_saved_bytes): the forward's records [B, nh, Nq, K] uint64, then from
+// saved_env_offset(P) on, per 4 x 8 query tile in CTA order, its raw envelope (8 int32: zlo, zhi, ylo,
+// yhi, xlo, xhi, 0, 0).
+__host__ __device__ inline long long saved_env_offset(const AttnParams& P) {
+  return ((static_cast<long long>(P.B) * P.nh * P.Nq * P.K * 8) + 255) & ~255LL;
+}
+long long saved_bytes(const AttnParams& P);
 bool tc_supported(const AttnParams& P);
 bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit);
 cudaError_t launch_attn_fwd_tc(const AttnParams& P, const TcLaunch& L, cudaStream_t s);

@@ -249,7 +249,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   const bool fsplit = split && !masks;  // chunks of a plane share one hit bucket: filter the hits
   if (masks) chunk_pair_planes(E, L.maxkeys);
 
-  // ---- records, frame-bucket counts and touched-tile masks; scores start at 0
+  // ---- records (interior / keep flags for the backward), frame-bucket counts and touched-tile masks;
+  //      scores start at 0
+  const uint64_t qglob = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
   for (int s = 0; s < jper; ++s) {
     const int j = js + s;
     int bk = -1, pa = -1, pb = -1;
@@ -263,8 +265,13 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
       unsigned long long v = 0ull;
       if (work && t0 + 1 >= E.zlo && t0 <= E.zhi) {  // a corner in a frame the K/V buffers hold
         const int dz = t0 - E.zlo + 1;
+        const bool keep = !P.drop_thresh ||
+                          dropout_keep(P.seed, (qglob * P.nh + T.head) * static_cast<uint64_t>(KG) + j, P.drop_thresh);
         v = pack_rec(pt - static_cast<float>(t0), ph - static_cast<float>(h0), pw - static_cast<float>(w0), dz,
-                     h0 - E.ylo, w0 - E.xlo);
+                     h0 - E.ylo, w0 - E.xlo) |
+            (clip_grad_mult(pt, P.T) != 0.f ? 1ull << kBitInT : 0ull) |
+            (clip_grad_mult(ph, P.H) != 0.f ? 1ull << kBitInH : 0ull) |
+            (clip_grad_mult(pw, P.W) != 0.f ? 1ull << kBitInW : 0ull) | (keep ? 1ull << kBitKeep : 0ull);
         bk = dz;
         if (masks) {
           const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
@@ -287,6 +294,18 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     for (int e = K + sub; e < KG; e += kLPQ) sacc[e] = 0.f;
   __syncthreads();
   if (warp == 0) scan_buckets(S.bcur, S.bstart);
+  if (P.saved) {  // the records and the raw envelope for the tensor-core backward
+    if (qvalid) {
+      unsigned long long* dst = static_cast<unsigned long long*>(P.saved) +
+                                ((static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow) * K;
+      for (int j = sub; j < K; j += kLPQ) dst[j] = S.rec[qbase + j];
+    }
+    if (threadIdx.x == 32) {
+      int4* env = reinterpret_cast<int4*>(static_cast<char*>(P.saved) + saved_env_offset(P)) + 2 * blockIdx.x;
+      env[0] = make_int4(S.env[0], S.env[1], S.env[2], S.env[3]);
+      env[1] = make_int4(S.env[4], S.env[5], 0, 0);
+    }
+  }
   __syncthreads();
   for (int s = 0; s < jper; ++s) {  // hit list: every active sample once, grouped by (chunk, frame) bucket
     const int j = js + s;
@@ -525,6 +544,12 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
 }  // namespace tc
 
 // ------------------------------------------------------------------------------ host side
+long long saved_bytes(const AttnParams& P) {
+  const long long tiles = static_cast<long long>(P.B) * P.q_frames * ((P.H + tc::t32::kTileH - 1) / tc::t32::kTileH) *
+                          ((P.W + tc::kTileW - 1) / tc::kTileW) * P.nh;
+  return saved_env_offset(P) + tiles * 32;
+}
+
 bool tc_supported(const AttnParams& P) {
   if (P.dtype != MSL_DTYPE_BF16) return false;
   if (P.d % 8 != 0 || P.d < 16 || P.d > 128) return false;

@@ -64,6 +64,9 @@ __device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t&
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g));
 }
+__device__ __forceinline__ void cp_async8(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(saddr), "l"(g));
+}
 __device__ __forceinline__ void cp_async4(uint32_t saddr, const void* g) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(saddr), "l"(g));
 }
@@ -430,6 +433,9 @@ __device__ __forceinline__ Rec decode_rec(unsigned long long v, const Env& E) {
 // (iy * nx + ix, when tile masks are kept, else 0); bucket = chunk * 32 + (t0 - zlo + 1).  The hits of
 // chunk c in plane zr are the buckets c * 32 + zr (upper corner there) and c * 32 + zr + 1 (lower):
 // one contiguous range [bstart[c * 32 + zr], bstart[c * 32 + zr + 2]).
+// record flags (both kernels; set by the forward, read by the backward): grid coordinate strictly
+// inside (0, S-1) along t / h / w, dropout keep
+constexpr int kBitInT = 57, kBitInH = 58, kBitInW = 59, kBitKeep = 60;
 constexpr int kBitChunk = 61;
 constexpr int kBuckets = 128;
 __device__ __forceinline__ int rec_bucket(unsigned long long v) {

@@ -37,8 +37,6 @@ namespace bwd {
 
 using namespace t32;
 
-// record flags: grid coordinate strictly inside (0, S-1) along t / h / w, dropout keep
-constexpr int kBitInT = 57, kBitInH = 58, kBitInW = 59, kBitKeep = 60;
 
 
 struct Smem {
@@ -87,7 +85,7 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   s.key_off = reinterpret_cast<int*>(base + off);
   off += static_cast<size_t>(L.maxkeys) * 4;
   s.env = reinterpret_cast<int*>(base + off);
-  off += kEnvWords * 4;
+  off += 16 * 4;  // envelope (the backward reads the forward's; no base-grid tables)
   s.dd = reinterpret_cast<float*>(base + off);
   off += kQ * 4;
   s.qsc = reinterpret_cast<float*>(base + off);
@@ -100,7 +98,6 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
   off += 32 * kMaxMaskChunks * 4;
   s.hits = reinterpret_cast<unsigned short*>(base + off);
   off += static_cast<size_t>(kQ) * P.K * 2;
-  // last: the setup's offset staging spills from the key buffer into the regions after it
   off = (off + 7) & ~static_cast<size_t>(7);
   s.kbar = reinterpret_cast<unsigned long long*>(base + off);
   s.dead = reinterpret_cast<int*>(base + off + 8);
@@ -109,7 +106,7 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const AttnParams& P, 
 
 // shared memory besides the key buffer, the two dense tiles and the key table
 size_t smem_fixed(const AttnParams& P, int rs) {
-  return static_cast<size_t>(kQ) * rs * 2 * 2 + static_cast<size_t>(kQ) * P.K * (8 + 4 + 12 + 2) + kEnvWords * 4 +
+  return static_cast<size_t>(kQ) * rs * 2 * 2 + static_cast<size_t>(kQ) * P.K * (8 + 4 + 12 + 2) + 16 * 4 +
          kQ * (8 + 4 + 16) + (2 * kBuckets + 4 + 32 * kMaxMaskChunks) * 4 + 24 + 256;
 }
 
@@ -219,13 +216,6 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   const long long qrow = (static_cast<long long>(T.tl) * P.H + qh) * P.W + qw;
   const int qbase = qi * K;  // this query's samples in rec / sv / g3
 
-  float* tabz = reinterpret_cast<float*>(S.env + 16);
-  float* taby = tabz + 96;
-  float* tabx = taby + 96;
-  if (threadIdx.x == 0) {
-    S.env[0] = 0x7fffffff; S.env[1] = -0x7fffffff; S.env[2] = 0x7fffffff;
-    S.env[3] = -0x7fffffff; S.env[4] = 0x7fffffff; S.env[5] = -0x7fffffff;
-  }
   if (threadIdx.x < kBuckets) S.bcur[threadIdx.x] = 0;
   if (threadIdx.x < 32 * kMaxMaskChunks) S.mask[threadIdx.x] = 0u;
   if (sub == 0) S.prow[qi] = (static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow;
@@ -240,20 +230,22 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     }
   }
   uint32_t kphase = 0;
-  fill_tabs(P, T, kTileH, tabz, taby, tabx);
 
-  // ---- stage the tile's offsets (this head), Q and dO rows with one wave of cp.async
-  const int K3 = 3 * K;
-  float* ostage = reinterpret_cast<float*>(S.kbuf);
+  // ---- stage the forward's records of the tile (this head), Q and dO rows with one wave of cp.async;
+  //      the tile's envelope as the forward computed it
+  const unsigned long long* recs = static_cast<const unsigned long long*>(P.saved);
   for (int q2 = warp; q2 < kQ; q2 += kWarps) {
     int sqh, sqw;
     query_hw(T, q2 >> 4, q2 & 15, sqh, sqw);
     const bool ok = sqh < P.H && sqw < P.W;
-    const long long grow = static_cast<long long>(T.b) * P.Nq + (static_cast<long long>(T.tl) * P.H + sqh) * P.W + sqw;
+    const long long prow = (static_cast<long long>(T.tl) * P.H + sqh) * P.W + sqw;
+    const long long grow = static_cast<long long>(T.b) * P.Nq + prow;
+    unsigned long long* rdst = S.rec + static_cast<size_t>(q2) * K;
     if (ok) {
-      const float* src = P.offsets + grow * P.off_ld + static_cast<long long>(T.head) * K3;
-      float* dst = ostage + static_cast<size_t>(q2) * K3;
-      for (int k = lane; k < K3; k += 32) cp_async4(smem_u32(dst + k), src + k);
+      const unsigned long long* src = recs + ((static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + prow) * K;
+      for (int k = lane; k < K; k += 32) cp_async8(smem_u32(rdst + k), src + k);
+    } else {
+      for (int k = lane; k < K; k += 32) rdst[k] = 0ull;
     }
     for (int ch = lane; ch < DCH; ch += 32) {
       __nv_bfloat16* dq_ = S.qs + static_cast<size_t>(q2) * L.rs + ch * 8;
@@ -267,10 +259,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
       }
     }
   }
+  if (threadIdx.x < 6) S.env[threadIdx.x] =
+      reinterpret_cast<const int*>(static_cast<const char*>(P.saved) + saved_env_offset(P))[8 * blockIdx.x + threadIdx.x];
   cp_async_wait_all();
   __syncthreads();
-  const Tabs tb{tabz, taby, tabx};
-  const int qy = qh - T.qh0, qx = qw - T.qw0;
 
   // ---- D = dO . O per query (the lanes of a query split the head dimension)
   {
@@ -287,52 +279,6 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     if (sub == 0) S.dd[qi] = dpart;
   }
 
-  // ---- sample coordinates -> envelope (raw coordinates parked in rec / sv)
-  const int kvlo = max(P.kv_frame0, 0), kvhi = min(P.kv_frame0 + P.kv_frames, P.T) - 1;
-  int zmn = 0x7fffffff, zmx = -0x7fffffff, ymn = 0x7fffffff, ymx = -0x7fffffff, xmn = 0x7fffffff, xmx = -0x7fffffff;
-  bool miss = false;
-  if (qvalid) {
-    const float* oq = ostage + static_cast<size_t>(qi) * K3;
-    WinIdx wi;
-    wi.init(js, P.kh, P.kw);
-    for (int j = js; j < je; ++j, wi.advance(1, P.kh, P.kw)) {
-      float pt, ph, pw;
-      tab_coords(P, tb, qy, qx, wi.it, wi.ih, wi.iw, oq[3 * j], oq[3 * j + 1], oq[3 * j + 2], pt, ph, pw);
-      S.rec[qbase + j] = (static_cast<unsigned long long>(__float_as_uint(ph)) << 32) | __float_as_uint(pt);
-      S.sv[qbase + j] = pw;
-      const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
-      for (int dt = 0; dt < 2; ++dt) {
-        const int tc = t0 + dt;
-        if (tc >= P.T) continue;
-        if (tc < kvlo || tc > kvhi) {
-          miss = true;
-          continue;
-        }
-        zmn = min(zmn, tc);
-        zmx = max(zmx, tc);
-      }
-      ymn = min(ymn, h0);
-      ymx = max(ymx, h0 + 1 < P.H ? h0 + 1 : h0);
-      xmn = min(xmn, w0);
-      xmx = max(xmx, w0 + 1 < P.W ? w0 + 1 : w0);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    zmn = min(zmn, __shfl_xor_sync(kFull, zmn, o));
-    zmx = max(zmx, __shfl_xor_sync(kFull, zmx, o));
-    ymn = min(ymn, __shfl_xor_sync(kFull, ymn, o));
-    ymx = max(ymx, __shfl_xor_sync(kFull, ymx, o));
-    xmn = min(xmn, __shfl_xor_sync(kFull, xmn, o));
-    xmx = max(xmx, __shfl_xor_sync(kFull, xmx, o));
-  }
-  if (lane == 0) {
-    atomicMin(S.env + 0, zmn); atomicMax(S.env + 1, zmx);
-    atomicMin(S.env + 2, ymn); atomicMax(S.env + 3, ymx);
-    atomicMin(S.env + 4, xmn); atomicMax(S.env + 5, xmx);
-  }
-  if (__any_sync(kFull, miss) && lane == 0 && P.status) atomicOr(P.status, MSL_STATUS_HALO_MISS);
-  __syncthreads();
   Env E;
   E.zlo = S.env[0]; E.zhi = S.env[1]; E.ylo = S.env[2]; E.yhi = S.env[3]; E.xlo = S.env[4]; E.xhi = S.env[5];
   const bool any = E.zlo <= E.zhi && E.ylo <= E.yhi && E.xlo <= E.xhi;
@@ -350,49 +296,36 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
   const bool fsplit = split && !masks;  // chunks of a plane share one hit bucket: filter the hits
 
-  // ---- records (interior / keep flags), frame-bucket counts and touched-tile masks
-  {
-    const uint64_t qglob = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
-    for (int s = 0; s < jper; ++s) {
-      const int j = js + s;
-      int bk = -1, pa = -1, pb = -1;
-      uint32_t bits = 0u;
-      if (qvalid && s < n) {
-        const unsigned long long raw = S.rec[qbase + j];
-        const float pt = __uint_as_float(static_cast<uint32_t>(raw)), ph = __uint_as_float(static_cast<uint32_t>(raw >> 32));
-        const float pw = S.sv[qbase + j];
-        const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));
-        unsigned long long v = 0ull;
-        if (work && t0 + 1 >= E.zlo && t0 <= E.zhi) {  // a corner in a frame the K/V buffers hold
-          bool keep = true;
-          if (P.drop_thresh)
-            keep = dropout_keep(P.seed, (qglob * P.nh + T.head) * static_cast<uint64_t>(K + P.G) + j, P.drop_thresh);
-          const unsigned long long flags = (clip_grad_mult(pt, P.T) != 0.f ? 1ull << kBitInT : 0ull) |
-                                           (clip_grad_mult(ph, P.H) != 0.f ? 1ull << kBitInH : 0ull) |
-                                           (clip_grad_mult(pw, P.W) != 0.f ? 1ull << kBitInW : 0ull) |
-                                           (keep ? 1ull << kBitKeep : 0ull);
-          const int dz = t0 - E.zlo + 1;
-          v = pack_rec(pt - static_cast<float>(t0), ph - static_cast<float>(h0), pw - static_cast<float>(w0), dz,
-                       h0 - E.ylo, w0 - E.xlo) |
-              flags;
-          bk = dz;
-          if (masks) {
-            const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
-            const int ya = E.ylo + iy * (E.R - 1), xa = E.xlo + ix * (E.cw - 1);
-            bits = corner_tiles((h0 - ya) * E.kst + (w0 - xa), E.kst, w0 + 1 < P.W, h0 + 1 < P.H);
-            const int chk = iy * E.nx + ix;
-            if (t0 >= E.zlo) pa = dz * kMaxMaskChunks + chk;           // plane z = t0 (zrel = dz)
-            if (t0 + 1 <= E.zhi) pb = (dz + 1) * kMaxMaskChunks + chk; // plane z = t0 + 1
-            v |= static_cast<unsigned long long>(chk) << kBitChunk;
-            bk += chk * 32;
-          }
+  // ---- the forward's records with this kernel's chunk bits; frame-bucket counts and touched-tile masks
+  for (int s = 0; s < jper; ++s) {
+    const int j = js + s;
+    int bk = -1, pa = -1, pb = -1;
+    uint32_t bits = 0u;
+    if (qvalid && s < n) {
+      unsigned long long v = S.rec[qbase + j];
+      if (!work) v = 0ull;
+      if (v >> 63) {  // a corner in a frame the K/V buffers hold
+        const int dz = static_cast<int>((v >> 36) & 0x1fu);
+        const int t0 = E.zlo - 1 + dz, h0 = E.ylo + static_cast<int>((v >> 41) & 0xffu),
+                  w0 = E.xlo + static_cast<int>((v >> 49) & 0xffu);
+        v &= ~(3ull << kBitChunk);
+        bk = dz;
+        if (masks) {
+          const int iy = axis_chunk_of(h0, E.ylo, E.R, E.ny), ix = axis_chunk_of(w0, E.xlo, E.cw, E.nx);
+          const int ya = E.ylo + iy * (E.R - 1), xa = E.xlo + ix * (E.cw - 1);
+          bits = corner_tiles((h0 - ya) * E.kst + (w0 - xa), E.kst, w0 + 1 < P.W, h0 + 1 < P.H);
+          const int chk = iy * E.nx + ix;
+          if (t0 >= E.zlo) pa = dz * kMaxMaskChunks + chk;           // plane z = t0 (zrel = dz)
+          if (t0 + 1 <= E.zhi) pb = (dz + 1) * kMaxMaskChunks + chk; // plane z = t0 + 1
+          v |= static_cast<unsigned long long>(chk) << kBitChunk;
+          bk += chk * 32;
         }
-        S.rec[qbase + j] = v;
       }
-      if (bk >= 0) atomicAdd(S.bcur + bk, 1);  // plain shared atomics: faster than warp-matched ones here
-      if (pa >= 0 && (S.mask[pa] & bits) != bits) atomicOr(S.mask + pa, bits);
-      if (pb >= 0 && (S.mask[pb] & bits) != bits) atomicOr(S.mask + pb, bits);
+      S.rec[qbase + j] = v;
     }
+    if (bk >= 0) atomicAdd(S.bcur + bk, 1);  // plain shared atomics: faster than warp-matched ones here
+    if (pa >= 0 && (S.mask[pa] & bits) != bits) atomicOr(S.mask + pa, bits);
+    if (pb >= 0 && (S.mask[pb] & bits) != bits) atomicOr(S.mask + pb, bits);
   }
   __syncthreads();
   if (warp == 0) scan_buckets(S.bcur, S.bstart);
@@ -620,6 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
     }
   }
   if (qvalid) {
+    const int K3 = 3 * K;
     float* drow = P.doffsets + (static_cast<long long>(T.b) * P.Nq + qrow) * P.doff_ld + static_cast<long long>(T.head) * K3;
     // d p / d grid = S/2 strictly inside the volume (0 on or beyond the border), times the offset
     // normalisation: channel 0 moved grid x (W) after division by (T-1), channel 1 grid y (H) by
@@ -645,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
 // ------------------------------------------------------------------------------ host side
 bool tc_bwd_supported(const AttnParams& P) {
   if (!tc_supported(P)) return false;
-  if (P.G != 0 || P.probs == nullptr) return false;
+  if (P.G != 0 || P.probs == nullptr || P.saved == nullptr) return false;
   if (static_cast<long long>(tc::bwd::kQ) * P.K > 65536) return false;  // hit-list entries are 16-bit
   return true;
 }
@@ -668,10 +602,6 @@ bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   L.sld = mk + 8;  // row stride = 8 or 24 (mod 32) words: mma fragment rows hit distinct banks
   // a transposed bf16 tile [maxkeys][40] must fit in a dense fp32 tile [32][sld]
   if (static_cast<size_t>(mk) * tc::bwd::kTRow * 2 > static_cast<size_t>(tc::bwd::kQ) * L.sld * 4) return false;
-  // the setup stages 32 queries x K x 3 offsets in the key buffer + the first dense tile
-  if (static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::bwd::kQ) * L.sld * 4 <
-      static_cast<size_t>(tc::bwd::kQ) * P.K * 12)
-    return false;
   L.smem = static_cast<size_t>(mk) * L.rs * 2 + 2 * static_cast<size_t>(tc::bwd::kQ) * L.sld * 4 +
            static_cast<size_t>(mk) * 4 + fixed;
   L.tiles = static_cast<long long>(P.B) * P.q_frames * L.tiles_h * L.tiles_w * P.nh;

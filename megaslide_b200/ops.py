@@ -124,9 +124,10 @@ class DsaShape:
 
 
 def wants_probs(shape: DsaShape, dtype: torch.dtype) -> bool:
-    """Host-side pre-check for the tensor-core backward, which needs the forward's softmax weights
-    (``probs``): bf16, no extra keys, head_dim a multiple of 8 in [16, 128], algo not forced to the
-    CUDA-core gather.  The library makes the final decision (alignment, shared-memory plan)."""
+    """Host-side pre-check for the tensor-core backward, which needs two outputs of the tensor-core
+    forward (``probs``, ``saved``): bf16, no extra keys, head_dim a multiple of 8 in [16, 128], algo
+    not forced to the CUDA-core gather.  The library makes the final decision (alignment,
+    shared-memory plan)."""
     return (dtype == torch.bfloat16 and shape.extra == 0 and shape.algo != _lib.MSL_ALGO_SIMT
             and shape.head_dim % 8 == 0 and 16 <= shape.head_dim <= 128)
 
@@ -134,6 +135,28 @@ def wants_probs(shape: DsaShape, dtype: torch.dtype) -> bool:
 def probs_buffer(shape: DsaShape, device) -> torch.Tensor:
     """float32 [B, nh, q_rows, K] buffer for the forward's per-sample softmax weights."""
     return torch.empty(shape.batch, shape.heads, shape.q_rows, shape.taps, device=device, dtype=torch.float32)
+
+
+def saved_buffer(shape: DsaShape, dtype: torch.dtype, device) -> torch.Tensor:
+    """uint8 buffer (msl_dsa_saved_bytes) for the tensor-core forward's per-sample records and tile
+    envelopes, which the tensor-core backward reads instead of recomputing the sample coordinates."""
+    g = shape.geometry(dtype)
+    n = int(_lib.load().msl_dsa_saved_bytes(ctypes.byref(g)))
+    if n <= 0:
+        raise ValueError("invalid geometry for the saved buffer")
+    return torch.empty(n, device=device, dtype=torch.uint8)
+
+
+def saved_buffers(shape: DsaShape, dtype: torch.dtype, device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(probs, saved): the tensor-core forward's outputs that the tensor-core backward needs."""
+    return probs_buffer(shape, device), saved_buffer(shape, dtype, device)
+
+
+def _check_saved(shape: DsaShape, dtype: torch.dtype, saved: torch.Tensor) -> None:
+    g = shape.geometry(dtype)
+    n = int(_lib.load().msl_dsa_saved_bytes(ctypes.byref(g)))
+    if saved.dtype != torch.uint8 or saved.numel() < n or not saved.is_contiguous():
+        raise ValueError(f"saved must be a contiguous uint8 tensor of at least {n} bytes (saved_buffer)")
 
 
 def _check_probs(shape: DsaShape, probs: torch.Tensor) -> None:
@@ -146,14 +169,15 @@ def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
              ek: Optional[torch.Tensor] = None, ev: Optional[torch.Tensor] = None,
              out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
              status: Optional[torch.Tensor] = None,
-             probs: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+             probs: Optional[torch.Tensor] = None,
+             saved: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Deformable gather attention forward.
 
     q: [B*q_rows, >=C] row view; k, v: [B*kv_rows, >=C]; offsets: float32 [B*q_rows, >=nh*K*3];
     ek, ev: [B*G, >=C] or None.  Returns (out [B*q_rows, C], lse float32 [B, nh, q_rows]).
-    probs (optional, see probs_buffer): filled with the per-sample softmax weights for the
-    tensor-core backward; the call raises MslError(MSL_ERR_UNSUPPORTED) when the tensor-core
-    forward does not apply to these operands.
+    probs, saved (optional, see saved_buffers): filled with the per-sample softmax weights and the
+    per-sample records for the tensor-core backward; the call raises MslError(MSL_ERR_UNSUPPORTED)
+    when the tensor-core forward does not apply to these operands.
     """
     _need_cuda(q, k, v, offsets, ek, ev)
     C = shape.heads * shape.head_dim
@@ -171,6 +195,10 @@ def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         _need_cuda(probs)
         _check_probs(shape, probs)
         io.probs = _ptr(probs)
+    if saved is not None:
+        _need_cuda(saved)
+        _check_saved(shape, dt, saved)
+        io.saved = _ptr(saved)
     g = shape.geometry(dt)
     with torch.cuda.device(q.device):
         rc = _call("msl_dsa_attn_fwd", q.device,
@@ -180,14 +208,15 @@ def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 
 def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=None, dq=None, dk=None, dv=None,
-             dk_acc=None, dv_acc=None, doffsets=None, dek=None, dev=None, workspace=None, status=None, probs=None):
+             dk_acc=None, dv_acc=None, doffsets=None, dek=None, dev=None, workspace=None, status=None, probs=None,
+             saved=None):
     """Deformable gather attention backward.
 
     Without dk_acc: dK/dV are written to dk/dv (allocated if None) in q's dtype, float32
     accumulators live in ``workspace`` (allocated if None).  With dk_acc/dv_acc (float32 views):
     dK/dV are ACCUMULATED there.  Returns (dq, dk, dv, doffsets, dek, dev); dk/dv are the
-    accumulators in accumulate mode.  probs: the forward's softmax weights (attn_fwd(probs=...));
-    given, the tensor-core backward runs where it applies.
+    accumulators in accumulate mode.  probs, saved: the tensor-core forward's outputs for these operands
+    (attn_fwd(probs=..., saved=...)); with both, the tensor-core backward runs where it applies.
     """
     _need_cuda(q, k, v, offsets, out, lse, dout, ek, ev)
     C = shape.heads * shape.head_dim
@@ -228,6 +257,10 @@ def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=N
         _need_cuda(probs)
         _check_probs(shape, probs)
         io.probs = _ptr(probs)
+    if saved is not None:
+        _need_cuda(saved)
+        _check_saved(shape, dt, saved)
+        io.saved = _ptr(saved)
     with torch.cuda.device(dev_):
         rc = _call("msl_dsa_attn_bwd", dev_,
                    lambda: lib.msl_dsa_attn_bwd(ctypes.byref(g), ctypes.byref(io), _ptr(workspace) if need else None,

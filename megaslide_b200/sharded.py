@@ -231,21 +231,21 @@ class DSA3DShardedFunction(torch.autograd.Function):
                           kv_frame0=win[0], kv_frames=win[1] - win[0], offset_scale=cfg.oscale,
                           dropout_p=cfg.dropout_p, dropout_seed=cfg.seed)
         train = any(ctx.needs_input_grad)
-        probs = None
+        probs = saved = None
         if train and ops.wants_probs(sh, dt):
-            probs = ops.probs_buffer(sh, x.device)
+            probs, saved = ops.saved_buffers(sh, dt, x.device)
             try:
-                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs)
+                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved)
             except MslError as e:
                 if e.code != MSL_ERR_UNSUPPORTED:
                     raise
-                probs = None
+                probs = saved = None
         if probs is None:
             attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev)
         y = torch.addmm(D, attn, wo.to(dt).t())
         if train:
             ctx.save_for_backward(xw, q, kv, hact, off, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc,
-                                  probs)
+                                  probs, saved)
             ctx.cfg, ctx.sh, ctx.plan, ctx.cw = cfg, sh, plan, cw
             ctx.in_dtype = x.dtype
             ctx.extra_dtype = extra_kv.dtype if extra_kv is not None else None
@@ -253,7 +253,7 @@ class DSA3DShardedFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        (xw, q, kv, hact, off, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc, probs) = ctx.saved_tensors
+        (xw, q, kv, hact, off, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc, probs, saved) = ctx.saved_tensors
         cfg: _ShardCfg = ctx.cfg
         sh: ops.DsaShape = ctx.sh
         plan: FramePlan = ctx.plan
@@ -294,7 +294,7 @@ class DSA3DShardedFunction(torch.autograd.Function):
             dkv = torch.empty_like(kv)
             k, v = kv[:, :C], kv[:, C:]
             _, _, _, doff, dek, dev = ops.attn_bwd(sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev, dq=dq,
-                                                   dk=dkv[:, :C], dv=dkv[:, C:], probs=probs)
+                                                   dk=dkv[:, :C], dv=dkv[:, C:], probs=probs, saved=saved)
             add_frames(_mm_f32(dq, wq.to(dt)), own)
             dxw += _mm_f32(dkv, wkv).view(B, nwin, HW, C)
             g_wq = _mm_f32(dq.t(), xo2)

@@ -482,13 +482,14 @@ def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False):
     shape = ops.DsaShape(B, T, H, W, nh, d, ks, dropout_p=dropout_p, dropout_seed=seed, algo=algo)
     offt = torch.from_numpy(off).to(DEV).reshape(B * N, -1)
     qt, kt_, vt, dot = t(q), t(k), t(v), t(dout)
-    probs = ops.probs_buffer(shape, DEV) if algo == 2 else None
+    probs, saved = ops.saved_buffers(shape, torch.bfloat16, DEV) if algo == 2 else (None, None)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
-    out, lse = ops.attn_fwd(shape, qt, kt_, vt, offt, probs=probs, status=status)
+    out, lse = ops.attn_fwd(shape, qt, kt_, vt, offt, probs=probs, saved=saved, status=status)
     kw = {}
     if accumulate:
         kw = dict(dk_acc=torch.full((B * N, C), 0.5, device=DEV), dv_acc=torch.full((B * N, C), -0.25, device=DEV))
-    dq, dk, dv, doff, _, _ = ops.attn_bwd(shape, qt, kt_, vt, offt, out, lse, dot, probs=probs, status=status, **kw)
+    dq, dk, dv, doff, _, _ = ops.attn_bwd(shape, qt, kt_, vt, offt, out, lse, dot, probs=probs, saved=saved,
+                                          status=status, **kw)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     if accumulate:
@@ -580,14 +581,15 @@ def test_tc_backward_requires_probs_when_forced():
 
 
 def test_module_bf16_training_uses_tensor_core_backward(monkeypatch):
-    """A bf16 training step of the module saves probs in the forward and hands them to the backward."""
+    """A bf16 training step of the module saves probs and the per-sample records in the forward and
+    hands them to the backward."""
     from megaslide_b200.attention import DeformableSlideAttention3D
 
     seen = []
     real_bwd = ops.attn_bwd
 
     def spy(*a, **kw):
-        seen.append(kw.get("probs") is not None)
+        seen.append(kw.get("probs") is not None and kw.get("saved") is not None)
         return real_bwd(*a, **kw)
 
     monkeypatch.setattr(ops, "attn_bwd", spy)

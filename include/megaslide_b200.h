@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MSL_ABI_VERSION 1
+#define MSL_ABI_VERSION 2  /* 2: msl_dsa_fwd_io / msl_dsa_bwd_io end with `saved` */
 
 /* return codes */
 #define MSL_OK 0

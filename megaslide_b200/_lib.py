@@ -136,7 +136,7 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
-            if lib.msl_abi_version() != 1:
+            if lib.msl_abi_version() != 2:
                 raise RuntimeError("libmegaslide_b200 ABI version mismatch")
             _lib = lib
     return _lib

@@ -597,7 +597,7 @@ struct alignas(64) KeyMaps {
 // stride).  False when TMA cannot serve the launch (the kernels then load with cp.async).
 bool make_key_maps(KeyMaps* maps, const AttnParams& P, int rs);
 
-// TMA path: warps 0-3 copy, for each chunk plane pl, rows [ya, yb] x columns [xa, xa + kst) into kbuf
+// TMA path: the last four warps copy, for each chunk plane pl, rows [ya, yb] x columns [xa, xa + kst) into kbuf
 // rows pl * kpp + (y - ya) * kst + x - xa: one box per chunk row (box width kst) when the launch has that
 // map, else one 8-key box per row segment.  Boxes whose keys are all in untouched tiles are skipped;
 // coordinates outside the volume / K-V window read as zeros, and the half tile past a plane's last key,
@@ -608,11 +608,12 @@ bool make_key_maps(KeyMaps* maps, const AttnParams& P, int rs);
 __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCtx& T, const Env& E, const Chunk& k,
                                                __nv_bfloat16* kbuf, int rs, const CUtensorMap* maps, int have,
                                                uint32_t bar, bool first) {
-  // box b is issued by warp b % 4: a warp's copies issue one lane after another, so four warps
-  // shorten the issue (measured: 4 ~ 8 warps > 16 > 1)
-  constexpr int kIW = 4;
-  if (threadIdx.x >= 32 * kIW) return;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  // box b is issued by warp kW0 + b % 4: a warp's copies issue one lane after another, so four warps
+  // shorten the issue (measured: 4 ~ 8 warps > 16 > 1); the last four warps, which have the least
+  // work in the phases the copies overlap (hit loops, zeroing, conversions stride from thread 0)
+  constexpr int kIW = 4, kW0 = kWarps - kIW;
+  if (threadIdx.x < 32 * kW0) return;
+  const int lane = threadIdx.x & 31, wid = (threadIdx.x >> 5) - kW0;
   const int nkeys = (chunk_yb(E, k) - chunk_ya(E, k) + 1) * E.kst;  // keys of one plane
   const int mi = (E.kst >> 3) - 1;
   const bool wide = mi < 4 && ((have >> mi) & 1);
@@ -640,7 +641,7 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
     tail[pl] = pl < np && (nkeys & 15) && ((k.m >> (kt >> 4)) & 1u);
   }
   const int cnt = __popc(__ballot_sync(0xffffffffu, on[0])) + __popc(__ballot_sync(0xffffffffu, on[1]));
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 32 * kW0) {
     if (first) fence_proxy_async();
     mbar_arrive_expect_tx(bar, static_cast<uint32_t>((cnt * bw + ((tail[0] ? 8 : 0) + (tail[1] ? 8 : 0))) * rs * 2));
   }
@@ -656,9 +657,9 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
     tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((pl * E.kpp + lb * bw) * rs * 2), wide ? maps + mi : maps, bar,
                 T.head * P.d, chunk_xa(E, k) + col, chunk_ya(E, k) + row, E.zlo + k.zr * E.pg + pl - P.kv_frame0, T.b);
   }
-  if (threadIdx.x < 2 && tail[threadIdx.x])  // columns W .. W+7: all outside the volume
-    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((threadIdx.x * E.kpp + nkeys) * rs * 2), maps, bar, T.head * P.d,
-                P.W, 0, 0, T.b);
+  if (wid == 0 && lane < 2 && tail[lane])  // columns W .. W+7: all outside the volume
+    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((lane * E.kpp + nkeys) * rs * 2), maps, bar, T.head * P.d, P.W,
+                0, 0, T.b);
 }
 
 // Waits for the TMA copies of phase `parity` on mbarrier bar.  Bounded: after about a second the CTA

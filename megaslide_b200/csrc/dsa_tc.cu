@@ -95,6 +95,10 @@ size_t smem_fixed(const AttnParams& P, int rs) {
          24 + 256;
 }
 
+// P~ . V: channel groups of a row group's 8 warps (all channel tiles per warp up to head_dim 72; two
+// groups above, for registers)
+__host__ __device__ constexpr int pv_channel_groups(int dch) { return dch <= 9 ? 1 : 2; }
+
 // loads G extra keys / values of this head into kbuf rows 0..G-1 (zero up to gp)
 template <int DCH>
 __device__ __forceinline__ void load_extra(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
@@ -427,12 +431,14 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   __syncthreads();
 
   // ---- pass 2: O = P~ . V (hits CTA-wide)
-  // the 8 warps of a row group: 4 channel ranges (sizes differ by at most one tile) x 2 halves of the
-  // touched tiles (every other one), so that every warp runs two short accumulation chains; the
-  // halves are added once at the end
-  constexpr int kCB = DCH / 4, kCX = DCH % 4;
+  // the 8 warps of a row group: kCG channel ranges (sizes differ by at most one tile) x kKS parts of the
+  // touched tiles (every kKS-th one): a P~ fragment and a V tile are read once per row group for
+  // head_dim <= 72 (all channel tiles per warp; measured faster than 2 or 4 ranges), the parts' partial
+  // sums are added once at the end
+  constexpr int kCG = pv_channel_groups(DCH), kKS = kWPG / kCG;
+  constexpr int kCB = DCH / kCG, kCX = DCH % kCG;
   constexpr int kTPW = kCB + (kCX ? 1 : 0);  // channel tiles per warp (at most)
-  const int cpart = part & 3, kpar = part >> 2;
+  const int cpart = part % kCG, kpar = part / kCG;
   const int nt0 = cpart * kCB + min(cpart, kCX), nt1 = nt0 + kCB + (cpart < kCX ? 1 : 0);
   float o[kTPW + 1][4];
 #pragma unroll
@@ -478,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         cp_async_wait_all();
       }
       __syncthreads();
-      dq_product<DCH, kTPW, 2>(tp, r, S.kbuf, L.rs, nt0, nt1, k.m, o, kpar);
+      dq_product<DCH, kTPW, kKS>(tp, r, S.kbuf, L.rs, nt0, nt1, k.m, o, kpar);
     }
   }
   if (P.G > 0) {  // extra values: their weights straight into the fixed-point rows
@@ -492,28 +498,31 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     __syncthreads();
     transpose_fixed<kMaxKeysFwd>(S.sbuf, L.sld, gmask, S.qsc + kQ);
     __syncthreads();
-    dq_product<DCH, kTPW, 2>(tp, r, S.kbuf, L.rs, nt0, nt1, gmask, o, kpar);
+    dq_product<DCH, kTPW, kKS>(tp, r, S.kbuf, L.rs, nt0, nt1, gmask, o, kpar);
   }
 
-  // ---- the warps of the second half of the tiles hand their partial sums to the first half
-  {
-    __syncthreads();  // every product is done with the dense tile
-    float4* red = reinterpret_cast<float4*>(S.sbuf) + ((r * 4 + cpart) * kTPW) * 32 + lane;  // [2][4][kTPW][32]
-    if (kpar == 1) {
+  // ---- the warps of the other key-tile parts hand their partial sums to part 0 (through the key
+  //      buffer and the dense tile, contiguous and free now: [2][kCG][kKS - 1][kTPW][32] float4)
+  if (kKS > 1) {
+    __syncthreads();  // every product is done with the key buffer and the dense tile
+    float4* red = reinterpret_cast<float4*>(S.kbuf) + ((r * kCG + cpart) * (kKS - 1) * kTPW) * 32 + lane;
+    if (kpar > 0) {
 #pragma unroll
       for (int j = 0; j < kTPW; ++j)
-        if (nt0 + j < nt1) red[j * 32] = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
+        if (nt0 + j < nt1) red[((kpar - 1) * kTPW + j) * 32] = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
     }
     __syncthreads();
     if (kpar == 0) {
+      for (int u = 0; u < kKS - 1; ++u) {
 #pragma unroll
-      for (int j = 0; j < kTPW; ++j) {
-        if (nt0 + j >= nt1) continue;
-        const float4 t = red[j * 32];
-        o[j][0] += t.x;
-        o[j][1] += t.y;
-        o[j][2] += t.z;
-        o[j][3] += t.w;
+        for (int j = 0; j < kTPW; ++j) {
+          if (nt0 + j >= nt1) continue;
+          const float4 t = red[(u * kTPW + j) * 32];
+          o[j][0] += t.x;
+          o[j][1] += t.y;
+          o[j][2] += t.z;
+          o[j][3] += t.w;
+        }
       }
     }
   }
@@ -580,8 +589,14 @@ bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   L.sld = mk + 8;  // row stride = 8 or 24 (mod 32) words: mma fragment rows hit distinct banks
   // a transposed bf16 tile [maxkeys][40] must fit in the dense fp32 tile [32][sld]
   if (static_cast<size_t>(mk) * tc::t32::kTRow * 2 > static_cast<size_t>(tc::t32::kQ) * L.sld * 4) return false;
-  // so must the output partial sums handed between the warp halves ([2][4][(dch + 3) / 4][32] float4)
-  if (static_cast<size_t>(4096) * ((dch + 3) / 4) > static_cast<size_t>(tc::t32::kQ) * L.sld * 4) return false;
+  // the output partial sums handed between the warps of a row group fit the key buffer + dense tile
+  {
+    const int cg = tc::fwd::pv_channel_groups(dch), ks = tc::t32::kWPG / cg;
+    const int tpw = (dch + cg - 1) / cg;
+    if (static_cast<size_t>(2) * cg * (ks - 1) * tpw * 512 >
+        static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4)
+      return false;
+  }
   // the setup stages 32 queries x K x 3 offsets in the key buffer + the dense tile
   if (static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4 <
       static_cast<size_t>(tc::t32::kQ) * P.K * 12)

@@ -132,6 +132,8 @@ __device__ __forceinline__ PlaneTerms plane_terms(const float* row, int k00, int
 }
 
 
+constexpr int kDqChannelGroups = 4;  // dQ product: channel ranges per row group (x 2 key-tile parts)
+
 // ------------------------------------------------------------------------------ chunk operands
 // accum[key][d] += A . X over the tiles of mask m: A = the transposed bf16 tile tb ([key][query], all
 // 32 queries, ldmatrix), X = 32 bf16 rows (Q or dO) in shared memory.  Items = (16-key tile, the
@@ -447,8 +449,13 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   __syncthreads();
 
   // ---- pass 2: K side (key part of the coordinate gradient, dQ, dK, dV), hits CTA-wide
-  constexpr int kTPW = (DCH + kWPG - 1) / kWPG;  // dQ channel tiles per warp
-  const int nt0 = min(DCH, part * kTPW), nt1 = min(DCH, nt0 + kTPW);
+  // dQ: the 8 warps of a row group = kCG channel ranges x kKS parts of the touched key tiles (measured
+  // at head_dim 72: 4 x 2 beats 8 x 1 and 2 x 4)
+  constexpr int kCG = kDqChannelGroups, kKS = kWPG / kCG;
+  constexpr int kCB = DCH / kCG, kCX = DCH % kCG;
+  constexpr int kTPW = kCB + (kCX ? 1 : 0);  // dQ channel tiles per warp (at most)
+  const int cpart = part % kCG, kpar = part / kCG;
+  const int nt0 = cpart * kCB + min(cpart, kCX), nt1 = nt0 + kCB + (cpart < kCX ? 1 : 0);
   float oq[kTPW + 1][4];
 #pragma unroll
   for (int i = 0; i < kTPW + 1; ++i) oq[i][0] = oq[i][1] = oq[i][2] = oq[i][3] = 0.f;
@@ -516,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
                           (rc.h0 - ya) * kst + (rc.w0 - xa), kst, rc,
                           pv * frac_weight(rc.ft, z != rc.t0) * S.qsc[2 * kQ + q], P.H, P.W);
       }
-      dq_product<DCH, kTPW>(tds, r, S.kbuf, L.rs, nt0, nt1, cur.m, oq);
+      dq_product<DCH, kTPW, kKS>(tds, r, S.kbuf, L.rs, nt0, nt1, cur.m, oq, kpar);
       kv_product_flush<DCH>(P, T, L, tds, S.qs, S.key_off, cur.m, P.dk_acc);
       __syncthreads();  // the key buffer is free
       have = chunk_next(E, S.mask, masks, nz, k);
@@ -534,8 +541,33 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   }
   __syncthreads();
 
+  // ---- the warps of the other key-tile parts hand their dQ partial sums to part 0 (through the key
+  //      buffer and the dense tiles, contiguous and free now: [2][kCG][kKS - 1][kTPW][32] float4)
+  if (kKS > 1) {
+    float4* red = reinterpret_cast<float4*>(S.kbuf) + ((r * kCG + cpart) * (kKS - 1) * kTPW) * 32 + lane;
+    if (kpar > 0) {
+#pragma unroll
+      for (int j = 0; j < kTPW; ++j)
+        if (nt0 + j < nt1) red[((kpar - 1) * kTPW + j) * 32] = make_float4(oq[j][0], oq[j][1], oq[j][2], oq[j][3]);
+    }
+    __syncthreads();
+    if (kpar == 0) {
+      for (int u = 0; u < kKS - 1; ++u) {
+#pragma unroll
+        for (int j = 0; j < kTPW; ++j) {
+          if (nt0 + j >= nt1) continue;
+          const float4 t = red[(u * kTPW + j) * 32];
+          oq[j][0] += t.x;
+          oq[j][1] += t.y;
+          oq[j][2] += t.z;
+          oq[j][3] += t.w;
+        }
+      }
+    }
+  }
+
   // ---- dQ (bf16) and the offset gradients
-  {
+  if (kpar == 0) {
     int qh0_, qw0_, qh1_, qw1_;
     query_hw(T, r, g, qh0_, qw0_);
     query_hw(T, r, g + 8, qh1_, qw1_);
@@ -602,6 +634,13 @@ bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   L.sld = mk + 8;  // row stride = 8 or 24 (mod 32) words: mma fragment rows hit distinct banks
   // a transposed bf16 tile [maxkeys][40] must fit in a dense fp32 tile [32][sld]
   if (static_cast<size_t>(mk) * tc::bwd::kTRow * 2 > static_cast<size_t>(tc::bwd::kQ) * L.sld * 4) return false;
+  // the dQ partial sums handed between the key-tile parts fit the key buffer + the two dense tiles
+  {
+    const int cg = tc::bwd::kDqChannelGroups, ks = tc::bwd::kWPG / cg, tpw = (dch + cg - 1) / cg;
+    if (static_cast<size_t>(2) * cg * (ks - 1) * tpw * 512 >
+        static_cast<size_t>(mk) * L.rs * 2 + 2 * static_cast<size_t>(tc::bwd::kQ) * L.sld * 4)
+      return false;
+  }
   L.smem = static_cast<size_t>(mk) * L.rs * 2 + 2 * static_cast<size_t>(tc::bwd::kQ) * L.sld * 4 +
            static_cast<size_t>(mk) * 4 + fixed;
   L.tiles = static_cast<long long>(P.B) * P.q_frames * L.tiles_h * L.tiles_w * P.nh;

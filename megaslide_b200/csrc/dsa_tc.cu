@@ -163,9 +163,17 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   uint32_t kphase = 0;
   fill_tabs(P, T, kTileH, tabz, taby, tabx);
 
-  // ---- stage the tile's offsets (this head) and Q rows with one wave of cp.async
+  // ---- stage the tile's offsets (this head) and Q rows with one wave of cp.async.  An offsets row
+  //      (3K floats at any 4-byte alignment) lands at row base + its misalignment so that its 16-byte
+  //      aligned body copies with 16-byte cp.async; the up to 3 floats before and after it with 4-byte
+  //      ones (no byte outside the row is read).
   const int K3 = 3 * K;
+  const int OS = (K3 + 3 + 3) & ~3;  // staged row stride (floats): 16-byte aligned rows
   float* ostage = reinterpret_cast<float*>(S.kbuf);
+  // misalignment (floats) of this thread's own query row, where its staged row starts
+  const int omis = static_cast<int>(
+      (reinterpret_cast<uintptr_t>(P.offsets + (static_cast<long long>(T.b) * P.Nq + qrow) * P.off_ld +
+                                   static_cast<long long>(T.head) * K3) >> 2) & 3u);
   for (int q2 = warp; q2 < kQ; q2 += kWarps) {
     int sqh, sqw;
     query_hw(T, q2 >> 4, q2 & 15, sqh, sqw);
@@ -173,8 +181,12 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     const long long grow = static_cast<long long>(T.b) * P.Nq + (static_cast<long long>(T.tl) * P.H + sqh) * P.W + sqw;
     if (ok) {
       const float* src = P.offsets + grow * P.off_ld + static_cast<long long>(T.head) * K3;
-      float* dst = ostage + static_cast<size_t>(q2) * K3;
-      for (int k = lane; k < K3; k += 32) cp_async4(smem_u32(dst + k), src + k);
+      const int mis = static_cast<int>((reinterpret_cast<uintptr_t>(src) >> 2) & 3u);
+      const int lead = (4 - mis) & 3, nb = (K3 - lead) >> 2, tail0 = lead + 4 * nb;
+      float* dst = ostage + static_cast<size_t>(q2) * OS + mis;  // dst + lead is 16-byte aligned
+      if (lane < lead) cp_async4(smem_u32(dst + lane), src + lane);
+      for (int c = lane; c < nb; c += 32) cp_async16(smem_u32(dst + lead + 4 * c), src + lead + 4 * c);
+      if (tail0 + lane < K3) cp_async4(smem_u32(dst + tail0 + lane), src + tail0 + lane);
     }
     for (int ch = lane; ch < DCH; ch += 32) {
       __nv_bfloat16* dq_ = S.qs + static_cast<size_t>(q2) * L.rs + ch * 8;
@@ -194,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   int zmn = 0x7fffffff, zmx = -0x7fffffff, ymn = 0x7fffffff, ymx = -0x7fffffff, xmn = 0x7fffffff, xmx = -0x7fffffff;
   bool miss = false;
   if (qvalid) {
-    const float* oq = ostage + static_cast<size_t>(qi) * K3;
+    const float* oq = ostage + static_cast<size_t>(qi) * OS + omis;
     WinIdx wi;
     wi.init(js, P.kh, P.kw);
     for (int j = js; j < je; ++j, wi.advance(1, P.kh, P.kw)) {
@@ -599,7 +611,7 @@ bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   }
   // the setup stages 32 queries x K x 3 offsets in the key buffer + the dense tile
   if (static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4 <
-      static_cast<size_t>(tc::t32::kQ) * P.K * 12)
+      static_cast<size_t>(tc::t32::kQ) * ((3 * P.K + 6) & ~3) * 4)
     return false;
   L.smem = static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4 + fixed;
   L.tiles = static_cast<long long>(P.B) * P.q_frames * L.tiles_h * L.tiles_w * P.nh;

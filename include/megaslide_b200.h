@@ -196,6 +196,7 @@ typedef struct msl_dwconv_geometry {
 #define MSL_EPI_NONE 0      /* y = conv(x) + bias + bias2 */
 #define MSL_EPI_GELU 1      /* y = gelu_erf(conv(x) + bias) */
 #define MSL_EPI_GELU_GRAD 2 /* y = aux * gelu_erf'(conv(x) + bias)  (offset_net backward) */
+#define MSL_EPI_ACCUM 3     /* y += conv(x) + bias + bias2  (float32 y only) */
 
 /* y[out frames] = epilogue(conv(x[in frames])).  bias, bias2 float32 [C] or NULL.  geom->dtype is
  * the element type of x; y_dtype (MSL_DTYPE_*) that of y and aux (a bf16 input can produce a float32
@@ -208,6 +209,11 @@ int msl_dwconv3d_fwd(const msl_dwconv_geometry* geom, const void* x, int64_t x_l
 /* dx[out frames] = conv_transpose(dy[in frames]) (gradient w.r.t. the conv input). */
 int msl_dwconv3d_bwd_data(const msl_dwconv_geometry* geom, const void* dy, int64_t dy_ld,
                           const float* weight, void* dx, int64_t dx_ld, void* stream);
+
+/* dx[out frames] (float32) += conv_transpose(dy[in frames]): the input gradient added into a float32
+ * buffer that already holds the other branches' terms (no temporary, no separate add pass). */
+int msl_dwconv3d_bwd_data_acc(const msl_dwconv_geometry* geom, const void* dy, int64_t dy_ld,
+                              const float* weight, float* dx, int64_t dx_ld, void* stream);
 
 /* dweight[kt*kh*kw, C] += sum over dy positions (out frames) of dy * shifted x (in frames);
  * dbias[C] += sum of dy (dbias may be NULL).  Accumulates: the caller clears.  geom->dtype is the

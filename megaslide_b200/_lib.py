@@ -30,6 +30,7 @@ MSL_ALGO_TC = 2
 MSL_EPI_NONE = 0
 MSL_EPI_GELU = 1
 MSL_EPI_GELU_GRAD = 2
+MSL_EPI_ACCUM = 3
 MSL_NOALLOC_SCRATCH_BYTES = 64 * 1024 * 1024
 
 _i32 = ctypes.c_int32
@@ -96,6 +97,7 @@ SIGNATURES = {
     "msl_dwconv3d_fwd": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _vp, _vp, _i32, _vp,
                                         _i64, _vp, _i64, _i32, _vp]),
     "msl_dwconv3d_bwd_data": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _vp, _i64, _vp]),
+    "msl_dwconv3d_bwd_data_acc": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _vp, _i64, _vp]),
     "msl_dwconv3d_bwd_weight": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _i32, _vp, _i64, _vp,
                                                _vp, _vp]),
     "msl_offsets_absmax": (ctypes.c_int, [_vp, _i64, _i64, _i32, _i32, _f32, _vp, _vp]),

@@ -40,6 +40,13 @@ def _mm_f32(a: Tensor, b: Tensor) -> Tensor:
     return torch.mm(a, b, out_dtype=torch.float32)
 
 
+def _addmm_f32(bias: Tensor, a: Tensor, b: Tensor) -> Tensor:
+    """bias + a @ b with a float32 result in one GEMM (the float32 bias [n] is added in its epilogue)."""
+    if a.dtype == torch.float32:
+        return torch.addmm(bias, a, b)
+    return torch.addmm(bias, a, b, out_dtype=torch.float32)
+
+
 class _Cfg:
     __slots__ = ("shape", "conv_k", "conv_3", "dtype", "param_dtypes", "G", "kernel")
 
@@ -73,8 +80,7 @@ class DSA3DFunction(torch.autograd.Function):
         hact = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
         O = w2.shape[0]
         w2m = w2.reshape(O, C)
-        off = _mm_f32(hact, w2m.to(dt).t())
-        off += b2.detach().float()
+        off = _addmm_f32(b2.detach().float(), hact, w2m.to(dt).t())
         # depthwise conv term with both biases (dw_conv and out_proj) fused
         wd_kc = ops.conv_weight_kc(wd)
         D = ops.dwconv_fwd(cfg.conv_k, x2, wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous(),
@@ -120,9 +126,7 @@ class DSA3DFunction(torch.autograd.Function):
             # out_proj
             dattn = torch.mm(dy2, wo.to(dt))
             g_wo = _mm_f32(dy2.t(), attn)
-            g_bo = dy2.float().sum(0)
-            # depthwise conv term; dx accumulates in float32 across the three branches
-            dx = ops.dwconv_bwd_data(cfg.conv_k, dy2, wd_kc).float()
+            g_bo = dy2.sum(0, dtype=torch.float32)
             g_wd = torch.zeros_like(wd_kc)
             g_bd = torch.zeros(C, device=dy2.device, dtype=torch.float32)
             ops.dwconv_bwd_weight(cfg.conv_k, dy2, x2, g_wd, g_bd)
@@ -132,10 +136,12 @@ class DSA3DFunction(torch.autograd.Function):
             _, _, _, doff, dek, dev = ops.attn_bwd(
                 sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev,
                 dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs, saved=saved)
-            # q/k/v projections
-            dx += _mm_f32(dqkv, wqkv)
+            # q/k/v projections; dx accumulates in float32 across the three branches (the depthwise
+            # convs add their transposed convolutions into it)
+            dx = _mm_f32(dqkv, wqkv)
+            ops.dwconv_bwd_data(cfg.conv_k, dy2, wd_kc, out=dx, accumulate=True)
             g_wqkv = _mm_f32(dqkv.t(), x2)
-            g_bqkv = dqkv.float().sum(0)
+            g_bqkv = dqkv.sum(0, dtype=torch.float32)
             g_wq, g_wk, g_wv = g_wqkv[:C], g_wqkv[C:2 * C], g_wqkv[2 * C:]
             g_bq, g_bk, g_bv = g_bqkv[:C], g_bqkv[C:2 * C], g_bqkv[2 * C:]
             d_extra = None
@@ -156,7 +162,7 @@ class DSA3DFunction(torch.autograd.Function):
             g_b2 = doff.sum(0)
             du = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh,
                                 out_dtype=torch.float32)
-            dx += ops.dwconv_bwd_data(cfg.conv_3, du, w1_kc)
+            ops.dwconv_bwd_data(cfg.conv_3, du, w1_kc, out=dx, accumulate=True)
             g_w1 = torch.zeros_like(w1_kc)
             g_b1 = torch.zeros(C, device=dy2.device, dtype=torch.float32)
             ops.dwconv_bwd_weight(cfg.conv_3, du, x2, g_w1, g_b1)

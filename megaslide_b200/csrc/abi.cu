@@ -359,8 +359,10 @@ int msl_dwconv3d_fwd(const msl_dwconv_geometry* geom, const void* x, int64_t x_l
   int rc = fill_conv(geom, P);
   if (rc) return rc;
   if (!x || !weight || !y) return fail(MSL_ERR_INVALID, "x, weight and y are required");
-  if (epilogue != MSL_EPI_NONE && epilogue != MSL_EPI_GELU && epilogue != MSL_EPI_GELU_GRAD)
+  if (epilogue != MSL_EPI_NONE && epilogue != MSL_EPI_GELU && epilogue != MSL_EPI_GELU_GRAD &&
+      epilogue != MSL_EPI_ACCUM)
     return fail(MSL_ERR_INVALID, "unknown epilogue %d", epilogue);
+  if (epilogue == MSL_EPI_ACCUM && y_dtype != MSL_DTYPE_F32) return fail(MSL_ERR_INVALID, "ACCUM needs a float32 y");
   if (epilogue == MSL_EPI_GELU_GRAD && (!aux || aux_ld < P.C)) return fail(MSL_ERR_INVALID, "GELU_GRAD needs aux rows");
   if (x_ld < P.C || y_ld < P.C) return fail(MSL_ERR_INVALID, "row strides must be >= channels");
   if (y_dtype != MSL_DTYPE_F32 && y_dtype != MSL_DTYPE_BF16) return fail(MSL_ERR_INVALID, "unknown y_dtype %d", y_dtype);
@@ -381,6 +383,20 @@ int msl_dwconv3d_bwd_data(const msl_dwconv_geometry* geom, const void* dy, int64
   cudaError_t e = msl::launch_dwconv_fwd(P, dy, dy_ld, weight, nullptr, nullptr, MSL_EPI_NONE, nullptr, 0, dx, dx_ld,
                                          P.dtype, true, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dwconv_fwd_kernel(transposed) launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return MSL_OK;
+}
+
+int msl_dwconv3d_bwd_data_acc(const msl_dwconv_geometry* geom, const void* dy, int64_t dy_ld, const float* weight,
+                              float* dx, int64_t dx_ld, void* stream) {
+  msl::ConvParams P;
+  int rc = fill_conv(geom, P);
+  if (rc) return rc;
+  if (!dy || !weight || !dx) return fail(MSL_ERR_INVALID, "dy, weight and dx are required");
+  if (dy_ld < P.C || dx_ld < P.C) return fail(MSL_ERR_INVALID, "row strides must be >= channels");
+  cudaError_t e = msl::launch_dwconv_fwd(P, dy, dy_ld, weight, nullptr, nullptr, MSL_EPI_ACCUM, nullptr, 0, dx, dx_ld,
+                                         MSL_DTYPE_F32, true, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dwconv_fwd_kernel(transposed, accumulate) launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return MSL_OK;
 }

@@ -297,6 +297,14 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   const bool work = any && !overflow;
   const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
   const bool fsplit = split && !masks;  // chunks of a plane share one hit bucket: filter the hits
+  // pass 1's first V chunk (plane zlo, chunk 0, every tile of it) loads while the setup runs
+  const bool early = tma && work;
+  if (early) {
+    Chunk k0;
+    k0.zr = k0.iy = k0.ix = 0;
+    k0.m = chunk_mask(E, S.mask, false, k0);
+    if (!*S.dead) issue_keys_tma(P, T, E, k0, S.kbuf, L.rs, maps.v, maps.have, kbar, true);
+  }
 
   // ---- the forward's records with this kernel's chunk bits; frame-bucket counts and touched-tile masks
   for (int s = 0; s < jper; ++s) {
@@ -362,9 +370,15 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   {
     Chunk k = k2;
     bool have = have2;
-    if (have) {
+    if (early && !(have && k.zr == 0 && k.iy == 0 && k.ix == 0)) {
+      // the early chunk is not the walk's first: let its copies land before the buffer is reused
+      wait_keys(kbar, kphase, S.dead, P.status);
+      kphase ^= 1u;
+      __syncthreads();
+    }
+    if (have && !(early && k.zr == 0 && k.iy == 0 && k.ix == 0)) {
       if (tma) {
-        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.v, maps.have, kbar, true);
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.v, maps.have, kbar, !early);
       } else {
         issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, vg, P.v_ld);
       }
@@ -510,18 +524,29 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
       zero_tiles<kQ>(S.sa, L.sld, cur.m);
       __syncthreads();
       // P~ scatter (into sa), dQ += dS~ . K_chunk, dK_chunk = dS~^T . Q
-      for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
-        const int idx = S.hits[i];
-        const unsigned long long v = S.rec[idx];
-        if (!((v >> kBitKeep) & 1ull)) continue;
-        const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
-        const Rec rc = decode_rec(v, E);
-        if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
-          continue;
-        const float pv = __ldg(P.probs + S.prow[q] * K + (idx - q * K)) * P.drop_keep_scale;
-        scatter_fixed_row(reinterpret_cast<int*>(S.sa) + static_cast<size_t>(q) * L.sld,
-                          (rc.h0 - ya) * kst + (rc.w0 - xa), kst, rc,
-                          pv * frac_weight(rc.ft, z != rc.t0) * S.qsc[2 * kQ + q], P.H, P.W);
+      // two hits per step, their softmax weights loaded first (global loads: overlap their latency)
+      for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += 2 * kThreads) {
+        const int i1 = i + kThreads;
+        const bool two = i1 < hhi;
+        const int idx0 = S.hits[i], idx1 = two ? S.hits[i1] : idx0;
+        const int q0 = static_cast<int>((static_cast<float>(idx0) + 0.5f) * invK);
+        const int q1 = static_cast<int>((static_cast<float>(idx1) + 0.5f) * invK);
+        const float p0 = __ldg(P.probs + S.prow[q0] * K + (idx0 - q0 * K));
+        const float p1 = two ? __ldg(P.probs + S.prow[q1] * K + (idx1 - q1 * K)) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          if (u == 1 && !two) break;
+          const int idx = u ? idx1 : idx0, q = u ? q1 : q0;
+          const unsigned long long v = S.rec[idx];
+          if (!((v >> kBitKeep) & 1ull)) continue;
+          const Rec rc = decode_rec(v, E);
+          if (fsplit && (axis_chunk_of(rc.h0, E.ylo, E.R, E.ny) != cur.iy || axis_chunk_of(rc.w0, E.xlo, E.cw, E.nx) != cur.ix))
+            continue;
+          const float pv = (u ? p1 : p0) * P.drop_keep_scale;
+          scatter_fixed_row(reinterpret_cast<int*>(S.sa) + static_cast<size_t>(q) * L.sld,
+                            (rc.h0 - ya) * kst + (rc.w0 - xa), kst, rc,
+                            pv * frac_weight(rc.ft, z != rc.t0) * S.qsc[2 * kQ + q], P.H, P.W);
+        }
       }
       dq_product<DCH, kTPW, kKS>(tds, r, S.kbuf, L.rs, nt0, nt1, cur.m, oq, kpar);
       kv_product_flush<DCH>(P, T, L, tds, S.qs, S.key_off, cur.m, P.dk_acc);

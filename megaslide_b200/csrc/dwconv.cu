@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(256) dwconv_fwd_kernel(const ConvParams P, con
   const long long orow = static_cast<long long>(b) * rows_out + row;
   float av[CV];
   if (epi == MSL_EPI_GELU_GRAD) ChanVec<TY, CV>::load(aux + orow * aux_ld + c, av);
+  if (epi == MSL_EPI_ACCUM) ChanVec<TY, CV>::load(y + orow * y_ld + c, av);  // the buffer's own terms
 #pragma unroll
   for (int e = 0; e < CV; ++e) {
     float u = acc[e] + (bias ? __ldg(bias + c + e) : 0.f);
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(256) dwconv_fwd_kernel(const ConvParams P, con
       u = av[e] * gelu_erf_grad(u);
     else if (bias2)
       u += __ldg(bias2 + c + e);
+    if (epi == MSL_EPI_ACCUM) u += av[e];
     out[e] = u;
   }
   ChanVec<TY, CV>::store(y + orow * y_ld + c, out);

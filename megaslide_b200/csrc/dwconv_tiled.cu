@@ -160,11 +160,18 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
     if (t + 1 < cp.tb && tn >= P.in_frame0 && tn < P.in_frame0 + P.in_frames)
       load_slice<T>(P, L, x, x_ld, ring + ((tn - base) % nslots) * slice_words, cp.b, tn, cp.h0, cp.w0, c0);
     if (active) {
+      const long long orow0 = (static_cast<long long>(cp.b) * P.out_frames + (t - P.out_frame0)) * P.HW +
+                              static_cast<long long>(h) * P.W + ws;
       float acc[kSeg][CV];
 #pragma unroll
       for (int j = 0; j < kSeg; ++j)
 #pragma unroll
         for (int e = 0; e < CV; ++e) acc[j][e] = 0.f;
+      if (epi == MSL_EPI_ACCUM) {  // start from the buffer's own terms (loads issued together, before the taps)
+#pragma unroll
+        for (int j = 0; j < kSeg; ++j)
+          if (ws + j < P.W) load_cv<TY, CV>(y + (orow0 + j) * y_ld + c, acc[j]);
+      }
       for (int it = 0; it < P.kt; ++it) {
         const int ti = t + it - pt;
         if (ti < P.in_frame0 || ti >= P.in_frame0 + P.in_frames) continue;  // zero outside the input frames
@@ -197,8 +204,6 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
               for (int e = 0; e < CV; ++e) acc[j][e] = fmaf(wv[iw][e], xin[j + iw][e], acc[j][e]);
         }
       }
-      const long long orow0 = (static_cast<long long>(cp.b) * P.out_frames + (t - P.out_frame0)) * P.HW +
-                              static_cast<long long>(h) * P.W + ws;
 #pragma unroll
       for (int j = 0; j < kSeg; ++j) {
         if (ws + j >= P.W) break;

@@ -330,17 +330,22 @@ def dwconv_fwd(shape: ConvShape, x: torch.Tensor, weight_kc: torch.Tensor, bias:
 
 
 def dwconv_bwd_data(shape: ConvShape, dy: torch.Tensor, weight_kc: torch.Tensor,
-                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """dx = conv_transpose(dy); the geometry's input window is dy's frames, output is dx's."""
+                    out: Optional[torch.Tensor] = None, accumulate: bool = False) -> torch.Tensor:
+    """dx = conv_transpose(dy); the geometry's input window is dy's frames, output is dx's.
+    accumulate=True adds into ``out`` (float32) instead: dx += conv_transpose(dy)."""
     _need_cuda(dy, weight_kc)
-    if out is None:
+    if accumulate:
+        if out is None or out.dtype != torch.float32:
+            raise TypeError("accumulate=True needs a float32 out")
+    elif out is None:
         out = torch.empty(shape.out_rows, shape.channels, device=dy.device, dtype=dy.dtype)
     g = shape.geometry(dy.dtype)
+    name = "msl_dwconv3d_bwd_data_acc" if accumulate else "msl_dwconv3d_bwd_data"
     with torch.cuda.device(dy.device):
-        rc = _call("msl_dwconv3d_bwd_data", dy.device, lambda: _lib.load().msl_dwconv3d_bwd_data(
+        rc = _call(name, dy.device, lambda: getattr(_lib.load(), name)(
             ctypes.byref(g), _ptr(dy), _rows(dy, "dy"), _ptr(weight_kc), _ptr(out), _rows(out, "dx"),
             _stream(dy.device)))
-    _lib.check("msl_dwconv3d_bwd_data", rc)
+    _lib.check(name, rc)
     return out
 
 

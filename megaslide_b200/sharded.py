@@ -33,7 +33,7 @@ from torch import Tensor, nn
 
 from . import ops
 from ._lib import MSL_EPI_GELU, MSL_EPI_GELU_GRAD, MSL_EPI_NONE, MSL_ERR_UNSUPPORTED, MslError
-from .attention import DeformableSlideAttention3D, _mm_f32
+from .attention import DeformableSlideAttention3D, _addmm_f32, _mm_f32
 
 Range = Tuple[int, int]
 
@@ -195,8 +195,7 @@ class DSA3DShardedFunction(torch.autograd.Function):
         b1f = b1.detach().float().contiguous()
         hact = ops.dwconv_fwd(conv3, xc2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
         w2m = w2.reshape(w2.shape[0], C)
-        off = _mm_f32(hact, w2m.to(dt).t())
-        off += b2.detach().float()
+        off = _addmm_f32(b2.detach().float(), hact, w2m.to(dt).t())
         wd_kc = ops.conv_weight_kc(wd)
         D = ops.dwconv_fwd(convk, xc2, wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous(),
                            epilogue=MSL_EPI_NONE)
@@ -273,7 +272,7 @@ class DSA3DShardedFunction(torch.autograd.Function):
             dy2 = dy.reshape(-1, C).to(dt).contiguous()
             dattn = torch.mm(dy2, wo.to(dt))
             g_wo = _mm_f32(dy2.t(), attn)
-            g_bo = dy2.float().sum(0)
+            g_bo = dy2.sum(0, dtype=torch.float32)
             dxw = torch.zeros(B, nwin, HW, C, dtype=torch.float32, device=xw.device)
 
             def add_frames(rows: Tensor, rng: Range) -> None:
@@ -298,9 +297,9 @@ class DSA3DShardedFunction(torch.autograd.Function):
             add_frames(_mm_f32(dq, wq.to(dt)), own)
             dxw += _mm_f32(dkv, wkv).view(B, nwin, HW, C)
             g_wq = _mm_f32(dq.t(), xo2)
-            g_bq = dq.float().sum(0)
+            g_bq = dq.sum(0, dtype=torch.float32)
             g_wkv = _mm_f32(dkv.t(), xw2)
-            g_bkv = dkv.float().sum(0)
+            g_bkv = dkv.sum(0, dtype=torch.float32)
             g_wk, g_wv = g_wkv[:C], g_wkv[C:]
             g_bk, g_bv = g_bkv[:C], g_bkv[C:]
             d_extra = None

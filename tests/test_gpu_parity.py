@@ -207,6 +207,29 @@ def test_dwconv_kernels_match_oracle():
             assert rel(gb.cpu().numpy(), gbo) < max(tol, 1e-5)
 
 
+@pytest.mark.parametrize("B,T,H,W,C,ks", [(1, 4, 5, 6, 16, (3, 7, 7)), (2, 3, 9, 40, 128, (3, 7, 7)),
+                                          (1, 5, 6, 33, 64, (3, 3, 3))])
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_dwconv_bwd_data_accumulates(B, T, H, W, C, ks, dt):
+    """dx (float32) += conv_transpose(dy): the generic and the tiled kernels, bf16 / float32 dy."""
+    rng = np.random.default_rng(17)
+    N = T * H * W
+    K = ks[0] * ks[1] * ks[2]
+    w = rng.normal(size=(K, C)).astype(np.float32)
+    dy = rng.normal(size=(B, N, C)).astype(np.float32)
+    base = rng.normal(size=(B, N, C)).astype(np.float32)
+    dyr = dy if dt == torch.float32 else _round_bf16(dy)
+    shape = ops.ConvShape(B, T, H, W, C, ks)
+    acc = torch.from_numpy(base).to(DEV).reshape(B * N, C).contiguous()
+    dyt = torch.from_numpy(dyr).to(DEV, dt).reshape(B * N, C)
+    out = ops.dwconv_bwd_data(shape, dyt, torch.from_numpy(w).to(DEV), out=acc, accumulate=True)
+    assert out.data_ptr() == acc.data_ptr()
+    dxo, _, _ = O.dwconv3d_backward(dyr, np.zeros_like(dyr), w, (T, H, W), ks)
+    assert rel(acc.cpu().numpy().reshape(B, N, C), base + dxo) < 1e-5
+    with pytest.raises(TypeError):
+        ops.dwconv_bwd_data(shape, dyt, torch.from_numpy(w).to(DEV), out=acc.bfloat16(), accumulate=True)
+
+
 # Shapes the shared-memory tiled kernels take (channels a multiple of 64 for bf16, 32 for float32; kernel
 # widths 1/3/5/7): several 32-column tiles with a ragged last one, tile rows that do not divide H,
 # frame chunks, frame windows (time shards), mixed dtypes and the fused epilogues.

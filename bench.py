@@ -204,12 +204,13 @@ def _alg_bytes_per_token(name, C, nh, K, es, probs=False):
     entry point once; float32 accumulators inside msl_dsa_attn_bwd are scratch, not counted).
     probs: the tensor-core path, whose forward also writes the per-sample softmax weights (float32
     [nh, K] per token) and records (8 bytes per sample, `saved`) that its backward reads instead of
-    the offsets."""
+    the offsets.  The backward writes the offset gradients in the compute dtype (es bytes)."""
     off = 4 * nh * K * 3
+    doff = es * nh * K * 3
     pr = 4 * nh * K if probs else 0
     rec = 8 * nh * K if probs else 0
     if name == "msl_dsa_attn_bwd":  # read q k v out dout lse, offsets or (probs, records); write dq dk dv doffsets
-        return 5 * C * es + (pr + rec if probs else off) + 4 * nh + 3 * C * es + off
+        return 5 * C * es + (pr + rec if probs else off) + 4 * nh + 3 * C * es + doff
     if name == "msl_dsa_attn_fwd":  # read q k v offsets, write out lse (probs, records)
         return 3 * C * es + off + C * es + 4 * nh + pr + rec
     if name == "msl_dwconv3d_bwd_weight":  # read dy, x

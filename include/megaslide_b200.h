@@ -30,7 +30,8 @@
 extern "C" {
 #endif
 
-#define MSL_ABI_VERSION 2  /* 2: msl_dsa_fwd_io / msl_dsa_bwd_io end with `saved` */
+#define MSL_ABI_VERSION 3  /* 2: msl_dsa_fwd_io / msl_dsa_bwd_io end with `saved`; 3: msl_dsa_bwd_io ends with
+                              `doff_dtype` */
 
 /* return codes */
 #define MSL_OK 0
@@ -108,8 +109,9 @@ typedef struct msl_dsa_fwd_io {
 } msl_dsa_fwd_io;
 
 /* Backward operands.  Inputs as in the forward plus out/lse from it and dout = dL/d out.
- * Outputs: dq [B, q rows, nh*d] (dtype, overwritten); doffsets float32 [B, q rows, nh*K*3]
- * (overwritten, gradient w.r.t. the RAW offsets, offset_scale included); dek, dev float32
+ * Outputs: dq [B, q rows, nh*d] (dtype, overwritten); doffsets [B, q rows, nh*K*3] of type doff_dtype
+ * (MSL_DTYPE_F32, the zero default, or MSL_DTYPE_BF16: the float32 value rounded to nearest even;
+ * overwritten, gradient w.r.t. the RAW offsets, offset_scale included); dek, dev float32
  * [B, G, nh*d] (overwritten; required when G > 0).
  * dK / dV, two modes:
  *   dk_acc == NULL: dk, dv [B, kv rows, nh*d] (dtype) are overwritten; float32 accumulators
@@ -132,11 +134,12 @@ typedef struct msl_dsa_bwd_io {
   void* dq;        int64_t dq_ld;
   void* dk;        void* dv;  int64_t dkv_ld;
   float* dk_acc;   float* dv_acc; int64_t acc_ld;
-  float* doffsets; int64_t doff_ld;
+  void* doffsets;  int64_t doff_ld;
   float* dek;      float* dev;
   uint32_t* status;
   const float* probs;
   const void* saved;
+  int32_t doff_dtype;
 } msl_dsa_bwd_io;
 
 /* Size in bytes of the `saved` buffer of msl_dsa_fwd_io / msl_dsa_bwd_io for this geometry

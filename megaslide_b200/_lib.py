@@ -72,7 +72,7 @@ class DsaBwdIO(ctypes.Structure):
         ("dq", _vp), ("dq_ld", _i64), ("dk", _vp), ("dv", _vp), ("dkv_ld", _i64),
         ("dk_acc", _vp), ("dv_acc", _vp), ("acc_ld", _i64),
         ("doffsets", _vp), ("doff_ld", _i64), ("dek", _vp), ("dev", _vp), ("status", _vp), ("probs", _vp),
-        ("saved", _vp),
+        ("saved", _vp), ("doff_dtype", ctypes.c_int32),
     ]
 
 
@@ -138,7 +138,7 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
-            if lib.msl_abi_version() != 2:
+            if lib.msl_abi_version() != 3:
                 raise RuntimeError("libmegaslide_b200 ABI version mismatch")
             _lib = lib
     return _lib

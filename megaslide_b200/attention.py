@@ -135,7 +135,7 @@ class DSA3DFunction(torch.autograd.Function):
             q, k, v = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
             _, _, _, doff, dek, dev = ops.attn_bwd(
                 sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev,
-                dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs, saved=saved)
+                dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs, saved=saved, doff_dtype=dt)
             # q/k/v projections; dx accumulates in float32 across the three branches (the depthwise
             # convs add their transposed convolutions into it)
             dx = _mm_f32(dqkv, wqkv)
@@ -155,11 +155,11 @@ class DSA3DFunction(torch.autograd.Function):
                 sums = dekv.sum(0)
                 g_bk = g_bk + sums[:C]
                 g_bv = g_bv + sums[C:]
-            # offset predictor; dh and du stay float32 (bf16 operands, fp32 results)
-            doff_c = doff.to(dt)
-            dh = _mm_f32(doff_c, w2m.to(dt))
-            g_w2 = _mm_f32(doff_c.t(), hact)
-            g_b2 = doff.sum(0)
+            # offset predictor (the kernel wrote doff in the compute dtype, the GEMMs' operand type); dh
+            # and du stay float32 (bf16 operands, fp32 results)
+            dh = _mm_f32(doff, w2m.to(dt))
+            g_w2 = _mm_f32(doff.t(), hact)
+            g_b2 = doff.sum(0, dtype=torch.float32)
             du = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh,
                                 out_dtype=torch.float32)
             ops.dwconv_bwd_data(cfg.conv_3, du, w1_kc, out=dx, accumulate=True)

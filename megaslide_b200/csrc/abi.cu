@@ -272,7 +272,10 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
   P.ek = io->ek; P.ev = io->ev; P.e_ld = io->e_ld;
   P.out = const_cast<void*>(io->out); P.out_ld = io->out_ld; P.lse = const_cast<float*>(io->lse);
   P.dout = io->dout; P.dout_ld = io->dout_ld; P.dq = io->dq; P.dq_ld = io->dq_ld;
-  P.doffsets = io->doffsets; P.doff_ld = io->doff_ld; P.status = io->status;
+  if (io->doff_dtype != MSL_DTYPE_F32 && io->doff_dtype != MSL_DTYPE_BF16)
+    return fail(MSL_ERR_INVALID, "unknown doff_dtype %d", io->doff_dtype);
+  P.doffsets = io->doffsets; P.doff_ld = io->doff_ld; P.doff_bf16 = io->doff_dtype == MSL_DTYPE_BF16;
+  P.status = io->status;
   P.probs = const_cast<float*>(io->probs);
   P.saved = const_cast<void*>(io->saved);
   if (io->saved && !aligned16(io->saved)) return fail(MSL_ERR_INVALID, "saved must be 16-byte aligned");

@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(256) dsa_bwd_kernel(const AttnParams P) {
   float* dkbase = P.dk_acc + static_cast<long long>(qp.b) * P.Nkv * P.acc_ld + qp.head * P.d;
   float* dvbase = P.dv_acc + static_cast<long long>(qp.b) * P.Nkv * P.acc_ld + qp.head * P.d;
   const float* orow = P.offsets + qrow_i * P.off_ld + static_cast<long long>(qp.head) * P.K * 3;
-  float* dorow_off = P.doffsets + qrow_i * P.doff_ld + static_cast<long long>(qp.head) * P.K * 3;
+  const long long dorow_off = qrow_i * P.doff_ld + static_cast<long long>(qp.head) * P.K * 3;
   const SampleGeom sg{P.T, P.H, P.W, P.kt, P.kh, P.kw, P.oscale};
   bool miss = false;
 
@@ -383,9 +383,9 @@ __global__ void __launch_bounds__(256) dsa_bwd_kernel(const AttnParams P) {
     if (jl < P.K) {
       // channel 0 moved grid x (W) after division by (T-1); channel 2 moved grid z (T) after
       // division by (W-1) (attention.py:118-127).
-      dorow_off[jl * 3 + 0] = (P.T > 1) ? __fdiv_rn(my_gw, static_cast<float>(P.T - 1)) * P.oscale : 0.f;
-      dorow_off[jl * 3 + 1] = (P.H > 1) ? __fdiv_rn(my_gh, static_cast<float>(P.H - 1)) * P.oscale : 0.f;
-      dorow_off[jl * 3 + 2] = (P.W > 1) ? __fdiv_rn(my_gt, static_cast<float>(P.W - 1)) * P.oscale : 0.f;
+      store_doff(P, dorow_off + jl * 3 + 0, (P.T > 1) ? __fdiv_rn(my_gw, static_cast<float>(P.T - 1)) * P.oscale : 0.f);
+      store_doff(P, dorow_off + jl * 3 + 1, (P.H > 1) ? __fdiv_rn(my_gh, static_cast<float>(P.H - 1)) * P.oscale : 0.f);
+      store_doff(P, dorow_off + jl * 3 + 2, (P.W > 1) ? __fdiv_rn(my_gt, static_cast<float>(P.W - 1)) * P.oscale : 0.f);
     }
   }
 

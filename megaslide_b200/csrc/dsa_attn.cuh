@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -34,11 +35,20 @@ struct AttnParams {
   const void* dout; long long dout_ld;
   void* dq; long long dq_ld;
   float* dk_acc; float* dv_acc; long long acc_ld;
-  float* doffsets; long long doff_ld;
+  void* doffsets; long long doff_ld;
+  int doff_bf16;      // doffsets element type: 0 float32, 1 bf16 (rounded to nearest even)
   float* extra_ds; float* extra_p;   // [B, nh, Nq, G] scratch
   float* dek; float* dev;            // [B, G, nh*d]
   uint32_t* status;
 };
+
+// element i of the offset gradients in their element type
+__device__ __forceinline__ void store_doff(const AttnParams& P, long long i, float v) {
+  if (P.doff_bf16)
+    static_cast<__nv_bfloat16*>(P.doffsets)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<float*>(P.doffsets)[i] = v;
+}
 
 // Launch plan of the tensor-core kernels (key-envelope chunk capacity and shared-memory layout).
 struct TcLaunch {

@@ -611,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   }
   if (qvalid) {
     const int K3 = 3 * K;
-    float* drow = P.doffsets + (static_cast<long long>(T.b) * P.Nq + qrow) * P.doff_ld + static_cast<long long>(T.head) * K3;
+    const long long drow = (static_cast<long long>(T.b) * P.Nq + qrow) * P.doff_ld + static_cast<long long>(T.head) * K3;
     // d p / d grid = S/2 strictly inside the volume (0 on or beyond the border), times the offset
     // normalisation: channel 0 moved grid x (W) after division by (T-1), channel 1 grid y (H) by
     // (H-1), channel 2 grid z (T) by (W-1)
@@ -625,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
       const unsigned long long v = S.rec[qbase + j];
       const float cc = c == 0 ? c0 : (c == 1 ? c1 : c2);
       const bool on = (v >> 63) && ((v >> (kBitInW - c)) & 1ull);
-      drow[e] = on ? S.g3[3 * (qbase + j) + 2 - c] * cc : 0.f;
+      store_doff(P, drow + e, on ? S.g3[3 * (qbase + j) + 2 - c] * cc : 0.f);
     }
   }
 }

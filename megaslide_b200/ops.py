@@ -209,7 +209,7 @@ def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=None, dq=None, dk=None, dv=None,
              dk_acc=None, dv_acc=None, doffsets=None, dek=None, dev=None, workspace=None, status=None, probs=None,
-             saved=None):
+             saved=None, doff_dtype=torch.float32):
     """Deformable gather attention backward.
 
     Without dk_acc: dK/dV are written to dk/dv (allocated if None) in q's dtype, float32
@@ -217,6 +217,8 @@ def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=N
     dK/dV are ACCUMULATED there.  Returns (dq, dk, dv, doffsets, dek, dev); dk/dv are the
     accumulators in accumulate mode.  probs, saved: the tensor-core forward's outputs for these operands
     (attn_fwd(probs=..., saved=...)); with both, the tensor-core backward runs where it applies.
+    doffsets (or doff_dtype when it is allocated here) is float32 or bf16 (the float32 gradient rounded
+    to nearest even).
     """
     _need_cuda(q, k, v, offsets, out, lse, dout, ek, ev)
     C = shape.heads * shape.head_dim
@@ -233,7 +235,9 @@ def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=N
         if dv is None:
             dv = torch.empty(rows_kv, C, device=dev_, dtype=dt)
     if doffsets is None:
-        doffsets = torch.empty(rows_q, shape.heads * shape.taps * 3, device=dev_, dtype=torch.float32)
+        doffsets = torch.empty(rows_q, shape.heads * shape.taps * 3, device=dev_, dtype=doff_dtype)
+    if doffsets.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("doffsets must be float32 or bfloat16")
     if shape.extra > 0:
         if dek is None:
             dek = torch.empty(shape.batch * shape.extra, C, device=dev_, dtype=torch.float32)
@@ -253,6 +257,7 @@ def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=N
         0 if accumulate else _rows(dk, "dk"),
         _ptr(dk_acc), _ptr(dv_acc), _rows(dk_acc, "dk_acc") if accumulate else 0,
         _ptr(doffsets), _rows(doffsets, "doffsets"), _ptr(dek), _ptr(dev), _ptr(status))
+    io.doff_dtype = dtype_code(doffsets.dtype)
     if probs is not None:
         _need_cuda(probs)
         _check_probs(shape, probs)

@@ -293,7 +293,8 @@ class DSA3DShardedFunction(torch.autograd.Function):
             dkv = torch.empty_like(kv)
             k, v = kv[:, :C], kv[:, C:]
             _, _, _, doff, dek, dev = ops.attn_bwd(sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev, dq=dq,
-                                                   dk=dkv[:, :C], dv=dkv[:, C:], probs=probs, saved=saved)
+                                                   dk=dkv[:, :C], dv=dkv[:, C:], probs=probs, saved=saved,
+                                                   doff_dtype=dt)
             add_frames(_mm_f32(dq, wq.to(dt)), own)
             dxw += _mm_f32(dkv, wkv).view(B, nwin, HW, C)
             g_wq = _mm_f32(dq.t(), xo2)
@@ -313,10 +314,9 @@ class DSA3DShardedFunction(torch.autograd.Function):
                 g_bk = g_bk + sums[:C]
                 g_bv = g_bv + sums[C:]
             # offset predictor
-            doff_c = doff.to(dt)
-            dh = _mm_f32(doff_c, w2m.to(dt))
-            g_w2 = _mm_f32(doff_c.t(), hact)
-            g_b2 = doff.sum(0)
+            dh = _mm_f32(doff, w2m.to(dt))
+            g_w2 = _mm_f32(doff.t(), hact)
+            g_b2 = doff.sum(0, dtype=torch.float32)
             conv3 = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=win[0], in_frames=nwin, out_frame0=own[0],
                                   out_frames=nown)
             du = ops.dwconv_fwd(conv3, xw2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh, out_dtype=torch.float32)

@@ -495,7 +495,7 @@ TC_BWD_CASES = [
 ]
 
 
-def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False):
+def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False, doff_dtype=torch.float32):
     """Forward with the softmax weights saved (algo 2) or not (algo 1), then the backward."""
     B, T, H, W, nh, d, ks, G, _ = case
     q, k, v, off, ek, ev, dout = arrays
@@ -512,13 +512,15 @@ def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False):
     if accumulate:
         kw = dict(dk_acc=torch.full((B * N, C), 0.5, device=DEV), dv_acc=torch.full((B * N, C), -0.25, device=DEV))
     dq, dk, dv, doff, _, _ = ops.attn_bwd(shape, qt, kt_, vt, offt, out, lse, dot, probs=probs, saved=saved,
-                                          status=status, **kw)
+                                          status=status, doff_dtype=doff_dtype, **kw)
+    assert doff.dtype == doff_dtype
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     if accumulate:
         dk, dv = dk - 0.5, dv + 0.25
     f = lambda a: a.float().cpu().numpy().reshape(B, -1, C)  # noqa: E731
-    res = dict(out=f(out), lse=lse.cpu().numpy(), dq=f(dq), dk=f(dk), dv=f(dv), doff=doff.cpu().numpy().reshape(B, N, -1))
+    res = dict(out=f(out), lse=lse.cpu().numpy(), dq=f(dq), dk=f(dk), dv=f(dv),
+               doff=doff.float().cpu().numpy().reshape(B, N, -1))
     if probs is not None:
         res["probs"] = probs.cpu().numpy()
     return res
@@ -529,6 +531,18 @@ def _compare_grads_bf16(got, ref, what):
     for key in ("dq", "dk", "dv", "doff"):
         ef, em = fro(got[key], ref[key]), rel(got[key], ref[key])
         assert ef < RTOL_BF16 and em < MAXREL_BF16_GRAD, f"{what} {key}: fro {ef:.3e} max {em:.3e}"
+
+
+@pytest.mark.parametrize("algo", [1, 2])
+def test_bwd_bf16_offset_gradients_are_the_rounded_float32_ones(algo):
+    """doff_dtype=bf16: both backward paths store the float32 offset gradient rounded to nearest even."""
+    case = TC_BWD_CASES[0]
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))
+                   for i, a in enumerate(_core_inputs(case, seed=23)))
+    full = _run_tc_train(case, arrays, algo=algo)["doff"]
+    half = _run_tc_train(case, arrays, algo=algo, doff_dtype=torch.bfloat16)["doff"]
+    expect = torch.from_numpy(full).bfloat16().float().numpy()
+    assert np.array_equal(half, expect)
 
 
 @pytest.mark.parametrize("case", TC_BWD_CASES, ids=_tc_ids)

@@ -30,8 +30,8 @@
 extern "C" {
 #endif
 
-#define MSL_ABI_VERSION 3  /* 2: msl_dsa_fwd_io / msl_dsa_bwd_io end with `saved`; 3: msl_dsa_bwd_io ends with
-                              `doff_dtype` */
+#define MSL_ABI_VERSION 4  /* 2: msl_dsa_fwd_io / msl_dsa_bwd_io end with `saved`; 3: msl_dsa_bwd_io ends with
+                              `doff_dtype`; 4: both end with `offset_bias`, msl_offsets_absmax takes a bias */
 
 /* return codes */
 #define MSL_OK 0
@@ -94,7 +94,10 @@ typedef struct msl_dsa_geometry {
  * saved: optional msl_dsa_saved_bytes(geom) bytes (16-byte aligned): the tensor-core forward's
  * per-sample records (trilinear corner, fractions, interior and dropout flags) and per-tile key
  * envelopes, which the tensor-core backward reads instead of recomputing the sample coordinates
- * from the offsets; written only by the tensor-core path.  NULL = not saved. */
+ * from the offsets; written only by the tensor-core path.  NULL = not saved.
+ * offset_bias: optional float32 [nh*kt*kh*kw*3] added to every offsets row before use (the offset
+ * predictor's 1x1-conv bias, attention.py:70-74: offsets[r, c] + offset_bias[c] in one float32
+ * rounding, exactly the materialised sum); NULL = the offsets are used as they are. */
 typedef struct msl_dsa_fwd_io {
   const void* q;   int64_t q_ld;
   const void* k;   int64_t k_ld;
@@ -106,6 +109,7 @@ typedef struct msl_dsa_fwd_io {
   uint32_t* status;
   float* probs;
   void* saved;
+  const float* offset_bias;
 } msl_dsa_fwd_io;
 
 /* Backward operands.  Inputs as in the forward plus out/lse from it and dout = dL/d out.
@@ -120,7 +124,7 @@ typedef struct msl_dsa_fwd_io {
  *                   ACCUMULATED into (not cleared), dk / dv are not touched.  Used by the
  *                   time-sharded path, which reduces halo rows across ranks before converting.
  * probs, saved: the tensor-core forward's optional outputs (see msl_dsa_fwd_io), from the forward of
- * the same operands.  When both are given (bf16, no extra keys) the tensor-core backward runs;
+ * the same operands; offset_bias as in msl_dsa_fwd_io (the same as the forward's).  When both are given (bf16, no extra keys) the tensor-core backward runs;
  * otherwise the CUDA-core backward. */
 typedef struct msl_dsa_bwd_io {
   const void* q;   int64_t q_ld;
@@ -140,6 +144,7 @@ typedef struct msl_dsa_bwd_io {
   const float* probs;
   const void* saved;
   int32_t doff_dtype;
+  const float* offset_bias;
 } msl_dsa_bwd_io;
 
 /* Size in bytes of the `saved` buffer of msl_dsa_fwd_io / msl_dsa_bwd_io for this geometry
@@ -230,9 +235,10 @@ int msl_dwconv3d_bwd_weight(const msl_dwconv_geometry* geom, const void* dy, int
  * ---------------------------------------------------------------------------------------------- */
 /* Per-axis maximum |offset*offset_scale| (in the reference's raw offset units) over a float32
  * offset tensor [rows, >=heads*taps*3] (row stride ld): out3[0..2] = max over channels 0, 1, 2 of
- * every tap.  out3 (device, float32[3]) must be zeroed by the caller; values are max-accumulated.
+ * every tap.  bias (float32 [heads*taps*3] or NULL) is added to every row first, as in offset_bias
+ * of msl_dsa_fwd_io.  out3 (device, float32[3]) must be zeroed by the caller; values are max-accumulated.
  * Used to size the time halo of the sharded path. */
-int msl_offsets_absmax(const float* offsets, int64_t rows, int64_t ld, int32_t heads,
+int msl_offsets_absmax(const float* offsets, int64_t rows, int64_t ld, const float* bias, int32_t heads,
                        int32_t taps, float offset_scale, float* out3, void* stream);
 
 /* Element-type conversion float32 -> dtype of a [rows, cols] matrix (row strides in elements). */

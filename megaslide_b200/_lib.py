@@ -59,6 +59,7 @@ class DsaFwdIO(ctypes.Structure):
         ("q", _vp), ("q_ld", _i64), ("k", _vp), ("k_ld", _i64), ("v", _vp), ("v_ld", _i64),
         ("offsets", _vp), ("off_ld", _i64), ("ek", _vp), ("ev", _vp), ("e_ld", _i64),
         ("out", _vp), ("out_ld", _i64), ("lse", _vp), ("status", _vp), ("probs", _vp), ("saved", _vp),
+        ("offset_bias", _vp),
     ]
 
 
@@ -72,7 +73,7 @@ class DsaBwdIO(ctypes.Structure):
         ("dq", _vp), ("dq_ld", _i64), ("dk", _vp), ("dv", _vp), ("dkv_ld", _i64),
         ("dk_acc", _vp), ("dv_acc", _vp), ("acc_ld", _i64),
         ("doffsets", _vp), ("doff_ld", _i64), ("dek", _vp), ("dev", _vp), ("status", _vp), ("probs", _vp),
-        ("saved", _vp), ("doff_dtype", ctypes.c_int32),
+        ("saved", _vp), ("doff_dtype", ctypes.c_int32), ("offset_bias", _vp),
     ]
 
 
@@ -100,7 +101,7 @@ SIGNATURES = {
     "msl_dwconv3d_bwd_data_acc": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _vp, _vp, _i64, _vp]),
     "msl_dwconv3d_bwd_weight": (ctypes.c_int, [ctypes.POINTER(DwconvGeometry), _vp, _i64, _i32, _vp, _i64, _vp,
                                                _vp, _vp]),
-    "msl_offsets_absmax": (ctypes.c_int, [_vp, _i64, _i64, _i32, _i32, _f32, _vp, _vp]),
+    "msl_offsets_absmax": (ctypes.c_int, [_vp, _i64, _i64, _vp, _i32, _i32, _f32, _vp, _vp]),
     "msl_convert_f32": (ctypes.c_int, [_vp, _i64, _vp, _i64, _i32, _i64, _i64, _vp]),
     "msl_host_accumulate": (ctypes.c_int, [_vp, _vp, _i32, _i64, _i32, ctypes.POINTER(ctypes.c_double)]),
     "msl_host_adamw": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _f32, _i64, _f32, _vp, _i32]),
@@ -138,7 +139,7 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
-            if lib.msl_abi_version() != 3:
+            if lib.msl_abi_version() != 4:
                 raise RuntimeError("libmegaslide_b200 ABI version mismatch")
             _lib = lib
     return _lib

@@ -40,13 +40,6 @@ def _mm_f32(a: Tensor, b: Tensor) -> Tensor:
     return torch.mm(a, b, out_dtype=torch.float32)
 
 
-def _addmm_f32(bias: Tensor, a: Tensor, b: Tensor) -> Tensor:
-    """bias + a @ b with a float32 result in one GEMM (the float32 bias [n] is added in its epilogue)."""
-    if a.dtype == torch.float32:
-        return torch.addmm(bias, a, b)
-    return torch.addmm(bias, a, b, out_dtype=torch.float32)
-
-
 class _Cfg:
     __slots__ = ("shape", "conv_k", "conv_3", "dtype", "param_dtypes", "G", "kernel")
 
@@ -80,7 +73,8 @@ class DSA3DFunction(torch.autograd.Function):
         hact = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
         O = w2.shape[0]
         w2m = w2.reshape(O, C)
-        off = _addmm_f32(b2.detach().float(), hact, w2m.to(dt).t())
+        off = _mm_f32(hact, w2m.to(dt).t())  # its bias b2 is added by the attention kernels as they read it
+        b2f = b2.detach().float().contiguous()
         # depthwise conv term with both biases (dw_conv and out_proj) fused
         wd_kc = ops.conv_weight_kc(wd)
         D = ops.dwconv_fwd(cfg.conv_k, x2, wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous(),
@@ -96,16 +90,16 @@ class DSA3DFunction(torch.autograd.Function):
             # the tensor-core backward reads the forward's per-sample softmax weights and records
             probs, saved = ops.saved_buffers(sh, dt, x2.device)
             try:
-                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved)
+                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved, offset_bias=b2f)
             except MslError as e:
                 if e.code != MSL_ERR_UNSUPPORTED:
                     raise
                 probs = saved = None
         if probs is None:
-            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev)
+            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f)
         y = torch.addmm(D, attn, wo.to(dt).t())
         if train:
-            ctx.save_for_backward(x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
+            ctx.save_for_backward(x2, qkv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
                                   saved)
             ctx.cfg = cfg
             ctx.in_dtype = x.dtype
@@ -114,7 +108,8 @@ class DSA3DFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        (x2, qkv, hact, off, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs, saved) = ctx.saved_tensors
+        (x2, qkv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
+         saved) = ctx.saved_tensors
         cfg: _Cfg = ctx.cfg
         sh: ops.DsaShape = cfg.shape
         dt = cfg.dtype
@@ -135,7 +130,8 @@ class DSA3DFunction(torch.autograd.Function):
             q, k, v = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
             _, _, _, doff, dek, dev = ops.attn_bwd(
                 sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev,
-                dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs, saved=saved, doff_dtype=dt)
+                dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs, saved=saved, doff_dtype=dt,
+                offset_bias=b2f)
             # q/k/v projections; dx accumulates in float32 across the three branches (the depthwise
             # convs add their transposed convolutions into it)
             dx = _mm_f32(dqkv, wqkv)

@@ -190,6 +190,7 @@ int msl_dsa_attn_fwd(const msl_dsa_geometry* geom, const msl_dsa_fwd_io* io, voi
   P.ek = io->ek; P.ev = io->ev; P.e_ld = io->e_ld;
   P.out = io->out; P.out_ld = io->out_ld; P.lse = io->lse; P.status = io->status; P.probs = io->probs;
   P.saved = io->saved;
+  P.off_bias = io->offset_bias;
   if (io->saved && !aligned16(io->saved)) return fail(MSL_ERR_INVALID, "saved must be 16-byte aligned");
   if (geom->algo != MSL_ALGO_SIMT) {
     bool ok = msl::tc_supported(P);
@@ -278,6 +279,7 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
   P.status = io->status;
   P.probs = const_cast<float*>(io->probs);
   P.saved = const_cast<void*>(io->saved);
+  P.off_bias = io->offset_bias;
   if (io->saved && !aligned16(io->saved)) return fail(MSL_ERR_INVALID, "saved must be 16-byte aligned");
   if (accumulate) {
     P.dk_acc = io->dk_acc; P.dv_acc = io->dv_acc; P.acc_ld = io->acc_ld;
@@ -419,13 +421,13 @@ int msl_dwconv3d_bwd_weight(const msl_dwconv_geometry* geom, const void* dy, int
   return MSL_OK;
 }
 
-int msl_offsets_absmax(const float* offsets, int64_t rows, int64_t ld, int32_t heads, int32_t taps,
+int msl_offsets_absmax(const float* offsets, int64_t rows, int64_t ld, const float* bias, int32_t heads, int32_t taps,
                        float offset_scale, float* out3, void* stream) {
   if (!offsets || !out3) return fail(MSL_ERR_INVALID, "offsets and out3 are required");
   if (rows < 0 || heads < 1 || taps < 1 || ld < static_cast<int64_t>(heads) * taps * 3)
     return fail(MSL_ERR_INVALID, "bad offsets shape");
   if (rows == 0) return MSL_OK;
-  cudaError_t e = msl::launch_offsets_absmax(offsets, rows, ld, heads, taps, offset_scale, out3,
+  cudaError_t e = msl::launch_offsets_absmax(offsets, rows, ld, bias, heads, taps, offset_scale, out3,
                                              static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "offsets_absmax_kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);

@@ -83,9 +83,11 @@ __global__ void __launch_bounds__(256) dsa_fwd_kernel(const AttnParams P) {
   for (int j0 = 0; j0 < P.K; j0 += 32) {
     float mpt = 0.f, mph = 0.f, mpw = 0.f;
     const int jl = j0 + lane;
-    if (jl < P.K)
-      sample_coords(sg, qp.tg, qp.h, qp.w, jl, __ldg(orow + jl * 3), __ldg(orow + jl * 3 + 1),
-                    __ldg(orow + jl * 3 + 2), mpt, mph, mpw);
+    if (jl < P.K) {
+      float o0, o1, o2;
+      load_off3(P, orow, qp.head, jl, o0, o1, o2);
+      sample_coords(sg, qp.tg, qp.h, qp.w, jl, o0, o1, o2, mpt, mph, mpw);
+    }
     const int ns = min(32, P.K - j0);
     for (int jj = 0; jj < ns; ++jj) {
       const float pt = __shfl_sync(kFull, mpt, jj);
@@ -281,9 +283,11 @@ __global__ void __launch_bounds__(256) dsa_bwd_kernel(const AttnParams P) {
   for (int j0 = 0; j0 < P.K; j0 += 32) {
     float mpt = 0.f, mph = 0.f, mpw = 0.f;
     const int jl = j0 + lane;
-    if (jl < P.K)
-      sample_coords(sg, qp.tg, qp.h, qp.w, jl, __ldg(orow + jl * 3), __ldg(orow + jl * 3 + 1),
-                    __ldg(orow + jl * 3 + 2), mpt, mph, mpw);
+    if (jl < P.K) {
+      float o0, o1, o2;
+      load_off3(P, orow, qp.head, jl, o0, o1, o2);
+      sample_coords(sg, qp.tg, qp.h, qp.w, jl, o0, o1, o2, mpt, mph, mpw);
+    }
     float my_gw = 0.f, my_gh = 0.f, my_gt = 0.f;
     const int ns = min(32, P.K - j0);
     for (int jj = 0; jj < ns; ++jj) {

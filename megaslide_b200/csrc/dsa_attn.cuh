@@ -32,6 +32,7 @@ struct AttnParams {
   float* lse;
   float* probs;       // [B, nh, Nq, K] softmax weights before dropout (optional; tensor-core paths)
   void* saved;        // tensor-core forward -> backward: per-sample records + tile envelopes (optional)
+  const float* off_bias;  // [nh*K*3] added to every offsets row (optional)
   const void* dout; long long dout_ld;
   void* dq; long long dq_ld;
   float* dk_acc; float* dv_acc; long long acc_ld;
@@ -41,6 +42,21 @@ struct AttnParams {
   float* dek; float* dev;            // [B, G, nh*d]
   uint32_t* status;
 };
+
+// the three offsets (channels 0, 1, 2) of window sample j of the offsets row `row` of head `head`, with
+// the optional per-column bias added in one float32 rounding (as the materialised offsets + bias)
+__device__ __forceinline__ void load_off3(const AttnParams& P, const float* row, int head, int j, float& o0, float& o1,
+                                          float& o2) {
+  o0 = row[3 * j];
+  o1 = row[3 * j + 1];
+  o2 = row[3 * j + 2];
+  if (P.off_bias) {
+    const float* b = P.off_bias + (static_cast<long long>(head) * P.K + j) * 3;
+    o0 = __fadd_rn(o0, __ldg(b));
+    o1 = __fadd_rn(o1, __ldg(b + 1));
+    o2 = __fadd_rn(o2, __ldg(b + 2));
+  }
+}
 
 // element i of the offset gradients in their element type
 __device__ __forceinline__ void store_doff(const AttnParams& P, long long i, float v) {
@@ -103,7 +119,7 @@ cudaError_t launch_dwconv_fwd_tiled(const ConvParams& P, const void* x, long lon
 cudaError_t launch_dwconv_wgrad_tiled(const ConvParams& P, const void* dy, long long dy_ld, int dy_dtype, const void* x,
                                       long long x_ld, float* dw, float* db, cudaStream_t s);
 
-cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, int heads, int taps,
+cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, const float* bias, int heads, int taps,
                                   float oscale, float* out3, cudaStream_t s);
 cudaError_t launch_convert_f32(const float* src, long long src_ld, void* dst, long long dst_ld,
                                int dtype, long long rows, long long cols, cudaStream_t s);

@@ -211,7 +211,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     wi.init(js, P.kh, P.kw);
     for (int j = js; j < je; ++j, wi.advance(1, P.kh, P.kw)) {
       float pt, ph, pw;
-      tab_coords(P, tb, qy, qx, wi.it, wi.ih, wi.iw, oq[3 * j], oq[3 * j + 1], oq[3 * j + 2], pt, ph, pw);
+      float o0, o1, o2;
+      load_off3(P, oq, T.head, j, o0, o1, o2);
+      tab_coords(P, tb, qy, qx, wi.it, wi.ih, wi.iw, o0, o1, o2, pt, ph, pw);
       S.rec[qbase + j] = (static_cast<unsigned long long>(__float_as_uint(ph)) << 32) | __float_as_uint(pt);
       sacc[j] = pw;
       const int t0 = static_cast<int>(floorf(pt)), h0 = static_cast<int>(floorf(ph)), w0 = static_cast<int>(floorf(pw));

@@ -251,14 +251,16 @@ cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long d
 
 // ------------------------------------------------------------------------------ utilities
 __global__ void __launch_bounds__(256) offsets_absmax_kernel(const float* __restrict__ off, long long rows, long long ld,
-                                                             int ncol, float oscale, float* out3) {
+                                                             const float* __restrict__ bias, int ncol, float oscale,
+                                                             float* out3) {
   float m0 = 0.f, m1 = 0.f, m2 = 0.f;
   const long long n = rows * ncol;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long r = i / ncol;
     const int cidx = static_cast<int>(i - r * ncol);
-    const float v = fabsf(off[r * ld + cidx] * oscale);
+    const float o = bias ? __fadd_rn(off[r * ld + cidx], __ldg(bias + cidx)) : off[r * ld + cidx];
+    const float v = fabsf(o * oscale);
     const int axis = cidx % 3;
     if (axis == 0) m0 = fmaxf(m0, v);
     else if (axis == 1) m1 = fmaxf(m1, v);
@@ -278,14 +280,14 @@ __global__ void __launch_bounds__(256) offsets_absmax_kernel(const float* __rest
   }
 }
 
-cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, int heads, int taps,
+cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, const float* bias, int heads, int taps,
                                   float oscale, float* out3, cudaStream_t s) {
   const int ncol = heads * taps * 3;
   const long long n = rows * ncol;
   long long blocks = (n + 255) / 256;
   if (blocks > 148LL * 16) blocks = 148LL * 16;
   if (blocks < 1) blocks = 1;
-  offsets_absmax_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, rows, ld, ncol, oscale, out3);
+  offsets_absmax_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, rows, ld, bias, ncol, oscale, out3);
   return cudaGetLastError();
 }
 

@@ -165,21 +165,29 @@ def _check_probs(shape: DsaShape, probs: torch.Tensor) -> None:
         raise ValueError(f"probs must be a contiguous float32 tensor of shape {want}")
 
 
+def _check_offset_bias(bias: Optional[torch.Tensor], n: int) -> None:
+    if bias is not None and (bias.dtype != torch.float32 or bias.numel() != n or not bias.is_contiguous()):
+        raise ValueError(f"offset_bias must be a contiguous float32 tensor of {n} elements")
+
+
 def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, offsets: torch.Tensor,
              ek: Optional[torch.Tensor] = None, ev: Optional[torch.Tensor] = None,
              out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
              status: Optional[torch.Tensor] = None,
              probs: Optional[torch.Tensor] = None,
-             saved: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+             saved: Optional[torch.Tensor] = None,
+             offset_bias: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Deformable gather attention forward.
 
     q: [B*q_rows, >=C] row view; k, v: [B*kv_rows, >=C]; offsets: float32 [B*q_rows, >=nh*K*3];
     ek, ev: [B*G, >=C] or None.  Returns (out [B*q_rows, C], lse float32 [B, nh, q_rows]).
     probs, saved (optional, see saved_buffers): filled with the per-sample softmax weights and the
     per-sample records for the tensor-core backward; the call raises MslError(MSL_ERR_UNSUPPORTED)
-    when the tensor-core forward does not apply to these operands.
+    when the tensor-core forward does not apply to these operands.  offset_bias (float32 [nh*K*3]):
+    added to every offsets row before use (offsets + bias, one float32 rounding).
     """
-    _need_cuda(q, k, v, offsets, ek, ev)
+    _need_cuda(q, k, v, offsets, ek, ev, offset_bias)
+    _check_offset_bias(offset_bias, shape.heads * shape.taps * 3)
     C = shape.heads * shape.head_dim
     dt = q.dtype
     if offsets.dtype != torch.float32:
@@ -199,6 +207,7 @@ def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         _need_cuda(saved)
         _check_saved(shape, dt, saved)
         io.saved = _ptr(saved)
+    io.offset_bias = _ptr(offset_bias)
     g = shape.geometry(dt)
     with torch.cuda.device(q.device):
         rc = _call("msl_dsa_attn_fwd", q.device,
@@ -209,7 +218,7 @@ def attn_fwd(shape: DsaShape, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=None, dq=None, dk=None, dv=None,
              dk_acc=None, dv_acc=None, doffsets=None, dek=None, dev=None, workspace=None, status=None, probs=None,
-             saved=None, doff_dtype=torch.float32):
+             saved=None, doff_dtype=torch.float32, offset_bias=None):
     """Deformable gather attention backward.
 
     Without dk_acc: dK/dV are written to dk/dv (allocated if None) in q's dtype, float32
@@ -218,9 +227,10 @@ def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=N
     accumulators in accumulate mode.  probs, saved: the tensor-core forward's outputs for these operands
     (attn_fwd(probs=..., saved=...)); with both, the tensor-core backward runs where it applies.
     doffsets (or doff_dtype when it is allocated here) is float32 or bf16 (the float32 gradient rounded
-    to nearest even).
+    to nearest even).  offset_bias: the forward's.
     """
-    _need_cuda(q, k, v, offsets, out, lse, dout, ek, ev)
+    _need_cuda(q, k, v, offsets, out, lse, dout, ek, ev, offset_bias)
+    _check_offset_bias(offset_bias, shape.heads * shape.taps * 3)
     C = shape.heads * shape.head_dim
     dt = q.dtype
     dev_ = q.device
@@ -258,6 +268,7 @@ def attn_bwd(shape: DsaShape, q, k, v, offsets, out, lse, dout, *, ek=None, ev=N
         _ptr(dk_acc), _ptr(dv_acc), _rows(dk_acc, "dk_acc") if accumulate else 0,
         _ptr(doffsets), _rows(doffsets, "doffsets"), _ptr(dek), _ptr(dev), _ptr(status))
     io.doff_dtype = dtype_code(doffsets.dtype)
+    io.offset_bias = _ptr(offset_bias)
     if probs is not None:
         _need_cuda(probs)
         _check_probs(shape, probs)
@@ -367,13 +378,15 @@ def dwconv_bwd_weight(shape: ConvShape, dy: torch.Tensor, x: torch.Tensor, dweig
 
 
 def offsets_absmax(offsets: torch.Tensor, heads: int, taps: int, offset_scale: float = 1.0,
-                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Per-axis max |offset * offset_scale| -> float32[3] on the device (channel 0, 1, 2)."""
-    _need_cuda(offsets)
+                   out: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per-axis max |(offset + bias) * offset_scale| -> float32[3] on the device (channel 0, 1, 2)."""
+    _need_cuda(offsets, bias)
+    _check_offset_bias(bias, heads * taps * 3)
     if out is None:
         out = torch.zeros(3, device=offsets.device, dtype=torch.float32)
     with torch.cuda.device(offsets.device):
-        rc = _lib.load().msl_offsets_absmax(_ptr(offsets), offsets.shape[0], _rows(offsets, "offsets"), heads, taps,
+        rc = _lib.load().msl_offsets_absmax(_ptr(offsets), offsets.shape[0], _rows(offsets, "offsets"), _ptr(bias),
+                                            heads, taps,
                                             float(offset_scale), _ptr(out), _stream(offsets.device))
     _lib.check("msl_offsets_absmax", rc)
     return out

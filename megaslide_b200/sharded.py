@@ -33,7 +33,7 @@ from torch import Tensor, nn
 
 from . import ops
 from ._lib import MSL_EPI_GELU, MSL_EPI_GELU_GRAD, MSL_EPI_NONE, MSL_ERR_UNSUPPORTED, MslError
-from .attention import DeformableSlideAttention3D, _addmm_f32, _mm_f32
+from .attention import DeformableSlideAttention3D, _mm_f32
 
 Range = Tuple[int, int]
 
@@ -195,11 +195,12 @@ class DSA3DShardedFunction(torch.autograd.Function):
         b1f = b1.detach().float().contiguous()
         hact = ops.dwconv_fwd(conv3, xc2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
         w2m = w2.reshape(w2.shape[0], C)
-        off = _addmm_f32(b2.detach().float(), hact, w2m.to(dt).t())
+        off = _mm_f32(hact, w2m.to(dt).t())  # its bias b2 is added by the kernels as they read it
+        b2f = b2.detach().float().contiguous()
         wd_kc = ops.conv_weight_kc(wd)
         D = ops.dwconv_fwd(convk, xc2, wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous(),
                            epilogue=MSL_EPI_NONE)
-        amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale)
+        amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale, bias=b2f)
         dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=cfg.group)
         dmax = float(amax[2].item())
         if not math.isfinite(dmax):
@@ -234,16 +235,16 @@ class DSA3DShardedFunction(torch.autograd.Function):
         if train and ops.wants_probs(sh, dt):
             probs, saved = ops.saved_buffers(sh, dt, x.device)
             try:
-                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved)
+                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved, offset_bias=b2f)
             except MslError as e:
                 if e.code != MSL_ERR_UNSUPPORTED:
                     raise
                 probs = saved = None
         if probs is None:
-            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev)
+            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f)
         y = torch.addmm(D, attn, wo.to(dt).t())
         if train:
-            ctx.save_for_backward(xw, q, kv, hact, off, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc,
+            ctx.save_for_backward(xw, q, kv, hact, off, b2f, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc,
                                   probs, saved)
             ctx.cfg, ctx.sh, ctx.plan, ctx.cw = cfg, sh, plan, cw
             ctx.in_dtype = x.dtype
@@ -252,7 +253,8 @@ class DSA3DShardedFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        (xw, q, kv, hact, off, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc, probs, saved) = ctx.saved_tensors
+        (xw, q, kv, hact, off, b2f, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
+         saved) = ctx.saved_tensors
         cfg: _ShardCfg = ctx.cfg
         sh: ops.DsaShape = ctx.sh
         plan: FramePlan = ctx.plan
@@ -294,7 +296,7 @@ class DSA3DShardedFunction(torch.autograd.Function):
             k, v = kv[:, :C], kv[:, C:]
             _, _, _, doff, dek, dev = ops.attn_bwd(sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev, dq=dq,
                                                    dk=dkv[:, :C], dv=dkv[:, C:], probs=probs, saved=saved,
-                                                   doff_dtype=dt)
+                                                   doff_dtype=dt, offset_bias=b2f)
             add_frames(_mm_f32(dq, wq.to(dt)), own)
             dxw += _mm_f32(dkv, wkv).view(B, nwin, HW, C)
             g_wq = _mm_f32(dq.t(), xo2)

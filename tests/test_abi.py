@@ -23,7 +23,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_version():
     lib = _lib.load()
-    assert lib.msl_abi_version() == 3
+    assert lib.msl_abi_version() == 4
     assert _lib.launch_count() >= 0
 
 

@@ -495,7 +495,8 @@ TC_BWD_CASES = [
 ]
 
 
-def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False, doff_dtype=torch.float32):
+def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False, doff_dtype=torch.float32,
+                  offset_bias=None):
     """Forward with the softmax weights saved (algo 2) or not (algo 1), then the backward."""
     B, T, H, W, nh, d, ks, G, _ = case
     q, k, v, off, ek, ev, dout = arrays
@@ -507,12 +508,13 @@ def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False, d
     qt, kt_, vt, dot = t(q), t(k), t(v), t(dout)
     probs, saved = ops.saved_buffers(shape, torch.bfloat16, DEV) if algo == 2 else (None, None)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
-    out, lse = ops.attn_fwd(shape, qt, kt_, vt, offt, probs=probs, saved=saved, status=status)
+    ob = None if offset_bias is None else torch.from_numpy(offset_bias).to(DEV)
+    out, lse = ops.attn_fwd(shape, qt, kt_, vt, offt, probs=probs, saved=saved, status=status, offset_bias=ob)
     kw = {}
     if accumulate:
         kw = dict(dk_acc=torch.full((B * N, C), 0.5, device=DEV), dv_acc=torch.full((B * N, C), -0.25, device=DEV))
     dq, dk, dv, doff, _, _ = ops.attn_bwd(shape, qt, kt_, vt, offt, out, lse, dot, probs=probs, saved=saved,
-                                          status=status, doff_dtype=doff_dtype, **kw)
+                                          status=status, doff_dtype=doff_dtype, offset_bias=ob, **kw)
     assert doff.dtype == doff_dtype
     torch.cuda.synchronize()
     assert int(status.item()) == 0
@@ -531,6 +533,26 @@ def _compare_grads_bf16(got, ref, what):
     for key in ("dq", "dk", "dv", "doff"):
         ef, em = fro(got[key], ref[key]), rel(got[key], ref[key])
         assert ef < RTOL_BF16 and em < MAXREL_BF16_GRAD, f"{what} {key}: fro {ef:.3e} max {em:.3e}"
+
+
+@pytest.mark.parametrize("algo", [1, 2])
+def test_offset_bias_equals_the_materialised_sum(algo):
+    """offset_bias: the kernels add the per-column bias as they read the offsets; the results are those of
+    offsets + bias materialised in float32 (bit for bit, but dK / dV: the order of their float32 atomics
+    differs from run to run, and the bf16 results then round a few elements the other way)."""
+    case = TC_BWD_CASES[0]
+    B, T, H, W, nh, d, ks, G, _ = case
+    arrays = tuple(None if a is None else (a if i == 3 else _round_bf16(a))
+                   for i, a in enumerate(_core_inputs(case, seed=29)))
+    bias = (np.random.default_rng(3).normal(size=(nh * ks[0] * ks[1] * ks[2] * 3,)) * 0.7).astype(np.float32)
+    summed = list(arrays)
+    summed[3] = (arrays[3] + bias).astype(np.float32)
+    ref = _run_tc_train(case, tuple(summed), algo=algo)
+    got = _run_tc_train(case, arrays, algo=algo, offset_bias=bias)
+    for key in ("out", "lse", "dq", "doff"):
+        assert np.array_equal(got[key], ref[key]), key
+    for key in ("dk", "dv"):
+        assert fro(got[key], ref[key]) < 1e-3, key
 
 
 @pytest.mark.parametrize("algo", [1, 2])
@@ -641,3 +663,18 @@ def test_module_bf16_training_uses_tensor_core_backward(monkeypatch):
     for p in m.parameters():
         assert p.grad is not None and torch.isfinite(p.grad.float()).all()
     assert seen == [True]
+
+
+def test_offsets_absmax_with_bias():
+    """Per-axis max |(offsets + bias) * scale| over a strided offsets view, with and without the bias."""
+    rng = np.random.default_rng(41)
+    heads, taps = 3, 27
+    n = heads * taps * 3
+    off = (rng.normal(size=(257, n + 5)) * 2.0).astype(np.float32)
+    bias = (rng.normal(size=(n,)) * 3.0).astype(np.float32)
+    offt = torch.from_numpy(off).to(DEV)[:, :n]
+    for b in (None, bias):
+        full = off[:, :n] + (0 if b is None else b)
+        want = np.abs(full.astype(np.float32) * np.float32(0.5)).reshape(-1, heads * taps, 3).max(axis=(0, 1))
+        got = ops.offsets_absmax(offt, heads, taps, 0.5, bias=None if b is None else torch.from_numpy(b).to(DEV))
+        assert np.array_equal(got.cpu().numpy(), want.astype(np.float32))

@@ -170,6 +170,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   const int K3 = 3 * K;
   const int OS = (K3 + 3 + 3) & ~3;  // staged row stride (floats): 16-byte aligned rows
   float* ostage = reinterpret_cast<float*>(S.kbuf);
+  float* bstage = ostage + static_cast<size_t>(kQ) * OS;  // this head's offset bias (K3 floats), if any
+  if (P.off_bias)
+    for (int e = threadIdx.x; e < K3; e += kThreads)
+      cp_async4(smem_u32(bstage + e), P.off_bias + static_cast<long long>(T.head) * K3 + e);
   // misalignment (floats) of this thread's own query row, where its staged row starts
   const int omis = static_cast<int>(
       (reinterpret_cast<uintptr_t>(P.offsets + (static_cast<long long>(T.b) * P.Nq + qrow) * P.off_ld +
@@ -211,8 +215,12 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     wi.init(js, P.kh, P.kw);
     for (int j = js; j < je; ++j, wi.advance(1, P.kh, P.kw)) {
       float pt, ph, pw;
-      float o0, o1, o2;
-      load_off3(P, oq, T.head, j, o0, o1, o2);
+      float o0 = oq[3 * j], o1 = oq[3 * j + 1], o2 = oq[3 * j + 2];
+      if (P.off_bias) {  // the lanes of the query pair read the same bias words: broadcasts
+        o0 = __fadd_rn(o0, bstage[3 * j]);
+        o1 = __fadd_rn(o1, bstage[3 * j + 1]);
+        o2 = __fadd_rn(o2, bstage[3 * j + 2]);
+      }
       tab_coords(P, tb, qy, qx, wi.it, wi.ih, wi.iw, o0, o1, o2, pt, ph, pw);
       S.rec[qbase + j] = (static_cast<unsigned long long>(__float_as_uint(ph)) << 32) | __float_as_uint(pt);
       sacc[j] = pw;
@@ -462,17 +470,18 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     Chunk k;
     for (bool have = chunk_first(E, S.mask, masks, nz, k); have; have = chunk_next(E, S.mask, masks, nz, k)) {
       __syncthreads();  // the previous chunk's product is done with the key buffer and the dense tile
-      // the values land while the weights are scattered and converted
-      if (tma) {
-        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.v, maps.have, kbar, P.G > 0);
-      } else {
-        issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, vg, P.v_ld);
-      }
       zero_tiles<kQ>(S.sbuf, L.sld, k.m);
       const int zb = E.zlo + k.zr * E.pg, ya = chunk_ya(E, k), xa = chunk_xa(E, k);
       const int hb = (masks ? k.iy * E.nx + k.ix : 0) * 32 + k.zr * E.pg;
       const int hlo = S.bstart[hb], hhi = S.bstart[hb + E.pg + 1];
       __syncthreads();
+      // the values land while the weights are scattered and converted (issued here, not in the short
+      // zeroing phase above: the issuing warps have the fewest hits below)
+      if (tma) {
+        if (!*S.dead) issue_keys_tma(P, T, E, k, S.kbuf, L.rs, maps.v, maps.have, kbar, P.G > 0);
+      } else {
+        issue_keys<DCH>(P, T, E, k, S.kbuf, L.rs, vg, P.v_ld);
+      }
       for (int i = hlo + static_cast<int>(threadIdx.x); i < hhi; i += kThreads) {
         const int idx = S.hits[i];
         const int q = static_cast<int>((static_cast<float>(idx) + 0.5f) * invK);
@@ -611,9 +620,10 @@ bool tc_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
         static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4)
       return false;
   }
-  // the setup stages 32 queries x K x 3 offsets in the key buffer + the dense tile
+  // the setup stages 32 queries x K x 3 offsets (rows padded to 16 bytes) and the head's K x 3 offset
+  // bias in the key buffer + the dense tile
   if (static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4 <
-      static_cast<size_t>(tc::t32::kQ) * ((3 * P.K + 6) & ~3) * 4)
+      (static_cast<size_t>(tc::t32::kQ) * ((3 * P.K + 6) & ~3) + 3 * P.K) * 4)
     return false;
   L.smem = static_cast<size_t>(mk) * L.rs * 2 + static_cast<size_t>(tc::t32::kQ) * L.sld * 4 + fixed;
   L.tiles = static_cast<long long>(P.B) * P.q_frames * L.tiles_h * L.tiles_w * P.nh;

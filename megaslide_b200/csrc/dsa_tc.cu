@@ -644,7 +644,8 @@ namespace tc {
 
 // One tensor map over head-sliced [B, Nkv, ld] bf16 rows: dims (channel, x, y, frame, sample), box
 // (rs channels, bw columns, 1, 1, 1), zero fill outside.
-static bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base, long long ld, int rs, int bw) {
+static bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base, long long ld, int rs, int bw,
+                         int bh) {
   using Encode = PFN_cuTensorMapEncodeTiled_v12000;
   static const Encode encode = []() -> Encode {
     void* fn = nullptr;
@@ -657,13 +658,14 @@ static bool make_key_map(CUtensorMap* map, const AttnParams& P, const void* base
   if (!encode || !base) return false;
   // 16-byte aligned base and row stride; the box within the tensor's extents
   if ((reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 2) & 15) || (rs * 2) % 16 != 0 || rs > 256) return false;
-  if (static_cast<long long>(P.nh) * P.d < rs || P.W < bw || ld < static_cast<long long>(P.nh) * P.d) return false;
+  if (static_cast<long long>(P.nh) * P.d < rs || P.W < bw || P.H < bh || ld < static_cast<long long>(P.nh) * P.d)
+    return false;
   const cuuint64_t dims[5] = {static_cast<cuuint64_t>(P.nh) * P.d, static_cast<cuuint64_t>(P.W),
                               static_cast<cuuint64_t>(P.H), static_cast<cuuint64_t>(P.kv_frames),
                               static_cast<cuuint64_t>(P.B)};
   const cuuint64_t row = static_cast<cuuint64_t>(ld) * 2;
   const cuuint64_t strides[4] = {row, row * P.W, row * P.W * P.H, row * static_cast<cuuint64_t>(P.Nkv)};
-  const cuuint32_t box[5] = {static_cast<cuuint32_t>(rs), static_cast<cuuint32_t>(bw), 1, 1, 1};
+  const cuuint32_t box[5] = {static_cast<cuuint32_t>(rs), static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh), 1, 1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   if (strides[3] >= (1ull << 40)) return false;
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
@@ -677,10 +679,11 @@ bool make_key_maps(KeyMaps* maps, const AttnParams& P, int rs) {
   const char* sel = getenv("MSL_TC_LOADS");
   if (sel && strcmp(sel, "cpasync") == 0) return false;
   for (int j = 0; j < 4; ++j)
-    if (make_key_map(&maps->k[j], P, P.k, P.k_ld, rs, 8 * (j + 1)) &&
-        make_key_map(&maps->v[j], P, P.v, P.v_ld, rs, 8 * (j + 1)))
-      maps->have |= 1 << j;
-  return maps->have & 1;  // the 8-column boxes serve every chunk width
+    for (int h = 0; h < 4; ++h)
+      if (make_key_map(&maps->k[j][h], P, P.k, P.k_ld, rs, 8 * (j + 1), 1 << h) &&
+          make_key_map(&maps->v[j][h], P, P.v, P.v_ld, rs, 8 * (j + 1), 1 << h))
+        maps->have |= 1 << (4 * j + h);
+  return maps->have & 1;  // the one-row 8-column boxes serve every chunk width
 }
 
 }  // namespace tc

@@ -586,10 +586,10 @@ __device__ __forceinline__ void issue_keys(const AttnParams& P, const TileCtx& T
   }
 }
 
-// Tensor maps of one launch: K and V, box widths 8, 16, 24 and 32 keys (index kst / 8 - 1); bit j of
-// `have` set when map j of both exists.
+// Tensor maps of one launch: K and V, box widths 8, 16, 24 and 32 keys (index j = kst / 8 - 1) and
+// heights 1, 2, 4 and 8 key rows (index h); bit 4 j + h of `have` set when map [j][h] of both exists.
 struct alignas(64) KeyMaps {
-  CUtensorMap k[4], v[4];
+  CUtensorMap k[4][4], v[4][4];
   int have;
 };
 
@@ -598,15 +598,17 @@ struct alignas(64) KeyMaps {
 bool make_key_maps(KeyMaps* maps, const AttnParams& P, int rs);
 
 // TMA path: the last four warps copy, for each chunk plane pl, rows [ya, yb] x columns [xa, xa + kst) into kbuf
-// rows pl * kpp + (y - ya) * kst + x - xa: one box per chunk row (box width kst) when the launch has that
-// map, else one 8-key box per row segment.  Boxes whose keys are all in untouched tiles are skipped;
-// coordinates outside the volume / K-V window read as zeros, and the half tile past a plane's last key,
-// when the plane ends inside a touched tile, is filled by one more 8-key box placed wholly outside the
-// volume (zeros).  The copies complete on mbarrier `bar`.  In TMA mode the key buffer is written only
-// by TMA, and its earlier generic reads are ordered by the CTA barrier before the call; `first` adds
-// the proxy fence for the setup's generic use of the buffer.  (boxes <= maxkeys / 8 <= 64: two per lane)
+// rows pl * kpp + (y - ya) * kst + x - xa.  With the maps of the chunk width a plane's nr rows take
+// nr / 8 boxes of 8 rows and one box per set bit of nr % 8 (4, 2, 1 rows; heights never exceed nr <= H,
+// so their maps exist); without a map of that width, one 8-key box per row segment.  Boxes whose keys
+// are all in untouched tiles are skipped; coordinates outside the volume / K-V window read as zeros,
+// and the half tile past a plane's last key, when the plane ends inside a touched tile, is filled by
+// one more 8-key box placed wholly outside the volume (zeros).  The copies complete on mbarrier `bar`.
+// In TMA mode the key buffer is written only by TMA, and its earlier generic reads are ordered by the
+// CTA barrier before the call; `first` adds the proxy fence for the setup's generic use of the buffer.
+// (boxes <= maxkeys / 8 <= 64: two per lane)
 __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCtx& T, const Env& E, const Chunk& k,
-                                               __nv_bfloat16* kbuf, int rs, const CUtensorMap* maps, int have,
+                                               __nv_bfloat16* kbuf, int rs, const CUtensorMap (*maps)[4], int have,
                                                uint32_t bar, bool first) {
   // box b is issued by warp kW0 + b % 4: a warp's copies issue one lane after another, so four warps
   // shorten the issue (measured: 4 ~ 8 warps > 16 > 1); the last four warps, which have the least
@@ -614,22 +616,51 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
   constexpr int kIW = 4, kW0 = kWarps - kIW;
   if (threadIdx.x < 32 * kW0) return;
   const int lane = threadIdx.x & 31, wid = (threadIdx.x >> 5) - kW0;
-  const int nkeys = (chunk_yb(E, k) - chunk_ya(E, k) + 1) * E.kst;  // keys of one plane
+  const int nr = chunk_yb(E, k) - chunk_ya(E, k) + 1;  // rows of one plane
+  const int nkeys = nr * E.kst;                         // keys of one plane
   const int mi = (E.kst >> 3) - 1;
-  const bool wide = mi < 4 && ((have >> mi) & 1);
-  const int bw = wide ? E.kst : 8;  // keys per box
-  const int nbp = nkeys / bw;       // boxes per plane
+  const int hm = mi < 4 ? (have >> (4 * mi)) & 15 : 0;  // heights available at this width
+  const int need = (nr >= 8 ? 8 : 0) | (nr & 7);        // heights the row decomposition uses
+  const bool wide = hm & 1;
+  const bool multi = wide && (need & ~hm) == 0;
+  const int nbp = multi ? (nr >> 3) + __popc(nr & 7) : (wide ? nr : nkeys >> 3);  // boxes per plane
   const int np = E.pg == 2 && E.zlo + k.zr * 2 + 1 <= E.zhi ? 2 : 1;
-  // boxes b = lane and lane + 32 (plane b / nbp); a box is issued when any of its keys lies in a touched tile
+  // boxes b = lane and lane + 32 (plane b / nbp): first row, rows, first column, keys per row, map
   bool on[2];
+  int brow[2], bh[2], bcol[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const int b = lane + 32 * u;
     on[u] = false;
+    brow[u] = 0, bh[u] = 1, bcol[u] = 0;
     if (b < np * nbp) {
-      const int pl = b >= nbp ? 1 : 0;
-      const int key0 = pl * E.kpp + (b - pl * nbp) * bw;
-      const int t0 = key0 >> 4, t1 = (key0 + bw - 1) >> 4;
+      const int pl = b >= nbp ? 1 : 0, lb = b - pl * nbp;
+      if (multi) {
+        if (lb < (nr >> 3)) {
+          brow[u] = 8 * lb;
+          bh[u] = 8;
+        } else {
+          int r0 = nr & ~7, kk = lb - (nr >> 3);
+          for (int bit = 4; bit >= 1; bit >>= 1) {
+            if (!(nr & bit)) continue;
+            if (kk == 0) {
+              bh[u] = bit;
+              break;
+            }
+            r0 += bit;
+            --kk;
+          }
+          brow[u] = r0;
+        }
+      } else if (wide) {
+        brow[u] = lb;
+      } else {
+        brow[u] = lb / (E.kst >> 3);
+        bcol[u] = (lb - brow[u] * (E.kst >> 3)) * 8;
+      }
+      const int key0 = pl * E.kpp + brow[u] * E.kst + bcol[u];
+      const int key1 = key0 + (wide ? bh[u] * E.kst : 8) - 1;
+      const int t0 = key0 >> 4, t1 = key1 >> 4;
       on[u] = ((k.m >> t0) & ((2u << (t1 - t0)) - 1u)) != 0u;
     }
   }
@@ -640,10 +671,11 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
     const int kt = pl * E.kpp + nkeys;
     tail[pl] = pl < np && (nkeys & 15) && ((k.m >> (kt >> 4)) & 1u);
   }
-  const int cnt = __popc(__ballot_sync(0xffffffffu, on[0])) + __popc(__ballot_sync(0xffffffffu, on[1]));
+  const int bw = wide ? E.kst : 8;  // keys per box row
+  const int rows_on = __reduce_add_sync(0xffffffffu, (on[0] ? bh[0] : 0) + (on[1] ? bh[1] : 0));
   if (threadIdx.x == 32 * kW0) {
     if (first) fence_proxy_async();
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>((cnt * bw + ((tail[0] ? 8 : 0) + (tail[1] ? 8 : 0))) * rs * 2));
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>((rows_on * bw + ((tail[0] ? 8 : 0) + (tail[1] ? 8 : 0))) * rs * 2));
   }
   __syncwarp();
   if (first && (on[0] || on[1])) fence_proxy_async();
@@ -651,15 +683,15 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
   for (int u = 0; u < 2; ++u) {
     if (!on[u] || (lane + 32 * u) % kIW != wid) continue;
     const int b = lane + 32 * u;
-    const int pl = b >= nbp ? 1 : 0, lb = b - pl * nbp;
-    const int row = wide ? lb : lb / (E.kst >> 3);
-    const int col = wide ? 0 : (lb - row * (E.kst >> 3)) * 8;
-    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((pl * E.kpp + lb * bw) * rs * 2), wide ? maps + mi : maps, bar,
-                T.head * P.d, chunk_xa(E, k) + col, chunk_ya(E, k) + row, E.zlo + k.zr * E.pg + pl - P.kv_frame0, T.b);
+    const int pl = b >= nbp ? 1 : 0;
+    const int hi = bh[u] == 8 ? 3 : (bh[u] == 4 ? 2 : (bh[u] == 2 ? 1 : 0));
+    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((pl * E.kpp + brow[u] * E.kst + bcol[u]) * rs * 2),
+                wide ? &maps[mi][hi] : &maps[0][0], bar, T.head * P.d, chunk_xa(E, k) + bcol[u],
+                chunk_ya(E, k) + brow[u], E.zlo + k.zr * E.pg + pl - P.kv_frame0, T.b);
   }
   if (wid == 0 && lane < 2 && tail[lane])  // columns W .. W+7: all outside the volume
-    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((lane * E.kpp + nkeys) * rs * 2), maps, bar, T.head * P.d, P.W,
-                0, 0, T.b);
+    tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((lane * E.kpp + nkeys) * rs * 2), &maps[0][0], bar,
+                T.head * P.d, P.W, 0, 0, T.b);
 }
 
 // Waits for the TMA copies of phase `parity` on mbarrier bar.  Bounded: after about a second the CTA

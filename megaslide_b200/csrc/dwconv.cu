@@ -302,9 +302,54 @@ __global__ void __launch_bounds__(256) convert_f32_kernel(const float* __restric
   }
 }
 
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// 8 elements per thread (two 16-byte loads, one 16-byte bf16 or two float32 stores); n = rows * cols / 8
+// vectors, below 2^31
+template <typename T>
+__global__ void __launch_bounds__(256) convert_f32_vec8_kernel(const float* __restrict__ src, long long src_ld,
+                                                               T* __restrict__ dst, long long dst_ld, unsigned cv,
+                                                               unsigned n) {
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned r = i / cv, c = (i - r * cv) * 8u;
+    const float4* s4 = reinterpret_cast<const float4*>(src + static_cast<long long>(r) * src_ld + c);
+    const float4 a = __ldg(s4), b = __ldg(s4 + 1);
+    T* d = dst + static_cast<long long>(r) * dst_ld + c;
+    if constexpr (sizeof(T) == 2) {
+      uint4 o;
+      o.x = bf16x2_bits(a.x, a.y);
+      o.y = bf16x2_bits(a.z, a.w);
+      o.z = bf16x2_bits(b.x, b.y);
+      o.w = bf16x2_bits(b.z, b.w);
+      *reinterpret_cast<uint4*>(d) = o;
+    } else {
+      reinterpret_cast<float4*>(d)[0] = a;
+      reinterpret_cast<float4*>(d)[1] = b;
+    }
+  }
+}
+
 cudaError_t launch_convert_f32(const float* src, long long src_ld, void* dst, long long dst_ld, int dtype,
                                long long rows, long long cols, cudaStream_t s) {
   const long long n = rows * cols;
+  const long long es = dtype == MSL_DTYPE_BF16 ? 2 : 4;
+  if (cols % 8 == 0 && n / 8 < (1LL << 31) && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 && src_ld % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(dst) & 15u) == 0 && (dst_ld * es) % 16 == 0) {
+    const unsigned nv = static_cast<unsigned>(n / 8), cv = static_cast<unsigned>(cols / 8);
+    long long vblocks = (nv + 255) / 256;
+    if (vblocks > 148LL * 16) vblocks = 148LL * 16;
+    if (vblocks < 1) vblocks = 1;
+    if (dtype == MSL_DTYPE_BF16)
+      convert_f32_vec8_kernel<__nv_bfloat16><<<static_cast<unsigned>(vblocks), 256, 0, s>>>(
+          src, src_ld, static_cast<__nv_bfloat16*>(dst), dst_ld, cv, nv);
+    else
+      convert_f32_vec8_kernel<float><<<static_cast<unsigned>(vblocks), 256, 0, s>>>(src, src_ld, static_cast<float*>(dst),
+                                                                                  dst_ld, cv, nv);
+    return cudaGetLastError();
+  }
   long long blocks = (n + 255) / 256;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
   if (blocks < 1) blocks = 1;

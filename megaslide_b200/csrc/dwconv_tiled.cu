@@ -172,6 +172,16 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
         for (int j = 0; j < kSeg; ++j)
           if (ws + j < P.W) load_cv<TY, CV>(y + (orow0 + j) * y_ld + c, acc[j]);
       }
+      // GELU_GRAD (the non-transposed instantiations only: registers): the aux rows, loaded together before
+      // the taps
+      float avs[FLIP ? 1 : kSeg][CV];
+      if constexpr (!FLIP) {
+        if (epi == MSL_EPI_GELU_GRAD) {
+#pragma unroll
+          for (int j = 0; j < kSeg; ++j)
+            if (ws + j < P.W) load_cv<TY, CV>(aux + (orow0 + j) * aux_ld + c, avs[j]);
+        }
+      }
       for (int it = 0; it < P.kt; ++it) {
         const int ti = t + it - pt;
         if (ti < P.in_frame0 || ti >= P.in_frame0 + P.in_frames) continue;  // zero outside the input frames
@@ -209,7 +219,14 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
         if (ws + j >= P.W) break;
         const long long orow = orow0 + j;
         float av[CV];
-        if (epi == MSL_EPI_GELU_GRAD) load_cv<TY, CV>(aux + orow * aux_ld + c, av);
+        if (epi == MSL_EPI_GELU_GRAD) {
+          if constexpr (FLIP) {
+            load_cv<TY, CV>(aux + orow * aux_ld + c, av);
+          } else {
+#pragma unroll
+            for (int e = 0; e < CV; ++e) av[e] = avs[j][e];
+          }
+        }
         float out[CV];
 #pragma unroll
         for (int e = 0; e < CV; ++e) {

@@ -678,3 +678,20 @@ def test_offsets_absmax_with_bias():
         want = np.abs(full.astype(np.float32) * np.float32(0.5)).reshape(-1, heads * taps, 3).max(axis=(0, 1))
         got = ops.offsets_absmax(offt, heads, taps, 0.5, bias=None if b is None else torch.from_numpy(b).to(DEV))
         assert np.array_equal(got.cpu().numpy(), want.astype(np.float32))
+
+
+@pytest.mark.parametrize("rows,cols,src_pad,dst_pad", [(1000, 1152, 0, 2304), (37, 72, 8, 0), (5, 13, 3, 1),
+                                                       (3, 64, 4, 0)])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_convert_f32_matches_torch(rows, cols, src_pad, dst_pad, dt):
+    """float32 -> dtype conversion of strided row views: the 8-wide path (aligned rows, cols % 8 == 0) and
+    the scalar one give torch's round-to-nearest-even conversion bit for bit."""
+    g = torch.Generator(device=DEV)
+    g.manual_seed(rows * 131 + cols)
+    src = torch.randn(rows, cols + src_pad, device=DEV, generator=g)[:, :cols]
+    dst_full = torch.zeros(rows, cols + dst_pad, device=DEV, dtype=dt)
+    dst = dst_full[:, dst_pad:] if dst_pad else dst_full
+    ops.convert_f32(src, dst)
+    assert torch.equal(dst, src.to(dt))
+    if dst_pad:
+        assert not dst_full[:, :dst_pad].any()

@@ -5,12 +5,13 @@
 A "step" is one forward + backward of the module over one batch of synthetic tokens (loss =
 sum(y * G) with a fixed G).  The default workload is BASELINE config 2: B=2, T=64, H=W=32
 (131,072 tokens), C=1152, 16 heads x 72, window (3,7,7), bf16 activations with float32
-accumulation, offset-conv weights ~N(0, 0.05).  Under torchrun each rank runs that workload on its
-own GPU (weak scaling); the time is the max over ranks.
+accumulation, offset-conv weights ~N(0, 0.05).  Under torchrun the same volume is split along time
+into one frame shard per rank (TimeShardedDSA3D: K/V halo exchange over NCCL; strong scaling); the
+time is the max over ranks.
 
 Prints one JSON line (rank 0): value = Mtokens/s with inputs resident in HBM; e2e = the same
 through the module's public API with the input copied from pinned host memory and the loss read
-back every step; roofline of the dominant kernel timed live with CUDA events; clocks sampled by
+back every step (the next step's copy runs on a side stream, double-buffered, while a step computes); roofline of the dominant kernel timed live with CUDA events; clocks sampled by
 nvidia-smi during the timed region; cpu_baseline = the CPU oracle (oracle/) on a bounded sample.
 
 ``--impl reference`` times the reference algorithm's CPU implementation instead (the oracle port,
@@ -350,22 +351,41 @@ def run_gpu(args):
 
     e2e = None
     if not args.no_e2e:
+        # End to end through the module: every step copies its input from pinned host memory and reads its
+        # loss back.  As in a training input pipeline, step i+1's input is copied on a side stream into the
+        # other of two device buffers while step i computes (the copy waits until the step before has
+        # finished with that buffer); every step's copy and read-back lie inside the timed region.
         xh = x.detach().cpu().pin_memory()
-        xd = torch.empty_like(x)
+        xd = [torch.empty_like(x), torch.empty_like(x)]
+        copy_stream = torch.cuda.Stream()
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        freed = [torch.cuda.Event(), torch.cuda.Event()]
         loss_h = torch.empty(1, dtype=torch.float32).pin_memory()
 
-        def e2e_step():
-            xd.copy_(xh, non_blocking=True)
-            y = step(xd)
-            loss = (y.float() * G.float()).sum()
-            loss_h.copy_(loss.view(1), non_blocking=True)
+        def issue_copy(i):
+            b = i % 2
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(freed[b])
+                xd[b].copy_(xh, non_blocking=True)
+                copied[b].record(copy_stream)
 
-        for _ in range(max(1, args.warmup)):
-            e2e_step()
+        def e2e_run(n):
+            copy_stream.wait_stream(stream)  # the first copy starts inside the caller's timed region
+            issue_copy(0)
+            for i in range(n):
+                b = i % 2
+                stream.wait_event(copied[b])
+                if i + 1 < n:
+                    issue_copy(i + 1)
+                y = step(xd[b])
+                freed[b].record(stream)
+                loss = (y * G).sum(dtype=torch.float32)
+                loss_h.copy_(loss.view(1), non_blocking=True)
+
+        e2e_run(max(1, args.warmup))
         barrier()
         e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
+        e2e_run(args.steps)
         e1.record(stream)
         barrier()
         ms2 = e0.elapsed_time(e1)
@@ -375,7 +395,8 @@ def run_gpu(args):
             ms2 = float(t.item())
         e2e = {"value": tokens * args.steps / (ms2 / 1e3) / 1e6, "unit": "Mtokens/s",
                "h2d_bytes_per_step": xh.numel() * xh.element_size(), "d2h_bytes_per_step": 4,
-               "ms_per_step": ms2 / args.steps}
+               "ms_per_step": ms2 / args.steps,
+               "h2d": "pinned host -> device on a copy stream, double-buffered: step i+1's input copies while step i runs"}
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:

@@ -7,8 +7,9 @@
 // outside the input window read as zero) with cp.async:
 // while output frame t is computed from slices t - kt/2 .. t + kt/2, slice t + kt/2 + 1 is loaded, so
 // every input frame is fetched once per chunk and the fetch overlaps the arithmetic.  A warp owns one
-// tile row and 16 consecutive columns; each lane one channel word; the kw taps of a kernel row slide
-// over 16 + kw - 1 register-resident inputs (16 * kw * channels FMAs per 16 + kw - 1 shared loads).
+// tile row and SEG consecutive columns (16, or 8 when the ring fits only 4 tile rows); each lane one
+// channel word; the kw taps of a kernel row slide over SEG + kw - 1 register-resident inputs
+// (SEG * kw * channels FMAs per SEG + kw - 1 shared loads).
 //
 // Replaces nn.Conv3d(C, C, k, padding=k//2, groups=C) of dw_conv (infinity/video/attention.py:58-65,
 // 102) and offset_net[0] (attention.py:70-72, 105), forward and autograd backward.
@@ -34,6 +35,26 @@ struct Plan {
   size_t smem;
   long long ctas;
 };
+
+// a0 += w0 * x0, a1 += w1 * x1 as one packed two-lane float32 FMA (sm_100 fma.rn.f32x2): each lane
+// rounds exactly like fmaf, and the pair costs one issue slot instead of two.
+__device__ __forceinline__ void fma_x2(float& a0, float& a1, float w0, float w1, float x0, float x1) {
+  asm("{\n\t.reg .b64 a, w, x;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 w, {%2, %3};\n\tmov.b64 x, {%4, %5};\n\t"
+      "fma.rn.f32x2 a, w, x, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(w0), "f"(w1), "f"(x0), "f"(x1));
+}
+
+// acc[e] += w[e] * x[e] over CV channels (packed pairs when CV == 2)
+template <int CV>
+__device__ __forceinline__ void fma_cv(float (&acc)[CV], const float (&w)[CV], const float (&x)[CV]) {
+  if constexpr (CV == 2) {
+    fma_x2(acc[0], acc[1], w[0], w[1], x[0], x[1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < CV; ++e) acc[e] = fmaf(w[e], x[e], acc[e]);
+  }
+}
 
 __device__ __forceinline__ float gelu_erf(float u) { return 0.5f * u * (1.f + erff(u * 0.70710678118654752f)); }
 
@@ -122,7 +143,10 @@ __device__ __forceinline__ CtaPos decode(const ConvParams& P, const Plan& L) {
 }
 
 // y[p] = epi(sum_taps w[tap] x[p + tap - pad] + bias) (FLIP: w[K-1-tap], the input gradient).
-template <typename T, typename TY, int KW, bool FLIP>
+// A warp owns SEG consecutive columns of one tile row: SEG = 16 when the tile has 8 rows (16 warps),
+// 8 when the ring only fits 4 rows (kernel height 7), so the CTA still has 16 warps to hide the
+// shared-memory and weight load latencies.
+template <typename T, typename TY, int KW, bool FLIP, int SEG>
 __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvParams P, const Plan L, const T* __restrict__ x,
                                                                long long x_ld, const float* __restrict__ wt,
                                                                const float* __restrict__ bias,
@@ -130,7 +154,8 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
                                                                const TY* __restrict__ aux, long long aux_ld,
                                                                TY* __restrict__ y, long long y_ld) {
   constexpr int CV = Word<T>::CV;
-  constexpr int NIN = kSeg + KW - 1;
+  constexpr int NIN = SEG + KW - 1;
+  constexpr int NSEG = kTW / SEG;
   extern __shared__ __align__(16) uint32_t ring[];
   const CtaPos cp = decode(P, L);
   const int pt = P.kt / 2;
@@ -145,8 +170,8 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
   __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = warp >> 1, seg = warp & 1;
-  const int h = cp.h0 + r, ws = cp.w0 + seg * kSeg;
+  const int r = warp / NSEG, seg = warp % NSEG;
+  const int h = cp.h0 + r, ws = cp.w0 + seg * SEG;
   const bool active = h < P.H && ws < P.W;
   const int c = c0 + lane * CV;
   float bsum[CV], b2v[CV];
@@ -162,23 +187,23 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
     if (active) {
       const long long orow0 = (static_cast<long long>(cp.b) * P.out_frames + (t - P.out_frame0)) * P.HW +
                               static_cast<long long>(h) * P.W + ws;
-      float acc[kSeg][CV];
+      float acc[SEG][CV];
 #pragma unroll
-      for (int j = 0; j < kSeg; ++j)
+      for (int j = 0; j < SEG; ++j)
 #pragma unroll
         for (int e = 0; e < CV; ++e) acc[j][e] = 0.f;
       if (epi == MSL_EPI_ACCUM) {  // start from the buffer's own terms (loads issued together, before the taps)
 #pragma unroll
-        for (int j = 0; j < kSeg; ++j)
+        for (int j = 0; j < SEG; ++j)
           if (ws + j < P.W) load_cv<TY, CV>(y + (orow0 + j) * y_ld + c, acc[j]);
       }
       // GELU_GRAD (the non-transposed instantiations only: registers): the aux rows, loaded together before
       // the taps
-      float avs[FLIP ? 1 : kSeg][CV];
+      float avs[FLIP ? 1 : SEG][CV];
       if constexpr (!FLIP) {
         if (epi == MSL_EPI_GELU_GRAD) {
 #pragma unroll
-          for (int j = 0; j < kSeg; ++j)
+          for (int j = 0; j < SEG; ++j)
             if (ws + j < P.W) load_cv<TY, CV>(aux + (orow0 + j) * aux_ld + c, avs[j]);
         }
       }
@@ -189,7 +214,7 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
         const uint32_t* sl = ring + ((ti - base) % nslots) * slice_words;
         for (int ih = 0; ih < P.kh; ++ih) {
           const int ihw = FLIP ? P.kh - 1 - ih : ih;
-          const uint32_t* rowp = sl + ((r + ih) * L.sc + seg * kSeg) * 32 + lane;
+          const uint32_t* rowp = sl + ((r + ih) * L.sc + seg * SEG) * 32 + lane;
           float xin[NIN][CV];
 #pragma unroll
           for (int j = 0; j < NIN; ++j) Word<T>::unpack(rowp[j * 32], xin[j]);
@@ -209,13 +234,11 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
 #pragma unroll
           for (int iw = 0; iw < KW; ++iw)
 #pragma unroll
-            for (int j = 0; j < kSeg; ++j)
-#pragma unroll
-              for (int e = 0; e < CV; ++e) acc[j][e] = fmaf(wv[iw][e], xin[j + iw][e], acc[j][e]);
+            for (int j = 0; j < SEG; ++j) fma_cv<CV>(acc[j], wv[iw], xin[j + iw]);
         }
       }
 #pragma unroll
-      for (int j = 0; j < kSeg; ++j) {
+      for (int j = 0; j < SEG; ++j) {
         if (ws + j >= P.W) break;
         const long long orow = orow0 + j;
         float av[CV];
@@ -345,9 +368,7 @@ __global__ void __launch_bounds__(256, 1) dwconv_wgrad_tiled_kernel(const ConvPa
 #pragma unroll
           for (int e = 0; e < CV; ++e) g[e] = to_f32<TDY>(dp[j * 32 * CV + e]);
 #pragma unroll
-          for (int iw = 0; iw < KW; ++iw)
-#pragma unroll
-            for (int e = 0; e < CV; ++e) acc[s][iw][e] = fmaf(g[e], xin[j + iw][e], acc[s][iw][e]);
+          for (int iw = 0; iw < KW; ++iw) fma_cv<CV>(acc[s][iw], g, xin[j + iw]);
         }
       }
     }
@@ -418,37 +439,46 @@ bool make_plan(const ConvParams& P, int cv, int dy_cv_bytes, int max_threads, Pl
   return L.ctas <= 0x7fffffffLL;
 }
 
-template <typename T, typename TY, int KW, bool FLIP>
+template <typename T, typename TY, int KW, bool FLIP, int SEG>
 cudaError_t fwd_launch(const ConvParams& P, const Plan& L, const void* x, long long x_ld, const float* wt,
                        const float* bias, const float* bias2, int epi, const void* aux, long long aux_ld, void* y,
                        long long y_ld, cudaStream_t s) {
-  auto k = dwconv_fwd_tiled_kernel<T, TY, KW, FLIP>;
+  auto k = dwconv_fwd_tiled_kernel<T, TY, KW, FLIP, SEG>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
-  k<<<static_cast<unsigned>(L.ctas), L.th * 64, L.smem, s>>>(P, L, static_cast<const T*>(x), x_ld, wt, bias, bias2, epi,
+  k<<<static_cast<unsigned>(L.ctas), L.th * (kTW / SEG) * 32, L.smem, s>>>(P, L, static_cast<const T*>(x), x_ld, wt, bias, bias2, epi,
                                                             static_cast<const TY*>(aux), aux_ld, static_cast<TY*>(y),
                                                             y_ld);
   return cudaGetLastError();
 }
 
-template <typename T, typename TY, bool FLIP>
+template <typename T, typename TY, bool FLIP, int SEG>
 cudaError_t fwd_kw(const ConvParams& P, const Plan& L, const void* x, long long x_ld, const float* wt, const float* bias,
                    const float* bias2, int epi, const void* aux, long long aux_ld, void* y, long long y_ld,
                    cudaStream_t s) {
   switch (P.kw) {
-    case 1: return fwd_launch<T, TY, 1, FLIP>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
-    case 3: return fwd_launch<T, TY, 3, FLIP>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
-    case 5: return fwd_launch<T, TY, 5, FLIP>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
-    default: return fwd_launch<T, TY, 7, FLIP>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+    case 1: return fwd_launch<T, TY, 1, FLIP, SEG>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+    case 3: return fwd_launch<T, TY, 3, FLIP, SEG>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+    case 5: return fwd_launch<T, TY, 5, FLIP, SEG>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+    default: return fwd_launch<T, TY, 7, FLIP, SEG>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
   }
+}
+
+// 8-column segments when the plan has 4 tile rows (16 warps instead of 8), else 16-column ones
+template <typename T, typename TY, bool FLIP>
+cudaError_t fwd_seg(const ConvParams& P, const Plan& L, const void* x, long long x_ld, const float* wt,
+                    const float* bias, const float* bias2, int epi, const void* aux, long long aux_ld, void* y,
+                    long long y_ld, cudaStream_t s) {
+  if (L.th == 4) return fwd_kw<T, TY, FLIP, 8>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+  return fwd_kw<T, TY, FLIP, kSeg>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
 }
 
 template <typename T, typename TY>
 cudaError_t fwd_flip(const ConvParams& P, const Plan& L, bool flip, const void* x, long long x_ld, const float* wt,
                      const float* bias, const float* bias2, int epi, const void* aux, long long aux_ld, void* y,
                      long long y_ld, cudaStream_t s) {
-  if (flip) return fwd_kw<T, TY, true>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
-  return fwd_kw<T, TY, false>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+  if (flip) return fwd_seg<T, TY, true>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
+  return fwd_seg<T, TY, false>(P, L, x, x_ld, wt, bias, bias2, epi, aux, aux_ld, y, y_ld, s);
 }
 
 template <typename T, typename TDY, int KW, int MAXI>

@@ -212,29 +212,40 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
         if (ti < P.in_frame0 || ti >= P.in_frame0 + P.in_frames) continue;  // zero outside the input frames
         const int itw = FLIP ? P.kt - 1 - it : it;
         const uint32_t* sl = ring + ((ti - base) % nslots) * slice_words;
-        for (int ih = 0; ih < P.kh; ++ih) {
+        // weights of kernel row ih (flipped for the input gradient)
+        auto load_w = [&](int ih, float (&dst)[KW][CV]) {
           const int ihw = FLIP ? P.kh - 1 - ih : ih;
-          const uint32_t* rowp = sl + ((r + ih) * L.sc + seg * SEG) * 32 + lane;
-          float xin[NIN][CV];
-#pragma unroll
-          for (int j = 0; j < NIN; ++j) Word<T>::unpack(rowp[j * 32], xin[j]);
           const float* wrow = wt + static_cast<long long>((itw * P.kh + ihw) * KW) * P.C + c;
-          float wv[KW][CV];
 #pragma unroll
           for (int iw = 0; iw < KW; ++iw) {
             const float* wp = wrow + static_cast<long long>(FLIP ? KW - 1 - iw : iw) * P.C;
             if constexpr (CV == 2) {
               const float2 v = __ldg(reinterpret_cast<const float2*>(wp));
-              wv[iw][0] = v.x;
-              wv[iw][CV - 1] = v.y;
+              dst[iw][0] = v.x;
+              dst[iw][CV - 1] = v.y;
             } else {
-              wv[iw][0] = __ldg(wp);
+              dst[iw][0] = __ldg(wp);
             }
           }
+        };
+        float wv[KW][CV];
+        load_w(0, wv);
+        for (int ih = 0; ih < P.kh; ++ih) {
+          const uint32_t* rowp = sl + ((r + ih) * L.sc + seg * SEG) * 32 + lane;
+          float xin[NIN][CV];
+#pragma unroll
+          for (int j = 0; j < NIN; ++j) Word<T>::unpack(rowp[j * 32], xin[j]);
+          // the next row's weights load while this row's FMAs run (the last row reloads itself)
+          float wn[KW][CV];
+          load_w(min(ih + 1, P.kh - 1), wn);
 #pragma unroll
           for (int iw = 0; iw < KW; ++iw)
 #pragma unroll
             for (int j = 0; j < SEG; ++j) fma_cv<CV>(acc[j], wv[iw], xin[j + iw]);
+#pragma unroll
+          for (int iw = 0; iw < KW; ++iw)
+#pragma unroll
+            for (int e = 0; e < CV; ++e) wv[iw][e] = wn[iw][e];
         }
       }
 #pragma unroll
@@ -267,6 +278,23 @@ __global__ void __launch_bounds__(512, 1) dwconv_fwd_tiled_kernel(const ConvPara
     }
     tc::cp_async_wait_all();
     __syncthreads();
+  }
+}
+
+// CV consecutive dy values of one lane from shared memory (one 4- or 8-byte load for a channel pair)
+template <typename TDY, int CV>
+__device__ __forceinline__ void load_dy(const TDY* p, float (&g)[CV]) {
+  if constexpr (CV == 2 && sizeof(TDY) == 2) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
+    g[0] = bf16_lo(w);
+    g[1] = bf16_hi(w);
+  } else if constexpr (CV == 2 && sizeof(TDY) == 4) {
+    const float2 v = *reinterpret_cast<const float2*>(p);
+    g[0] = v.x;
+    g[1] = v.y;
+  } else {
+#pragma unroll
+    for (int e = 0; e < CV; ++e) g[e] = to_f32<TDY>(p[e]);
   }
 }
 
@@ -365,8 +393,7 @@ __global__ void __launch_bounds__(256, 1) dwconv_wgrad_tiled_kernel(const ConvPa
 #pragma unroll
         for (int j = 0; j < kSeg; ++j) {
           float g[CV];
-#pragma unroll
-          for (int e = 0; e < CV; ++e) g[e] = to_f32<TDY>(dp[j * 32 * CV + e]);
+          load_dy<TDY, CV>(dp + j * 32 * CV, g);
 #pragma unroll
           for (int iw = 0; iw < KW; ++iw) fma_cv<CV>(acc[s][iw], g, xin[j + iw]);
         }

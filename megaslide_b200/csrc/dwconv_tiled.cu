@@ -25,6 +25,9 @@ namespace dwt {
 
 constexpr int kTW = 32;   // tile columns
 constexpr int kSeg = 16;  // consecutive outputs per thread along w
+// weight gradient: 16 warps per CTA whatever the tile height, so the (kernel row, segment) items of a
+// CTA spread over enough warps to hide the shared-memory latencies (at most 4 tile rows fit the ring)
+constexpr int kWgradThreads = 512;
 
 struct Plan {
   int th;        // tile rows (2 warps per row)
@@ -303,7 +306,7 @@ __device__ __forceinline__ void load_dy(const TDY* p, float (&g)[CV]) {
 // for the whole CTA, accumulates them in registers over the chunk's frames and tile rows, and adds
 // them to dw / db with one atomic per channel and tap at the end.
 template <typename T, typename TDY, int KW, int MAXI>
-__global__ void __launch_bounds__(256, 1) dwconv_wgrad_tiled_kernel(const ConvParams P, const Plan L,
+__global__ void __launch_bounds__(kWgradThreads, 1) dwconv_wgrad_tiled_kernel(const ConvParams P, const Plan L,
                                                                  const TDY* __restrict__ dy, long long dy_ld,
                                                                  const T* __restrict__ x, long long x_ld,
                                                                  float* __restrict__ dw, float* __restrict__ db) {
@@ -514,7 +517,7 @@ cudaError_t wgrad_launch(const ConvParams& P, const Plan& L, const void* dy, lon
   auto k = dwconv_wgrad_tiled_kernel<T, TDY, KW, MAXI>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
-  k<<<static_cast<unsigned>(L.ctas), L.th * 64, L.smem, s>>>(P, L, static_cast<const TDY*>(dy), dy_ld,
+  k<<<static_cast<unsigned>(L.ctas), kWgradThreads, L.smem, s>>>(P, L, static_cast<const TDY*>(dy), dy_ld,
                                                             static_cast<const T*>(x), x_ld, dw, db);
   return cudaGetLastError();
 }
@@ -568,7 +571,7 @@ cudaError_t launch_dwconv_wgrad_tiled(const ConvParams& P, const void* dy, long 
   if (!dwt::aligned(dy, 16) || (dy_ld * ys) % 16 != 0) return cudaErrorNotSupported;
   dwt::Plan L{};
   if (!dwt::make_plan(P, cv, static_cast<int>(cv * ys), 256, L)) return cudaErrorNotSupported;
-  const int nwarps = L.th * 2;
+  const int nwarps = dwt::kWgradThreads / 32;
   const int nitems = (P.kt * P.kh + (db ? 1 : 0)) * 2;
   const int maxi = (nitems + nwarps - 1) / nwarps;
   if (maxi > 6) return cudaErrorNotSupported;

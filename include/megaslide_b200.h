@@ -178,7 +178,8 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
  * Its float32 scratch lives in one static device array of MSL_NOALLOC_SCRATCH_BYTES per GPU; a
  * problem needing more (msl_dsa_attn_bwd_workspace_bytes) is rejected with MSL_ERR_WORKSPACE.
  * The first call on a device looks the array's address up (call it once before any stream
- * capture).  Every call shares the array and clears what it accumulates into, so two calls whose
+ * capture); the address is kept for the life of the process, so the entry point must not be used
+ * after cudaDeviceReset on that device (a new context places the array elsewhere).  Every call shares the array and clears what it accumulates into, so two calls whose
  * work overlaps on the GPU (different streams, or different threads) race and must be ordered by
  * the caller.  Arguments and results are those of msl_dsa_attn_bwd. */
 int msl_dsa_attn_bwd_noalloc(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, void* stream);

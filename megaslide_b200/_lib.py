@@ -130,10 +130,18 @@ def load() -> ctypes.CDLL:
         return _lib
     with _lock:
         if _lib is None:
-            if not _LIB_PATH.exists():
-                raise RuntimeError(
-                    f"megaslide_b200 CUDA library not found at {_LIB_PATH}; build it with "
-                    "`python -m megaslide_b200.build` (nvcc, sm_100a). There is no CPU fallback.")
+            from . import build as _build
+
+            if not _build.is_current():
+                # missing, or built from other sources: rebuild from the present ones (nvcc, sm_100a) so a
+                # stale binary never runs
+                try:
+                    _build.build()
+                except Exception as e:
+                    raise RuntimeError(
+                        f"megaslide_b200 CUDA library at {_LIB_PATH} is missing or out of date and could not be "
+                        f"built ({e}); build it with `python -m megaslide_b200.build` (nvcc, sm_100a). "
+                        "There is no CPU fallback.") from e
             lib = ctypes.CDLL(str(_LIB_PATH))
             for name, (res, args) in SIGNATURES.items():
                 fn = getattr(lib, name)

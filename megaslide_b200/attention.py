@@ -41,9 +41,9 @@ def _mm_f32(a: Tensor, b: Tensor) -> Tensor:
 
 
 class _Cfg:
-    __slots__ = ("shape", "conv_k", "conv_3", "dtype", "param_dtypes", "G", "kernel")
+    __slots__ = ("shape", "conv_k", "conv_3", "dtype", "param_dtypes", "G", "kernel", "capture")
 
-    def __init__(self, shape, conv_k, conv_3, dtype, param_dtypes, G, kernel):
+    def __init__(self, shape, conv_k, conv_3, dtype, param_dtypes, G, kernel, capture=None):
         self.shape = shape
         self.conv_k = conv_k
         self.conv_3 = conv_3
@@ -51,13 +51,14 @@ class _Cfg:
         self.param_dtypes = param_dtypes
         self.G = G
         self.kernel = kernel
+        self.capture = capture  # dict that receives the call's intermediates (parity checks), or None
 
 
 class DSA3DFunction(torch.autograd.Function):
     """Forward/backward of DeformableSlideAttention3D (attention.py:82-192) on the B200 kernels."""
 
     @staticmethod
-    def forward(ctx, cfg: _Cfg, x, extra_kv, wq, bq, wk, bk, wv, bv, wo, bo, wd, bd, w1, b1, w2, b2):
+    def forward(ctx, cfg: _Cfg, x, extra_kv, off_in, wq, bq, wk, bk, wv, bv, wo, bo, wd, bd, w1, b1, w2, b2):
         sh: ops.DsaShape = cfg.shape
         dt = cfg.dtype
         B, N, C = x.shape
@@ -67,14 +68,20 @@ class DSA3DFunction(torch.autograd.Function):
         bqkv = torch.cat([bq, bk, bv], 0).to(dt)
         qkv = torch.addmm(bqkv, x2, wqkv.t())  # [BN, 3C]
         q, k, v = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
-        # offset predictor: GELU(dw3^3(x) + b1) fused, then the 1x1 conv as a GEMM with fp32 output
-        w1_kc = ops.conv_weight_kc(w1)
-        b1f = b1.detach().float().contiguous()
-        hact = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
         O = w2.shape[0]
         w2m = w2.reshape(O, C)
-        off = _mm_f32(hact, w2m.to(dt).t())  # its bias b2 is added by the attention kernels as they read it
-        b2f = b2.detach().float().contiguous()
+        w1_kc = ops.conv_weight_kc(w1)
+        b1f = b1.detach().float().contiguous()
+        if off_in is None:
+            # offset predictor: GELU(dw3^3(x) + b1) fused, then the 1x1 conv as a GEMM with fp32 output
+            hact = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
+            off = _mm_f32(hact, w2m.to(dt).t())  # its bias b2 is added by the attention kernels as they read it
+            b2f = b2.detach().float().contiguous()
+        else:
+            # raw offsets given by the caller in place of the offset predictor's output (its bias included)
+            hact = None
+            off = off_in.reshape(B * N, O)
+            b2f = None
         # depthwise conv term with both biases (dw_conv and out_proj) fused
         wd_kc = ops.conv_weight_kc(wd)
         D = ops.dwconv_fwd(cfg.conv_k, x2, wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous(),
@@ -98,11 +105,14 @@ class DSA3DFunction(torch.autograd.Function):
         if probs is None:
             attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f)
         y = torch.addmm(D, attn, wo.to(dt).t())
+        if cfg.capture is not None:
+            cfg.capture.update(x2=x2, qkv=qkv, hact=hact, off=off, offset_bias=b2f, attn=attn, lse=lse, y=y)
         if train:
             ctx.save_for_backward(x2, qkv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
                                   saved)
             ctx.cfg = cfg
             ctx.in_dtype = x.dtype
+            ctx.off_dtype = off_in.dtype if off_in is not None else None
             ctx.extra_dtype = extra_kv.dtype if extra_kv is not None else None
         return y.view(B, N, C)
 
@@ -151,17 +161,23 @@ class DSA3DFunction(torch.autograd.Function):
                 sums = dekv.sum(0)
                 g_bk = g_bk + sums[:C]
                 g_bv = g_bv + sums[C:]
-            # offset predictor (the kernel wrote doff in the compute dtype, the GEMMs' operand type); dh
-            # and du stay float32 (bf16 operands, fp32 results)
-            dh = _mm_f32(doff, w2m.to(dt))
-            g_w2 = _mm_f32(doff.t(), hact)
-            g_b2 = doff.sum(0, dtype=torch.float32)
-            du = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh,
-                                out_dtype=torch.float32)
-            ops.dwconv_bwd_data(cfg.conv_3, du, w1_kc, out=dx, accumulate=True)
-            g_w1 = torch.zeros_like(w1_kc)
-            g_b1 = torch.zeros(C, device=dy2.device, dtype=torch.float32)
-            ops.dwconv_bwd_weight(cfg.conv_3, du, x2, g_w1, g_b1)
+            if cfg.capture is not None:
+                cfg.capture.update(dy2=dy2, dattn=dattn, dqkv=dqkv, doff=doff, dx=dx)
+            d_off_in = None
+            if hact is not None:
+                # offset predictor (the kernel wrote doff in the compute dtype, the GEMMs' operand type); dh
+                # and du stay float32 (bf16 operands, fp32 results)
+                dh = _mm_f32(doff, w2m.to(dt))
+                g_w2 = _mm_f32(doff.t(), hact)
+                g_b2 = doff.sum(0, dtype=torch.float32)
+                du = ops.dwconv_fwd(cfg.conv_3, x2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh,
+                                    out_dtype=torch.float32)
+                ops.dwconv_bwd_data(cfg.conv_3, du, w1_kc, out=dx, accumulate=True)
+                g_w1 = torch.zeros_like(w1_kc)
+                g_b1 = torch.zeros(C, device=dy2.device, dtype=torch.float32)
+                ops.dwconv_bwd_weight(cfg.conv_3, du, x2, g_w1, g_b1)
+            elif ctx.needs_input_grad[3]:
+                d_off_in = doff.view(B, BN // B, -1).to(ctx.off_dtype)
 
         pd = cfg.param_dtypes
         kt, kh, kw = cfg.kernel
@@ -172,12 +188,15 @@ class DSA3DFunction(torch.autograd.Function):
         grads = (
             g_wq.to(pd[0]), g_bq.to(pd[1]), g_wk.to(pd[2]), g_bk.to(pd[3]), g_wv.to(pd[4]), g_bv.to(pd[5]),
             g_wo.to(pd[6]), g_bo.to(pd[7]), conv_w(g_wd, (kt, kh, kw)).to(pd[8]), g_bd.to(pd[9]),
-            conv_w(g_w1, (3, 3, 3)).to(pd[10]), g_b1.to(pd[11]),
-            g_w2.reshape(w2m.shape[0], C, 1, 1, 1).to(pd[12]), g_b2.to(pd[13]),
         )
+        if hact is not None:
+            grads += (conv_w(g_w1, (3, 3, 3)).to(pd[10]), g_b1.to(pd[11]),
+                      g_w2.reshape(w2m.shape[0], C, 1, 1, 1).to(pd[12]), g_b2.to(pd[13]))
+        else:  # the offset predictor did not run: no gradient for its parameters
+            grads += (None, None, None, None)
         dx_out = dx.view(B, BN // B, C).to(ctx.in_dtype)
         de = d_extra.to(ctx.extra_dtype) if d_extra is not None else None
-        return (None, dx_out, de) + grads
+        return (None, dx_out, de, d_off_in) + grads
 
 
 class DeformableSlideAttention3D(nn.Module):
@@ -190,6 +209,10 @@ class DeformableSlideAttention3D(nn.Module):
             volume only for odd k — the reference's dw term fails to reshape otherwise).
         offset_scale: scale of the learned offsets.
         dropout: dropout on the softmax weights (counter-based in-kernel mask in training mode).
+
+    ``capture`` (not a parameter; None by default): a dict set here receives references to the
+    intermediates of the next forward / backward (q/k/v, offsets, attention output, lse and their
+    gradients), which a checker compares with an independent implementation at sampled rows.
     """
 
     def __init__(self, hidden_size: int, num_heads: int, kernel_size: Tuple[int, int, int] = (3, 7, 7),
@@ -218,6 +241,7 @@ class DeformableSlideAttention3D(nn.Module):
         nn.init.zeros_(self.offset_net[-1].weight)
         nn.init.zeros_(self.offset_net[-1].bias)
         self.dropout = nn.Dropout(dropout)
+        self.capture: Optional[dict] = None
 
     def _params(self):
         return (self.q_proj.weight, self.q_proj.bias, self.k_proj.weight, self.k_proj.bias,
@@ -228,6 +252,27 @@ class DeformableSlideAttention3D(nn.Module):
     def forward(self, x: Tensor, video_shape: Tuple[int, int, int], extra_kv: Optional[Tensor] = None) -> Tensor:
         """x: [B, N, D] tokens (N = T*H*W); video_shape: (T, H, W); extra_kv: optional [B, G, D]
         appended to every neighbourhood.  Returns [B, N, D]."""
+        return self._run(x, video_shape, extra_kv, None)
+
+    def forward_with_offsets(self, x: Tensor, video_shape: Tuple[int, int, int], offsets: Tensor,
+                             extra_kv: Optional[Tensor] = None) -> Tensor:
+        """The forward with the offset predictor replaced by given raw offsets (float32 [B, N, nh*K*3]
+        in the 1x1 conv's channel order, i.e. what offset_net(x) computes at attention.py:105-106,
+        bias included; offset_scale still applies).  Used to drive the op with synthetic offsets of a
+        chosen distribution; gradients flow to x, the projection / dw_conv parameters and `offsets`
+        (the offset_net parameters get none)."""
+        if offsets.dtype != torch.float32:
+            raise TypeError("offsets must be float32")
+        B, N = x.shape[:2]
+        want = (B, N, self.num_heads * self.k_t * self.k_h * self.k_w * 3)
+        if tuple(offsets.shape) != want:
+            raise ValueError(f"offsets must have shape {want}, got {tuple(offsets.shape)}")
+        if not offsets.is_cuda or offsets.device != x.device:
+            raise RuntimeError("offsets must be on x's CUDA device")
+        return self._run(x, video_shape, extra_kv, offsets.contiguous())
+
+    def _run(self, x: Tensor, video_shape: Tuple[int, int, int], extra_kv: Optional[Tensor],
+             offsets: Optional[Tensor]) -> Tensor:
         B, N, D = x.shape
         T, H, W = video_shape
         assert N == T * H * W, f"Expected N={T * H * W} but got {N}"
@@ -258,6 +303,7 @@ class DeformableSlideAttention3D(nn.Module):
         cfg = _Cfg(shape,
                    ops.ConvShape(B, T, H, W, D, (self.k_t, self.k_h, self.k_w)),
                    ops.ConvShape(B, T, H, W, D, (3, 3, 3)),
-                   dt, tuple(t.dtype for t in self._params()), G, (self.k_t, self.k_h, self.k_w))
+                   dt, tuple(t.dtype for t in self._params()), G, (self.k_t, self.k_h, self.k_w),
+                   capture=self.capture)
         with torch.autocast("cuda", enabled=False):
-            return DSA3DFunction.apply(cfg, x, extra_kv, *self._params())
+            return DSA3DFunction.apply(cfg, x, extra_kv, offsets, *self._params())

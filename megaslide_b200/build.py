@@ -8,6 +8,7 @@ Usage: ``python -m megaslide_b200.build [--force] [--verbose]``.  The library la
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -50,11 +51,39 @@ def lib_path() -> Path:
     return LIBDIR / LIBNAME
 
 
+def stamp_path() -> Path:
+    return LIBDIR / (LIBNAME + ".srchash")
+
+
+def source_hash() -> str:
+    """sha256 over every source, header and flag the library is built from: the stamp that ties a built
+    library to the sources it came from (file times do not survive copies to another machine)."""
+    h = hashlib.sha256()
+    for p in sorted(CSRC.glob("*.cu")) + _headers():
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    h.update(" ".join(ARCH_FLAGS + NVCC_FLAGS).encode())
+    return h.hexdigest()
+
+
+def is_current() -> bool:
+    """True when the built library exists and was built from the present sources."""
+    try:
+        return lib_path().exists() and stamp_path().read_text().strip() == source_hash()
+    except OSError:
+        return False
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compiles every ``csrc/*.cu`` for sm_100a and links the shared library; returns its path."""
+    """Compiles every ``csrc/*.cu`` for sm_100a and links the shared library; returns its path.  Object
+    files are reused only while the library's source stamp matches the sources (else everything is
+    recompiled)."""
     nvcc = _nvcc()
     OBJDIR.mkdir(exist_ok=True)
     LIBDIR.mkdir(exist_ok=True)
+    want = source_hash()
+    if not is_current():
+        force = True
     hdr_mtime = max((p.stat().st_mtime for p in _headers()), default=0.0)
     objs = []
     for src in sorted(CSRC.glob("*.cu")):
@@ -73,6 +102,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
+    stamp_path().write_text(want + "\n")
     return out
 
 

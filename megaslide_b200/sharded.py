@@ -159,14 +159,14 @@ def return_halo_grads(dwin: Tensor, plan: FramePlan, rank: int, group=None) -> T
 
 class _ShardCfg:
     __slots__ = ("T", "H", "W", "rank", "world", "owns", "group", "heads", "head_dim", "kernel", "oscale",
-                 "dropout_p", "seed", "dtype", "param_dtypes", "G")
+                 "dropout_p", "seed", "dtype", "param_dtypes", "G", "offset_bound", "capture")
 
 
 class DSA3DShardedFunction(torch.autograd.Function):
     """Forward/backward of one rank's frames of a time-sharded DeformableSlideAttention3D."""
 
     @staticmethod
-    def forward(ctx, cfg: _ShardCfg, x, extra_kv, wq, bq, wk, bk, wv, bv, wo, bo, wd, bd, w1, b1, w2, b2):
+    def forward(ctx, cfg: _ShardCfg, x, extra_kv, off_in, wq, bq, wk, bk, wv, bv, wo, bo, wd, bd, w1, b1, w2, b2):
         T, H, W, rank = cfg.T, cfg.H, cfg.W, cfg.rank
         HW = H * W
         own = cfg.owns[rank]
@@ -193,16 +193,26 @@ class DSA3DShardedFunction(torch.autograd.Function):
                               out_frame0=own[0], out_frames=nown)
         w1_kc = ops.conv_weight_kc(w1)
         b1f = b1.detach().float().contiguous()
-        hact = ops.dwconv_fwd(conv3, xc2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
         w2m = w2.reshape(w2.shape[0], C)
-        off = _mm_f32(hact, w2m.to(dt).t())  # its bias b2 is added by the kernels as they read it
-        b2f = b2.detach().float().contiguous()
+        if off_in is None:
+            hact = ops.dwconv_fwd(conv3, xc2, w1_kc, b1f, epilogue=MSL_EPI_GELU)
+            off = _mm_f32(hact, w2m.to(dt).t())  # its bias b2 is added by the kernels as they read it
+            b2f = b2.detach().float().contiguous()
+        else:  # raw offsets of the own frames given by the caller (the offset predictor does not run)
+            hact = None
+            off = off_in.reshape(B * nown * HW, -1)
+            b2f = None
         wd_kc = ops.conv_weight_kc(wd)
         D = ops.dwconv_fwd(convk, xc2, wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous(),
                            epilogue=MSL_EPI_NONE)
-        amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale, bias=b2f)
-        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=cfg.group)
-        dmax = float(amax[2].item())
+        if cfg.offset_bound is not None:
+            # the caller bounds |raw offset| (e.g. clipped synthetic offsets): the K/V window follows from the
+            # bound alone, with no reduction and no host synchronisation
+            dmax = float(cfg.offset_bound) * abs(cfg.oscale)
+        else:
+            amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale, bias=b2f)
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=cfg.group)
+            dmax = float(amax[2].item())
         if not math.isfinite(dmax):
             raise FloatingPointError("non-finite offsets: the K/V halo cannot be bounded")
         # 3. K/V window of every rank (deterministic on all ranks), fetch the remaining frames
@@ -243,11 +253,15 @@ class DSA3DShardedFunction(torch.autograd.Function):
         if probs is None:
             attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f)
         y = torch.addmm(D, attn, wo.to(dt).t())
+        if cfg.capture is not None:
+            cfg.capture.update(xw=xw, win=win, own=own, q=q, kv=kv, hact=hact, off=off, offset_bias=b2f, attn=attn,
+                               lse=lse, y=y)
         if train:
             ctx.save_for_backward(xw, q, kv, hact, off, b2f, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc,
                                   probs, saved)
             ctx.cfg, ctx.sh, ctx.plan, ctx.cw = cfg, sh, plan, cw
             ctx.in_dtype = x.dtype
+            ctx.off_dtype = off_in.dtype if off_in is not None else None
             ctx.extra_dtype = extra_kv.dtype if extra_kv is not None else None
         return y.view(B, N, C)
 
@@ -315,23 +329,32 @@ class DSA3DShardedFunction(torch.autograd.Function):
                 sums = dekv.sum(0)
                 g_bk = g_bk + sums[:C]
                 g_bv = g_bv + sums[C:]
-            # offset predictor
-            dh = _mm_f32(doff, w2m.to(dt))
-            g_w2 = _mm_f32(doff.t(), hact)
-            g_b2 = doff.sum(0, dtype=torch.float32)
-            conv3 = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=win[0], in_frames=nwin, out_frame0=own[0],
-                                  out_frames=nown)
-            du = ops.dwconv_fwd(conv3, xw2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh, out_dtype=torch.float32)
-            p3 = conv_window(T, own, 1)
-            conv3_t = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=own[0], in_frames=nown, out_frame0=p3[0],
-                                    out_frames=p3[1] - p3[0], zero_outside=True)
-            add_frames(ops.dwconv_bwd_data(conv3_t, du, w1_kc), p3)
-            g_w1 = torch.zeros_like(w1_kc)
-            g_b1 = torch.zeros(C, device=xw.device, dtype=torch.float32)
-            ops.dwconv_bwd_weight(conv3, du, xw2, g_w1, g_b1)
+            if cfg.capture is not None:
+                cfg.capture.update(dy2=dy2, dattn=dattn, dq=dq, dkv=dkv, doff=doff)
+            predictor = hact is not None
+            d_off_in = None
+            if predictor:
+                dh = _mm_f32(doff, w2m.to(dt))
+                g_w2 = _mm_f32(doff.t(), hact)
+                g_b2 = doff.sum(0, dtype=torch.float32)
+                conv3 = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=win[0], in_frames=nwin, out_frame0=own[0],
+                                      out_frames=nown)
+                du = ops.dwconv_fwd(conv3, xw2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh,
+                                    out_dtype=torch.float32)
+                p3 = conv_window(T, own, 1)
+                conv3_t = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=own[0], in_frames=nown, out_frame0=p3[0],
+                                        out_frames=p3[1] - p3[0], zero_outside=True)
+                add_frames(ops.dwconv_bwd_data(conv3_t, du, w1_kc), p3)
+                g_w1 = torch.zeros_like(w1_kc)
+                g_b1 = torch.zeros(C, device=xw.device, dtype=torch.float32)
+                ops.dwconv_bwd_weight(conv3, du, xw2, g_w1, g_b1)
+            elif ctx.needs_input_grad[3]:
+                d_off_in = doff.view(B, nown * HW, -1).to(ctx.off_dtype)
             # halo gradients back to their owners; parameter gradients summed over the ranks
             dx_own = return_halo_grads(dxw, plan, rank, cfg.group)
-            parts = [g_wq, g_bq, g_wk, g_bk, g_wv, g_bv, g_wo, g_bo, g_wd, g_bd, g_w1, g_b1, g_w2, g_b2]
+            parts = [g_wq, g_bq, g_wk, g_bk, g_wv, g_bv, g_wo, g_bo, g_wd, g_bd]
+            if predictor:
+                parts += [g_w1, g_b1, g_w2, g_b2]
             if d_extra is not None:
                 parts.append(d_extra)
             flat = torch.cat([p.reshape(-1).float() for p in parts])
@@ -340,8 +363,10 @@ class DSA3DShardedFunction(torch.autograd.Function):
             for p in parts:
                 outs.append(flat[o:o + p.numel()].view(p.shape))
                 o += p.numel()
-        (g_wq, g_bq, g_wk, g_bk, g_wv, g_bv, g_wo, g_bo, g_wd, g_bd, g_w1, g_b1, g_w2, g_b2) = outs[:14]
-        d_extra = outs[14] if G else None
+        (g_wq, g_bq, g_wk, g_bk, g_wv, g_bv, g_wo, g_bo, g_wd, g_bd) = outs[:10]
+        if predictor:
+            g_w1, g_b1, g_w2, g_b2 = outs[10:14]
+        d_extra = outs[-1] if G else None
         pd = cfg.param_dtypes
 
         def conv_w(gkc, k3):
@@ -350,12 +375,15 @@ class DSA3DShardedFunction(torch.autograd.Function):
         grads = (
             g_wq.to(pd[0]), g_bq.to(pd[1]), g_wk.to(pd[2]), g_bk.to(pd[3]), g_wv.to(pd[4]), g_bv.to(pd[5]),
             g_wo.to(pd[6]), g_bo.to(pd[7]), conv_w(g_wd, (kt, kh, kw)).to(pd[8]), g_bd.to(pd[9]),
-            conv_w(g_w1, (3, 3, 3)).to(pd[10]), g_b1.to(pd[11]),
-            g_w2.reshape(w2m.shape[0], C, 1, 1, 1).to(pd[12]), g_b2.to(pd[13]),
         )
+        if predictor:
+            grads += (conv_w(g_w1, (3, 3, 3)).to(pd[10]), g_b1.to(pd[11]),
+                      g_w2.reshape(w2m.shape[0], C, 1, 1, 1).to(pd[12]), g_b2.to(pd[13]))
+        else:
+            grads += (None, None, None, None)
         dx_out = dx_own.reshape(B, nown * HW, C).to(ctx.in_dtype)
         de = d_extra.to(ctx.extra_dtype) if d_extra is not None else None
-        return (None, dx_out, de) + grads
+        return (None, dx_out, de, d_off_in) + grads
 
 
 class TimeShardedDSA3D(nn.Module):
@@ -366,7 +394,13 @@ class TimeShardedDSA3D(nn.Module):
     the module output for the own frames; gradients w.r.t. x_local and the (replicated) parameters
     equal those of the unsharded module (parameter gradients are summed over the ranks inside the
     backward, so every rank ends with the full gradient).  Frame ranges: `shard_ranges(T, world)`
-    unless `frame_ranges` is given (the same list on every rank)."""
+    unless `frame_ranges` is given (the same list on every rank).
+
+    forward_with_offsets(x_local, video_shape, offsets_local, offset_bound=None) runs the op on given
+    raw offsets of the own frames (float32 [B, own_frames*H*W, nh*K*3]; the offset predictor does not
+    run).  With `offset_bound` (a bound on |raw offset| that the caller guarantees, e.g. for offsets
+    clipped to +-3) the K/V window of every rank follows from the bound: no reduction of the largest
+    offset and no host synchronisation.  ``capture``: as DeformableSlideAttention3D.capture."""
 
     def __init__(self, module: DeformableSlideAttention3D, group=None,
                  frame_ranges: Optional[Sequence[Range]] = None):
@@ -375,8 +409,25 @@ class TimeShardedDSA3D(nn.Module):
         self.group = group
         self.frame_ranges = list(frame_ranges) if frame_ranges is not None else None
         self._joined = False
+        self.capture: Optional[dict] = None
 
     def forward(self, x: Tensor, video_shape: Tuple[int, int, int], extra_kv: Optional[Tensor] = None) -> Tensor:
+        return self._run(x, video_shape, extra_kv, None, None)
+
+    def forward_with_offsets(self, x: Tensor, video_shape: Tuple[int, int, int], offsets: Tensor,
+                             offset_bound: Optional[float] = None, extra_kv: Optional[Tensor] = None) -> Tensor:
+        m = self.module
+        if offsets.dtype != torch.float32:
+            raise TypeError("offsets must be float32")
+        want = tuple(x.shape[:2]) + (m.num_heads * m.k_t * m.k_h * m.k_w * 3,)
+        if tuple(offsets.shape) != want:
+            raise ValueError(f"offsets must have shape {want}, got {tuple(offsets.shape)}")
+        if offset_bound is not None and not (offset_bound >= 0 and math.isfinite(offset_bound)):
+            raise ValueError("offset_bound must be a finite non-negative number")
+        return self._run(x, video_shape, extra_kv, offsets.contiguous(), offset_bound)
+
+    def _run(self, x: Tensor, video_shape: Tuple[int, int, int], extra_kv: Optional[Tensor],
+             offsets: Optional[Tensor], offset_bound: Optional[float]) -> Tensor:
         m = self.module
         T, H, W = video_shape
         world = dist.get_world_size(self.group)
@@ -414,5 +465,7 @@ class TimeShardedDSA3D(nn.Module):
         cfg.oscale, cfg.dropout_p, cfg.seed, cfg.dtype = float(m.offset_scale), float(p), seed, dt
         cfg.param_dtypes = tuple(t.dtype for t in m._params())
         cfg.G = G
+        cfg.offset_bound = offset_bound
+        cfg.capture = self.capture
         with torch.autocast("cuda", enabled=False):
-            return DSA3DShardedFunction.apply(cfg, x, extra_kv, *m._params())
+            return DSA3DShardedFunction.apply(cfg, x, extra_kv, offsets, *m._params())

@@ -340,6 +340,172 @@ void oracle_dsa_bwd(const oracle_geom* g, const double* q, const double* k, cons
   }
 }
 
+/* Element i of a float32 (dtype 0) or bf16 (dtype 1, raw uint16 bits) array, as a double. */
+static double load_el(const void* p, long i, int dtype) {
+  if (dtype == 0) return (double)((const float*)p)[i];
+  const uint32_t bits = (uint32_t)((const uint16_t*)p)[i] << 16;
+  float f;
+  memcpy(&f, &bits, sizeof f);
+  return (double)f;
+}
+
+/* The core op (forward and backward, no extra keys) at a LIST of query rows of a large, possibly
+ * time-sharded run, so that a run far too large for oracle_dsa_fwd / oracle_dsa_bwd can still be
+ * checked row by row (attention.py:113-186; the same arithmetic as those two functions).
+ *
+ * The geometry names the GLOBAL volume.  The query rows of the run are frames
+ * [q_frame0, q_frame0 + q_frames) of every sample; the K/V buffers hold frames
+ * [kv_frame0, kv_frame0 + kv_frames).  qidx[i] = b * (q_frames*H*W) + local query row.
+ * Per listed query i (all heads): q_rows / dout_rows [nq, >=C] (row stride row_ld), off_rows float32
+ * [nq, nh*K*3] (the raw offsets, before offset_bias), bias float32 [nh*K*3] or NULL (added to the
+ * offsets in one float32 rounding); k, v: the run's whole K/V buffers [B, kv_frames*H*W, >=C] (row
+ * stride kv_ld).  Elements are float32 (dtype 0) or bf16 (dtype 1).
+ * Outputs (double): out [nq, C], lse [nq, nh] (natural log), and when dout_rows is given dq [nq, C],
+ * doff [nq, nh*K*3].  kv_slot (int32 [B*kv_rows], -1 = not watched; or NULL): dK / dV of the
+ * listed queries are accumulated into dk_w / dv_w [nw, C] (overwritten) at the watched K/V rows.
+ * Returns the number of sample corners that fell inside the volume but outside the K/V window
+ * (those are skipped; a correct plan makes it 0). */
+long oracle_dsa_rows(const oracle_geom* g, int q_frame0, int q_frames, int kv_frame0, int kv_frames, long nq,
+                     const int64_t* qidx, const void* q_rows, const void* dout_rows, long row_ld,
+                     const float* off_rows, const float* bias, const void* k, const void* v, long kv_ld, int dtype,
+                     double* out, double* lse, double* dq, double* doff, const int32_t* kv_slot, long nw,
+                     double* dk_w, double* dv_w) {
+  const int K = g->kt * g->kh * g->kw, d = g->d, nh = g->nh;
+  const long HW = (long)g->H * g->W, C = (long)nh * d, NQ = (long)q_frames * HW, NKV = (long)kv_frames * HW;
+  const long nO = (long)nh * K * 3;
+  const uint32_t thr = drop_threshold(g->dropout_p);
+  const int want_bwd = dout_rows != NULL;
+  long misses = 0;
+  if (nw > 0) {
+    memset(dk_w, 0, sizeof(double) * nw * C);
+    memset(dv_w, 0, sizeof(double) * nw * C);
+  }
+#pragma omp parallel reduction(+ : misses)
+  {
+    double* s = (double*)malloc(sizeof(double) * K);
+    double* kdc = (double*)malloc(sizeof(double) * K * 8);
+    double* vdc = (double*)malloc(sizeof(double) * K * 8);
+    double* dpv = (double*)malloc(sizeof(double) * K);
+    double* qd = (double*)malloc(sizeof(double) * d);
+    double* dod = (double*)malloc(sizeof(double) * d);
+    double* acc = (double*)malloc(sizeof(double) * d);
+    long* rows = (long*)malloc(sizeof(long) * K * 8);
+    corner8* cs = (corner8*)malloc(sizeof(corner8) * K);
+    float* pts = (float*)malloc(sizeof(float) * 3 * K);
+    double* pdk = nw > 0 ? (double*)calloc(nw * C, sizeof(double)) : NULL;
+    double* pdv = nw > 0 ? (double*)calloc(nw * C, sizeof(double)) : NULL;
+#pragma omp for schedule(dynamic, 4)
+    for (long item = 0; item < nq * nh; ++item) {
+      const long i = item / nh;
+      const int head = (int)(item % nh);
+      const int b = (int)(qidx[i] / NQ);
+      const long n = qidx[i] % NQ;
+      const int t = q_frame0 + (int)(n / HW), h = (int)((n / g->W) % g->H), w = (int)(n % g->W);
+      for (int c = 0; c < d; ++c) {
+        qd[c] = load_el(q_rows, i * row_ld + head * d + c, dtype);
+        dod[c] = want_bwd ? load_el(dout_rows, i * row_ld + head * d + c, dtype) : 0.0;
+      }
+      double m = -INFINITY;
+      for (int j = 0; j < K; ++j) {
+        float o3[3];
+        for (int a = 0; a < 3; ++a) {
+          const long ci = (long)head * K * 3 + 3 * j + a;
+          o3[a] = bias ? off_rows[i * nO + ci] + bias[ci] : off_rows[i * nO + ci];
+        }
+        float pt, ph, pw;
+        coords(g, t, h, w, j, o3, &pt, &ph, &pw);
+        pts[3 * j] = pt; pts[3 * j + 1] = ph; pts[3 * j + 2] = pw;
+        make_corners(g, pt, ph, pw, &cs[j]);
+        double sj = 0.0, dpj = 0.0;
+        for (int c = 0; c < 8; ++c) {
+          double kd = 0.0, vd = 0.0;
+          rows[j * 8 + c] = -1;
+          if (cs[j].valid[c]) {
+            const long tg = cs[j].row[c] / HW;
+            if (tg < kv_frame0 || tg >= kv_frame0 + kv_frames) {
+              if (cs[j].w[c] != 0.0) ++misses;
+            } else {
+              const long r = (long)b * NKV + cs[j].row[c] - (long)kv_frame0 * HW;
+              rows[j * 8 + c] = r;
+              for (int e = 0; e < d; ++e) {
+                kd += qd[e] * load_el(k, r * kv_ld + head * d + e, dtype);
+                if (want_bwd) vd += dod[e] * load_el(v, r * kv_ld + head * d + e, dtype);
+              }
+            }
+          }
+          kdc[j * 8 + c] = kd;
+          vdc[j * 8 + c] = vd;
+          sj += cs[j].w[c] * kd;
+          dpj += cs[j].w[c] * vd;
+        }
+        s[j] = sj * g->softmax_scale;
+        dpv[j] = dpj;
+        if (s[j] > m) m = s[j];
+      }
+      double l = 0.0;
+      for (int j = 0; j < K; ++j) l += exp(s[j] - m);
+      lse[i * nh + head] = m + log(l);
+      for (int e = 0; e < d; ++e) acc[e] = 0.0;
+      for (int j = 0; j < K; ++j) {
+        const double p = exp(s[j] - m) / l * keep_factor(g, thr, b, t, h, w, head, j);
+        if (p == 0.0) continue;
+        for (int c = 0; c < 8; ++c) {
+          if (rows[j * 8 + c] < 0) continue;
+          const double pw_ = p * cs[j].w[c];
+          for (int e = 0; e < d; ++e) acc[e] += pw_ * load_el(v, rows[j * 8 + c] * kv_ld + head * d + e, dtype);
+        }
+      }
+      for (int e = 0; e < d; ++e) out[i * C + head * d + e] = acc[e];
+      if (!want_bwd) continue;
+      double D = 0.0;
+      for (int j = 0; j < K; ++j) D += exp(s[j] - m) / l * keep_factor(g, thr, b, t, h, w, head, j) * dpv[j];
+      for (int e = 0; e < d; ++e) acc[e] = 0.0;
+      for (int j = 0; j < K; ++j) {
+        const double p = exp(s[j] - m) / l;
+        const double kf = keep_factor(g, thr, b, t, h, w, head, j);
+        const double dsq = p * (dpv[j] * kf - D) * g->softmax_scale;
+        const double pv = p * kf;
+        double gx = 0.0, gy = 0.0, gz = 0.0;
+        for (int c = 0; c < 8; ++c) {
+          const long r = rows[j * 8 + c];
+          if (r < 0) continue;
+          const double cq = dsq * cs[j].w[c], cv = pv * cs[j].w[c];
+          const int slot = kv_slot ? kv_slot[r] : -1;
+          for (int e = 0; e < d; ++e) acc[e] += cq * load_el(k, r * kv_ld + head * d + e, dtype);
+          if (slot >= 0) {
+            for (int e = 0; e < d; ++e) {
+              pdk[(long)slot * C + head * d + e] += cq * qd[e];
+              pdv[(long)slot * C + head * d + e] += cv * dod[e];
+            }
+          }
+          const double gc = dsq * kdc[j * 8 + c] + pv * vdc[j * 8 + c];
+          gx += cs[j].dwx[c] * gc;
+          gy += cs[j].dwy[c] * gc;
+          gz += cs[j].dwz[c] * gc;
+        }
+        gx *= clip_mult(pts[3 * j + 2], g->W);
+        gy *= clip_mult(pts[3 * j + 1], g->H);
+        gz *= clip_mult(pts[3 * j + 0], g->T);
+        double* dr = doff + i * nO + (long)head * K * 3 + 3 * j;
+        dr[0] = g->T > 1 ? gx / (double)(g->T - 1) * g->offset_scale : 0.0;
+        dr[1] = g->H > 1 ? gy / (double)(g->H - 1) * g->offset_scale : 0.0;
+        dr[2] = g->W > 1 ? gz / (double)(g->W - 1) * g->offset_scale : 0.0;
+      }
+      for (int e = 0; e < d; ++e) dq[i * C + head * d + e] = acc[e];
+    }
+    if (nw > 0) {
+#pragma omp critical
+      for (long e = 0; e < nw * C; ++e) {
+        dk_w[e] += pdk[e];
+        dv_w[e] += pdv[e];
+      }
+    }
+    free(s); free(kdc); free(vdc); free(dpv); free(qd); free(dod); free(acc); free(rows); free(cs); free(pts);
+    free(pdk); free(pdv);
+  }
+  return misses;
+}
+
 /* Depthwise 3D convolution, zero padding k//2, x/y [B, T*H*W, C], weight [kt*kh*kw, C]. */
 void oracle_dwconv3d(int B, int T, int H, int W, int C, int kt, int kh, int kw, const double* x, const double* wt,
                      const double* bias, double* y) {

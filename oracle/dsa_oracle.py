@@ -64,6 +64,10 @@ def _lib() -> ctypes.CDLL:
         P = ctypes.c_void_p
         lib.oracle_dsa_fwd.argtypes = [ctypes.POINTER(_Geom), P, P, P, P, P, P, P, P]
         lib.oracle_dsa_bwd.argtypes = [ctypes.POINTER(_Geom)] + [P] * 13
+        lib.oracle_dsa_rows.argtypes = ([ctypes.POINTER(_Geom)] + [ctypes.c_int] * 4 + [ctypes.c_long, P, P, P,
+                                        ctypes.c_long, P, P, P, P, ctypes.c_long, ctypes.c_int, P, P, P, P, P,
+                                        ctypes.c_long, P, P])
+        lib.oracle_dsa_rows.restype = ctypes.c_long
         i = ctypes.c_int
         lib.oracle_dwconv3d.argtypes = [i] * 8 + [P] * 4
         lib.oracle_dwconv3d_bwd.argtypes = [i] * 8 + [P] * 6
@@ -144,6 +148,73 @@ def attn_backward(q, k, v, offsets, dout, video_shape, heads, kernel_size, ek=No
     return dq, dk, dv, doff, dek, dev
 
 
+def _raw(a: np.ndarray) -> tuple:
+    """(contiguous array, dtype code) for float32 or bf16 (uint16 bit patterns) element arrays."""
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.float32:
+        return a, 0
+    if a.dtype == np.uint16:
+        return a, 1
+    raise TypeError(f"expected float32 or bf16 bits (uint16), got {a.dtype}")
+
+
+def attn_rows(q_rows, offsets_rows, k, v, qidx, video_shape, heads, kernel_size, *, dout_rows=None,
+              offset_bias=None, q_frame0=0, q_frames=None, kv_frame0=0, kv_frames=None, watch_rows=None,
+              softmax_scale=None, offset_scale=1.0, dropout_p=0.0, seed=0):
+    """The core op (forward and, with dout_rows, backward; no extra keys) at a list of query rows of
+    a run too large for attn_forward / attn_backward, from the run's own operands.
+
+    q_rows, dout_rows: [nq, C] rows of the listed queries; offsets_rows: float32 [nq, nh*K*3] (raw,
+    before offset_bias); k, v: the run's K/V buffers [B * kv_frames*H*W, C]; qidx: int64 [nq] =
+    b * (q_frames*H*W) + local query row.  Elements are float32 or bf16 bit patterns (uint16), the
+    same type for q, k, v and dout.  Query frames [q_frame0, +q_frames) and K/V frames
+    [kv_frame0, +kv_frames) are global frame windows of the volume video_shape (time sharding).
+    watch_rows: int64 K/V buffer rows whose dK / dV (from the listed queries only) are returned.
+    Returns dict(out, lse (natural log), dq, doff, dk, dv, misses) of float64 arrays (dq/doff/dk/dv
+    None without dout_rows / watch_rows); misses = sample corners outside the K/V window."""
+    T, H, W = video_shape
+    q_frames = T if q_frames is None else q_frames
+    kv_frames = T if kv_frames is None else kv_frames
+    qr, dt = _raw(q_rows)
+    kr, dtk = _raw(k)
+    vr, dtv = _raw(v)
+    if not (dt == dtk == dtv):
+        raise TypeError("q, k, v must share one element type")
+    nq, C = qr.shape
+    d = C // heads
+    kt, kh, kw = kernel_size
+    K = kt * kh * kw
+    off = np.ascontiguousarray(offsets_rows, dtype=np.float32).reshape(nq, heads * K * 3)
+    bias = None if offset_bias is None else np.ascontiguousarray(offset_bias, dtype=np.float32)
+    dor = None
+    if dout_rows is not None:
+        dor, dtd = _raw(dout_rows)
+        if dtd != dt or dor.shape != qr.shape:
+            raise TypeError("dout_rows must match q_rows")
+    qidx = np.ascontiguousarray(qidx, dtype=np.int64)
+    B = 1 + int(qidx.max()) // (q_frames * H * W) if nq else 1
+    kv_rows = kr.shape[0]
+    g = _geom(video_shape, heads, d, kernel_size, B, 0, softmax_scale, offset_scale, dropout_p, seed)
+    out = np.zeros((nq, C))
+    lse = np.zeros((nq, heads))
+    dq = np.zeros((nq, C)) if dor is not None else None
+    doff = np.zeros((nq, heads * K * 3)) if dor is not None else None
+    slot = dk = dv = None
+    nw = 0
+    if watch_rows is not None and dor is not None:
+        watch_rows = np.asarray(watch_rows, dtype=np.int64)
+        nw = len(watch_rows)
+        slot = np.full(kv_rows, -1, dtype=np.int32)
+        slot[watch_rows] = np.arange(nw, dtype=np.int32)
+        dk = np.zeros((nw, C))
+        dv = np.zeros((nw, C))
+    misses = _lib().oracle_dsa_rows(
+        ctypes.byref(g), int(q_frame0), int(q_frames), int(kv_frame0), int(kv_frames), nq, _ptr(qidx), _ptr(qr),
+        _ptr(dor), C, _ptr(off), _ptr(bias), _ptr(kr), _ptr(vr), kr.shape[1], dt, _ptr(out), _ptr(lse), _ptr(dq),
+        _ptr(doff), _ptr(slot), nw, _ptr(dk), _ptr(dv))
+    return dict(out=out, lse=lse, dq=dq, doff=doff, dk=dk, dv=dv, misses=int(misses))
+
+
 def dwconv3d(x, w_kc, bias, video_shape, kernel_size):
     """Depthwise conv, zero padding k//2.  x [B, N, C], w_kc [kt*kh*kw, C]."""
     x, w_kc = _f64(x), _f64(w_kc)
@@ -189,18 +260,24 @@ def _conv_w_kc(w):
 
 
 def module_forward(params: dict, x, video_shape, extra_kv=None, *, heads: int, kernel_size=(3, 7, 7),
-                   offset_scale: float = 1.0, dropout_p: float = 0.0, seed: int = 0):
-    """Forward of DeformableSlideAttention3D (attention.py:82-192).  Returns (y, cache)."""
+                   offset_scale: float = 1.0, dropout_p: float = 0.0, seed: int = 0, offsets=None):
+    """Forward of DeformableSlideAttention3D (attention.py:82-192).  Returns (y, cache).
+    offsets: raw offsets [B, N, nh*K*3] used in place of the offset predictor's output (the
+    predictor does not run; module_backward then returns d(offsets) as grads["offsets"])."""
     x = _f64(x)
     B, N, C = x.shape
     T, H, W = video_shape
     assert N == T * H * W, f"Expected N={T * H * W} but got {N}"
     P = {kk: _f64(vv) for kk, vv in params.items()}
     dw = dwconv3d(x, _conv_w_kc(P["dw_conv.weight"]), P["dw_conv.bias"], video_shape, kernel_size)
-    u = dwconv3d(x, _conv_w_kc(P["offset_net.0.weight"]), P["offset_net.0.bias"], video_shape, (3, 3, 3))
-    hact = gelu(u)
-    W2 = P["offset_net.2.weight"].reshape(P["offset_net.2.weight"].shape[0], C)
-    off = hact @ W2.T + P["offset_net.2.bias"]
+    if offsets is None:
+        u = dwconv3d(x, _conv_w_kc(P["offset_net.0.weight"]), P["offset_net.0.bias"], video_shape, (3, 3, 3))
+        hact = gelu(u)
+        W2 = P["offset_net.2.weight"].reshape(P["offset_net.2.weight"].shape[0], C)
+        off = hact @ W2.T + P["offset_net.2.bias"]
+    else:
+        u = hact = None
+        off = np.asarray(offsets)
     off32 = off.astype(np.float32)
     q = x @ P["q_proj.weight"].T + P["q_proj.bias"]
     k = x @ P["k_proj.weight"].T + P["k_proj.bias"]
@@ -248,6 +325,9 @@ def module_backward(cache: dict, dy):
         grads["k_proj.bias"] = grads["k_proj.bias"] + flat(dek).sum(0)
         grads["v_proj.weight"] = grads["v_proj.weight"] + flat(dev).T @ flat(e)
         grads["v_proj.bias"] = grads["v_proj.bias"] + flat(dev).sum(0)
+    if cache["hact"] is None:  # offsets were given: their gradient instead of the predictor's
+        grads["offsets"] = doff
+        return dx, grads, d_extra
     W2 = P["offset_net.2.weight"].reshape(P["offset_net.2.weight"].shape[0], C)
     dh = doff @ W2
     grads["offset_net.2.weight"] = (flat(doff).T @ flat(cache["hact"])).reshape(P["offset_net.2.weight"].shape)

@@ -141,3 +141,11 @@ def test_dwconv_halo_coverage_is_checked():
     g = _lib.DwconvGeometry(1, 4, 4, 4, 16, 3, 3, 3, 0, 4, 0, 4, 0)
     rc = lib.msl_dwconv3d_fwd(ctypes.byref(g), 16, 16, 16, None, None, 9, None, 0, 16, 16, 0, None)
     assert rc == _lib.MSL_ERR_INVALID and "epilogue" in _err()
+
+
+def test_noalloc_capacity_matches_header():
+    """The ctypes mirror of MSL_NOALLOC_SCRATCH_BYTES equals the header's #define."""
+    m = re.search(r"#define\s+MSL_NOALLOC_SCRATCH_BYTES\s+\(([^)]*)\)", HEADER.read_text())
+    assert m, "MSL_NOALLOC_SCRATCH_BYTES not found in the header"
+    value = eval(m.group(1).replace("u", ""), {"__builtins__": {}})  # e.g. 64u * 1024u * 1024u
+    assert value == _lib.MSL_NOALLOC_SCRATCH_BYTES

@@ -91,7 +91,7 @@ def _conv_rows(xbuf: torch.Tensor, frame0: int, nframes: int, b: np.ndarray, t: 
                 if np.any(ok & ((tt < frame0) | (tt >= frame0 + nframes))):
                     raise ValueError("conv tap outside the buffer's frames")
                 rows = np.where(ok, ((b * nframes + (tt - frame0)) * H + hh) * W + ww, 0)
-                xr = xbuf.index_select(0, torch.from_numpy(rows).to(xbuf.device)).double().cpu().numpy()
+                xr = xbuf.detach().index_select(0, torch.from_numpy(rows).to(xbuf.device)).double().cpu().numpy()
                 out += np.where(ok[:, None], xr * w_kc[tap], 0.0)
                 tap += 1
     return out
@@ -132,6 +132,7 @@ def check(module, cap: dict, video_shape, *, batch: int, dtype: torch.dtype, n_r
     tol = _tols(dtype)
     rng = np.random.default_rng(seed)
     sharded = "kv" in cap
+    cap = {k: (v.detach() if isinstance(v, torch.Tensor) else v) for k, v in cap.items()}
     if sharded:
         qb, kb, vb = cap["q"], cap["kv"][:, :C], cap["kv"][:, C:]
         dqb, dkb, dvb = cap["dq"], cap["dkv"][:, :C], cap["dkv"][:, C:]

@@ -370,7 +370,7 @@ class Workload:
         torch.cuda.synchronize()
         kw = {}
         if self.world > 1:
-            own, win = cap["own"], cap["win"]
+            own, win = cap["own"], cap["kvwin"]
             kw = dict(q_frame0=own[0], q_frames=own[1] - own[0], kv_frame0=win[0], kv_frames=win[1] - win[0],
                       world=self.world)
         t0 = time.perf_counter()
@@ -378,7 +378,7 @@ class Workload:
                             n_rows=max(64, n_rows // self.world), seed=seed + self.rank,
                             injected=self.off is not None, **kw)
         res["seconds"] = time.perf_counter() - t0
-        halo = [cap["own"][0] - cap["win"][0], cap["win"][1] - cap["own"][1]] if self.world > 1 else [0, 0]
+        halo = [cap["own"][0] - cap["kvwin"][0], cap["kvwin"][1] - cap["own"][1]] if self.world > 1 else [0, 0]
         for p in self.params:
             p.grad = None
         del cap

@@ -250,44 +250,72 @@ cudaError_t launch_dwconv_wgrad(const ConvParams& P, const void* dy, long long d
 }
 
 // ------------------------------------------------------------------------------ utilities
+// Per-axis max |(offset + bias) * oscale|.  Blocks stride over rows; in a row the threads stride over
+// column quads (16-byte loads when every row start is 16-byte aligned).  Column 4i + e has axis
+// (4i + e) mod 3 = (i + e) mod 3.
+template <bool VEC>
 __global__ void __launch_bounds__(256) offsets_absmax_kernel(const float* __restrict__ off, long long rows, long long ld,
                                                              const float* __restrict__ bias, int ncol, float oscale,
                                                              float* out3) {
-  float m0 = 0.f, m1 = 0.f, m2 = 0.f;
-  const long long n = rows * ncol;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / ncol;
-    const int cidx = static_cast<int>(i - r * ncol);
-    const float o = bias ? __fadd_rn(off[r * ld + cidx], __ldg(bias + cidx)) : off[r * ld + cidx];
-    const float v = fabsf(o * oscale);
-    const int axis = cidx % 3;
-    if (axis == 0) m0 = fmaxf(m0, v);
-    else if (axis == 1) m1 = fmaxf(m1, v);
-    else m2 = fmaxf(m2, v);
+  float m[3] = {0.f, 0.f, 0.f};
+  const int nq = VEC ? ncol / 4 : 0;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* row = off + r * ld;
+    if (VEC) {
+      for (int i = threadIdx.x; i < nq; i += blockDim.x) {
+        float4 v = __ldcs(reinterpret_cast<const float4*>(row) + i);
+        if (bias) {
+          const float4 b = __ldg(reinterpret_cast<const float4*>(bias) + i);
+          v.x = __fadd_rn(v.x, b.x); v.y = __fadd_rn(v.y, b.y); v.z = __fadd_rn(v.z, b.z); v.w = __fadd_rn(v.w, b.w);
+        }
+        const int a = i % 3;
+        const float e0 = fabsf(v.x * oscale), e1 = fabsf(v.y * oscale), e2 = fabsf(v.z * oscale),
+                    e3 = fabsf(v.w * oscale);
+        // axes of the four elements: a, a+1, a+2, a (mod 3)
+        if (a == 0) { m[0] = fmaxf(m[0], fmaxf(e0, e3)); m[1] = fmaxf(m[1], e1); m[2] = fmaxf(m[2], e2); }
+        else if (a == 1) { m[1] = fmaxf(m[1], fmaxf(e0, e3)); m[2] = fmaxf(m[2], e1); m[0] = fmaxf(m[0], e2); }
+        else { m[2] = fmaxf(m[2], fmaxf(e0, e3)); m[0] = fmaxf(m[0], e1); m[1] = fmaxf(m[1], e2); }
+      }
+    }
+    for (int c = 4 * nq + threadIdx.x; c < ncol; c += blockDim.x) {  // tail columns, or every column
+      const float o = bias ? __fadd_rn(row[c], __ldg(bias + c)) : row[c];
+      const int a = c % 3;
+      m[a] = fmaxf(m[a], fabsf(o * oscale));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    m0 = fmaxf(m0, __shfl_xor_sync(kFull, m0, o));
-    m1 = fmaxf(m1, __shfl_xor_sync(kFull, m1, o));
-    m2 = fmaxf(m2, __shfl_xor_sync(kFull, m2, o));
+    m[0] = fmaxf(m[0], __shfl_xor_sync(kFull, m[0], o));
+    m[1] = fmaxf(m[1], __shfl_xor_sync(kFull, m[1], o));
+    m[2] = fmaxf(m[2], __shfl_xor_sync(kFull, m[2], o));
   }
+  __shared__ float red[3][8];
+  const int warp = threadIdx.x >> 5;
   if ((threadIdx.x & 31) == 0) {
+    red[0][warp] = m[0];
+    red[1][warp] = m[1];
+    red[2][warp] = m[2];
+  }
+  __syncthreads();
+  if (threadIdx.x < 3) {
+    float v = 0.f;
+    for (int w = 0; w < (blockDim.x >> 5); ++w) v = fmaxf(v, red[threadIdx.x][w]);
     // non-negative floats order like their bit patterns
-    atomicMax(reinterpret_cast<int*>(out3) + 0, __float_as_int(m0));
-    atomicMax(reinterpret_cast<int*>(out3) + 1, __float_as_int(m1));
-    atomicMax(reinterpret_cast<int*>(out3) + 2, __float_as_int(m2));
+    atomicMax(reinterpret_cast<int*>(out3) + threadIdx.x, __float_as_int(v));
   }
 }
 
 cudaError_t launch_offsets_absmax(const float* off, long long rows, long long ld, const float* bias, int heads, int taps,
                                   float oscale, float* out3, cudaStream_t s) {
   const int ncol = heads * taps * 3;
-  const long long n = rows * ncol;
-  long long blocks = (n + 255) / 256;
-  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  long long blocks = rows < 148LL * 8 ? rows : 148LL * 8;
   if (blocks < 1) blocks = 1;
-  offsets_absmax_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, rows, ld, bias, ncol, oscale, out3);
+  const bool vec = (reinterpret_cast<uintptr_t>(off) & 15u) == 0 && (ld & 3) == 0 && ncol >= 4 &&
+                   (!bias || (reinterpret_cast<uintptr_t>(bias) & 15u) == 0);
+  if (vec)
+    offsets_absmax_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, rows, ld, bias, ncol, oscale, out3);
+  else
+    offsets_absmax_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, rows, ld, bias, ncol, oscale, out3);
   return cudaGetLastError();
 }
 

@@ -90,12 +90,27 @@ class FramePlan:
     windows: List[Range]
 
 
-def exchange_into(buf: Tensor, buf_range: Range, local: Tensor, plan: FramePlan, fetch: Sequence[List[Range]],
-                  rank: int, group=None) -> None:
-    """Fills the frames `fetch[rank]` of `buf` (frames `buf_range`, laid out [B, frames, HW, C]) from
-    their owners; sends the own frames every other rank fetches.  `local` [B, own frames, HW, C]
-    holds this rank's frames.  fetch[s] = frame intervals rank s wants (the same list on every rank).
-    """
+class _Pending:
+    """Point-to-point transfers started on the process group's stream (NCCL: its own stream, so they
+    overlap the compute queued after them); finish() makes the caller's stream wait for them and
+    lands the received frames."""
+
+    def __init__(self, reqs, on_finish):
+        self.reqs = reqs
+        self.on_finish = on_finish
+
+    def finish(self):
+        for req in self.reqs:
+            req.wait()
+        return self.on_finish()
+
+
+def start_exchange(buf: Tensor, buf_range: Range, local: Tensor, plan: FramePlan, fetch: Sequence[List[Range]],
+                   rank: int, group=None) -> _Pending:
+    """Starts filling the frames `fetch[rank]` of `buf` (frames `buf_range`, laid out [B, frames, HW, X])
+    from their owners, and sending the own frames every other rank fetches.  `local` [B, own frames, HW, X]
+    holds this rank's frames (any strides).  fetch[s] = frame intervals rank s wants (the same list on
+    every rank).  Returns the pending transfers; finish() lands them in `buf`."""
     world = len(plan.owns)
     own = plan.owns[rank]
     ops_: list = []
@@ -108,7 +123,6 @@ def exchange_into(buf: Tensor, buf_range: Range, local: Tensor, plan: FramePlan,
             if ov:
                 t = local[:, ov[0] - own[0]:ov[1] - own[0]].contiguous()
                 ops_.append(dist.P2POp(dist.isend, t, s, group))
-                recv_tmp.append(None)
     for iv in fetch[rank]:
         for r in range(world):
             if r == rank:
@@ -119,19 +133,26 @@ def exchange_into(buf: Tensor, buf_range: Range, local: Tensor, plan: FramePlan,
                                 device=buf.device)
                 ops_.append(dist.P2POp(dist.irecv, t, r, group))
                 recv_tmp.append((ov, t))
-    if ops_:
-        for req in dist.batch_isend_irecv(ops_):
-            req.wait()
-    for item in recv_tmp:
-        if item is not None:
-            ov, t = item
+    reqs = dist.batch_isend_irecv(ops_) if ops_ else []
+
+    def land():
+        for ov, t in recv_tmp:
             buf[:, ov[0] - buf_range[0]:ov[1] - buf_range[0]].copy_(t)
 
+    return _Pending(reqs, land)
 
-def return_halo_grads(dwin: Tensor, plan: FramePlan, rank: int, group=None) -> Tensor:
-    """Reverse of the forward exchanges: sends the gradient rows of `dwin` ([B, window frames, HW, C],
-    frames plan.windows[rank]) that belong to other ranks to their owners, adds what the other ranks
-    send for the own frames, and returns the own frames [B, own frames, HW, C]."""
+
+def exchange_into(buf: Tensor, buf_range: Range, local: Tensor, plan: FramePlan, fetch: Sequence[List[Range]],
+                  rank: int, group=None) -> None:
+    """start_exchange(...).finish(): fills the frames `fetch[rank]` of `buf` from their owners."""
+    start_exchange(buf, buf_range, local, plan, fetch, rank, group).finish()
+
+
+def start_halo_return(dwin: Tensor, plan: FramePlan, rank: int, group=None) -> _Pending:
+    """Reverse of the forward exchanges, started: sends the gradient rows of `dwin` ([B, window frames,
+    HW, X], frames plan.windows[rank]) that belong to other ranks to their owners and receives what the
+    other ranks computed for the own frames; finish() adds those into the own frames of `dwin` (in
+    place) and returns that view [B, own frames, HW, X]."""
     world = len(plan.owns)
     win, own = plan.windows[rank], plan.owns[rank]
     ops_: list = []
@@ -148,13 +169,50 @@ def return_halo_grads(dwin: Tensor, plan: FramePlan, rank: int, group=None) -> T
                             device=dwin.device)
             ops_.append(dist.P2POp(dist.irecv, t, r, group))
             recvs.append((ov, t))
-    if ops_:
-        for req in dist.batch_isend_irecv(ops_):
-            req.wait()
-    out = dwin[:, own[0] - win[0]:own[1] - win[0]].clone()
-    for ov, t in recvs:
-        out[:, ov[0] - own[0]:ov[1] - own[0]] += t
-    return out
+    reqs = dist.batch_isend_irecv(ops_) if ops_ else []
+    mine = dwin[:, own[0] - win[0]:own[1] - win[0]]
+
+    def add():
+        for ov, t in recvs:
+            mine[:, ov[0] - own[0]:ov[1] - own[0]] += t
+        return mine
+
+    return _Pending(reqs, add)
+
+
+def return_halo_grads(dwin: Tensor, plan: FramePlan, rank: int, group=None) -> Tensor:
+    """Sends the gradient rows of `dwin` that belong to other ranks to their owners, adds what the other
+    ranks send for the own frames, and returns the own frames [B, own frames, HW, X] (a new tensor;
+    `dwin` is left as it was)."""
+    return start_halo_return(dwin.clone(), plan, rank, group).finish()
+
+
+class _GradBuckets:
+    """Parameter gradients summed over the ranks in buckets: each bucket's all-reduce starts as soon as
+    its gradients exist (asynchronous, on the process group's stream) and overlaps the rest of the
+    backward; wait() returns every bucket's summed gradients.  All ranks add the same buckets in the
+    same order."""
+
+    def __init__(self, group):
+        self.group = group
+        self.items: list = []
+
+    def add(self, parts: List[Tensor]) -> None:
+        flat = torch.cat([p.reshape(-1).float() for p in parts])
+        work = dist.all_reduce(flat, group=self.group, async_op=True)
+        self.items.append((flat, [p.shape for p in parts], work))
+
+    def wait(self) -> List[List[Tensor]]:
+        out = []
+        for flat, shapes, work in self.items:
+            work.wait()
+            views, o = [], 0
+            for shp in shapes:
+                n = math.prod(shp)
+                views.append(flat[o:o + n].view(shp))
+                o += n
+            out.append(views)
+        return out
 
 
 class _ShardCfg:
@@ -163,7 +221,17 @@ class _ShardCfg:
 
 
 class DSA3DShardedFunction(torch.autograd.Function):
-    """Forward/backward of one rank's frames of a time-sharded DeformableSlideAttention3D."""
+    """Forward/backward of one rank's frames of a time-sharded DeformableSlideAttention3D.
+
+    Forward: the conv halo of x (max(1, kt//2) frames per side: the offset predictor's 3x3x3 conv and
+    the dw_conv read them) is exchanged while q/k/v of the OWN frames are projected (one GEMM); the
+    offsets and the dw_conv term follow; the K/V window of every rank comes from the largest temporal
+    offset (or the caller's bound); the projected K/V rows of the halo frames are exchanged (not x:
+    no projection runs twice); the attention kernels run on the own queries against the window.
+    Backward: dK/dV accumulate in a float32 window buffer; its halo rows go back to their owners and
+    are added there (so every GEMM is own-frame sized); the transposed convs spread into the conv
+    halo, whose rows also go back; parameter gradients are summed in buckets that overlap the rest
+    of the backward."""
 
     @staticmethod
     def forward(ctx, cfg: _ShardCfg, x, extra_kv, off_in, wq, bq, wk, bk, wv, bv, wo, bo, wd, bd, w1, b1, w2, b2):
@@ -176,7 +244,8 @@ class DSA3DShardedFunction(torch.autograd.Function):
         kt, kh, kw = cfg.kernel
         nh, d, G = cfg.heads, cfg.head_dim, cfg.G
         xl = x.to(dt).reshape(B, nown, HW, C).contiguous()
-        # 1. conv halo (the offset net's 3x3x3 conv and the dw_conv read kt//2 frames around)
+        xo2 = xl.view(-1, C)
+        # 1. conv halo of x, exchanged while q / k / v of the own frames are projected
         cpad = max(1, kt // 2)
         cwins = [conv_window(T, o, cpad) for o in cfg.owns]
         cw = cwins[rank]
@@ -184,9 +253,12 @@ class DSA3DShardedFunction(torch.autograd.Function):
         xc[:, own[0] - cw[0]:own[1] - cw[0]].copy_(xl)
         fetch1 = [[iv for iv in ((cwins[s][0], cfg.owns[s][0]), (cfg.owns[s][1], cwins[s][1])) if iv[0] < iv[1]]
                   for s in range(cfg.world)]
-        exchange_into(xc, cw, xl, FramePlan(cfg.owns, cwins), fetch1, rank, cfg.group)
+        pend = start_exchange(xc, cw, xl, FramePlan(cfg.owns, cwins), fetch1, rank, cfg.group)
+        wqkv = torch.cat([wq, wk, wv], 0).to(dt)
+        qkv = torch.addmm(torch.cat([bq, bk, bv], 0).to(dt), xo2, wqkv.t())  # [own rows, 3C]
+        pend.finish()
         xc2 = xc.view(-1, C)
-        # 2. offsets of the own frames, then the global largest temporal offset
+        # 2. offsets and the dw_conv term of the own frames
         conv3 = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=cw[0], in_frames=cw[1] - cw[0],
                               out_frame0=own[0], out_frames=nown)
         convk = ops.ConvShape(B, T, H, W, C, (kt, kh, kw), in_frame0=cw[0], in_frames=cw[1] - cw[0],
@@ -203,42 +275,51 @@ class DSA3DShardedFunction(torch.autograd.Function):
             off = off_in.reshape(B * nown * HW, -1)
             b2f = None
         wd_kc = ops.conv_weight_kc(wd)
-        D = ops.dwconv_fwd(convk, xc2, wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous(),
-                           epilogue=MSL_EPI_NONE)
+        dwk = (wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous())
         if cfg.offset_bound is not None:
             # the caller bounds |raw offset| (e.g. clipped synthetic offsets): the K/V window follows from the
             # bound alone, with no reduction and no host synchronisation
             dmax = float(cfg.offset_bound) * abs(cfg.oscale)
+            D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
         else:
+            # the largest temporal offset over all ranks sizes every rank's K/V window: it is copied to pinned
+            # host memory right after its reduction, and the host waits for that copy only, while the dw_conv
+            # term (independent of the window) keeps the GPU busy
             amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale, bias=b2f)
             dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=cfg.group)
-            dmax = float(amax[2].item())
+            amax_h = torch.empty(3, dtype=torch.float32, pin_memory=True)
+            amax_h.copy_(amax, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record()
+            D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
+            ready.synchronize()
+            dmax = float(amax_h[2])
         if not math.isfinite(dmax):
             raise FloatingPointError("non-finite offsets: the K/V halo cannot be bounded")
-        # 3. K/V window of every rank (deterministic on all ranks), fetch the remaining frames
+        # 3. K/V window of every rank (deterministic on all ranks): the own projected rows plus the halo
+        #    frames' rows from their owners
         kwins = [kv_frame_range(T, W, kt, o, dmax) for o in cfg.owns]
-        wins = [(min(kwins[s][0], cwins[s][0]), max(kwins[s][1], cwins[s][1])) for s in range(cfg.world)]
-        win = wins[rank]
-        xw = torch.empty(B, win[1] - win[0], HW, C, dtype=dt, device=x.device)
-        xw[:, cw[0] - win[0]:cw[1] - win[0]].copy_(xc)
-        fetch2 = [[iv for iv in ((wins[s][0], cwins[s][0]), (cwins[s][1], wins[s][1])) if iv[0] < iv[1]]
+        kwins = [(min(k[0], o[0]), max(k[1], o[1])) for k, o in zip(kwins, cfg.owns)]
+        kwin = kwins[rank]
+        nkw = kwin[1] - kwin[0]
+        kvw = torch.empty(B, nkw, HW, 2 * C, dtype=dt, device=x.device)
+        kv_own = qkv.view(B, nown, HW, 3 * C)[..., C:]
+        kvw[:, own[0] - kwin[0]:own[1] - kwin[0]].copy_(kv_own)
+        kplan = FramePlan(cfg.owns, kwins)
+        fetch2 = [[iv for iv in ((kwins[s][0], cfg.owns[s][0]), (cfg.owns[s][1], kwins[s][1])) if iv[0] < iv[1]]
                   for s in range(cfg.world)]
-        plan = FramePlan(cfg.owns, wins)
-        exchange_into(xw, win, xl, plan, fetch2, rank, cfg.group)
-        xw2 = xw.view(-1, C)
-        xo2 = xl.view(-1, C)
-        # 4. projections: q on the own rows, k / v on the window
-        wkv = torch.cat([wk, wv], 0).to(dt)
-        q = torch.addmm(bq.to(dt), xo2, wq.to(dt).t())
-        kv = torch.addmm(torch.cat([bk, bv], 0).to(dt), xw2, wkv.t())
+        exchange_into(kvw, kwin, kv_own, kplan, fetch2, rank, cfg.group)
+        kv = kvw.view(-1, 2 * C)
+        q = qkv[:, :C]
         k, v = kv[:, :C], kv[:, C:]
         ek = ev = e2 = None
+        wkv = wqkv[C:]
         if G:
             e2 = extra_kv.reshape(B * G, C).to(dt).contiguous()
             ekv = torch.addmm(torch.cat([bk, bv], 0).to(dt), e2, wkv.t())
             ek, ev = ekv[:, :C], ekv[:, C:]
         sh = ops.DsaShape(B, T, H, W, nh, d, (kt, kh, kw), extra=G, q_frame0=own[0], q_frames=nown,
-                          kv_frame0=win[0], kv_frames=win[1] - win[0], offset_scale=cfg.oscale,
+                          kv_frame0=kwin[0], kv_frames=nkw, offset_scale=cfg.oscale,
                           dropout_p=cfg.dropout_p, dropout_seed=cfg.seed)
         train = any(ctx.needs_input_grad)
         probs = saved = None
@@ -254,12 +335,12 @@ class DSA3DShardedFunction(torch.autograd.Function):
             attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f)
         y = torch.addmm(D, attn, wo.to(dt).t())
         if cfg.capture is not None:
-            cfg.capture.update(xw=xw, win=win, own=own, q=q, kv=kv, hact=hact, off=off, offset_bias=b2f, attn=attn,
-                               lse=lse, y=y)
+            cfg.capture.update(xw=xc, xwin=cw, kvwin=kwin, own=own, q=q, kv=kv, hact=hact, off=off, offset_bias=b2f,
+                               attn=attn, lse=lse, y=y)
         if train:
-            ctx.save_for_backward(xw, q, kv, hact, off, b2f, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc,
-                                  probs, saved)
-            ctx.cfg, ctx.sh, ctx.plan, ctx.cw = cfg, sh, plan, cw
+            ctx.save_for_backward(xc, qkv, kv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f,
+                                  wd_kc, probs, saved)
+            ctx.cfg, ctx.sh, ctx.kplan, ctx.cplan = cfg, sh, kplan, FramePlan(cfg.owns, cwins)
             ctx.in_dtype = x.dtype
             ctx.off_dtype = off_in.dtype if off_in is not None else None
             ctx.extra_dtype = extra_kv.dtype if extra_kv is not None else None
@@ -267,106 +348,104 @@ class DSA3DShardedFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        (xw, q, kv, hact, off, b2f, attn, lse, e2, ek, ev, wq, wkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
+        (xc, qkv, kv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
          saved) = ctx.saved_tensors
         cfg: _ShardCfg = ctx.cfg
         sh: ops.DsaShape = ctx.sh
-        plan: FramePlan = ctx.plan
-        cw = ctx.cw
+        kplan: FramePlan = ctx.kplan
+        cplan: FramePlan = ctx.cplan
         T, H, W, rank = cfg.T, cfg.H, cfg.W, cfg.rank
         HW = H * W
-        own, win = plan.owns[rank], plan.windows[rank]
-        nown, nwin = own[1] - own[0], win[1] - win[0]
-        B = xw.shape[0]
-        C = xw.shape[-1]
+        own, kwin, cw = kplan.owns[rank], kplan.windows[rank], cplan.windows[rank]
+        nown, nkw, ncw = own[1] - own[0], kwin[1] - kwin[0], cw[1] - cw[0]
+        B = xc.shape[0]
+        C = xc.shape[-1]
         dt = cfg.dtype
         kt, kh, kw = cfg.kernel
         G = cfg.G
-        xw2 = xw.view(-1, C)
-        xo2 = xw[:, own[0] - win[0]:own[1] - win[0]].reshape(-1, C)
+        xc2 = xc.view(-1, C)
+        xo2 = xc[:, own[0] - cw[0]:own[1] - cw[0]].reshape(-1, C)
         with torch.autocast("cuda", enabled=False):
             dy2 = dy.reshape(-1, C).to(dt).contiguous()
             dattn = torch.mm(dy2, wo.to(dt))
+            # attention core: dq on the own rows into the [own rows, 3C] gradient buffer, dK / dV accumulated
+            # in float32 over the K/V window; the window's halo rows go back to their owners while the
+            # out_proj and dw_conv gradients run
+            dqkv = torch.empty_like(qkv)
+            dkv_acc = torch.zeros(B * nkw * HW, 2 * C, dtype=torch.float32, device=xc.device)
+            k, v = kv[:, :C], kv[:, C:]
+            _, _, _, doff, dek, dev = ops.attn_bwd(sh, qkv[:, :C], k, v, off, attn, lse, dattn, ek=ek, ev=ev,
+                                                   dq=dqkv[:, :C], dk_acc=dkv_acc[:, :C], dv_acc=dkv_acc[:, C:],
+                                                   probs=probs, saved=saved, doff_dtype=dt, offset_bias=b2f)
+            if cfg.capture is not None:
+                cfg.capture.update(dy2=dy2, dattn=dattn, dq=dqkv[:, :C], dkv=dkv_acc.clone(), doff=doff)
+            kv_ret = start_halo_return(dkv_acc.view(B, nkw, HW, 2 * C), kplan, rank, cfg.group)
             g_wo = _mm_f32(dy2.t(), attn)
             g_bo = dy2.sum(0, dtype=torch.float32)
-            dxw = torch.zeros(B, nwin, HW, C, dtype=torch.float32, device=xw.device)
-
-            def add_frames(rows: Tensor, rng: Range) -> None:
-                dxw[:, rng[0] - win[0]:rng[1] - win[0]] += rows.view(B, rng[1] - rng[0], HW, C).float()
-
-            # dw_conv term: its transposed conv spreads the own dy over the frames kt//2 around
-            pk = conv_window(T, own, kt // 2)
-            convk_t = ops.ConvShape(B, T, H, W, C, (kt, kh, kw), in_frame0=own[0], in_frames=nown,
-                                    out_frame0=pk[0], out_frames=pk[1] - pk[0], zero_outside=True)
-            add_frames(ops.dwconv_bwd_data(convk_t, dy2, wd_kc), pk)
-            convk = ops.ConvShape(B, T, H, W, C, (kt, kh, kw), in_frame0=win[0], in_frames=nwin,
+            convk = ops.ConvShape(B, T, H, W, C, (kt, kh, kw), in_frame0=cw[0], in_frames=ncw,
                                   out_frame0=own[0], out_frames=nown)
             g_wd = torch.zeros_like(wd_kc)
-            g_bd = torch.zeros(C, device=xw.device, dtype=torch.float32)
-            ops.dwconv_bwd_weight(convk, dy2, xw2, g_wd, g_bd)
-            # attention core: dq on the own rows, dk / dv on the window
-            dq = torch.empty_like(q)
-            dkv = torch.empty_like(kv)
-            k, v = kv[:, :C], kv[:, C:]
-            _, _, _, doff, dek, dev = ops.attn_bwd(sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev, dq=dq,
-                                                   dk=dkv[:, :C], dv=dkv[:, C:], probs=probs, saved=saved,
-                                                   doff_dtype=dt, offset_bias=b2f)
-            add_frames(_mm_f32(dq, wq.to(dt)), own)
-            dxw += _mm_f32(dkv, wkv).view(B, nwin, HW, C)
-            g_wq = _mm_f32(dq.t(), xo2)
-            g_bq = dq.sum(0, dtype=torch.float32)
-            g_wkv = _mm_f32(dkv.t(), xw2)
-            g_bkv = dkv.sum(0, dtype=torch.float32)
-            g_wk, g_wv = g_wkv[:C], g_wkv[C:]
-            g_bk, g_bv = g_bkv[:C], g_bkv[C:]
-            d_extra = None
-            if G:
-                dekv = torch.cat([dek, dev], 1)
-                d_extra = torch.mm(dekv, wkv.float()).view(B, G, C)
-                g_ekv = torch.mm(dekv.t(), e2.float())
-                g_wk = g_wk + g_ekv[:C]
-                g_wv = g_wv + g_ekv[C:]
-                sums = dekv.sum(0)
-                g_bk = g_bk + sums[:C]
-                g_bv = g_bv + sums[C:]
-            if cfg.capture is not None:
-                cfg.capture.update(dy2=dy2, dattn=dattn, dq=dq, dkv=dkv, doff=doff)
+            g_bd = torch.zeros(C, device=xc.device, dtype=torch.float32)
+            ops.dwconv_bwd_weight(convk, dy2, xc2, g_wd, g_bd)
+            # parameter gradients are summed over the ranks bucket by bucket, overlapping the backward
+            buckets = _GradBuckets(cfg.group)
+            buckets.add([g_wo, g_bo, g_wd, g_bd])
+            # transposed convs: the dw_conv term and the offset predictor spread into the conv halo
+            dxc = torch.zeros(B * ncw * HW, C, dtype=torch.float32, device=xc.device)
+            convk_t = ops.ConvShape(B, T, H, W, C, (kt, kh, kw), in_frame0=own[0], in_frames=nown,
+                                    out_frame0=cw[0], out_frames=ncw, zero_outside=True)
+            ops.dwconv_bwd_data(convk_t, dy2, wd_kc, out=dxc, accumulate=True)
             predictor = hact is not None
             d_off_in = None
             if predictor:
                 dh = _mm_f32(doff, w2m.to(dt))
                 g_w2 = _mm_f32(doff.t(), hact)
                 g_b2 = doff.sum(0, dtype=torch.float32)
-                conv3 = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=win[0], in_frames=nwin, out_frame0=own[0],
+                conv3 = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=cw[0], in_frames=ncw, out_frame0=own[0],
                                       out_frames=nown)
-                du = ops.dwconv_fwd(conv3, xw2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh,
+                du = ops.dwconv_fwd(conv3, xc2, w1_kc, b1f, epilogue=MSL_EPI_GELU_GRAD, aux=dh,
                                     out_dtype=torch.float32)
-                p3 = conv_window(T, own, 1)
-                conv3_t = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=own[0], in_frames=nown, out_frame0=p3[0],
-                                        out_frames=p3[1] - p3[0], zero_outside=True)
-                add_frames(ops.dwconv_bwd_data(conv3_t, du, w1_kc), p3)
+                conv3_t = ops.ConvShape(B, T, H, W, C, (3, 3, 3), in_frame0=own[0], in_frames=nown, out_frame0=cw[0],
+                                        out_frames=ncw, zero_outside=True)
+                ops.dwconv_bwd_data(conv3_t, du, w1_kc, out=dxc, accumulate=True)
                 g_w1 = torch.zeros_like(w1_kc)
-                g_b1 = torch.zeros(C, device=xw.device, dtype=torch.float32)
-                ops.dwconv_bwd_weight(conv3, du, xw2, g_w1, g_b1)
+                g_b1 = torch.zeros(C, device=xc.device, dtype=torch.float32)
+                ops.dwconv_bwd_weight(conv3, du, xc2, g_w1, g_b1)
+                buckets.add([g_w1, g_b1, g_w2, g_b2])
             elif ctx.needs_input_grad[3]:
                 d_off_in = doff.view(B, nown * HW, -1).to(ctx.off_dtype)
-            # halo gradients back to their owners; parameter gradients summed over the ranks
-            dx_own = return_halo_grads(dxw, plan, rank, cfg.group)
-            parts = [g_wq, g_bq, g_wk, g_bk, g_wv, g_bv, g_wo, g_bo, g_wd, g_bd]
-            if predictor:
-                parts += [g_w1, g_b1, g_w2, g_b2]
-            if d_extra is not None:
-                parts.append(d_extra)
-            flat = torch.cat([p.reshape(-1).float() for p in parts])
-            dist.all_reduce(flat, group=cfg.group)
-            outs, o = [], 0
-            for p in parts:
-                outs.append(flat[o:o + p.numel()].view(p.shape))
-                o += p.numel()
-        (g_wq, g_bq, g_wk, g_bk, g_wv, g_bv, g_wo, g_bo, g_wd, g_bd) = outs[:10]
+            conv_ret = start_halo_return(dxc.view(B, ncw, HW, C), cplan, rank, cfg.group)
+            # the own K/V rows, with every rank's contributions, in the compute dtype next to dq
+            dkv_own = kv_ret.finish()  # [B, nown, HW, 2C] float32 view of the window accumulator
+            rows_s = nown * HW
+            for b in range(B):
+                ops.convert_f32(dkv_own[b].reshape(rows_s, 2 * C), dqkv[b * rows_s:(b + 1) * rows_s, C:])
+            d_extra = None
+            g_ekv = sums = None
+            if G:
+                dekv = torch.cat([dek, dev], 1)
+                d_extra = torch.mm(dekv, wqkv[C:].float()).view(B, G, C)
+                g_ekv = torch.mm(dekv.t(), e2.float())
+                sums = dekv.sum(0)
+            g_wqkv = _mm_f32(dqkv.t(), xo2)
+            g_bqkv = dqkv.sum(0, dtype=torch.float32)
+            if G:
+                g_wqkv[C:] += g_ekv
+                g_bqkv[C:] += sums
+            buckets.add([g_wqkv, g_bqkv] + ([d_extra] if d_extra is not None else []))
+            dx = _mm_f32(dqkv, wqkv)  # [own rows, C] float32
+            dx_conv = conv_ret.finish()  # [B, nown, HW, C] float32
+            dx = dx.view(B, nown, HW, C).add_(dx_conv)
+            summed = buckets.wait()
+        g_wo, g_bo, g_wd, g_bd = summed[0]
+        i = 1
         if predictor:
-            g_w1, g_b1, g_w2, g_b2 = outs[10:14]
-        d_extra = outs[-1] if G else None
+            g_w1, g_b1, g_w2, g_b2 = summed[1]
+            i = 2
+        g_wqkv, g_bqkv = summed[i][:2]
+        d_extra = summed[i][2] if G else None
+        g_wq, g_wk, g_wv = g_wqkv[:C], g_wqkv[C:2 * C], g_wqkv[2 * C:]
+        g_bq, g_bk, g_bv = g_bqkv[:C], g_bqkv[C:2 * C], g_bqkv[2 * C:]
         pd = cfg.param_dtypes
 
         def conv_w(gkc, k3):
@@ -381,7 +460,7 @@ class DSA3DShardedFunction(torch.autograd.Function):
                       g_w2.reshape(w2m.shape[0], C, 1, 1, 1).to(pd[12]), g_b2.to(pd[13]))
         else:
             grads += (None, None, None, None)
-        dx_out = dx_own.reshape(B, nown * HW, C).to(ctx.in_dtype)
+        dx_out = dx.reshape(B, nown * HW, C).to(ctx.in_dtype)
         de = d_extra.to(ctx.extra_dtype) if d_extra is not None else None
         return (None, dx_out, de, d_off_in) + grads
 

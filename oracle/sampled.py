@@ -136,7 +136,8 @@ def check(module, cap: dict, video_shape, *, batch: int, dtype: torch.dtype, n_r
     if sharded:
         qb, kb, vb = cap["q"], cap["kv"][:, :C], cap["kv"][:, C:]
         dqb, dkb, dvb = cap["dq"], cap["dkv"][:, :C], cap["dkv"][:, C:]
-        xbuf_t, xf0, xnf = cap["xw"].reshape(-1, C), cap["win"][0], cap["win"][1] - cap["win"][0]
+        xr = cap.get("xwin", cap.get("win"))  # frames of the captured x buffer
+        xbuf_t, xf0, xnf = cap["xw"].reshape(-1, C), xr[0], xr[1] - xr[0]
     else:
         qb, kb, vb = cap["qkv"][:, :C], cap["qkv"][:, C:2 * C], cap["qkv"][:, 2 * C:]
         dqb, dkb, dvb = cap["dqkv"][:, :C], cap["dqkv"][:, C:2 * C], cap["dqkv"][:, 2 * C:]

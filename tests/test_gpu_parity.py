@@ -665,12 +665,13 @@ def test_module_bf16_training_uses_tensor_core_backward(monkeypatch):
     assert seen == [True]
 
 
-def test_offsets_absmax_with_bias():
-    """Per-axis max |(offsets + bias) * scale| over a strided offsets view, with and without the bias."""
-    rng = np.random.default_rng(41)
-    heads, taps = 3, 27
+@pytest.mark.parametrize("heads,taps,pad", [(3, 27, 5), (3, 27, 1), (4, 147, 0)])
+def test_offsets_absmax_with_bias(heads, taps, pad):
+    """Per-axis max |(offsets + bias) * scale| over a strided offsets view, with and without the bias:
+    scalar rows (row stride not a multiple of 4), 16-byte rows with a tail, 16-byte rows only."""
+    rng = np.random.default_rng(41 + pad)
     n = heads * taps * 3
-    off = (rng.normal(size=(257, n + 5)) * 2.0).astype(np.float32)
+    off = (rng.normal(size=(257, n + pad)) * 2.0).astype(np.float32)
     bias = (rng.normal(size=(n,)) * 3.0).astype(np.float32)
     offt = torch.from_numpy(off).to(DEV)[:, :n]
     for b in (None, bias):

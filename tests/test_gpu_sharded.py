@@ -30,7 +30,7 @@ def _fro(a, b):
     return float((a - b).norm() / b.norm().clamp_min(1e-30))
 
 
-def _worker(rank, world, port, dtype_name, q):
+def _worker(rank, world, port, dtype_name, q, B=1, inject=False):
     import torch.distributed as dist
 
     import megaslide_b200 as msl
@@ -44,7 +44,7 @@ def _worker(rank, world, port, dtype_name, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
     try:
         dt = getattr(torch, dtype_name)
-        B, T, H, W, C, nh, ks = 1, 8, 6, 10, 64, 2, (3, 5, 5)
+        T, H, W, C, nh, ks = 8, 6, 10, 64, 2, (3, 5, 5)
         torch.manual_seed(7)
         m = msl.DeformableSlideAttention3D(C, nh, ks, offset_scale=3.0)
         with torch.no_grad():
@@ -55,24 +55,35 @@ def _worker(rank, world, port, dtype_name, q):
         g.manual_seed(11)
         x = torch.randn(B, T * H * W, C, device=dev, dtype=dt, generator=g)
         gy = torch.randn(B, T * H * W, C, device=dev, dtype=dt, generator=g)
+        off = None
+        if inject:  # raw offsets clipped to +-2 (x offset_scale 3 = up to 6 voxels) in place of the predictor's
+            K3 = nh * ks[0] * ks[1] * ks[2] * 3
+            off = (torch.randn(B, T * H * W, K3, device=dev, generator=g) * 1.5).clamp_(-2.0, 2.0)
         # unsharded
         xf = x.clone().requires_grad_(True)
-        yf = m(xf, (T, H, W))
+        yf = m(xf, (T, H, W)) if off is None else m.forward_with_offsets(xf, (T, H, W), off)
         yf.backward(gy)
-        ref_grads = [p.grad.clone() for p in m.parameters()]
+        ref_grads = [None if p.grad is None else p.grad.clone() for p in m.parameters()]
         for p in m.parameters():
             p.grad = None
         # sharded
         own = shard_ranges(T, world)[rank]
         rows = slice(own[0] * H * W, own[1] * H * W)
         xs = x[:, rows].clone().requires_grad_(True)
-        ys = TimeShardedDSA3D(m)(xs, (T, H, W))
+        sm = TimeShardedDSA3D(m)
+        if off is None:
+            ys = sm(xs, (T, H, W))
+        else:
+            ys = sm.forward_with_offsets(xs, (T, H, W), off[:, rows].contiguous(), offset_bound=2.0)
         ys.backward(gy[:, rows])
         torch.cuda.synchronize()
         res = {"y": _rel(ys, yf[:, rows]), "dx": _fro(xs.grad, xf.grad[:, rows]),
                "dx_max": _rel(xs.grad, xf.grad[:, rows])}
-        scale = max(float(rg.double().norm()) for rg in ref_grads)
+        scale = max(float(rg.double().norm()) for rg in ref_grads if rg is not None)
         for (name, p), rg in zip(m.named_parameters(), ref_grads):
+            if rg is None:  # the offset predictor with injected offsets: no gradient on either side
+                assert p.grad is None, name
+                continue
             if name == "k_proj.bias":
                 # exactly zero in exact arithmetic (a key bias shifts all scores of a query
                 # equally): both sides are rounding noise, compared with the gradient scale
@@ -84,8 +95,10 @@ def _worker(rank, world, port, dtype_name, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("dtype_name,tol", [("float32", 1e-4), ("bfloat16", 2e-2)])
-def test_time_sharded_matches_unsharded_on_two_gpus(dtype_name, tol):
+@pytest.mark.parametrize("dtype_name,tol,B,inject", [("float32", 1e-4, 1, False), ("bfloat16", 2e-2, 1, False),
+                                                     ("bfloat16", 2e-2, 2, True)])
+def test_time_sharded_matches_unsharded_on_two_gpus(dtype_name, tol, B, inject):
+    """Learned offsets (float32 and bf16), and injected offsets with a caller bound on a batch of 2."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -94,7 +107,7 @@ def test_time_sharded_matches_unsharded_on_two_gpus(dtype_name, tol):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, dtype_name, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, dtype_name, q, B, inject)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]

@@ -46,11 +46,15 @@ extern "C" {
 
 /* bits of the optional device status word */
 #define MSL_STATUS_HALO_MISS 1u  /* a sample corner fell in a frame the K/V buffers do not hold */
-#define MSL_STATUS_TC_RANGE 2u   /* tensor-core path: a tile's key envelope needed more than 255
-                                    chunks per axis (offsets of hundreds of voxels); its results are
-                                    not valid - rerun with MSL_ALGO_SIMT */
+#define MSL_STATUS_TC_RANGE 2u   /* tensor-core path: a tile's key envelope exceeded what its sample
+                                    records encode (a temporal span over 29 frames, or over 255 rows or
+                                    columns: offsets of tens of voxels); the kernel computed that tile
+                                    with the CUDA-core gather instead, forward and backward alike, so
+                                    the results are valid (informational) */
 #define MSL_STATUS_TIMEOUT 4u    /* tensor-core path: a CTA's TMA copies did not complete within a second;
-                                    it stopped waiting and its results are not valid */
+                                    it stopped waiting, skipped every phase that reads the copied keys,
+                                    and its results are not valid (copies it issued may have still been
+                                    in flight when it exited) */
 
 /* kernel family */
 #define MSL_ALGO_AUTO 0 /* tensor-core envelope kernels when supported (bf16, head_dim % 8 == 0, <= 128) */

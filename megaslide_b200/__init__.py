@@ -6,8 +6,10 @@ hand-written kernels of ``libmegaslide_b200.so`` (C ABI in ``include/megaslide_b
 """
 
 from . import ops
+from .ops import check_status
 from ._lib import MslError, launch_count, library_path
 from .attention import DeformableSlideAttention3D, DSA3DFunction
 
-__all__ = ["DeformableSlideAttention3D", "DSA3DFunction", "MslError", "ops", "launch_count", "library_path"]
+__all__ = ["DeformableSlideAttention3D", "DSA3DFunction", "MslError", "ops", "launch_count", "library_path",
+           "check_status"]
 __version__ = "0.1.0"

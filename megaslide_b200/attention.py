@@ -92,18 +92,22 @@ class DSA3DFunction(torch.autograd.Function):
             ekv = torch.addmm(torch.cat([bk, bv], 0).to(dt), e2, torch.cat([wk, wv], 0).to(dt).t())
             ek, ev = ekv[:, :C], ekv[:, C:]
         train = any(ctx.needs_input_grad)
+        sw = ops.status_word(x2.device)
+        sw.poll()  # raises if an earlier call produced invalid results
         probs = saved = None
         if train and ops.wants_probs(sh, dt):
             # the tensor-core backward reads the forward's per-sample softmax weights and records
             probs, saved = ops.saved_buffers(sh, dt, x2.device)
             try:
-                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved, offset_bias=b2f)
+                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved, offset_bias=b2f,
+                                         status=sw.word)
             except MslError as e:
                 if e.code != MSL_ERR_UNSUPPORTED:
                     raise
                 probs = saved = None
         if probs is None:
-            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f)
+            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f, status=sw.word)
+        sw.post()
         y = torch.addmm(D, attn, wo.to(dt).t())
         if cfg.capture is not None:
             cfg.capture.update(x2=x2, qkv=qkv, hact=hact, off=off, offset_bias=b2f, attn=attn, lse=lse, y=y)
@@ -138,10 +142,12 @@ class DSA3DFunction(torch.autograd.Function):
             # deformable attention core -> dq, dk, dv written straight into one [BN, 3C] buffer
             dqkv = torch.empty_like(qkv)
             q, k, v = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
+            sw = ops.status_word(dy2.device)
             _, _, _, doff, dek, dev = ops.attn_bwd(
                 sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev,
                 dq=dqkv[:, :C], dk=dqkv[:, C:2 * C], dv=dqkv[:, 2 * C:], probs=probs, saved=saved, doff_dtype=dt,
-                offset_bias=b2f)
+                offset_bias=b2f, status=sw.word)
+            sw.post()
             # q/k/v projections; dx accumulates in float32 across the three branches (the depthwise
             # convs add their transposed convolutions into it)
             dx = _mm_f32(dqkv, wqkv)

@@ -333,6 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
     }
   }
   __syncthreads();
+  if (overflow) {  // the records cannot encode this envelope: the CUDA-core gather computes the tile
+    tile_fallback<DCH, false>(P, T);
+    return;  // no copy was issued yet
+  }
   for (int s = 0; s < jper; ++s) {  // hit list: every active sample once, grouped by (chunk, frame) bucket
     const int j = js + s;
     int bk = -1;
@@ -371,6 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         cp_async_wait_all();
       }
       __syncthreads();
+      if (tma && tile_dead(S.dead)) break;  // a wait gave up: nothing more reads the key buffer
       dense_tiles<DCH, kWPG>(S.kbuf, qgrp, L.rs, grow_s, L.sld, part, cur.m);
       __syncthreads();
       have = chunk_next(E, S.mask, masks, nz, k);
@@ -507,6 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
         cp_async_wait_all();
       }
       __syncthreads();
+      if (tma && tile_dead(S.dead)) break;  // a wait gave up: nothing more reads the key buffer
       dq_product<DCH, kTPW, kKS>(tp, r, S.kbuf, L.rs, nt0, nt1, k.m, o, kpar);
     }
   }
@@ -683,6 +689,10 @@ bool make_key_maps(KeyMaps* maps, const AttnParams& P, int rs) {
       if (make_key_map(&maps->k[j][h], P, P.k, P.k_ld, rs, 8 * (j + 1), 1 << h) &&
           make_key_map(&maps->v[j][h], P, P.v, P.v_ld, rs, 8 * (j + 1), 1 << h))
         maps->have |= 1 << (4 * j + h);
+  // test hook for the bounded TMA wait: MSL_TEST_TMA_NO_COPY=1 arms every chunk's byte count but issues
+  // no copy, so each CTA's first wait runs out (about a second) and sets MSL_STATUS_TIMEOUT
+  const char* nocopy = getenv("MSL_TEST_TMA_NO_COPY");
+  if (nocopy && strcmp(nocopy, "1") == 0 && (maps->have & 1)) maps->have |= static_cast<int>(0x80000000u);
   return maps->have & 1;  // the one-row 8-column boxes serve every chunk width
 }
 

@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include "dsa_attn.cuh"
+#include "dsa_simt.cuh"
 #include "msl_common.cuh"
 
 namespace msl {
@@ -616,6 +617,9 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
   constexpr int kIW = 4, kW0 = kWarps - kIW;
   if (threadIdx.x < 32 * kW0) return;
   const int lane = threadIdx.x & 31, wid = (threadIdx.x >> 5) - kW0;
+  // bit 31 of `have` (set only by the MSL_TEST_TMA_NO_COPY=1 test hook): arm the barrier's byte count
+  // but issue no copy, so the bounded wait runs out with nothing in flight
+  const bool nocopy = have < 0;
   const int nr = chunk_yb(E, k) - chunk_ya(E, k) + 1;  // rows of one plane
   const int nkeys = nr * E.kst;                         // keys of one plane
   const int mi = (E.kst >> 3) - 1;
@@ -681,7 +685,7 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
   if (first && (on[0] || on[1])) fence_proxy_async();
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
-    if (!on[u] || (lane + 32 * u) % kIW != wid) continue;
+    if (nocopy || !on[u] || (lane + 32 * u) % kIW != wid) continue;
     const int b = lane + 32 * u;
     const int pl = b >= nbp ? 1 : 0;
     const int hi = bh[u] == 8 ? 3 : (bh[u] == 4 ? 2 : (bh[u] == 2 ? 1 : 0));
@@ -689,13 +693,16 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
                 wide ? &maps[mi][hi] : &maps[0][0], bar, T.head * P.d, chunk_xa(E, k) + bcol[u],
                 chunk_ya(E, k) + brow[u], E.zlo + k.zr * E.pg + pl - P.kv_frame0, T.b);
   }
-  if (wid == 0 && lane < 2 && tail[lane])  // columns W .. W+7: all outside the volume
+  if (!nocopy && wid == 0 && lane < 2 && tail[lane])  // columns W .. W+7: all outside the volume
     tma_load_5d(smem_u32(kbuf) + static_cast<uint32_t>((lane * E.kpp + nkeys) * rs * 2), &maps[0][0], bar,
                 T.head * P.d, P.W, 0, 0, T.b);
 }
 
 // Waits for the TMA copies of phase `parity` on mbarrier bar.  Bounded: after about a second the CTA
-// stops waiting and issuing (flag *dead, status MSL_STATUS_TIMEOUT); its results are then invalid.
+// stops waiting and issuing (flag *dead, status MSL_STATUS_TIMEOUT); after the CTA barrier that follows
+// every wait, the chunk loops read *dead (tile_dead) and leave before any phase that reads the key
+// buffer.  The tile's results are then invalid, and copies that were issued but never completed may
+// still be in flight when the CTA exits.
 __device__ __forceinline__ void wait_keys(uint32_t bar, uint32_t parity, volatile int* dead, uint32_t* status) {
   if (mbar_try_wait(bar, parity) || *dead) return;
   const unsigned long long t0 = global_ns();
@@ -708,6 +715,9 @@ __device__ __forceinline__ void wait_keys(uint32_t bar, uint32_t parity, volatil
     }
   }
 }
+
+// true once a TMA wait of this CTA gave up (read after a CTA barrier: the same on every thread)
+__device__ __forceinline__ bool tile_dead(const int* dead) { return *reinterpret_cast<const volatile int*>(dead) != 0; }
 
 // zeroes rows 0..ROWS-1 of the 16-key tiles of mask m in a dense fp32 / int32 tile
 template <int ROWS>
@@ -865,6 +875,33 @@ __device__ __forceinline__ void dq_product(const __nv_bfloat16* tb, int r, const
         mma16816(o[jj], a, b0, b1);
       }
     }
+  }
+}
+
+// The tile's queries through the CUDA-core gather (dsa_simt.cuh), forward (BWD false: out, lse) or
+// backward (dq, d(offsets), dK / dV atomics into the float32 accumulators): used when the tile's key
+// envelope does not fit the sample records (temporal span over 29 frames, or over 255 rows or columns).
+// The forward and the backward take this decision from the same envelope, so a tile runs the same
+// formulation both ways.  Every thread of the CTA calls it; warp w takes queries w and w + 16.
+template <int DCH, bool BWD>
+__device__ __forceinline__ void tile_fallback(const AttnParams& P, const TileCtx& T) {
+  constexpr int MAXC = (DCH + 3) / 4;
+  const int warp = threadIdx.x >> 5;
+  for (int q = warp; q < kQ; q += kWarps) {
+    int qh, qw;
+    query_hw(T, q >> 4, q & 15, qh, qw);
+    if (qh >= P.H || qw >= P.W) continue;  // warp-uniform
+    QueryPos qp;
+    qp.b = T.b;
+    qp.head = T.head;
+    qp.tg = T.tg;
+    qp.h = qh;
+    qp.w = qw;
+    qp.r = (static_cast<long long>(T.tl) * P.H + qh) * P.W + qw;
+    if constexpr (BWD)
+      bwd_query<__nv_bfloat16, 8, MAXC>(P, qp);
+    else
+      fwd_query<__nv_bfloat16, 8, MAXC>(P, qp);
   }
 }
 

@@ -294,6 +294,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   // records hold t0 - zlo + 1 in 5 bits and h0 - ylo, w0 - xlo in 8 bits
   const bool overflow = any && (E.zhi - E.zlo + 2 > 31 || E.yhi - E.ylo > 255 || E.xhi - E.xlo > 255);
   if (overflow && threadIdx.x == 0 && P.status) atomicOr(P.status, MSL_STATUS_TC_RANGE);
+  if (overflow) {  // the forward computed this tile with the CUDA-core gather: so does the backward
+    tile_fallback<DCH, true>(P, T);
+    return;  // no copy was issued yet
+  }
   const bool work = any && !overflow;
   const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
   const bool fsplit = split && !masks;  // chunks of a plane share one hit bucket: filter the hits
@@ -392,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
         cp_async_wait_all();
       }
       __syncthreads();
+      if (tma && tile_dead(S.dead)) break;  // a wait gave up: nothing more reads the key buffer
       dense_tiles<DCH, kWPG>(S.kbuf, S.dos + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, cur.m);
       __syncthreads();
       have = chunk_next(E, S.mask, masks, nz, k);
@@ -492,6 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
         cp_async_wait_all();
       }
       __syncthreads();  // keys landed; the previous chunk's dV flush is done with key_off and sa
+      if (tma && tile_dead(S.dead)) break;  // a wait gave up: nothing more reads the key buffer
       for (int i = threadIdx.x; i < __popc(cur.m) * 16; i += kThreads) {
         const int key = nth_bit(cur.m, i >> 4) * 16 + (i & 15);
         S.key_off[key] = chunk_key_row(P, E, cur, key);

@@ -72,6 +72,72 @@ def _call(name: str, dev: torch.device, fn):
     return rc
 
 
+class StatusWord:
+    """The per-device status word the attention kernels OR their MSL_STATUS_* bits into (device int32),
+    read back without stalling the host: after every call an asynchronous copy into pinned memory is
+    enqueued with an event, and the next call (poll) reads that copy once its event has completed.  A
+    halo miss or a timed-out TMA wait (results not valid) raises MslError there, at most one call late;
+    check() reads the word synchronously.  MSL_STATUS_TC_RANGE is informational (the kernels computed
+    such tiles with the CUDA-core gather)."""
+
+    BAD = _lib.MSL_STATUS_HALO_MISS | _lib.MSL_STATUS_TIMEOUT
+
+    def __init__(self, device: torch.device):
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event: Optional[torch.cuda.Event] = None
+        self.seen = 0  # every bit observed so far (TC_RANGE included)
+
+    def post(self) -> None:
+        with torch.cuda.device(self.word.device):
+            self.host.copy_(self.word, non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record()
+
+    def _raise_if_bad(self, v: int) -> None:
+        self.seen |= v
+        if v & self.BAD:
+            self.word.zero_()
+            what = []
+            if v & _lib.MSL_STATUS_HALO_MISS:
+                what.append("a sample corner fell outside the K/V frames the call was given (halo miss)")
+            if v & _lib.MSL_STATUS_TIMEOUT:
+                what.append("a tensor-core CTA's TMA copies did not complete within a second")
+            raise _lib.MslError("msl_dsa_attn", _lib.MSL_ERR_CUDA,
+                                "a previous attention call produced invalid results: " + "; ".join(what))
+
+    def poll(self) -> None:
+        if self.event is not None and self.event.query():
+            self.event = None
+            self._raise_if_bad(int(self.host[0]))
+
+    def check(self) -> int:
+        """Synchronous: raises on a bad bit (and clears the word), else returns the word's bits
+        (MSL_STATUS_TC_RANGE once a tile took the CUDA-core fallback)."""
+        self.event = None
+        v = int(self.word.item())
+        self._raise_if_bad(v)
+        return v
+
+
+_STATUS: dict = {}
+
+
+def status_word(device: torch.device) -> StatusWord:
+    """The process-wide StatusWord of a CUDA device."""
+    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    sw = _STATUS.get(key)
+    if sw is None:
+        sw = _STATUS[key] = StatusWord(torch.device("cuda", key))
+    return sw
+
+
+def check_status(device=None) -> int:
+    """Synchronously checks the attention kernels' status word of `device` (default: current): raises
+    MslError if a call produced invalid results, else returns the informational bits seen so far."""
+    return status_word(device if device is not None else torch.device("cuda", torch.cuda.current_device())).check()
+
+
 def _need_cuda(*ts):
     for t in ts:
         if t is not None and not t.is_cuda:

@@ -255,7 +255,10 @@ class DSA3DShardedFunction(torch.autograd.Function):
                   for s in range(cfg.world)]
         pend = start_exchange(xc, cw, xl, FramePlan(cfg.owns, cwins), fetch1, rank, cfg.group)
         wqkv = torch.cat([wq, wk, wv], 0).to(dt)
-        qkv = torch.addmm(torch.cat([bq, bk, bv], 0).to(dt), xo2, wqkv.t())  # [own rows, 3C]
+        bqkv = torch.cat([bq, bk, bv], 0).to(dt)
+        learned = off_in is None and cfg.offset_bound is None
+        if not learned:  # no host wait below: the projection overlaps the conv-halo exchange
+            qkv = torch.addmm(bqkv, xo2, wqkv.t())  # [own rows, 3C]
         pend.finish()
         xc2 = xc.view(-1, C)
         # 2. offsets and the dw_conv term of the own frames
@@ -283,14 +286,15 @@ class DSA3DShardedFunction(torch.autograd.Function):
             D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
         else:
             # the largest temporal offset over all ranks sizes every rank's K/V window: it is copied to pinned
-            # host memory right after its reduction, and the host waits for that copy only, while the dw_conv
-            # term (independent of the window) keeps the GPU busy
+            # host memory right after its reduction, and the host waits for that copy only, while the q/k/v
+            # projection and the dw_conv term (independent of the window) keep the GPU busy
             amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale, bias=b2f)
             dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=cfg.group)
             amax_h = torch.empty(3, dtype=torch.float32, pin_memory=True)
             amax_h.copy_(amax, non_blocking=True)
             ready = torch.cuda.Event()
             ready.record()
+            qkv = torch.addmm(bqkv, xo2, wqkv.t())  # [own rows, 3C]: GPU work while the host waits
             D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
             ready.synchronize()
             dmax = float(amax_h[2])
@@ -322,17 +326,21 @@ class DSA3DShardedFunction(torch.autograd.Function):
                           kv_frame0=kwin[0], kv_frames=nkw, offset_scale=cfg.oscale,
                           dropout_p=cfg.dropout_p, dropout_seed=cfg.seed)
         train = any(ctx.needs_input_grad)
+        sw = ops.status_word(x.device)
+        sw.poll()  # raises if an earlier call produced invalid results (e.g. a halo miss)
         probs = saved = None
         if train and ops.wants_probs(sh, dt):
             probs, saved = ops.saved_buffers(sh, dt, x.device)
             try:
-                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved, offset_bias=b2f)
+                attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, probs=probs, saved=saved, offset_bias=b2f,
+                                         status=sw.word)
             except MslError as e:
                 if e.code != MSL_ERR_UNSUPPORTED:
                     raise
                 probs = saved = None
         if probs is None:
-            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f)
+            attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f, status=sw.word)
+        sw.post()
         y = torch.addmm(D, attn, wo.to(dt).t())
         if cfg.capture is not None:
             cfg.capture.update(xw=xc, xwin=cw, kvwin=kwin, own=own, q=q, kv=kv, hact=hact, off=off, offset_bias=b2f,
@@ -374,9 +382,12 @@ class DSA3DShardedFunction(torch.autograd.Function):
             dqkv = torch.empty_like(qkv)
             dkv_acc = torch.zeros(B * nkw * HW, 2 * C, dtype=torch.float32, device=xc.device)
             k, v = kv[:, :C], kv[:, C:]
+            sw = ops.status_word(xc.device)
             _, _, _, doff, dek, dev = ops.attn_bwd(sh, qkv[:, :C], k, v, off, attn, lse, dattn, ek=ek, ev=ev,
                                                    dq=dqkv[:, :C], dk_acc=dkv_acc[:, :C], dv_acc=dkv_acc[:, C:],
-                                                   probs=probs, saved=saved, doff_dtype=dt, offset_bias=b2f)
+                                                   probs=probs, saved=saved, doff_dtype=dt, offset_bias=b2f,
+                                                   status=sw.word)
+            sw.post()
             if cfg.capture is not None:
                 cfg.capture.update(dy2=dy2, dattn=dattn, dq=dqkv[:, :C], dkv=dkv_acc.clone(), doff=doff)
             kv_ret = start_halo_return(dkv_acc.view(B, nkw, HW, 2 * C), kplan, rank, cfg.group)

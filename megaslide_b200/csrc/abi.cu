@@ -293,7 +293,7 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
     P.extra_p = reinterpret_cast<float*>(ws + L.xp);
     P.dek = io->dek; P.dev = io->dev;
   }
-  // tensor-core backward: bf16, no extra keys, softmax weights saved by the forward, aligned rows
+  // tensor-core backward: bf16, softmax weights saved by the forward, aligned rows
   msl::TcLaunch TL{};
   bool use_tc = false;
   if (geom->algo != MSL_ALGO_SIMT && P.probs && P.saved) {
@@ -306,8 +306,9 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
     if (use_tc) use_tc = msl::tc_bwd_plan(P, TL, tc_smem_limit());
   }
   if (geom->algo == MSL_ALGO_TC && !use_tc)
-    return fail(MSL_ERR_UNSUPPORTED, "tensor-core backward needs probs and saved from the tensor-core forward, bf16, no extra keys, "
-                                     "head_dim %% 8 == 0 in [16,128] and 16-byte aligned rows");
+    return fail(MSL_ERR_UNSUPPORTED, "tensor-core backward needs probs and saved from the tensor-core forward, bf16, "
+                                     "at most one key-buffer chunk of extra keys, head_dim %% 8 == 0 in [16,128] and "
+                                     "16-byte aligned rows");
   int vec = 1, maxc = 1;
   rc = choose_chunking(P, {{io->q, io->q_ld}, {io->k, io->k_ld}, {io->v, io->v_ld}, {io->out, io->out_ld},
                            {io->dout, io->dout_ld}, {io->dq, io->dq_ld},
@@ -335,13 +336,14 @@ int msl_dsa_attn_bwd(const msl_dsa_geometry* geom, const msl_dsa_bwd_io* io, voi
     if (e != cudaSuccess) return cuda_fail(e, "clearing dek/dev");
   }
   if (use_tc) {
-    e = msl::launch_attn_bwd_tc(P, TL, s);
+    e = msl::launch_attn_bwd_tc(P, TL, s);  // the tensor-core kernel, then its CUDA-core fallback tiles
     if (e != cudaSuccess) return cuda_fail(e, "dsa_bwd_tc_kernel launch");
+    g_launches.fetch_add(2, std::memory_order_relaxed);
   } else {
     e = msl::launch_attn_bwd(P, vec, maxc, s);
     if (e != cudaSuccess) return cuda_fail(e, "dsa_bwd_kernel launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
   }
-  g_launches.fetch_add(1, std::memory_order_relaxed);
   if (P.G > 0) {
     e = msl::launch_attn_extra_grad(P, s);
     if (e != cudaSuccess) return cuda_fail(e, "dsa_extra_grad_kernel launch");

@@ -99,23 +99,6 @@ size_t smem_fixed(const AttnParams& P, int rs) {
 // groups above, for registers)
 __host__ __device__ constexpr int pv_channel_groups(int dch) { return dch <= 9 ? 1 : 2; }
 
-// loads G extra keys / values of this head into kbuf rows 0..G-1 (zero up to gp)
-template <int DCH>
-__device__ __forceinline__ void load_extra(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
-                                           const void* src, int gp) {
-  const __nv_bfloat16* eb = static_cast<const __nv_bfloat16*>(src) + static_cast<long long>(T.b) * P.G * P.e_ld +
-                            T.head * P.d;
-  for (int idx = threadIdx.x; idx < gp * DCH; idx += kThreads) {
-    const int key = idx / DCH, ch = idx - (idx / DCH) * DCH;
-    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs + ch * 8;
-    if (key < P.G)
-      cp_async16(smem_u32(dst), eb + static_cast<long long>(key) * P.e_ld + ch * 8);
-    else
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-  }
-  cp_async_wait_all();
-}
-
 template <int DCH>
 __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParams P, const TcLaunch L,
                                                                   const __grid_constant__ KeyMaps maps) {
@@ -268,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_fwd_tc_kernel(const AttnParam
   }
   const bool split = E.ny * E.nx > 1;
   // records hold t0 - zlo + 1 in 5 bits and h0 - ylo, w0 - xlo in 8 bits
-  const bool overflow = any && (E.zhi - E.zlo + 2 > 31 || E.yhi - E.ylo > 255 || E.xhi - E.xlo > 255);
+  const bool overflow = env_overflow(E.zlo, E.zhi, E.ylo, E.yhi, E.xlo, E.xhi);
   if (overflow && threadIdx.x == 0 && P.status) atomicOr(P.status, MSL_STATUS_TC_RANGE);
   const bool work = any && !overflow;
   const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;

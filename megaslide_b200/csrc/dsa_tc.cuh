@@ -780,6 +780,23 @@ __device__ __forceinline__ void dense_tiles(const __nv_bfloat16* kbuf, const __n
   }
 }
 
+// loads G extra keys / values of this head into kbuf rows 0..G-1 (zero up to gp)
+template <int DCH>
+__device__ __forceinline__ void load_extra(const AttnParams& P, const TileCtx& T, __nv_bfloat16* kbuf, int rs,
+                                           const void* src, int gp) {
+  const __nv_bfloat16* eb = static_cast<const __nv_bfloat16*>(src) + static_cast<long long>(T.b) * P.G * P.e_ld +
+                            T.head * P.d;
+  for (int idx = threadIdx.x; idx < gp * DCH; idx += kThreads) {
+    const int key = idx / DCH, ch = idx - (idx / DCH) * DCH;
+    __nv_bfloat16* dst = kbuf + static_cast<size_t>(key) * rs + ch * 8;
+    if (key < P.G)
+      cp_async16(smem_u32(dst), eb + static_cast<long long>(key) * P.e_ld + ch * 8);
+    else
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  cp_async_wait_all();
+}
+
 // ------------------------------------------------------------------------------ 32-query tiles
 // Geometry shared by the kernels that use 4 x 8 query tiles (two 16-query row groups, 8 warps each,
 // 16 lanes per query for the per-sample work).
@@ -883,11 +900,14 @@ __device__ __forceinline__ void dq_product(const __nv_bfloat16* tb, int r, const
 // envelope does not fit the sample records (temporal span over 29 frames, or over 255 rows or columns).
 // The forward and the backward take this decision from the same envelope, so a tile runs the same
 // formulation both ways.  Every thread of the CTA calls it; warp w takes queries w and w + 16.
-template <int DCH, bool BWD>
+// (The backward runs it in its own kernel, dsa_bwd_tc_fallback_kernel: inlined into the tensor-core
+// backward, its register demand changed that kernel's register allocation, +2% measured, and called out
+// of line it forced the kernel's parameters into local memory, +50%.)  NWARPS = warps of the caller.
+template <int DCH, bool BWD, int NWARPS = kWarps>
 __device__ __forceinline__ void tile_fallback(const AttnParams& P, const TileCtx& T) {
   constexpr int MAXC = (DCH + 3) / 4;
   const int warp = threadIdx.x >> 5;
-  for (int q = warp; q < kQ; q += kWarps) {
+  for (int q = warp; q < kQ; q += NWARPS) {
     int qh, qw;
     query_hw(T, q >> 4, q & 15, qh, qw);
     if (qh >= P.H || qw >= P.W) continue;  // warp-uniform
@@ -903,6 +923,13 @@ __device__ __forceinline__ void tile_fallback(const AttnParams& P, const TileCtx
     else
       fwd_query<__nv_bfloat16, 8, MAXC>(P, qp);
   }
+}
+
+// true when the tile's envelope [zlo, zhi] x [ylo, yhi] x [xlo, xhi] exceeds what the sample records
+// encode (t0 - zlo + 1 in 5 bits, h0 - ylo and w0 - xlo in 8 bits): the CUDA-core fallback takes it
+__device__ __forceinline__ bool env_overflow(int zlo, int zhi, int ylo, int yhi, int xlo, int xhi) {
+  const bool any = zlo <= zhi && ylo <= yhi && xlo <= xhi;
+  return any && (zhi - zlo + 2 > 31 || yhi - ylo > 255 || xhi - xlo > 255);
 }
 
 }  // namespace t32

@@ -292,12 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   }
   const bool split = E.ny * E.nx > 1;
   // records hold t0 - zlo + 1 in 5 bits and h0 - ylo, w0 - xlo in 8 bits
-  const bool overflow = any && (E.zhi - E.zlo + 2 > 31 || E.yhi - E.ylo > 255 || E.xhi - E.xlo > 255);
+  const bool overflow = env_overflow(E.zlo, E.zhi, E.ylo, E.yhi, E.xlo, E.xhi);
   if (overflow && threadIdx.x == 0 && P.status) atomicOr(P.status, MSL_STATUS_TC_RANGE);
-  if (overflow) {  // the forward computed this tile with the CUDA-core gather: so does the backward
-    tile_fallback<DCH, true>(P, T);
-    return;  // no copy was issued yet
-  }
+  if (overflow) return;  // the forward computed this tile with the CUDA-core gather: so does
+                         // dsa_bwd_tc_fallback_kernel (no copy was issued yet)
   const bool work = any && !overflow;
   const bool masks = work && E.ny * E.nx <= kMaxMaskChunks;
   const bool fsplit = split && !masks;  // chunks of a plane share one hit bucket: filter the hits
@@ -572,6 +570,56 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
   }
   __syncthreads();
 
+  // ---- extra keys / values shared by every query of the sample (attention.py:159-173): dO . EV^T and
+  //      Q . EK^T on the tensor cores, the softmax weights from the forward's log-sum-exp; every
+  //      (query, extra key) dS and weight goes to extra_ds / extra_p (dsa_extra_grad_kernel reduces them
+  //      over the queries into d(ek), d(ev)), and dQ += dS_extra . EK on the tensor cores
+  if (P.G > 0 && !(tma && tile_dead(S.dead))) {
+    const int gp = (P.G + 15) & ~15;
+    const uint32_t gmask = gp >= 512 ? 0xffffffffu : (1u << (gp >> 4)) - 1u;
+    load_extra<DCH>(P, T, S.kbuf, L.rs, P.ev, gp);
+    __syncthreads();
+    dense_tiles<DCH, kWPG>(S.kbuf, S.dos + static_cast<size_t>(r) * 16 * L.rs, L.rs,
+                           S.sb + static_cast<size_t>(r) * 16 * L.sld, L.sld, part, gmask);
+    __syncthreads();
+    load_extra<DCH>(P, T, S.kbuf, L.rs, P.ek, gp);
+    __syncthreads();
+    dense_tiles<DCH, kWPG>(S.kbuf, S.qs + static_cast<size_t>(r) * 16 * L.rs, L.rs, grow_a, L.sld, part, gmask);
+    __syncthreads();
+    if (qvalid) {  // dS in place of dP: each element is read and written by one thread
+      const float lse2 = P.lse[(static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow];
+      const float dq_d = S.dd[qi];
+      const uint64_t qg = ((static_cast<uint64_t>(T.b) * P.T + T.tg) * P.H + qh) * P.W + qw;
+      const long long xrow = ((static_cast<long long>(T.b) * P.nh + T.head) * P.Nq + qrow) * P.G;
+      for (int e = sub; e < P.G; e += kLPQ) {
+        const float p = exp2f(S.sa[static_cast<size_t>(qi) * L.sld + e] * P.scale_log2 - lse2);
+        float ks = 1.f;
+        if (P.drop_thresh)
+          ks = dropout_keep(P.seed, (qg * P.nh + T.head) * static_cast<uint64_t>(K + P.G) + K + e, P.drop_thresh)
+                   ? P.drop_keep_scale
+                   : 0.f;
+        float* dpe = S.sb + static_cast<size_t>(qi) * L.sld + e;
+        const float dsq = p * (*dpe * ks - dq_d) * P.scale;
+        P.extra_ds[xrow + e] = dsq;
+        P.extra_p[xrow + e] = p * ks;
+        *dpe = dsq;
+      }
+    }
+    __syncthreads();
+    // dS_extra^T as a bf16 tile [key][query] in sa (zero for padding keys and queries outside the volume)
+    __nv_bfloat16* te = reinterpret_cast<__nv_bfloat16*>(S.sa);
+    for (int i = threadIdx.x; i < gp * kQ; i += kThreads) {
+      const int e = i / kQ, q = i - (i / kQ) * kQ;
+      int qh2, qw2;
+      query_hw(T, q >> 4, q & 15, qh2, qw2);
+      const bool ok = e < P.G && qh2 < P.H && qw2 < P.W;
+      te[static_cast<size_t>(e) * kTRow + q] = __float2bfloat16_rn(ok ? S.sb[static_cast<size_t>(q) * L.sld + e] : 0.f);
+    }
+    __syncthreads();
+    dq_product<DCH, kTPW, kKS>(te, r, S.kbuf, L.rs, nt0, nt1, gmask, oq, kpar);
+    __syncthreads();
+  }
+
   // ---- the warps of the other key-tile parts hand their dQ partial sums to part 0 (through the key
   //      buffer and the dense tiles, contiguous and free now: [2][kCG][kKS - 1][kTPW][32] float4)
   if (kKS > 1) {
@@ -642,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsa_bwd_tc_kernel(const AttnParam
 // ------------------------------------------------------------------------------ host side
 bool tc_bwd_supported(const AttnParams& P) {
   if (!tc_supported(P)) return false;
-  if (P.G != 0 || P.probs == nullptr || P.saved == nullptr) return false;
+  if (P.probs == nullptr || P.saved == nullptr) return false;
   if (static_cast<long long>(tc::bwd::kQ) * P.K > 65536) return false;  // hit-list entries are 16-bit
   return true;
 }
@@ -661,6 +709,7 @@ bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   mk &= ~15;
   if (mk < 64) return false;
   if (mk > tc::bwd::kMaxKeys) mk = tc::bwd::kMaxKeys;
+  if (((P.G + 15) & ~15) > mk) return false;  // the extra keys are one chunk of the key buffer
   L.maxkeys = mk;
   L.sld = mk + 8;  // row stride = 8 or 24 (mod 32) words: mma fragment rows hit distinct banks
   // a transposed bf16 tile [maxkeys][40] must fit in a dense fp32 tile [32][sld]
@@ -678,6 +727,23 @@ bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
   return L.tiles <= 0x7fffffffLL && L.smem <= static_cast<size_t>(smem_limit);
 }
 
+namespace tc {
+namespace bwd {
+// The backward of the tiles the tensor-core kernels leave to the CUDA-core gather (key envelopes the
+// sample records cannot encode: env_overflow on the forward's saved envelope), one CTA per tile like
+// dsa_bwd_tc_kernel: every other CTA reads its tile's envelope and exits.
+constexpr int kFallbackWarps = 4;
+template <int DCH>
+__global__ void __launch_bounds__(32 * kFallbackWarps) dsa_bwd_tc_fallback_kernel(const AttnParams P, const TcLaunch L) {
+  const int* env =
+      reinterpret_cast<const int*>(static_cast<const char*>(P.saved) + saved_env_offset(P)) + 8 * static_cast<long long>(blockIdx.x);
+  if (!env_overflow(env[0], env[1], env[2], env[3], env[4], env[5])) return;
+  const TileCtx T = decode_tile(P, L, kTileH);
+  tile_fallback<DCH, true, kFallbackWarps>(P, T);
+}
+}  // namespace bwd
+}  // namespace tc
+
 template <int DCH>
 static cudaError_t launch_bwd_tc_t(const AttnParams& P, const TcLaunch& L, const tc::KeyMaps& maps,
                                    cudaStream_t s) {
@@ -685,6 +751,9 @@ static cudaError_t launch_bwd_tc_t(const AttnParams& P, const TcLaunch& L, const
                                        static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
   tc::bwd::dsa_bwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L, maps);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  tc::bwd::dsa_bwd_tc_fallback_kernel<DCH><<<static_cast<unsigned>(L.tiles), 32 * tc::bwd::kFallbackWarps, 0, s>>>(P, L);
   return cudaGetLastError();
 }
 

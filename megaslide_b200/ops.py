@@ -191,10 +191,10 @@ class DsaShape:
 
 def wants_probs(shape: DsaShape, dtype: torch.dtype) -> bool:
     """Host-side pre-check for the tensor-core backward, which needs two outputs of the tensor-core
-    forward (``probs``, ``saved``): bf16, no extra keys, head_dim a multiple of 8 in [16, 128], algo
-    not forced to the CUDA-core gather.  The library makes the final decision (alignment,
+    forward (``probs``, ``saved``): bf16, at most 256 extra keys, head_dim a multiple of 8 in [16, 128],
+    algo not forced to the CUDA-core gather.  The library makes the final decision (alignment,
     shared-memory plan)."""
-    return (dtype == torch.bfloat16 and shape.extra == 0 and shape.algo != _lib.MSL_ALGO_SIMT
+    return (dtype == torch.bfloat16 and shape.extra <= 256 and shape.algo != _lib.MSL_ALGO_SIMT
             and shape.head_dim % 8 == 0 and 16 <= shape.head_dim <= 128)
 
 

@@ -492,6 +492,8 @@ TC_BWD_CASES = [
     (1, 2, 32, 32, 1, 16, (1, 3, 3), 0, 20.0),    # offsets of ~10 voxels: envelope split in chunks
     (1, 1, 5, 5, 2, 40, (1, 3, 3), 0, 0.0),       # T=1, zero offsets (samples on grid points)
     (1, 4, 5, 6, 1, 32, (3, 3, 3), 0, 6.0),       # many samples clamped onto the borders
+    (2, 2, 16, 16, 2, 64, (3, 7, 7), 3, 0.5),     # extra keys (hybrid attention): dS . EK into dQ, d(ek), d(ev)
+    (1, 3, 9, 11, 2, 72, (3, 7, 7), 64, 1.0),     # 64 extra keys, config-2 head_dim
 ]
 
 
@@ -502,19 +504,21 @@ def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False, d
     q, k, v, off, ek, ev, dout = arrays
     N = T * H * W
     C = nh * d
-    t = lambda a: torch.from_numpy(a).to(DEV, torch.bfloat16).reshape(-1, C)  # noqa: E731
-    shape = ops.DsaShape(B, T, H, W, nh, d, ks, dropout_p=dropout_p, dropout_seed=seed, algo=algo)
+    t = lambda a: None if a is None else torch.from_numpy(a).to(DEV, torch.bfloat16).reshape(-1, C)  # noqa: E731
+    shape = ops.DsaShape(B, T, H, W, nh, d, ks, extra=G, dropout_p=dropout_p, dropout_seed=seed, algo=algo)
     offt = torch.from_numpy(off).to(DEV).reshape(B * N, -1)
-    qt, kt_, vt, dot = t(q), t(k), t(v), t(dout)
+    qt, kt_, vt, dot, ekt, evt = t(q), t(k), t(v), t(dout), t(ek), t(ev)
     probs, saved = ops.saved_buffers(shape, torch.bfloat16, DEV) if algo == 2 else (None, None)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     ob = None if offset_bias is None else torch.from_numpy(offset_bias).to(DEV)
-    out, lse = ops.attn_fwd(shape, qt, kt_, vt, offt, probs=probs, saved=saved, status=status, offset_bias=ob)
+    out, lse = ops.attn_fwd(shape, qt, kt_, vt, offt, ekt, evt, probs=probs, saved=saved, status=status,
+                            offset_bias=ob)
     kw = {}
     if accumulate:
         kw = dict(dk_acc=torch.full((B * N, C), 0.5, device=DEV), dv_acc=torch.full((B * N, C), -0.25, device=DEV))
-    dq, dk, dv, doff, _, _ = ops.attn_bwd(shape, qt, kt_, vt, offt, out, lse, dot, probs=probs, saved=saved,
-                                          status=status, doff_dtype=doff_dtype, offset_bias=ob, **kw)
+    dq, dk, dv, doff, dek, dev_ = ops.attn_bwd(shape, qt, kt_, vt, offt, out, lse, dot, ek=ekt, ev=evt, probs=probs,
+                                               saved=saved, status=status, doff_dtype=doff_dtype, offset_bias=ob,
+                                               **kw)
     assert doff.dtype == doff_dtype
     torch.cuda.synchronize()
     assert int(status.item()) == expect_status
@@ -523,6 +527,8 @@ def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False, d
     f = lambda a: a.float().cpu().numpy().reshape(B, -1, C)  # noqa: E731
     res = dict(out=f(out), lse=lse.cpu().numpy(), dq=f(dq), dk=f(dk), dv=f(dv),
                doff=doff.float().cpu().numpy().reshape(B, N, -1))
+    if G:
+        res["dek"], res["dev"] = f(dek), f(dev_)
     if probs is not None:
         res["probs"] = probs.cpu().numpy()
     return res
@@ -530,7 +536,7 @@ def _run_tc_train(case, arrays, algo, dropout_p=0.0, seed=0, accumulate=False, d
 
 def _compare_grads_bf16(got, ref, what):
     assert rel(got["out"], ref["out"]) < RTOL_BF16, f"{what} out"
-    for key in ("dq", "dk", "dv", "doff"):
+    for key in ("dq", "dk", "dv", "doff") + (("dek", "dev") if got.get("dek") is not None else ()):
         ef, em = fro(got[key], ref[key]), rel(got[key], ref[key])
         assert ef < RTOL_BF16 and em < MAXREL_BF16_GRAD, f"{what} {key}: fro {ef:.3e} max {em:.3e}"
 
@@ -662,7 +668,12 @@ def test_module_bf16_training_uses_tensor_core_backward(monkeypatch):
     assert torch.isfinite(x.grad.float()).all()
     for p in m.parameters():
         assert p.grad is not None and torch.isfinite(p.grad.float()).all()
-    assert seen == [True]
+    # with extra keys (HybridAttention3D's register tokens) as well
+    e = torch.randn(1, 16, C, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    m(x, (T, H, W), extra_kv=e).float().square().mean().backward()
+    torch.cuda.synchronize()
+    assert e.grad is not None and torch.isfinite(e.grad.float()).all()
+    assert seen == [True, True]
 
 
 @pytest.mark.parametrize("heads,taps,pad", [(3, 27, 5), (3, 27, 1), (4, 147, 0)])
@@ -724,7 +735,7 @@ def _timeout_worker(q):
 
     try:
         dev = "cuda:0"
-        B, T, H, W, nh, d, ks = 1, 2, 4, 8, 1, 64, (3, 3, 3)
+        B, T, H, W, nh, d, ks = 1, 2, 4, 8, 2, 64, (3, 3, 3)  # nh*d >= the 72-channel TMA box
         N, C = T * H * W, nh * d
         g = torch.Generator(device=dev).manual_seed(5)
         q_, k_, v_ = (torch.randn(B * N, C, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))

@@ -112,10 +112,9 @@ struct TileCtx {
   int b, head, tl, tg, qh0, qw0;
 };
 
-// CTA -> (sample, local frame, tile row, tile column, head); heads vary fastest so the CTAs that run
-// together share their K/V rows in L2.
-__device__ __forceinline__ TileCtx decode_tile(const AttnParams& P, const TcLaunch& L, int tile_h) {
-  long long t = blockIdx.x;
+// tile index -> (sample, local frame, tile row, tile column, head); heads vary fastest so the CTAs that
+// run together share their K/V rows in L2.
+__device__ __forceinline__ TileCtx decode_tile_index(const AttnParams& P, const TcLaunch& L, int tile_h, long long t) {
   TileCtx c;
   c.head = static_cast<int>(t % P.nh);
   t /= P.nh;
@@ -129,6 +128,10 @@ __device__ __forceinline__ TileCtx decode_tile(const AttnParams& P, const TcLaun
   c.qh0 = ih * tile_h;
   c.qw0 = iw * kTileW;
   return c;
+}
+// the CTA's tile (one CTA per tile)
+__device__ __forceinline__ TileCtx decode_tile(const AttnParams& P, const TcLaunch& L, int tile_h) {
+  return decode_tile_index(P, L, tile_h, blockIdx.x);
 }
 
 // query c (0..15) of row group r: tile rows 2r, 2r+1

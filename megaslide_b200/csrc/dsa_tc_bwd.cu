@@ -730,16 +730,32 @@ bool tc_bwd_plan(const AttnParams& P, TcLaunch& L, int smem_limit) {
 namespace tc {
 namespace bwd {
 // The backward of the tiles the tensor-core kernels leave to the CUDA-core gather (key envelopes the
-// sample records cannot encode: env_overflow on the forward's saved envelope), one CTA per tile like
-// dsa_bwd_tc_kernel: every other CTA reads its tile's envelope and exits.
+// sample records cannot encode: env_overflow on the forward's saved envelope).  A CTA checks 32
+// consecutive tiles' envelopes (one per lane of warp 0) and runs the gather for those that overflow;
+// in the common case every CTA exits after that one check.
 constexpr int kFallbackWarps = 4;
+constexpr int kFallbackTiles = 32;
 template <int DCH>
 __global__ void __launch_bounds__(32 * kFallbackWarps) dsa_bwd_tc_fallback_kernel(const AttnParams P, const TcLaunch L) {
-  const int* env =
-      reinterpret_cast<const int*>(static_cast<const char*>(P.saved) + saved_env_offset(P)) + 8 * static_cast<long long>(blockIdx.x);
-  if (!env_overflow(env[0], env[1], env[2], env[3], env[4], env[5])) return;
-  const TileCtx T = decode_tile(P, L, kTileH);
-  tile_fallback<DCH, true, kFallbackWarps>(P, T);
+  __shared__ uint32_t over;
+  const long long t0 = static_cast<long long>(blockIdx.x) * kFallbackTiles;
+  if (threadIdx.x < 32) {
+    const long long t = t0 + threadIdx.x;
+    bool o = false;
+    if (t < L.tiles) {
+      const int4* env = reinterpret_cast<const int4*>(static_cast<const char*>(P.saved) + saved_env_offset(P)) + 2 * t;
+      const int4 a = env[0], b = env[1];
+      o = env_overflow(a.x, a.y, a.z, a.w, b.x, b.y);
+    }
+    const uint32_t m = __ballot_sync(0xffffffffu, o);
+    if (threadIdx.x == 0) over = m;
+  }
+  __syncthreads();
+  for (uint32_t m = over; m; m &= m - 1u) {
+    const long long tile = t0 + __ffs(m) - 1;
+    const TileCtx T = decode_tile_index(P, L, kTileH, tile);
+    tile_fallback<DCH, true, kFallbackWarps>(P, T);
+  }
 }
 }  // namespace bwd
 }  // namespace tc
@@ -753,7 +769,8 @@ static cudaError_t launch_bwd_tc_t(const AttnParams& P, const TcLaunch& L, const
   tc::bwd::dsa_bwd_tc_kernel<DCH><<<static_cast<unsigned>(L.tiles), tc::kThreads, L.smem, s>>>(P, L, maps);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  tc::bwd::dsa_bwd_tc_fallback_kernel<DCH><<<static_cast<unsigned>(L.tiles), 32 * tc::bwd::kFallbackWarps, 0, s>>>(P, L);
+  const long long nfb = (L.tiles + tc::bwd::kFallbackTiles - 1) / tc::bwd::kFallbackTiles;
+  tc::bwd::dsa_bwd_tc_fallback_kernel<DCH><<<static_cast<unsigned>(nfb), 32 * tc::bwd::kFallbackWarps, 0, s>>>(P, L);
   return cudaGetLastError();
 }
 

@@ -660,6 +660,21 @@ def run_c4_leg(args, world, rank, dev, barrier, local):
     return info
 
 
+def _host_memory():
+    """Host RAM and cores of this box, and whether config 5's host state would fit: 33e9 parameters
+    as an fp32 master, two fp32 AdamW moments, an fp32 gradient accumulator and a bf16 staging copy
+    (18 bytes per parameter, ~594 GB) plus the fp32 model the trainer is built from (~132 GB)."""
+    try:
+        import psutil
+
+        vm = psutil.virtual_memory()
+        need = 33e9 * (18 + 4)
+        return {"ram_total_gb": vm.total / 1e9, "ram_available_gb": vm.available / 1e9, "cores": os.cpu_count(),
+                "c5_host_state_gb": need / 1e9, "c5_fits_host_ram": bool(vm.available > 1.15 * need)}
+    except Exception as e:  # pragma: no cover
+        return {"error": repr(e)}
+
+
 def run_dit(args):
     """DiT step time (fwd + bwd + AdamW) of the streaming CPU-master trainer on one GPU."""
     import torch
@@ -722,6 +737,18 @@ def run_dit(args):
     d2h = (trainer.d2h_bytes - d0) / args.steps
     tokens = cfg.num_patches
     resident = bool(trainer.resident)
+    # one more step with the per-block event timeline (weight H2D / gradient D2H on their side streams
+    # against block compute), after the timed region
+    trainer.timeline = []
+    origin = torch.cuda.Event(enable_timing=True)
+    origin.record(torch.cuda.current_stream())
+    step()
+    trainer.get_parameters()
+    torch.cuda.synchronize()
+    from megaslide_b200.stream import timeline_summary
+
+    timeline = timeline_summary(trainer.timeline, origin)
+    trainer.timeline = None
     trainer.cleanup()
     line = {
         "metric": "DiT step time (fwd+bwd+AdamW, CPU-master streaming)", "value": sec, "unit": "s/step",
@@ -739,8 +766,10 @@ def run_dit(args):
         "e2e": {"value": sec, "unit": "s/step", "h2d_bytes_per_step": int(h2d + 2 * lat.numel() * 4 + 8),
                 "d2h_bytes_per_step": int(d2h + 4)},
         "stream": {"weight_h2d_gbs": h2d / sec / 1e9, "grad_d2h_gbs": d2h / sec / 1e9,
-                   "weight_bytes_per_step": h2d, "grad_bytes_per_step": d2h, "loss": loss},
+                   "weight_bytes_per_step": h2d, "grad_bytes_per_step": d2h, "loss": loss,
+                   "timeline": timeline},
         "phases_per_step": {k: v / (1 if k == "final_drain_s" else args.steps) for k, v in phases.items()},
+        "host": _host_memory(),
         "clocks": clocks, "gpu_launches": launches,
     }
     print(json.dumps(line), flush=True)

@@ -122,6 +122,10 @@ class CPUMasterVideoDiT:
         self._setup_host_buffers()
         self._setup_gpu()
         self.resident: Optional[bool] = None  # decided at the first step (needs the token count)
+        # a list set here receives (kind, block, stream, start event, end event) for every weight copy
+        # ("h2d"), block forward / recompute / backward ("fwd", "recompute", "bwd") and gradient copy
+        # ("d2h") of the next steps: the streaming timeline (timeline_summary)
+        self.timeline: Optional[list] = None
         self._worker_q: "queue.Queue" = queue.Queue()
         self._worker_err: List[BaseException] = []
         self._worker = threading.Thread(target=self._work_loop, daemon=True)
@@ -237,8 +241,10 @@ class CPUMasterVideoDiT:
         if not self.stage_ready[i].wait(timeout=600.0):
             raise RuntimeError(f"block {i}: host optimizer update did not finish")
         with torch.cuda.stream(self.weight_stream):
+            ev = self._mark(self.weight_stream)
             self.res_buf[i].copy_(self.stage[i], non_blocking=True)
             self.res_ready[i].record(self.weight_stream)
+            self._mark_end("h2d", i, "weight", self.weight_stream, ev)
         self.res_dirty[i] = False
         self.h2d_bytes += self.block_numel[i] * self.stage[i].element_size()
 
@@ -255,14 +261,18 @@ class CPUMasterVideoDiT:
             for p in _flat_params(blk):
                 p.requires_grad_(True)
             inp = x.detach().requires_grad_(True)
+            ev = self._mark(self.compute_stream)
             out = blk(inp, vshape, te, tm)
+            self._mark_end("fwd", i, "compute", self.compute_stream, ev)
             saved.append((inp, out))
             x = out.detach()
         loss, grad_hidden, fwd_end = head_fn(x)
         for i in range(self.num_blocks - 1, -1, -1):
             inp, out = saved[i]
             params = _flat_params(self.res_blocks[i])
+            ev = self._mark(self.compute_stream)
             grads = torch.autograd.grad(out, (inp, *params), grad_outputs=grad_hidden, allow_unused=True)
+            self._mark_end("bwd", i, "compute", self.compute_stream, ev)
             for p in params:
                 p.requires_grad_(False)
             grad_hidden = grads[0].detach()
@@ -303,19 +313,37 @@ class CPUMasterVideoDiT:
         n = self.block_numel[i]
         with torch.cuda.stream(self.weight_stream):
             self.weight_stream.wait_event(self.slot_free[s])
+            ev = self._mark(self.weight_stream)
             self.slot_buf[s][:n].copy_(self.stage[i], non_blocking=True)
             self.slot_ready[s].record(self.weight_stream)
+            self._mark_end("h2d", i, "weight", self.weight_stream, ev)
         self.slot_block[s] = i
         self.h2d_bytes += n * self.stage[i].element_size()
         return s
 
-    def _run(self, i: int, x: Tensor, vshape, text_embeds, text_mask, prefetch: Optional[int] = None):
+    def _mark(self, stream) -> Optional[torch.cuda.Event]:
+        if self.timeline is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        return ev
+
+    def _mark_end(self, kind: str, block: int, sname: str, stream, start: Optional[torch.cuda.Event]) -> None:
+        if self.timeline is not None and start is not None:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record(stream)
+            self.timeline.append((kind, block, sname, start, end))
+
+    def _run(self, i: int, x: Tensor, vshape, text_embeds, text_mask, prefetch: Optional[int] = None,
+             kind: str = "fwd"):
         s = self._load(i)
         self._last_slot = s
         if prefetch is not None and 0 <= prefetch < self.num_blocks:
             self._load(prefetch)
         self.compute_stream.wait_event(self.slot_ready[s])
+        ev = self._mark(self.compute_stream)
         y = self.gpu_blocks[s](x, vshape, text_embeds, text_mask)
+        self._mark_end(kind, i, "compute", self.compute_stream, ev)
         self.slot_free[s].record(self.compute_stream)
         return y
 
@@ -338,9 +366,11 @@ class CPUMasterVideoDiT:
         self.d2h_bytes += n * self.gflat.element_size()
         with torch.cuda.stream(self.grad_stream):
             self.grad_stream.wait_event(packed)
+            ev = self._mark(self.grad_stream)
             self.slabs[slab_i][:n].copy_(self.gflat[:n], non_blocking=True)
             self.slab_done[slab_i].record(self.grad_stream)
             self.gflat_free.record(self.grad_stream)
+            self._mark_end("d2h", i, "grad", self.grad_stream, ev)
 
         def accumulate(i=i, slab_i=slab_i, n=n):
             self.slab_done[slab_i].synchronize()
@@ -416,7 +446,7 @@ class CPUMasterVideoDiT:
             with torch.no_grad():
                 h = ckpt[b0]
                 for j in range(b0, b1 - 1):
-                    h = self._run(j, h, vshape, te, tm, prefetch=j + 1)
+                    h = self._run(j, h, vshape, te, tm, prefetch=j + 1, kind="recompute")
                     inputs[j + 1] = h
             for i in range(b1 - 1, b0 - 1, -1):
                 s = self._load(i)
@@ -432,8 +462,10 @@ class CPUMasterVideoDiT:
                 for p in params:
                     p.requires_grad_(True)
                 inp = inputs[i].detach().requires_grad_(True)
+                ev = self._mark(self.compute_stream)
                 out = gb(inp, vshape, te, tm)
                 grads = torch.autograd.grad(out, (inp, *params), grad_outputs=grad_hidden, allow_unused=True)
+                self._mark_end("bwd", i, "compute", self.compute_stream, ev)
                 for p in params:
                     p.requires_grad_(False)
                 grad_hidden = grads[0].detach()
@@ -529,3 +561,24 @@ class CPUMasterVideoDiT:
         if self.resident:
             self.res_dirty = [True] * self.num_blocks
         self.step_count = int(ck["step"])
+
+
+def timeline_summary(timeline: list, origin: torch.cuda.Event) -> dict:
+    """Per-kind totals and the overlap of the side-stream copies with block compute for a recorded
+    CPUMasterVideoDiT.timeline (events must be complete): intervals in ms from `origin`; overlap = the
+    share of copy time during which a block computes on the compute stream."""
+    iv = [(k, b, sname, origin.elapsed_time(s), origin.elapsed_time(e)) for k, b, sname, s, e in timeline]
+    comp = sorted((a, z) for k, _, sname, a, z in iv if sname == "compute")
+
+    def overlap(a: float, z: float) -> float:
+        return sum(max(0.0, min(z, cz) - max(a, ca)) for ca, cz in comp)
+
+    out: dict = {"intervals": len(iv)}
+    for kind in ("h2d", "d2h", "fwd", "recompute", "bwd"):
+        sel = [(a, z) for k, _, _, a, z in iv if k == kind]
+        tot = sum(z - a for a, z in sel)
+        out[kind] = {"count": len(sel), "ms": tot}
+        if kind in ("h2d", "d2h") and tot > 0:
+            out[kind]["overlapped_with_compute_frac"] = sum(overlap(a, z) for a, z in sel) / tot
+    out["first_blocks"] = [[k, b, round(a, 3), round(z, 3)] for k, b, _, a, z in sorted(iv, key=lambda r: r[3])[:24]]
+    return out

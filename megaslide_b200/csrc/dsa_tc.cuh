@@ -112,18 +112,20 @@ struct TileCtx {
   int b, head, tl, tg, qh0, qw0;
 };
 
-// tile index -> (sample, local frame, tile row, tile column, head); heads vary fastest so the CTAs that
-// run together share their K/V rows in L2.
+// tile index -> (sample, tile row, tile column, local frame, head).  Heads vary fastest, then frames:
+// the CTAs that run together are the heads and neighbouring frames of one spatial tile, whose key
+// envelopes overlap (samples reach several frames away), so their K/V chunk reads and dK/dV
+// accumulator adds meet in L2 instead of being spread over the whole launch.
 __device__ __forceinline__ TileCtx decode_tile_index(const AttnParams& P, const TcLaunch& L, int tile_h, long long t) {
   TileCtx c;
   c.head = static_cast<int>(t % P.nh);
   t /= P.nh;
+  c.tl = static_cast<int>(t % P.q_frames);
+  t /= P.q_frames;
   const int iw = static_cast<int>(t % L.tiles_w);
   t /= L.tiles_w;
   const int ih = static_cast<int>(t % L.tiles_h);
-  t /= L.tiles_h;
-  c.tl = static_cast<int>(t % P.q_frames);
-  c.b = static_cast<int>(t / P.q_frames);
+  c.b = static_cast<int>(t / L.tiles_h);
   c.tg = P.q_frame0 + c.tl;
   c.qh0 = ih * tile_h;
   c.qw0 = iw * kTileW;

@@ -184,12 +184,25 @@ __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const Tile
     const int o0 = key_off[tile * 16 + g], o1 = key_off[tile * 16 + g + 8];
     float* const a0 = abase + static_cast<long long>(max(o0, 0)) * P.acc_ld + nt0 * 8;
     float* const a1 = abase + static_cast<long long>(max(o1, 0)) * P.acc_ld + nt0 * 8;
+    // a key no sample corner touched has an all-zero row (about a fifth of the flushed keys): its
+    // accumulator row is skipped (the four lanes of a row agree through two shuffles)
+    bool nz0 = false, nz1 = false;
+#pragma unroll
+    for (int j = 0; j < NG; ++j) {
+      if (nt0 + j >= DCH) break;
+      nz0 |= (c[j][0] != 0.f) | (c[j][1] != 0.f);
+      nz1 |= (c[j][2] != 0.f) | (c[j][3] != 0.f);
+    }
+    const int nzb = (nz0 ? 1 : 0) | (nz1 ? 2 : 0);
+    const int nzr = nzb | __shfl_xor_sync(kFull, nzb, 1) | __shfl_xor_sync(kFull, nzb, 2) |
+                    __shfl_xor_sync(kFull, nzb, 3);
+    const bool w0 = o0 >= 0 && (nzr & 1), w1 = o1 >= 0 && (nzr & 2);
 #pragma unroll
     for (int j = 0; j < NG; ++j) {
       if (nt0 + j >= DCH) break;  // warp-uniform
       // the fragment's own pairs: key g (c0, c1) and key g + 8 (c2, c3), channels 8 (nt0 + j) + 2t4, +1
-      if (o0 >= 0) atomicAdd(reinterpret_cast<float2*>(a0 + j * 8), make_float2(c[j][0], c[j][1]));
-      if (o1 >= 0) atomicAdd(reinterpret_cast<float2*>(a1 + j * 8), make_float2(c[j][2], c[j][3]));
+      if (w0) atomicAdd(reinterpret_cast<float2*>(a0 + j * 8), make_float2(c[j][0], c[j][1]));
+      if (w1) atomicAdd(reinterpret_cast<float2*>(a1 + j * 8), make_float2(c[j][2], c[j][3]));
     }
   }
 }

@@ -324,7 +324,9 @@ class Workload:
             from megaslide_b200.sharded import TimeShardedDSA3D, shard_ranges
 
             self.owns = shard_ranges(self.T, world)
-            self.fwd = TimeShardedDSA3D(self.mod, frame_ranges=self.owns)
+            # learned offsets: the K/V window of a step is planned from the previous step's largest offset
+            # (checked exactly by the kernels' halo-miss bit, reported by the status word after the run)
+            self.fwd = TimeShardedDSA3D(self.mod, frame_ranges=self.owns, speculative_window=not self.clip)
         else:
             self.owns = [(0, self.T)]
             self.fwd = self.mod
@@ -549,6 +551,15 @@ def measure_e2e(wl, steps, warmup, barrier, world, dev):
             "h2d": "pinned host -> device on a copy stream, double-buffered: step i+1's input copies while step i runs"}
 
 
+def msl_status_bits():
+    """Synchronous read of this GPU's attention status word: raises MslError if any call of the run
+    reported invalid results (a halo miss of the K/V window, a timed-out TMA wait); returns the
+    informational bits (MSL_STATUS_TC_RANGE: tiles computed by the CUDA-core fallback)."""
+    import megaslide_b200 as msl
+
+    return int(msl.check_status())
+
+
 def _c4_bytes_estimate(world):
     """Device bytes a c4 fwd+bwd needs on one rank (inputs, saved forward state, backward buffers)."""
     c = CONFIGS["c4"]
@@ -593,7 +604,9 @@ def run_gpu(args):
     x_mb = wl.x.numel() * wl.x.element_size() / 1e6
     main_cfg = {"workload": _workload_name(args.config, wl.c), "tokens_per_step": wl.tokens,
                 "parallelism": (f"time-sharded x{world}: {wl.T}-frame volume split into {wl.T // world}-frame shards, "
-                                "K/V halo exchange over NCCL") if world > 1 else "single GPU",
+                                "projected K/V halo rows exchanged over NCCL, K/V window planned from the previous "
+                                "step's largest offset (verified by the kernels' halo-miss bit: status_ok)")
+                               if world > 1 else "single GPU",
                 "l2": f"inputs larger than L2 (x = {x_mb:.0f} MB per GPU)" if x_mb > 126 else
                       f"x = {x_mb:.0f} MB per GPU (below L2)"}
     del wl
@@ -602,6 +615,8 @@ def run_gpu(args):
     c4 = None
     if not args.no_c4 and args.config != "c4" and not args.config.endswith("_prof"):
         c4 = run_c4_leg(args, world, rank, dev, barrier, local)
+
+    status_bits = msl_status_bits()  # raises if any step of the run (c4 included) reported invalid results
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -618,6 +633,7 @@ def run_gpu(args):
             "config": main_cfg,
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": launches,
             "kernels": kernels, "parity": parity, "c4": c4,
+            "status_ok": True, "status_bits": status_bits,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

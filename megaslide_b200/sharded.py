@@ -217,7 +217,31 @@ class _GradBuckets:
 
 class _ShardCfg:
     __slots__ = ("T", "H", "W", "rank", "world", "owns", "group", "heads", "head_dim", "kernel", "oscale",
-                 "dropout_p", "seed", "dtype", "param_dtypes", "G", "offset_bound", "capture")
+                 "dropout_p", "seed", "dtype", "param_dtypes", "G", "offset_bound", "capture", "spec")
+
+
+class _SpeculativeWindow:
+    """The K/V window of a learned-offset step planned from the previous step's largest temporal
+    offset (exact, reduced over the ranks on the device and read back without waiting), widened by a
+    margin.  Whether the plan held is checked exactly by the attention kernels: a sample corner in a
+    frame the window does not hold sets MSL_STATUS_HALO_MISS, which the next call raises."""
+
+    def __init__(self):
+        self.known: Optional[float] = None  # the last largest |temporal offset| read back
+        self.pending: Optional[tuple] = None  # (event, pinned value) of the last step's maximum
+
+    def refresh(self) -> None:
+        if self.pending is not None and self.pending[0].query():
+            v = float(self.pending[1][2])
+            self.known = v if self.known is None else max(v, 0.0)
+            self.pending = None
+
+    def plan(self) -> Optional[float]:
+        """The bound to plan with, or None when no earlier step's maximum is known yet."""
+        self.refresh()
+        if self.known is None or not math.isfinite(self.known):
+            return None
+        return self.known * 1.25 + 0.5
 
 
 class DSA3DShardedFunction(torch.autograd.Function):
@@ -256,8 +280,7 @@ class DSA3DShardedFunction(torch.autograd.Function):
         pend = start_exchange(xc, cw, xl, FramePlan(cfg.owns, cwins), fetch1, rank, cfg.group)
         wqkv = torch.cat([wq, wk, wv], 0).to(dt)
         bqkv = torch.cat([bq, bk, bv], 0).to(dt)
-        learned = off_in is None and cfg.offset_bound is None
-        if not learned:  # no host wait below: the projection overlaps the conv-halo exchange
+        if cfg.offset_bound is not None:  # no host wait below: the projection overlaps the conv-halo exchange
             qkv = torch.addmm(bqkv, xo2, wqkv.t())  # [own rows, 3C]
         pend.finish()
         xc2 = xc.view(-1, C)
@@ -279,10 +302,25 @@ class DSA3DShardedFunction(torch.autograd.Function):
             b2f = None
         wd_kc = ops.conv_weight_kc(wd)
         dwk = (wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous())
+        spec_plan = cfg.spec.plan() if (cfg.spec is not None and cfg.offset_bound is None) else None
         if cfg.offset_bound is not None:
             # the caller bounds |raw offset| (e.g. clipped synthetic offsets): the K/V window follows from the
             # bound alone, with no reduction and no host synchronisation
             dmax = float(cfg.offset_bound) * abs(cfg.oscale)
+            D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
+        elif spec_plan is not None:
+            # speculative window: planned from the previous step's maximum; this step's maximum is reduced
+            # and read back without waiting (the next step plans with it), and the kernels' halo-miss bit
+            # checks the plan exactly
+            dmax = spec_plan
+            amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale, bias=b2f)
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=cfg.group)
+            amax_h = torch.empty(3, dtype=torch.float32, pin_memory=True)
+            amax_h.copy_(amax, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record()
+            cfg.spec.pending = (ready, amax_h)
+            qkv = torch.addmm(bqkv, xo2, wqkv.t())
             D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
         else:
             # the largest temporal offset over all ranks sizes every rank's K/V window: it is copied to pinned
@@ -298,6 +336,8 @@ class DSA3DShardedFunction(torch.autograd.Function):
             D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
             ready.synchronize()
             dmax = float(amax_h[2])
+            if cfg.spec is not None:
+                cfg.spec.known = dmax
         if not math.isfinite(dmax):
             raise FloatingPointError("non-finite offsets: the K/V halo cannot be bounded")
         # 3. K/V window of every rank (deterministic on all ranks): the own projected rows plus the halo
@@ -490,16 +530,26 @@ class TimeShardedDSA3D(nn.Module):
     raw offsets of the own frames (float32 [B, own_frames*H*W, nh*K*3]; the offset predictor does not
     run).  With `offset_bound` (a bound on |raw offset| that the caller guarantees, e.g. for offsets
     clipped to +-3) the K/V window of every rank follows from the bound: no reduction of the largest
-    offset and no host synchronisation.  ``capture``: as DeformableSlideAttention3D.capture."""
+    offset and no host synchronisation.  ``capture``: as DeformableSlideAttention3D.capture.
+
+    speculative_window=True (learned offsets): from the second step on, the K/V window is planned from
+    the previous step's largest temporal offset (times 1.25, plus 0.5) instead of waiting for this
+    step's; this step's maximum is still reduced on the device and read back for the next plan.  The
+    plan is checked exactly: a sample corner outside the window sets MSL_STATUS_HALO_MISS, and the
+    next call (or megaslide_b200.check_status()) raises MslError - a step whose offsets jumped past the
+    margin is reported, never silently wrong."""
 
     def __init__(self, module: DeformableSlideAttention3D, group=None,
-                 frame_ranges: Optional[Sequence[Range]] = None):
+                 frame_ranges: Optional[Sequence[Range]] = None, speculative_window: bool = False):
         super().__init__()
         self.module = module
         self.group = group
         self.frame_ranges = list(frame_ranges) if frame_ranges is not None else None
         self._joined = False
         self.capture: Optional[dict] = None
+        # learned offsets: plan the K/V window from the previous step's largest offset (no host wait;
+        # the kernels' halo-miss bit verifies the plan and the next call raises if it did not hold)
+        self._spec = _SpeculativeWindow() if speculative_window else None
 
     def forward(self, x: Tensor, video_shape: Tuple[int, int, int], extra_kv: Optional[Tensor] = None) -> Tensor:
         return self._run(x, video_shape, extra_kv, None, None)
@@ -557,5 +607,6 @@ class TimeShardedDSA3D(nn.Module):
         cfg.G = G
         cfg.offset_bound = offset_bound
         cfg.capture = self.capture
+        cfg.spec = self._spec
         with torch.autocast("cuda", enabled=False):
             return DSA3DShardedFunction.apply(cfg, x, extra_kv, offsets, *m._params())

@@ -30,7 +30,7 @@ def _fro(a, b):
     return float((a - b).norm() / b.norm().clamp_min(1e-30))
 
 
-def _worker(rank, world, port, dtype_name, q, B=1, inject=False):
+def _worker(rank, world, port, dtype_name, q, B=1, inject=False, speculative=False):
     import torch.distributed as dist
 
     import megaslide_b200 as msl
@@ -70,7 +70,12 @@ def _worker(rank, world, port, dtype_name, q, B=1, inject=False):
         own = shard_ranges(T, world)[rank]
         rows = slice(own[0] * H * W, own[1] * H * W)
         xs = x[:, rows].clone().requires_grad_(True)
-        sm = TimeShardedDSA3D(m)
+        sm = TimeShardedDSA3D(m, speculative_window=speculative)
+        if speculative:  # a first step plans exactly; the checked step below plans from its maximum
+            sm(xs.detach().clone().requires_grad_(True), (T, H, W)).backward(gy[:, rows])
+            torch.cuda.synchronize()
+            for p in m.parameters():
+                p.grad = None
         if off is None:
             ys = sm(xs, (T, H, W))
         else:
@@ -79,6 +84,7 @@ def _worker(rank, world, port, dtype_name, q, B=1, inject=False):
         torch.cuda.synchronize()
         res = {"y": _rel(ys, yf[:, rows]), "dx": _fro(xs.grad, xf.grad[:, rows]),
                "dx_max": _rel(xs.grad, xf.grad[:, rows])}
+        msl.check_status()  # raises if the speculative window missed a corner
         scale = max(float(rg.double().norm()) for rg in ref_grads if rg is not None)
         for (name, p), rg in zip(m.named_parameters(), ref_grads):
             if rg is None:  # the offset predictor with injected offsets: no gradient on either side
@@ -95,10 +101,12 @@ def _worker(rank, world, port, dtype_name, q, B=1, inject=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("dtype_name,tol,B,inject", [("float32", 1e-4, 1, False), ("bfloat16", 2e-2, 1, False),
-                                                     ("bfloat16", 2e-2, 2, True)])
-def test_time_sharded_matches_unsharded_on_two_gpus(dtype_name, tol, B, inject):
-    """Learned offsets (float32 and bf16), and injected offsets with a caller bound on a batch of 2."""
+@pytest.mark.parametrize("dtype_name,tol,B,inject,speculative", [
+    ("float32", 1e-4, 1, False, False), ("bfloat16", 2e-2, 1, False, False), ("bfloat16", 2e-2, 2, True, False),
+    ("bfloat16", 2e-2, 1, False, True)])
+def test_time_sharded_matches_unsharded_on_two_gpus(dtype_name, tol, B, inject, speculative):
+    """Learned offsets (float32 and bf16), injected offsets with a caller bound on a batch of 2, and the
+    speculative window (second step planned from the first step's largest offset)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -107,7 +115,8 @@ def test_time_sharded_matches_unsharded_on_two_gpus(dtype_name, tol, B, inject):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, dtype_name, q, B, inject)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, dtype_name, q, B, inject, speculative))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]

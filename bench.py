@@ -48,14 +48,15 @@ CONFIGS = {
     # the 1M-token long-sequence config: raw offsets ~N(0,1) clipped to +-3 injected in place of the
     # offset predictor's output (seeded per global frame, identical for every GPU count)
     "c4": dict(B=1, T=256, H=64, W=64, C=1536, nh=24, kernel=(3, 7, 7), dtype="bfloat16", clip=3.0),
-    # c4's widths and offsets on 16 frames: the case profiled with ncu
+    # c4's widths and offsets on 16 frames (timing probes) and on 8 frames (ncu captures: a few GB)
     "c4_prof": dict(B=1, T=16, H=64, W=64, C=1536, nh=24, kernel=(3, 7, 7), dtype="bfloat16", clip=3.0),
+    "c4_ncu": dict(B=1, T=8, H=64, W=64, C=1536, nh=24, kernel=(3, 7, 7), dtype="bfloat16", clip=3.0),
 }
 METRIC = "3D-DSA fwd+bwd Mtokens/s"
 # reduced-volume sample of a config timed on the CPU (same C, heads, window; fewer frames)
 CPU_SAMPLE = {"c1": dict(B=1, T=8, H=16, W=16), "c2": dict(B=1, T=8, H=16, W=16),
               "c2_prof": dict(B=1, T=8, H=16, W=16), "c4": dict(B=1, T=8, H=16, W=16),
-              "c4_prof": dict(B=1, T=8, H=16, W=16)}
+              "c4_prof": dict(B=1, T=8, H=16, W=16), "c4_ncu": dict(B=1, T=8, H=16, W=16)}
 
 
 # DiT step time with CPU-master streaming (the reference's MegaSlideDiT architecture:
@@ -207,6 +208,8 @@ class ClockSampler:
         self.file = None
 
     def start(self):
+        """Starts nvidia-smi and returns once it has written its first sample (its start-up queries the
+        driver and must not overlap a timed region), or after 10 s."""
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
@@ -214,6 +217,13 @@ class ClockSampler:
                                          stdout=self.file, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 10.0 and self.proc.poll() is None:
+            if os.path.getsize(self.file.name) > 0:
+                break
+            time.sleep(0.05)
+        time.sleep(0.25)
 
     def stop(self):
         if self.proc is None:
@@ -423,7 +433,9 @@ def time_steps(wl, steps, warmup, barrier, local, world, dev):
     barrier()
     sampler = ClockSampler(local)
     sampler.start()
-    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()  # every rank's sampler is up before the timed region
+    torch.cuda.synchronize()
     n0 = msl.launch_count()
     stream = torch.cuda.current_stream()
     e0 = torch.cuda.Event(enable_timing=True)

@@ -241,7 +241,7 @@ class _SpeculativeWindow:
         self.refresh()
         if self.known is None or not math.isfinite(self.known):
             return None
-        return self.known * 1.25 + 0.5
+        return self.known * 1.05 + 0.1
 
 
 class DSA3DShardedFunction(torch.autograd.Function):
@@ -280,8 +280,32 @@ class DSA3DShardedFunction(torch.autograd.Function):
         pend = start_exchange(xc, cw, xl, FramePlan(cfg.owns, cwins), fetch1, rank, cfg.group)
         wqkv = torch.cat([wq, wk, wv], 0).to(dt)
         bqkv = torch.cat([bq, bk, bv], 0).to(dt)
-        if cfg.offset_bound is not None:  # no host wait below: the projection overlaps the conv-halo exchange
-            qkv = torch.addmm(bqkv, xo2, wqkv.t())  # [own rows, 3C]
+
+        def kv_window(dmax_: float):
+            """K/V window of every rank (deterministic on all ranks) for a largest temporal offset; the
+            window buffer with the own projected rows in place; the frames every rank fetches."""
+            if not math.isfinite(dmax_):
+                raise FloatingPointError("non-finite offsets: the K/V halo cannot be bounded")
+            kw_ = [kv_frame_range(T, W, kt, o, dmax_) for o in cfg.owns]
+            kw_ = [(min(a[0], o[0]), max(a[1], o[1])) for a, o in zip(kw_, cfg.owns)]
+            buf = torch.empty(B, kw_[rank][1] - kw_[rank][0], HW, 2 * C, dtype=dt, device=x.device)
+            own_kv = qkv.view(B, nown, HW, 3 * C)[..., C:]
+            buf[:, own[0] - kw_[rank][0]:own[1] - kw_[rank][0]].copy_(own_kv)
+            fetch = [[iv for iv in ((kw_[s_][0], cfg.owns[s_][0]), (cfg.owns[s_][1], kw_[s_][1])) if iv[0] < iv[1]]
+                     for s_ in range(cfg.world)]
+            return kw_, buf, own_kv, fetch
+
+        # the K/V window is known before the offsets when the caller bounds them or when it is planned from
+        # the previous step (speculative): then the projected K/V halo rows travel while the offset
+        # predictor and the dw_conv term compute
+        spec_plan = cfg.spec.plan() if (cfg.spec is not None and cfg.offset_bound is None) else None
+        early = float(cfg.offset_bound) * abs(cfg.oscale) if cfg.offset_bound is not None else spec_plan
+        kv_pend = None
+        if early is not None:
+            qkv = torch.addmm(bqkv, xo2, wqkv.t())  # [own rows, 3C], overlapping the conv-halo exchange
+            dmax = early
+            kwins, kvw, kv_own, fetch2 = kv_window(dmax)
+            kv_pend = start_exchange(kvw, kwins[rank], kv_own, FramePlan(cfg.owns, kwins), fetch2, rank, cfg.group)
         pend.finish()
         xc2 = xc.view(-1, C)
         # 2. offsets and the dw_conv term of the own frames
@@ -302,17 +326,14 @@ class DSA3DShardedFunction(torch.autograd.Function):
             b2f = None
         wd_kc = ops.conv_weight_kc(wd)
         dwk = (wd_kc, bd.detach().float().contiguous(), bo.detach().float().contiguous())
-        spec_plan = cfg.spec.plan() if (cfg.spec is not None and cfg.offset_bound is None) else None
         if cfg.offset_bound is not None:
-            # the caller bounds |raw offset| (e.g. clipped synthetic offsets): the K/V window follows from the
+            # the caller bounds |raw offset| (e.g. clipped synthetic offsets): the K/V window followed from the
             # bound alone, with no reduction and no host synchronisation
-            dmax = float(cfg.offset_bound) * abs(cfg.oscale)
             D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
         elif spec_plan is not None:
-            # speculative window: planned from the previous step's maximum; this step's maximum is reduced
-            # and read back without waiting (the next step plans with it), and the kernels' halo-miss bit
-            # checks the plan exactly
-            dmax = spec_plan
+            # speculative window (planned from the previous step's maximum): this step's maximum is reduced
+            # and read back without waiting for the next step's plan; the kernels' halo-miss bit checks the
+            # plan exactly
             amax = ops.offsets_absmax(off, nh, kt * kh * kw, cfg.oscale, bias=b2f)
             dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=cfg.group)
             amax_h = torch.empty(3, dtype=torch.float32, pin_memory=True)
@@ -320,7 +341,6 @@ class DSA3DShardedFunction(torch.autograd.Function):
             ready = torch.cuda.Event()
             ready.record()
             cfg.spec.pending = (ready, amax_h)
-            qkv = torch.addmm(bqkv, xo2, wqkv.t())
             D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
         else:
             # the largest temporal offset over all ranks sizes every rank's K/V window: it is copied to pinned
@@ -338,21 +358,13 @@ class DSA3DShardedFunction(torch.autograd.Function):
             dmax = float(amax_h[2])
             if cfg.spec is not None:
                 cfg.spec.known = dmax
-        if not math.isfinite(dmax):
-            raise FloatingPointError("non-finite offsets: the K/V halo cannot be bounded")
-        # 3. K/V window of every rank (deterministic on all ranks): the own projected rows plus the halo
-        #    frames' rows from their owners
-        kwins = [kv_frame_range(T, W, kt, o, dmax) for o in cfg.owns]
-        kwins = [(min(k[0], o[0]), max(k[1], o[1])) for k, o in zip(kwins, cfg.owns)]
+            # 3. the K/V window: the own projected rows plus the halo frames' rows from their owners
+            kwins, kvw, kv_own, fetch2 = kv_window(dmax)
+            kv_pend = start_exchange(kvw, kwins[rank], kv_own, FramePlan(cfg.owns, kwins), fetch2, rank, cfg.group)
+        kv_pend.finish()
         kwin = kwins[rank]
         nkw = kwin[1] - kwin[0]
-        kvw = torch.empty(B, nkw, HW, 2 * C, dtype=dt, device=x.device)
-        kv_own = qkv.view(B, nown, HW, 3 * C)[..., C:]
-        kvw[:, own[0] - kwin[0]:own[1] - kwin[0]].copy_(kv_own)
         kplan = FramePlan(cfg.owns, kwins)
-        fetch2 = [[iv for iv in ((kwins[s][0], cfg.owns[s][0]), (cfg.owns[s][1], kwins[s][1])) if iv[0] < iv[1]]
-                  for s in range(cfg.world)]
-        exchange_into(kvw, kwin, kv_own, kplan, fetch2, rank, cfg.group)
         kv = kvw.view(-1, 2 * C)
         q = qkv[:, :C]
         k, v = kv[:, :C], kv[:, C:]
@@ -533,7 +545,7 @@ class TimeShardedDSA3D(nn.Module):
     offset and no host synchronisation.  ``capture``: as DeformableSlideAttention3D.capture.
 
     speculative_window=True (learned offsets): from the second step on, the K/V window is planned from
-    the previous step's largest temporal offset (times 1.25, plus 0.5) instead of waiting for this
+    the previous step's largest temporal offset (times 1.05, plus 0.1) instead of waiting for this
     step's; this step's maximum is still reduced on the device and read back for the next plan.  The
     plan is checked exactly: a sample corner outside the window sets MSL_STATUS_HALO_MISS, and the
     next call (or megaslide_b200.check_status()) raises MslError - a step whose offsets jumped past the

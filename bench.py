@@ -677,7 +677,8 @@ def run_c4_leg(args, world, rank, dev, barrier, local):
                     steps=steps, warmup=warmup, peak_mem_gb=peak / 1e9, fits_one_gpu=(world == 1) or None,
                     halo_frames_per_side=parity["halo_frames_max"] if parity else None,
                     kernels={n: {"ms_per_launch": v[0] / v[1], "launches": v[1]} for n, v in per.items()},
-                    roofline={k: roof[k] for k in ("kernel", "launch_ms", "achieved", "frac", "binding_roof")},
+                    roofline={k: roof[k] for k in ("kernel", "launch_ms", "achieved", "frac", "traffic",
+                                                   "waste_ratio", "binding_roof")},
                     clocks=clocks, gpu_launches=launches, parity=parity)
         del wl
     except torch.OutOfMemoryError as e:

@@ -222,23 +222,27 @@ class _ShardCfg:
 
 class _SpeculativeWindow:
     """The K/V window of a learned-offset step planned from the previous step's largest temporal
-    offset (exact, reduced over the ranks on the device and read back without waiting), widened by a
+    offset (exact, reduced over the ranks on the device and copied to pinned memory), widened by a
     margin.  Whether the plan held is checked exactly by the attention kernels: a sample corner in a
-    frame the window does not hold sets MSL_STATUS_HALO_MISS, which the next call raises."""
+    frame the window does not hold sets MSL_STATUS_HALO_MISS, which the next call raises.
+
+    Every rank must plan the same windows (they fix the sizes of the halo exchange), so the plan waits
+    for the previous step's reduced value instead of using whichever value happens to have arrived: the
+    wait ends once the GPU has passed that step's reduction, which lies early in its forward, while the
+    rest of that step (its backward included) is still queued behind it."""
 
     def __init__(self):
-        self.known: Optional[float] = None  # the last largest |temporal offset| read back
+        self.known: Optional[float] = None  # the previous step's largest |temporal offset|, all ranks
         self.pending: Optional[tuple] = None  # (event, pinned value) of the last step's maximum
 
-    def refresh(self) -> None:
-        if self.pending is not None and self.pending[0].query():
-            v = float(self.pending[1][2])
-            self.known = v if self.known is None else max(v, 0.0)
-            self.pending = None
-
     def plan(self) -> Optional[float]:
-        """The bound to plan with, or None when no earlier step's maximum is known yet."""
-        self.refresh()
+        """The bound to plan with, or None when no earlier step's maximum is known yet (the same on
+        every rank: each rank takes the same steps, and the value is reduced over all of them)."""
+        if self.pending is not None:
+            ready, value = self.pending
+            ready.synchronize()
+            self.known = float(value[2])
+            self.pending = None
         if self.known is None or not math.isfinite(self.known):
             return None
         return self.known * 1.05 + 0.1

@@ -11,8 +11,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from megaslide_b200.sharded import (FramePlan, conv_window, exchange_into, kv_frame_range, return_halo_grads,
-                                    shard_ranges)
+from megaslide_b200.sharded import (FramePlan, _SpeculativeWindow, conv_window, exchange_into, kv_frame_range,
+                                    return_halo_grads, shard_ranges)
 
 
 def test_shard_ranges_cover_the_volume():
@@ -113,3 +113,30 @@ def test_frame_exchange_two_gloo_ranks(T):
     for rank, ok_fwd, ok_bwd in res:
         assert ok_fwd, f"rank {rank}: forward window differs from the global volume"
         assert ok_bwd, f"rank {rank}: returned halo gradients do not sum up"
+
+
+class _SlowEvent:
+    """An event whose query() says 'not yet' until synchronize() is called (a GPU running behind)."""
+
+    def __init__(self):
+        self.done = False
+
+    def query(self):
+        return self.done
+
+    def synchronize(self):
+        self.done = True
+
+
+def test_speculative_plan_uses_the_previous_steps_value_on_every_rank():
+    """The window plan must not depend on how far a rank's GPU has got: each plan waits for the
+    previous step's reduced maximum, so ranks that run at different speeds plan the same window."""
+    spec = _SpeculativeWindow()
+    assert spec.plan() is None  # no step seen yet: the exact path
+    spec.known = 2.0  # the exact path of step 1 stores its reduced value
+    assert spec.plan() == pytest.approx(2.0 * 1.05 + 0.1)
+    spec.pending = (_SlowEvent(), torch.tensor([0.0, 0.0, 3.0]))  # step 2's value, copy still queued
+    assert spec.plan() == pytest.approx(3.0 * 1.05 + 0.1)
+    assert spec.pending is None
+    spec.pending = (_SlowEvent(), torch.tensor([0.0, 0.0, float("inf")]))  # non-finite: back to the exact path
+    assert spec.plan() is None

@@ -48,15 +48,23 @@ CONFIGS = {
     # the 1M-token long-sequence config: raw offsets ~N(0,1) clipped to +-3 injected in place of the
     # offset predictor's output (seeded per global frame, identical for every GPU count)
     "c4": dict(B=1, T=256, H=64, W=64, C=1536, nh=24, kernel=(3, 7, 7), dtype="bfloat16", clip=3.0),
-    # c4's widths and offsets on 16 frames (timing probes) and on 8 frames (ncu captures: a few GB)
+    # c4's widths and offsets on 16 frames (timing probes) and on 8 frames (ncu captures: a few GB).  The
+    # reference divides the offset that moves the time axis by W-1 and the one that moves the width axis
+    # by T-1, so fewer frames turn c4's +-6.1-frame temporal spread into a +-6.4 (T=16) or +-13.7 (T=8)
+    # column spread: these two cases have other envelopes than c4
     "c4_prof": dict(B=1, T=16, H=64, W=64, C=1536, nh=24, kernel=(3, 7, 7), dtype="bfloat16", clip=3.0),
     "c4_ncu": dict(B=1, T=8, H=64, W=64, C=1536, nh=24, kernel=(3, 7, 7), dtype="bfloat16", clip=3.0),
+    # bands of fewer rows keep T and W and so the sample spread of c2 / c4 (the height offsets do not depend
+    # on T or W; more samples clamp at the upper and lower border): the reduced cases that stand for them
+    "c2_band": dict(B=1, T=64, H=8, W=32, C=1152, nh=16, kernel=(3, 7, 7), dtype="bfloat16", ostd=0.05),
+    "c4_band": dict(B=1, T=256, H=8, W=64, C=1536, nh=24, kernel=(3, 7, 7), dtype="bfloat16", clip=3.0),
 }
 METRIC = "3D-DSA fwd+bwd Mtokens/s"
 # reduced-volume sample of a config timed on the CPU (same C, heads, window; fewer frames)
 CPU_SAMPLE = {"c1": dict(B=1, T=8, H=16, W=16), "c2": dict(B=1, T=8, H=16, W=16),
               "c2_prof": dict(B=1, T=8, H=16, W=16), "c4": dict(B=1, T=8, H=16, W=16),
-              "c4_prof": dict(B=1, T=8, H=16, W=16), "c4_ncu": dict(B=1, T=8, H=16, W=16)}
+              "c4_prof": dict(B=1, T=8, H=16, W=16), "c4_ncu": dict(B=1, T=8, H=16, W=16),
+              "c2_band": dict(B=1, T=8, H=16, W=16), "c4_band": dict(B=1, T=8, H=16, W=16)}
 
 
 # DiT step time with CPU-master streaming (the reference's MegaSlideDiT architecture:
@@ -625,7 +633,7 @@ def run_gpu(args):
     torch.cuda.empty_cache()
 
     c4 = None
-    if not args.no_c4 and args.config != "c4" and not args.config.endswith("_prof"):
+    if not args.no_c4 and args.config != "c4" and not args.config.endswith(("_prof", "_ncu", "_band")):
         c4 = run_c4_leg(args, world, rank, dev, barrier, local)
 
     status_bits = msl_status_bits()  # raises if any step of the run (c4 included) reported invalid results

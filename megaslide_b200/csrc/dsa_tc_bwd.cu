@@ -137,10 +137,11 @@ constexpr int kDqChannelGroups = 4;  // dQ product: channel ranges per row group
 // ------------------------------------------------------------------------------ chunk operands
 // accum[key][d] += A . X over the tiles of mask m: A = the transposed bf16 tile tb ([key][query], all
 // 32 queries, ldmatrix), X = 32 bf16 rows (Q or dO) in shared memory.  Items = (16-key tile, the
-// head's channel tiles, or half of them for even counts and head_dim > 72: registers), round robin
-// over the 16 warps: one A fragment serves every accumulator chain of the item (measured at
-// head_dim 72: whole-head items beat 3 or 5 channel tiles).  Each lane adds its fragment pairs to the float32 accumulator rows key_off[key]
-// with float2 atomics (no shuffles or zero tests: fewer instructions measured faster).
+// head's channel tiles when their count is odd and at most 9, else half of them), round robin over
+// the 16 warps: one A fragment serves every accumulator chain of the item (measured: at head_dim 72
+// whole-head items beat 3 or 5 channel tiles; at head_dim 64 half-head items beat whole-head ones,
+// the warps get twice the items).  Each lane adds its fragment pairs to the float32 accumulator rows
+// key_off[key] with float2 atomics, skipping the rows of keys no sample corner touched (all zero).
 template <int DCH>
 __device__ __forceinline__ void kv_product_flush(const AttnParams& P, const TileCtx& T, const TcLaunch& L,
                                                  const __nv_bfloat16* tb, const __nv_bfloat16* xs, const int* key_off,

@@ -52,9 +52,9 @@ extern "C" {
                                     with the CUDA-core gather instead, forward and backward alike, so
                                     the results are valid (informational) */
 #define MSL_STATUS_TIMEOUT 4u    /* tensor-core path: a CTA's TMA copies did not complete within a second;
-                                    it stopped waiting, skipped every phase that reads the copied keys,
-                                    and its results are not valid (copies it issued may have still been
-                                    in flight when it exited) */
+                                    it stopped waiting, waited at most one more second for the copies it
+                                    had issued, skipped every phase that reads the copied keys, and its
+                                    results are not valid */
 
 /* kernel family */
 #define MSL_ALGO_AUTO 0 /* tensor-core envelope kernels when supported (bf16, head_dim % 8 == 0, <= 128) */

@@ -704,10 +704,11 @@ __device__ __forceinline__ void issue_keys_tma(const AttnParams& P, const TileCt
 }
 
 // Waits for the TMA copies of phase `parity` on mbarrier bar.  Bounded: after about a second the CTA
-// stops waiting and issuing (flag *dead, status MSL_STATUS_TIMEOUT); after the CTA barrier that follows
-// every wait, the chunk loops read *dead (tile_dead) and leave before any phase that reads the key
-// buffer.  The tile's results are then invalid, and copies that were issued but never completed may
-// still be in flight when the CTA exits.
+// stops waiting and issuing (flag *dead, status MSL_STATUS_TIMEOUT); the thread that gave up then
+// waits once more, again for at most about a second, for the copies of that phase that were issued
+// (no later phase issues any), so that none lands in shared memory the SM may already have given to
+// the next CTA.  After the CTA barrier that follows every wait, the chunk loops read *dead
+// (tile_dead) and leave before any phase that reads the key buffer; the tile's results are invalid.
 __device__ __forceinline__ void wait_keys(uint32_t bar, uint32_t parity, volatile int* dead, uint32_t* status) {
   if (mbar_try_wait(bar, parity) || *dead) return;
   const unsigned long long t0 = global_ns();
@@ -716,6 +717,9 @@ __device__ __forceinline__ void wait_keys(uint32_t bar, uint32_t parity, volatil
     if (global_ns() - t0 > 1000000000ull) {
       *dead = 1;
       if (status) atomicOr(status, MSL_STATUS_TIMEOUT);
+      const unsigned long long t1 = global_ns();
+      while (!mbar_try_wait(bar, parity) && global_ns() - t1 < 1000000000ull) {
+      }
       return;
     }
   }

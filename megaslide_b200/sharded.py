@@ -110,9 +110,13 @@ def start_exchange(buf: Tensor, buf_range: Range, local: Tensor, plan: FramePlan
     """Starts filling the frames `fetch[rank]` of `buf` (frames `buf_range`, laid out [B, frames, HW, X])
     from their owners, and sending the own frames every other rank fetches.  `local` [B, own frames, HW, X]
     holds this rank's frames (any strides).  fetch[s] = frame intervals rank s wants (the same list on
-    every rank).  Returns the pending transfers; finish() lands them in `buf`."""
+    every rank).  Returns the pending transfers; finish() lands them in `buf`.
+
+    One message per sample: a sample's frames are contiguous in `buf` (and in `local` when its rows
+    are), so they are received in place and sent without a staging copy."""
     world = len(plan.owns)
     own = plan.owns[rank]
+    B = buf.shape[0]
     ops_: list = []
     recv_tmp = []
     for s in range(world):
@@ -121,23 +125,28 @@ def start_exchange(buf: Tensor, buf_range: Range, local: Tensor, plan: FramePlan
         for iv in fetch[s]:  # frames rank s wants that this rank owns
             ov = _overlap(iv, own)
             if ov:
-                t = local[:, ov[0] - own[0]:ov[1] - own[0]].contiguous()
-                ops_.append(dist.P2POp(dist.isend, t, s, group))
+                for b in range(B):
+                    t = local[b, ov[0] - own[0]:ov[1] - own[0]]
+                    ops_.append(dist.P2POp(dist.isend, t if t.is_contiguous() else t.contiguous(), s, group))
     for iv in fetch[rank]:
         for r in range(world):
             if r == rank:
                 continue
             ov = _overlap(iv, plan.owns[r])
             if ov:
-                t = torch.empty((buf.shape[0], ov[1] - ov[0]) + tuple(buf.shape[2:]), dtype=buf.dtype,
-                                device=buf.device)
-                ops_.append(dist.P2POp(dist.irecv, t, r, group))
-                recv_tmp.append((ov, t))
+                for b in range(B):
+                    dst = buf[b, ov[0] - buf_range[0]:ov[1] - buf_range[0]]
+                    if dst.is_contiguous():
+                        ops_.append(dist.P2POp(dist.irecv, dst, r, group))
+                    else:
+                        t = torch.empty(dst.shape, dtype=dst.dtype, device=dst.device)
+                        ops_.append(dist.P2POp(dist.irecv, t, r, group))
+                        recv_tmp.append((dst, t))
     reqs = dist.batch_isend_irecv(ops_) if ops_ else []
 
     def land():
-        for ov, t in recv_tmp:
-            buf[:, ov[0] - buf_range[0]:ov[1] - buf_range[0]].copy_(t)
+        for dst, t in recv_tmp:
+            dst.copy_(t)
 
     return _Pending(reqs, land)
 
@@ -152,9 +161,11 @@ def start_halo_return(dwin: Tensor, plan: FramePlan, rank: int, group=None) -> _
     """Reverse of the forward exchanges, started: sends the gradient rows of `dwin` ([B, window frames,
     HW, X], frames plan.windows[rank]) that belong to other ranks to their owners and receives what the
     other ranks computed for the own frames; finish() adds those into the own frames of `dwin` (in
-    place) and returns that view [B, own frames, HW, X]."""
+    place) and returns that view [B, own frames, HW, X].  One message per sample (contiguous rows: no
+    staging copy, and the adds run on contiguous blocks)."""
     world = len(plan.owns)
     win, own = plan.windows[rank], plan.owns[rank]
+    B = dwin.shape[0]
     ops_: list = []
     recvs = []
     for r in range(world):
@@ -162,19 +173,21 @@ def start_halo_return(dwin: Tensor, plan: FramePlan, rank: int, group=None) -> _
             continue
         ov = _overlap(win, plan.owns[r])
         if ov:
-            ops_.append(dist.P2POp(dist.isend, dwin[:, ov[0] - win[0]:ov[1] - win[0]].contiguous(), r, group))
+            for b in range(B):
+                src = dwin[b, ov[0] - win[0]:ov[1] - win[0]]
+                ops_.append(dist.P2POp(dist.isend, src if src.is_contiguous() else src.contiguous(), r, group))
         ov = _overlap(plan.windows[r], own)
         if ov:
-            t = torch.empty((dwin.shape[0], ov[1] - ov[0]) + tuple(dwin.shape[2:]), dtype=dwin.dtype,
-                            device=dwin.device)
-            ops_.append(dist.P2POp(dist.irecv, t, r, group))
-            recvs.append((ov, t))
+            for b in range(B):
+                t = torch.empty((ov[1] - ov[0],) + tuple(dwin.shape[2:]), dtype=dwin.dtype, device=dwin.device)
+                ops_.append(dist.P2POp(dist.irecv, t, r, group))
+                recvs.append((b, ov, t))
     reqs = dist.batch_isend_irecv(ops_) if ops_ else []
     mine = dwin[:, own[0] - win[0]:own[1] - win[0]]
 
     def add():
-        for ov, t in recvs:
-            mine[:, ov[0] - own[0]:ov[1] - own[0]] += t
+        for b, ov, t in recvs:
+            mine[b, ov[0] - own[0]:ov[1] - own[0]] += t
         return mine
 
     return _Pending(reqs, add)
@@ -278,7 +291,8 @@ class DSA3DShardedFunction(torch.autograd.Function):
         cwins = [conv_window(T, o, cpad) for o in cfg.owns]
         cw = cwins[rank]
         xc = torch.empty(B, cw[1] - cw[0], HW, C, dtype=dt, device=x.device)
-        xc[:, own[0] - cw[0]:own[1] - cw[0]].copy_(xl)
+        for b in range(B):  # per sample: contiguous blocks (vectorised copies)
+            xc[b, own[0] - cw[0]:own[1] - cw[0]].copy_(xl[b])
         fetch1 = [[iv for iv in ((cwins[s][0], cfg.owns[s][0]), (cfg.owns[s][1], cwins[s][1])) if iv[0] < iv[1]]
                   for s in range(cfg.world)]
         pend = start_exchange(xc, cw, xl, FramePlan(cfg.owns, cwins), fetch1, rank, cfg.group)
@@ -293,8 +307,8 @@ class DSA3DShardedFunction(torch.autograd.Function):
             kw_ = [kv_frame_range(T, W, kt, o, dmax_) for o in cfg.owns]
             kw_ = [(min(a[0], o[0]), max(a[1], o[1])) for a, o in zip(kw_, cfg.owns)]
             buf = torch.empty(B, kw_[rank][1] - kw_[rank][0], HW, 2 * C, dtype=dt, device=x.device)
-            own_kv = qkv.view(B, nown, HW, 3 * C)[..., C:]
-            buf[:, own[0] - kw_[rank][0]:own[1] - kw_[rank][0]].copy_(own_kv)
+            own_kv = buf[:, own[0] - kw_[rank][0]:own[1] - kw_[rank][0]]  # sent from here: contiguous per sample
+            own_kv.copy_(qkv.view(B, nown, HW, 3 * C)[..., C:])
             fetch = [[iv for iv in ((kw_[s_][0], cfg.owns[s_][0]), (cfg.owns[s_][1], kw_[s_][1])) if iv[0] < iv[1]]
                      for s_ in range(cfg.world)]
             return kw_, buf, own_kv, fetch
@@ -502,7 +516,9 @@ class DSA3DShardedFunction(torch.autograd.Function):
             buckets.add([g_wqkv, g_bqkv] + ([d_extra] if d_extra is not None else []))
             dx = _mm_f32(dqkv, wqkv)  # [own rows, C] float32
             dx_conv = conv_ret.finish()  # [B, nown, HW, C] float32
-            dx = dx.view(B, nown, HW, C).add_(dx_conv)
+            dx = dx.view(B, nown, HW, C)
+            for b in range(B):  # per sample: contiguous blocks (vectorised adds)
+                dx[b].add_(dx_conv[b])
             summed = buckets.wait()
         g_wo, g_bo, g_wd, g_bd = summed[0]
         i = 1

@@ -108,7 +108,7 @@ class DSA3DFunction(torch.autograd.Function):
         if probs is None:
             attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f, status=sw.word)
         sw.post()
-        y = torch.addmm(D, attn, wo.to(dt).t())
+        y = D.addmm_(attn, wo.to(dt).t())  # in place: D is not used again
         if cfg.capture is not None:
             cfg.capture.update(x2=x2, qkv=qkv, hact=hact, off=off, offset_bias=b2f, attn=attn, lse=lse, y=y)
         if train:

@@ -299,16 +299,25 @@ class DSA3DShardedFunction(torch.autograd.Function):
         wqkv = torch.cat([wq, wk, wv], 0).to(dt)
         bqkv = torch.cat([bq, bk, bv], 0).to(dt)
 
-        def kv_window(dmax_: float):
+        wq_, wkv = wqkv[:C], wqkv[C:]
+        bq_, bkv = bqkv[:C], bqkv[C:]
+
+        def kv_window(dmax_: float, kv_rows: Optional[Tensor] = None):
             """K/V window of every rank (deterministic on all ranks) for a largest temporal offset; the
-            window buffer with the own projected rows in place; the frames every rank fetches."""
+            window buffer with the own K/V rows in place (projected straight into it per sample, or copied
+            from `kv_rows` [own rows, 2C]); the frames every rank fetches."""
             if not math.isfinite(dmax_):
                 raise FloatingPointError("non-finite offsets: the K/V halo cannot be bounded")
             kw_ = [kv_frame_range(T, W, kt, o, dmax_) for o in cfg.owns]
             kw_ = [(min(a[0], o[0]), max(a[1], o[1])) for a, o in zip(kw_, cfg.owns)]
             buf = torch.empty(B, kw_[rank][1] - kw_[rank][0], HW, 2 * C, dtype=dt, device=x.device)
             own_kv = buf[:, own[0] - kw_[rank][0]:own[1] - kw_[rank][0]]  # sent from here: contiguous per sample
-            own_kv.copy_(qkv.view(B, nown, HW, 3 * C)[..., C:])
+            for b in range(B):
+                dst = own_kv[b].view(nown * HW, 2 * C)
+                if kv_rows is None:
+                    torch.addmm(bkv, xl[b].view(nown * HW, C), wkv.t(), out=dst)
+                else:
+                    dst.copy_(kv_rows[b * nown * HW:(b + 1) * nown * HW])
             fetch = [[iv for iv in ((kw_[s_][0], cfg.owns[s_][0]), (cfg.owns[s_][1], kw_[s_][1])) if iv[0] < iv[1]]
                      for s_ in range(cfg.world)]
             return kw_, buf, own_kv, fetch
@@ -320,7 +329,8 @@ class DSA3DShardedFunction(torch.autograd.Function):
         early = float(cfg.offset_bound) * abs(cfg.oscale) if cfg.offset_bound is not None else spec_plan
         kv_pend = None
         if early is not None:
-            qkv = torch.addmm(bqkv, xo2, wqkv.t())  # [own rows, 3C], overlapping the conv-halo exchange
+            # q and the own K/V rows (into the window buffer), overlapping the conv-halo exchange
+            q = torch.addmm(bq_, xo2, wq_.t())
             dmax = early
             kwins, kvw, kv_own, fetch2 = kv_window(dmax)
             kv_pend = start_exchange(kvw, kwins[rank], kv_own, FramePlan(cfg.owns, kwins), fetch2, rank, cfg.group)
@@ -370,24 +380,23 @@ class DSA3DShardedFunction(torch.autograd.Function):
             amax_h.copy_(amax, non_blocking=True)
             ready = torch.cuda.Event()
             ready.record()
-            qkv = torch.addmm(bqkv, xo2, wqkv.t())  # [own rows, 3C]: GPU work while the host waits
+            q = torch.addmm(bq_, xo2, wq_.t())  # GPU work while the host waits
+            kvo = torch.addmm(bkv, xo2, wkv.t())  # [own rows, 2C]
             D = ops.dwconv_fwd(convk, xc2, *dwk, epilogue=MSL_EPI_NONE)
             ready.synchronize()
             dmax = float(amax_h[2])
             if cfg.spec is not None:
                 cfg.spec.known = dmax
             # 3. the K/V window: the own projected rows plus the halo frames' rows from their owners
-            kwins, kvw, kv_own, fetch2 = kv_window(dmax)
+            kwins, kvw, kv_own, fetch2 = kv_window(dmax, kvo)
             kv_pend = start_exchange(kvw, kwins[rank], kv_own, FramePlan(cfg.owns, kwins), fetch2, rank, cfg.group)
         kv_pend.finish()
         kwin = kwins[rank]
         nkw = kwin[1] - kwin[0]
         kplan = FramePlan(cfg.owns, kwins)
         kv = kvw.view(-1, 2 * C)
-        q = qkv[:, :C]
         k, v = kv[:, :C], kv[:, C:]
         ek = ev = e2 = None
-        wkv = wqkv[C:]
         if G:
             e2 = extra_kv.reshape(B * G, C).to(dt).contiguous()
             ekv = torch.addmm(torch.cat([bk, bv], 0).to(dt), e2, wkv.t())
@@ -411,12 +420,12 @@ class DSA3DShardedFunction(torch.autograd.Function):
         if probs is None:
             attn, lse = ops.attn_fwd(sh, q, k, v, off, ek, ev, offset_bias=b2f, status=sw.word)
         sw.post()
-        y = torch.addmm(D, attn, wo.to(dt).t())
+        y = D.addmm_(attn, wo.to(dt).t())  # in place: D is not used again
         if cfg.capture is not None:
             cfg.capture.update(xw=xc, xwin=cw, kvwin=kwin, own=own, q=q, kv=kv, hact=hact, off=off, offset_bias=b2f,
                                attn=attn, lse=lse, y=y)
         if train:
-            ctx.save_for_backward(xc, qkv, kv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f,
+            ctx.save_for_backward(xc, xl, q, kv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f,
                                   wd_kc, probs, saved)
             ctx.cfg, ctx.sh, ctx.kplan, ctx.cplan = cfg, sh, kplan, FramePlan(cfg.owns, cwins)
             ctx.in_dtype = x.dtype
@@ -426,7 +435,7 @@ class DSA3DShardedFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        (xc, qkv, kv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
+        (xc, xl, q, kv, hact, off, b2f, attn, lse, e2, ek, ev, wqkv, wo, w2m, w1_kc, b1f, wd_kc, probs,
          saved) = ctx.saved_tensors
         cfg: _ShardCfg = ctx.cfg
         sh: ops.DsaShape = ctx.sh
@@ -442,18 +451,18 @@ class DSA3DShardedFunction(torch.autograd.Function):
         kt, kh, kw = cfg.kernel
         G = cfg.G
         xc2 = xc.view(-1, C)
-        xo2 = xc[:, own[0] - cw[0]:own[1] - cw[0]].reshape(-1, C)
+        xo2 = xl.view(-1, C)  # the own frames, contiguous
         with torch.autocast("cuda", enabled=False):
             dy2 = dy.reshape(-1, C).to(dt).contiguous()
             dattn = torch.mm(dy2, wo.to(dt))
             # attention core: dq on the own rows into the [own rows, 3C] gradient buffer, dK / dV accumulated
             # in float32 over the K/V window; the window's halo rows go back to their owners while the
             # out_proj and dw_conv gradients run
-            dqkv = torch.empty_like(qkv)
+            dqkv = torch.empty(q.shape[0], 3 * C, dtype=q.dtype, device=q.device)
             dkv_acc = torch.zeros(B * nkw * HW, 2 * C, dtype=torch.float32, device=xc.device)
             k, v = kv[:, :C], kv[:, C:]
             sw = ops.status_word(xc.device)
-            _, _, _, doff, dek, dev = ops.attn_bwd(sh, qkv[:, :C], k, v, off, attn, lse, dattn, ek=ek, ev=ev,
+            _, _, _, doff, dek, dev = ops.attn_bwd(sh, q, k, v, off, attn, lse, dattn, ek=ek, ev=ev,
                                                    dq=dqkv[:, :C], dk_acc=dkv_acc[:, :C], dv_acc=dkv_acc[:, C:],
                                                    probs=probs, saved=saved, doff_dtype=dt, offset_bias=b2f,
                                                    status=sw.word)

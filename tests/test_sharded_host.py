@@ -1,6 +1,6 @@
 """Host logic of the time-sharded path (megaslide_b200/sharded.py), on CPU: the frame plan, the K/V
-halo bound (against a brute-force float32 evaluation of the reference's coordinate formulas), and
-the two exchange steps run as two gloo ranks (world_size 2) on CPU tensors."""
+halo bound (against a brute-force float32 evaluation of the reference's coordinate formulas), the
+two exchange steps run as 2 and 4 gloo ranks on CPU tensors, and the speculative window plan."""
 
 import os
 import socket
@@ -61,7 +61,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, T, HW, C, q):
+def _worker(rank, world, port, T, HW, C, q, strided_local=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -71,6 +71,8 @@ def _worker(rank, world, port, T, HW, C, q):
         owns = shard_ranges(T, world)
         own = owns[rank]
         local = g[:, own[0]:own[1]].contiguous()
+        if strided_local:  # the own rows as a column slice of a wider buffer (like q/k/v views of one GEMM)
+            local = torch.cat([torch.zeros_like(local), local], dim=-1)[..., C:]
         # forward: windows of different sizes per rank, fetched in two phases as the module does
         cw = [conv_window(T, o, 1) for o in owns]
         wins = [conv_window(T, o, 3 if r % 2 == 0 else 2) for r, o in enumerate(owns)]
@@ -97,13 +99,15 @@ def _worker(rank, world, port, T, HW, C, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T", [8, 5])
-def test_frame_exchange_two_gloo_ranks(T):
-    world = 2
+@pytest.mark.parametrize("world,T,strided", [(2, 8, False), (2, 5, True), (4, 12, False), (4, 9, True)])
+def test_frame_exchange_gloo_ranks(world, T, strided):
+    """Forward window fill and backward halo return on 2 and 4 CPU ranks (4: interior ranks with two
+    neighbours; T=9: windows that reach past a neighbour's 2-frame shard), B = 2, contiguous and
+    column-strided own rows."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, T, 3, 2, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T, 3, 2, q, strided)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(world)]

@@ -1,6 +1,7 @@
 """Host logic of the time-sharded path (megaslide_b200/sharded.py), on CPU: the frame plan, the K/V
 halo bound (against a brute-force float32 evaluation of the reference's coordinate formulas), the
-two exchange steps run as 2 and 4 gloo ranks on CPU tensors, and the speculative window plan."""
+two exchange steps run as 2 and 4 gloo ranks on CPU tensors, the speculative window plan and the
+parameter-gradient buckets (3 gloo ranks)."""
 
 import os
 import socket
@@ -11,8 +12,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from megaslide_b200.sharded import (FramePlan, _SpeculativeWindow, conv_window, exchange_into, kv_frame_range,
-                                    return_halo_grads, shard_ranges)
+from megaslide_b200.sharded import (FramePlan, _GradBuckets, _SpeculativeWindow, conv_window, exchange_into,
+                                    kv_frame_range, return_halo_grads, shard_ranges)
 
 
 def test_shard_ranges_cover_the_volume():
@@ -144,3 +145,41 @@ def test_speculative_plan_uses_the_previous_steps_value_on_every_rank():
     assert spec.pending is None
     spec.pending = (_SlowEvent(), torch.tensor([0.0, 0.0, float("inf")]))  # non-finite: back to the exact path
     assert spec.plan() is None
+
+
+def _bucket_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        b = _GradBuckets(None)
+        parts1 = [torch.full((3, 2), float(rank + 1)), torch.arange(4, dtype=torch.float32) * (rank + 1)]
+        parts2 = [torch.full((5,), 0.5 * (rank + 1), dtype=torch.bfloat16)]  # summed in float32
+        b.add(parts1)
+        b.add(parts2)
+        out = b.wait()
+        tot = sum(range(1, world + 1))
+        ok = (len(out) == 2 and [t.shape for t in out[0]] == [(3, 2), (4,)] and out[1][0].shape == (5,)
+              and torch.equal(out[0][0], torch.full((3, 2), float(tot)))
+              and torch.equal(out[0][1], torch.arange(4, dtype=torch.float32) * tot)
+              and out[1][0].dtype == torch.float32 and torch.allclose(out[1][0], torch.full((5,), 0.5 * tot)))
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_buckets_sum_over_ranks():
+    """Parameter-gradient buckets: each bucket's all-reduce starts when it is added; wait() hands back
+    every bucket's float32 sums in the shapes that went in, the same on every rank."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bucket_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok in res), res

@@ -760,9 +760,12 @@ def run_dit(args):
     sampler.start()
     time.sleep(0.3)
     n0, h0, d0 = msl.launch_count(), trainer.h2d_bytes, trainer.d2h_bytes
+    from megaslide_b200 import ops
+
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        loss = step(record=True)
+    with ops.kernel_timer() as rec:  # device time of this library's entry points inside the steps
+        for _ in range(args.steps):
+            loss = step(record=True)
     t_drain = time.perf_counter()
     trainer.get_parameters()  # the last step's host AdamW is part of the step
     phases["final_drain_s"] = time.perf_counter() - t_drain
@@ -770,6 +773,12 @@ def run_dit(args):
     sec = (time.perf_counter() - t0) / args.steps
     clocks = sampler.stop()
     launches = msl.launch_count() - n0
+    per = {}
+    for name, s_ev, e_ev in rec:
+        tot, cnt = per.get(name, (0.0, 0))
+        per[name] = (tot + s_ev.elapsed_time(e_ev), cnt + 1)
+    kernels = {n: {"ms_per_step": t / args.steps, "launches_per_step": c / args.steps}
+               for n, (t, c) in sorted(per.items(), key=lambda kv: -kv[1][0])}
     h2d = (trainer.h2d_bytes - h0) / args.steps
     d2h = (trainer.d2h_bytes - d0) / args.steps
     tokens = cfg.num_patches
@@ -806,6 +815,7 @@ def run_dit(args):
                    "weight_bytes_per_step": h2d, "grad_bytes_per_step": d2h, "loss": loss,
                    "timeline": timeline},
         "phases_per_step": {k: v / (1 if k == "final_drain_s" else args.steps) for k, v in phases.items()},
+        "kernels": kernels,
         "host": _host_memory(),
         "clocks": clocks, "gpu_launches": launches,
     }
